@@ -1,0 +1,160 @@
+/*
+ * ddtree_b200 — C ABI of the B200 (sm_100a) DDTree verification hot path.
+ *
+ * All entry points take raw device pointers, sizes/strides and a cudaStream_t (passed
+ * as void*), launch asynchronously on that stream, never allocate, never synchronise
+ * the host, and return 0 or a negative DDT_ERR_* code.  Buffers (outputs and the
+ * workspaces sized by the *_workspace_bytes queries) are owned by the caller.
+ * Entry points are stateless and reentrant; concurrent calls must use distinct
+ * workspaces.
+ *
+ * Reference interfaces replaced (paths are files of the DDTree research code):
+ *   ddt_topk_tree        ddtree.py:84-166  build_ddtree_tree (fp32 topk + logsumexp,
+ *                        best-first heap, visibility) fused with ddtree.py:227-267
+ *                        compile_ddtree_tree (verify ids / positions); the visibility
+ *                        matrix becomes per-node ancestor bitmasks
+ *   ddt_argmax           model/utils.py:28-30  sample() at temperature 0
+ *                        (torch.argmax over [N, V] logits, ddtree.py:478)
+ *   ddt_accept_compact   ddtree.py:270-281 follow_verified_tree fused with
+ *                        ddtree.py:284-335 compact_dynamic_cache
+ *   ddt_compact_kv       ddtree.py:31-58 compact_tail_inplace (inline C++ extension)
+ *                        applied to every layer's K and V in one launch
+ *   ddt_tree_attn        transformers/integrations/sdpa_attention.py:40-103
+ *                        (scaled_dot_product_attention with the additive tree mask of
+ *                        ddtree.py:262-264), reached from the verify forward at
+ *                        ddtree.py:467 through transformers' attention registry
+ *   ddt_attn_merge       no reference counterpart: merges split-KV partial results
+ *                        (within one GPU, and across GPUs after an NCCL exchange)
+ *   ddt_mask_to_bits     ddtree.py:262-264 read backwards: additive mask block ->
+ *                        ancestor bitmasks, for callers that only hold the mask
+ */
+#ifndef DDTREE_B200_H_
+#define DDTREE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define DDT_OK 0
+#define DDT_ERR_INVALID (-1)   /* bad argument: null pointer, negative size, bad stride */
+#define DDT_ERR_CAPACITY (-2)  /* exceeds a compiled limit (budget, depth, nodes, ...) */
+#define DDT_ERR_DTYPE (-3)     /* unsupported element type */
+#define DDT_ERR_ALIGN (-4)     /* pointer or stride misaligned for vector / TMA access */
+#define DDT_ERR_CUDA (-5)      /* CUDA runtime / launch error */
+#define DDT_ERR_TIMEOUT (-6)   /* a bounded device-side wait expired (status word) */
+#define DDT_ERR_WORKSPACE (-7) /* workspace too small */
+
+/* element types */
+#define DDT_F32 0
+#define DDT_BF16 1
+
+/* compiled limits */
+#define DDT_MAX_BUDGET 1024 /* tree nodes excluding the root */
+#define DDT_MAX_DEPTH 20    /* drafted depths (block_size - 1) */
+#define DDT_MAX_NODES (DDT_MAX_BUDGET + 1)
+
+const char* ddt_error_string(int code);
+int ddt_version(void);
+
+/* ---- tree construction --------------------------------------------------
+ * draft_logits: [depths, vocab] (row stride `row_stride` elements), dtype DDT_F32 or
+ * DDT_BF16.  k = min(budget, vocab).  Outputs (device):
+ *   top_log_probs f32 [depths, k], top_token_ids i64 [depths, k]   (may be NULL)
+ *   node_token_ids i64 [budget], node_depths i64 [budget], parents i32 [budget + 1]
+ *   node_count i32 [1]
+ *   anc_bits u32 [budget + 1, anc_words]  (bit j of row i: node j is an ancestor-or-self
+ *                                          of node i; anc_words >= ceil((budget+1)/32))
+ *   verify_ids i64 [budget + 1], verify_pos i64 [budget + 1]  (may be NULL; root token
+ *   read from root_token (device i64), positions start + depth)
+ * The workspace must be zero-filled before its first use; every launch leaves its
+ * counters at zero again. */
+size_t ddt_topk_tree_workspace_bytes(int64_t depths, int64_t vocab, int64_t budget);
+int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths, int64_t vocab,
+                  int64_t row_stride, int64_t budget, float* top_log_probs,
+                  int64_t* top_token_ids, int64_t* node_token_ids, int64_t* node_depths,
+                  int32_t* parents, int32_t* node_count, uint32_t* anc_bits,
+                  int64_t anc_words, const int64_t* root_token, int64_t start,
+                  int64_t* verify_ids, int64_t* verify_pos, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* ---- greedy posterior ---------------------------------------------------
+ * logits [rows, cols] (row stride in elements) -> out i64 [rows]; ties go to the lowest
+ * index, NaN counts as the largest value. */
+int ddt_argmax(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t row_stride,
+               int64_t* out, void* stream);
+
+/* ---- accept walk + KV compaction ----------------------------------------
+ * KV cache: n_tensors tensors (K and V of every layer) whose device base pointers are in
+ * the DEVICE array kv_ptrs; each is [heads, seq, head_dim] with the given element
+ * strides (head_dim contiguous), element size elem_bytes (2 or 4).  The tree window
+ * starts at row past_length.
+ * ddt_accept_compact: walks the tree from the root following posterior (i64 [n_nodes])
+ * through parents / node_token_ids (node i >= 1 carries node_token_ids[i - 1]), writes
+ * accepted (i64, capacity n_nodes), n_accepted (i32), next_token (i64), and moves cache
+ * rows past_length + accepted[j] to past_length + j in every tensor.
+ * ddt_compact_kv: the same move for a given keep list (device i64 [keep_count]). */
+int ddt_accept_compact(const int64_t* posterior, const int32_t* parents,
+                       const int64_t* node_token_ids, int64_t n_nodes, void* const* kv_ptrs,
+                       int64_t n_tensors, int64_t heads, int64_t head_dim, int64_t head_stride,
+                       int64_t seq_stride, int64_t elem_bytes, int64_t past_length,
+                       int64_t* accepted, int32_t* n_accepted, int64_t* next_token,
+                       void* stream);
+int ddt_compact_kv(const int64_t* keep, int64_t keep_count, void* const* kv_ptrs,
+                   int64_t n_tensors, int64_t heads, int64_t head_dim, int64_t head_stride,
+                   int64_t seq_stride, int64_t elem_bytes, int64_t past_length, void* stream);
+
+/* ---- tree attention -----------------------------------------------------
+ * q: [n_nodes, q_heads, head_dim] bf16 at element strides (q_node_stride, q_head_stride);
+ * k, v: [kv_heads, past_length + n_nodes, head_dim] bf16 at (kv_head_stride,
+ * kv_seq_stride); out: [n_nodes, q_heads, head_dim] bf16 at (o_node_stride,
+ * o_head_stride).  head_dim must be 128; q_heads a multiple of kv_heads.
+ * mask_mode DDT_MASK_TREE: node i sees every prefix key and the tree keys of its
+ * ancestors-or-self (anc_bits [n_nodes, anc_words]); DDT_MASK_CAUSAL: node i sees keys
+ * < past_length + i + 1 (anc_bits unused).
+ * kv_splits: number of KV partitions per (head, query tile); 0 picks one.  Partial
+ * results go to the workspace and are merged in the same call.
+ * status: device i32 (zeroed by the caller), set non-zero if a bounded wait expired. */
+#define DDT_MASK_TREE 0
+#define DDT_MASK_CAUSAL 1
+size_t ddt_tree_attn_workspace_bytes(int64_t n_nodes, int64_t q_heads, int64_t head_dim,
+                                     int64_t kv_splits);
+int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride, const void* k,
+                  const void* v, int64_t kv_head_stride, int64_t kv_seq_stride, void* out,
+                  int64_t o_node_stride, int64_t o_head_stride, int64_t n_nodes,
+                  int64_t past_length, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                  const uint32_t* anc_bits, int64_t anc_words, int mask_mode, float scale,
+                  int64_t kv_splits, void* workspace, size_t workspace_bytes, int32_t* status,
+                  void* stream);
+
+/* Partial-result attention: like ddt_tree_attn but writes un-normalised fp32 partials
+ * (o_part [n_nodes, q_heads, head_dim], row max m and row sum l [n_nodes, q_heads]) over
+ * the key range [key_begin, key_end) of this shard, for a cross-GPU split-KV merge.
+ * Keys are indexed globally: this shard's k/v pointers address key key_begin. */
+int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                          const void* k, const void* v, int64_t kv_head_stride,
+                          int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
+                          float* o_part, float* m_part, float* l_part, int64_t n_nodes,
+                          int64_t past_length, int64_t q_heads, int64_t kv_heads,
+                          int64_t head_dim, const uint32_t* anc_bits, int64_t anc_words,
+                          int mask_mode, float scale, int32_t* status, void* stream);
+
+/* Merge n_parts partials laid out [n_parts, rows, head_dim] / [n_parts, rows]
+ * (rows = n_nodes * q_heads) into out (bf16, [n_nodes, q_heads, head_dim] at the given
+ * strides). */
+int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_parts,
+                   int64_t n_parts, int64_t n_nodes, int64_t q_heads, int64_t head_dim,
+                   void* out, int64_t o_node_stride, int64_t o_head_stride, void* stream);
+
+/* additive mask block [n_nodes, n_nodes] (row stride in elements; 0 = visible) ->
+ * anc_bits [n_nodes, anc_words]. */
+int ddt_mask_to_bits(const void* mask, int dtype, int64_t n_nodes, int64_t row_stride,
+                     uint32_t* anc_bits, int64_t anc_words, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DDTREE_B200_H_ */

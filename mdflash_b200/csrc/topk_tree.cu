@@ -1,0 +1,686 @@
+// Draft-tree construction: per-depth log Z + top-k over the vocabulary, best-first
+// expansion and ancestor bitmasks, in ONE launch.
+//
+// Replaces build_ddtree_tree (ddtree.py:84-166) and the id / position part of
+// compile_ddtree_tree (ddtree.py:248-257).  The reference sorts on the device, copies
+// the top-k to the host and runs a Python heapq loop plus an O(N^2) numpy visibility
+// loop; here everything stays on the device.
+//
+// Grid: depths x chunks CTAs of 512 threads.
+//   phase 1 (every CTA): one chunk of one depth row is read once from HBM (16-byte
+//     vector loads), giving the chunk max, sum exp(x - max) in double, and the exact
+//     top-k of the chunk under the canonical order (value desc, index asc) by a
+//     radix select on the 64-bit composite (order key << 32 | ~index).
+//   phase 2 (last CTA of a row, by atomic counter): merges the chunks' candidates,
+//     log Z = max + log(sum) in double rounded once to float, top log-probs
+//     lp = value - logZ in float (ddtree.py:109), sorted by the canonical order.
+//   phase 3 (last row to finish): one warp replays the reference heap exactly
+//     (ddtree.py:116-147: keys (-logw, rank tuple) with logw accumulated in double in
+//     the reference's operation order), then all threads emit node ids, depths,
+//     parents, verify ids / positions and the ancestor bitmasks.
+// No CTA waits on another (last-arriver pattern only), so nothing can hang.
+#include <float.h>
+
+#include "common.cuh"
+
+namespace ddt {
+namespace topk {
+
+constexpr int kThreads = 512;
+constexpr int kEPT = 32;                    // elements per thread held in registers
+constexpr int kChunk = kThreads * kEPT;     // max elements per chunk (16384)
+constexpr int kMaxCand = kThreads * kEPT;   // max candidates merged per row
+constexpr int kRankBits = 12;               // bits per level in the packed rank tuple
+constexpr int kLevelsPerWord = 5;
+
+struct RadixShared {
+  uint32_t hist[256];
+  uint32_t warp_tot[8];
+  unsigned long long prefix;
+  unsigned long long mask;
+  uint32_t remaining;
+  int done;
+  uint32_t out_count;
+  int is_last;
+  float fred[32];
+  double dred[32];
+};
+
+struct WsLayout {
+  size_t counters, chunk_max, chunk_sum, cand, cand_count, top_lp, top_ids, total;
+};
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+__host__ __device__ inline int num_chunks(int64_t vocab) {
+  return static_cast<int>((vocab + kChunk - 1) / kChunk);
+}
+__host__ __device__ inline int64_t chunk_len(int64_t vocab, int chunks) {
+  int64_t c = (vocab + chunks - 1) / chunks;
+  return (c + 7) / 8 * 8;
+}
+
+__host__ __device__ inline WsLayout ws_layout(int64_t L, int64_t V, int64_t k) {
+  const int C = num_chunks(V);
+  WsLayout w;
+  size_t o = 0;
+  w.counters = o;   o = align_up(o + sizeof(uint32_t) * (L + 1), 256);
+  w.chunk_max = o;  o = align_up(o + sizeof(float) * L * C, 256);
+  w.chunk_sum = o;  o = align_up(o + sizeof(double) * L * C, 256);
+  w.cand = o;       o = align_up(o + sizeof(unsigned long long) * L * C * k, 256);
+  w.cand_count = o; o = align_up(o + sizeof(uint32_t) * L * C, 256);
+  w.top_lp = o;     o = align_up(o + sizeof(float) * L * k, 256);
+  w.top_ids = o;    o = align_up(o + sizeof(uint32_t) * L * k, 256);
+  w.total = o;
+  return w;
+}
+
+// dynamic shared memory: max over the merge phase and the heap phase
+__host__ inline size_t smem_bytes(int64_t L, int64_t k, int64_t budget) {
+  int64_t kpad = 1;
+  while (kpad < k) kpad <<= 1;
+  size_t merge = sizeof(unsigned long long) * kpad;
+  const int64_t fcap = budget + 1;
+  size_t heap = align_up(sizeof(float) * L * k, 16) + sizeof(double) * fcap +
+                4 * sizeof(unsigned long long) * fcap + sizeof(uint32_t) * fcap +
+                sizeof(uint32_t) * budget;
+  return align_up(merge > heap ? merge : heap, 16);
+}
+
+// ---- block radix select over register-resident 64-bit composites ----------------
+// Finds (prefix, mask) such that exactly `k` valid composites satisfy
+// (c & mask) >= prefix.  Composites are unique; 0 marks an invalid slot.
+// Radix passes run over the value key first, then over the index bits.  bf16 keys
+// occupy bits 63..48 only (bits 47..32 are zero), so their passes skip that byte pair.
+template <bool kBF16>
+__device__ __forceinline__ int pass_shift(int p) {
+  if (kBF16) return p < 2 ? 56 - 8 * p : 24 - 8 * (p - 2);
+  return 56 - 8 * p;
+}
+template <bool kBF16>
+__device__ __forceinline__ int num_passes() { return kBF16 ? 6 : 8; }
+
+template <int EPT, bool kBF16>
+__device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, RadixShared& s) {
+  const int npass = num_passes<kBF16>();
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  if (tid == 0) {
+    s.prefix = 0ull;
+    s.mask = 0ull;
+    s.remaining = k;
+    s.done = 0;
+  }
+  __syncthreads();
+  for (int p = 0; p < npass; ++p) {
+    if (s.done) break;
+    const int sh = pass_shift<kBF16>(p);
+    if (tid < 256) s.hist[tid] = 0;
+    __syncthreads();
+    const unsigned long long prefix = s.prefix, mask = s.mask;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const bool act = comp[j] != 0ull && (comp[j] & mask) == prefix;
+      const uint32_t digit = static_cast<uint32_t>(comp[j] >> sh) & 255u;
+      const unsigned am = __ballot_sync(DDT_FULL_MASK, act);
+      if (act) {
+        const unsigned peers = __match_any_sync(am, digit);
+        if (lane == __ffs(peers) - 1) atomicAdd(&s.hist[digit], static_cast<uint32_t>(__popc(peers)));
+      }
+    }
+    __syncthreads();
+    uint32_t v = 0, x = 0;
+    if (tid < 256) {
+      v = s.hist[255 - tid];
+      x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(DDT_FULL_MASK, x, o);
+        if (lane >= o) x += y;
+      }
+      if (lane == 31) s.warp_tot[tid >> 5] = x;
+    }
+    __syncthreads();
+    if (tid < 256) {
+      uint32_t base = 0;
+      for (int w = 0; w < (tid >> 5); ++w) base += s.warp_tot[w];
+      const uint32_t cum = base + x;
+      const uint32_t prev = cum - v;
+      const uint32_t rem = s.remaining;
+      if (prev < rem && cum >= rem) {
+        const uint32_t b = 255u - tid;
+        const uint32_t nrem = rem - prev;
+        s.prefix = prefix | (static_cast<unsigned long long>(b) << sh);
+        s.mask = mask | (255ull << sh);
+        s.remaining = nrem;
+        if (v == nrem) s.done = 1;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__device__ __forceinline__ bool selected(unsigned long long c, const RadixShared& s) {
+  return c != 0ull && (c & s.mask) >= s.prefix;
+}
+
+__device__ __forceinline__ float block_max_f(float v, RadixShared& s) {
+  v = warp_max_f(v);
+  if ((threadIdx.x & 31) == 0) s.fred[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float w = threadIdx.x < (blockDim.x >> 5) ? s.fred[threadIdx.x] : -INFINITY;
+    w = warp_max_f(w);
+    if (threadIdx.x == 0) s.fred[0] = w;
+  }
+  __syncthreads();
+  float r = s.fred[0];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ double block_sum_d(double v, RadixShared& s) {
+  v = warp_sum_d(v);
+  if ((threadIdx.x & 31) == 0) s.dred[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double w = threadIdx.x < (blockDim.x >> 5) ? s.dred[threadIdx.x] : 0.0;
+    w = warp_sum_d(w);
+    if (threadIdx.x == 0) s.dred[0] = w;
+  }
+  __syncthreads();
+  double r = s.dred[0];
+  __syncthreads();
+  return r;
+}
+
+// ---- packed rank tuples -------------------------------------------------------------
+// Level j (0-based) holds rank + 1 in 12 bits of word j / 5, most significant level
+// first, so comparing the 4 words as unsigned integers equals Python's tuple order
+// (element-wise, a shorter prefix first).
+__device__ __forceinline__ int rank_shift(int level) {
+  return (kLevelsPerWord - 1 - level % kLevelsPerWord) * kRankBits + 4;
+}
+
+struct Frontier {
+  double* logw;
+  unsigned long long* r;  // [4][fcap]
+  uint32_t* meta;         // parent | depth << 12 | rank << 17
+  int fcap;
+  __device__ unsigned long long& rw(int w, int s) { return r[w * fcap + s]; }
+};
+
+__device__ __forceinline__ uint32_t pack_meta(int parent, int depth, int rank) {
+  return static_cast<uint32_t>(parent) | (static_cast<uint32_t>(depth) << 12) |
+         (static_cast<uint32_t>(rank) << 17);
+}
+
+__device__ __forceinline__ bool ranks_less(const unsigned long long (&a)[4],
+                                           const unsigned long long (&b)[4]) {
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    if (a[w] != b[w]) return a[w] < b[w];
+  }
+  return false;
+}
+
+// One warp replays ddtree.py:116-147.  Returns the node count (on every lane).
+__device__ int heap_build(const float* lp, int L, int k, int budget, Frontier f,
+                          uint32_t* node_meta) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) {
+    f.logw[0] = static_cast<double>(lp[0]);
+    f.rw(0, 0) = 1ull << rank_shift(0);
+    f.rw(1, 0) = 0ull;
+    f.rw(2, 0) = 0ull;
+    f.rw(3, 0) = 0ull;
+    f.meta[0] = pack_meta(0, 1, 0);
+  }
+  __syncwarp();
+  int count = 0, fcount = 1;
+  while (count < budget && fcount > 0) {
+    // lane-local best among slots lane, lane + 32, ...
+    int bs = -1;
+    double bl = -DBL_MAX;
+    for (int s = lane; s < fcount; s += 32) {
+      const double x = f.logw[s];
+      bool take = (bs < 0) || (x > bl);
+      if (!take && x == bl) {
+        unsigned long long ra[4] = {f.rw(0, s), f.rw(1, s), f.rw(2, s), f.rw(3, s)};
+        unsigned long long rb[4] = {f.rw(0, bs), f.rw(1, bs), f.rw(2, bs), f.rw(3, bs)};
+        take = ranks_less(ra, rb);
+      }
+      if (take) {
+        bs = s;
+        bl = x;
+      }
+    }
+    double m = (bs >= 0) ? bl : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(DDT_FULL_MASK, m, o));
+    const unsigned tied = __ballot_sync(DDT_FULL_MASK, bs >= 0 && bl == m);
+    int wl;
+    if (__popc(tied) == 1) {
+      wl = __ffs(tied) - 1;
+    } else {
+      const bool mine = (tied >> lane) & 1u;
+      unsigned long long r[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) r[w] = mine ? f.rw(w, bs) : ~0ull;
+      int cand = mine ? lane : 32;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long q[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) q[w] = __shfl_xor_sync(DDT_FULL_MASK, r[w], o);
+        const int qc = __shfl_xor_sync(DDT_FULL_MASK, cand, o);
+        const bool qless = ranks_less(q, r) || (!ranks_less(r, q) && qc < cand);
+        if (qless) {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) r[w] = q[w];
+          cand = qc;
+        }
+      }
+      wl = cand;
+    }
+    const int slot = __shfl_sync(DDT_FULL_MASK, bs, wl);
+    const double logw = f.logw[slot];
+    unsigned long long rk[4] = {f.rw(0, slot), f.rw(1, slot), f.rw(2, slot), f.rw(3, slot)};
+    const uint32_t meta = f.meta[slot];
+    const int depth = (meta >> 12) & 31;
+    const int rank = static_cast<int>(meta >> 17);
+    const int cur = count + 1;
+    __syncwarp();
+    if (lane == 0) {
+      node_meta[count] = meta;
+      int fc = fcount;
+      if (rank + 1 < k) {
+        // ddtree.py:141: logw - lp[d-1, rank] + lp[d-1, rank+1], left to right in double
+        const double sib = (logw - static_cast<double>(lp[(depth - 1) * k + rank])) +
+                           static_cast<double>(lp[(depth - 1) * k + rank + 1]);
+        f.logw[slot] = sib;
+        const int lv = depth - 1;
+        f.rw(0, slot) = rk[0];
+        f.rw(1, slot) = rk[1];
+        f.rw(2, slot) = rk[2];
+        f.rw(3, slot) = rk[3];
+        f.rw(lv / kLevelsPerWord, slot) = rk[lv / kLevelsPerWord] + (1ull << rank_shift(lv));
+        f.meta[slot] = pack_meta(static_cast<int>(meta & 0xfffu), depth, rank + 1);
+      } else {
+        const int last = fc - 1;
+        if (slot != last) {
+          f.logw[slot] = f.logw[last];
+          for (int w = 0; w < 4; ++w) f.rw(w, slot) = f.rw(w, last);
+          f.meta[slot] = f.meta[last];
+        }
+        fc = last;
+      }
+      if (depth < L) {
+        // ddtree.py:146: logw + lp[depth, 0]
+        const double ch = logw + static_cast<double>(lp[depth * k]);
+        f.logw[fc] = ch;
+        for (int w = 0; w < 4; ++w) f.rw(w, fc) = rk[w];
+        f.rw(depth / kLevelsPerWord, fc) = rk[depth / kLevelsPerWord] + (1ull << rank_shift(depth));
+        f.meta[fc] = pack_meta(cur, depth + 1, 0);
+        fc += 1;
+      }
+      fcount = fc;
+    }
+    fcount = __shfl_sync(DDT_FULL_MASK, fcount, 0);
+    count += 1;
+    __syncwarp();
+  }
+  return count;
+}
+
+template <bool kBF16>
+__global__ void __launch_bounds__(kThreads, 1)
+topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_stride, int k,
+                 int budget, float* __restrict__ out_top_lp, int64_t* __restrict__ out_top_ids,
+                 int64_t* __restrict__ node_token_ids, int64_t* __restrict__ node_depths,
+                 int32_t* __restrict__ parents, int32_t* __restrict__ node_count,
+                 uint32_t* __restrict__ anc_bits, int anc_words,
+                 const int64_t* __restrict__ root_token, int64_t start,
+                 int64_t* __restrict__ verify_ids, int64_t* __restrict__ verify_pos,
+                 unsigned char* __restrict__ ws, int vec_ok) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ RadixShared rs;
+  const int C = gridDim.x / L;
+  const int d = blockIdx.x / C;
+  const int c = blockIdx.x % C;
+  const int tid = threadIdx.x;
+  const WsLayout wl = ws_layout(L, V, k);
+  uint32_t* counters = reinterpret_cast<uint32_t*>(ws + wl.counters);
+  float* chunk_max = reinterpret_cast<float*>(ws + wl.chunk_max);
+  double* chunk_sum = reinterpret_cast<double*>(ws + wl.chunk_sum);
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(ws + wl.cand);
+  uint32_t* cand_count = reinterpret_cast<uint32_t*>(ws + wl.cand_count);
+  float* top_lp = reinterpret_cast<float*>(ws + wl.top_lp);
+  uint32_t* top_ids = reinterpret_cast<uint32_t*>(ws + wl.top_ids);
+
+  // ------------------------------ phase 1 ----------------------------------------
+  const int64_t CH = chunk_len(V, C);
+  const int64_t c0 = static_cast<int64_t>(c) * CH;
+  const int64_t c1 = (c0 + CH < V) ? c0 + CH : V;
+  const int64_t n = c1 > c0 ? c1 - c0 : 0;
+  unsigned long long comp[kEPT];
+  float vals[kEPT];
+  if constexpr (kBF16) {
+    const uint16_t* row = static_cast<const uint16_t*>(logits) + d * row_stride + c0;
+    if (vec_ok) {
+#pragma unroll
+      for (int j = 0; j < kEPT / 8; ++j) {
+        const int64_t e0 = (static_cast<int64_t>(j) * kThreads + tid) * 8;
+        uint4 q = make_uint4(0, 0, 0, 0);
+        if (e0 < n) q = __ldcs(reinterpret_cast<const uint4*>(row + e0));  // streamed once
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int64_t idx = e0 + e;
+          const uint16_t b = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
+          const bool ok = idx < n;
+          vals[j * 8 + e] = ok ? bf16_bits_to_f32(b) : -INFINITY;
+          comp[j * 8 + e] = ok ? ((static_cast<unsigned long long>(bf16_key(b)) << 48) |
+                                  static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
+                               : 0ull;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kEPT; ++j) {
+        const int64_t idx = static_cast<int64_t>(j) * kThreads + tid;
+        const bool ok = idx < n;
+        const uint16_t b = ok ? row[idx] : 0;
+        vals[j] = ok ? bf16_bits_to_f32(b) : -INFINITY;
+        comp[j] = ok ? ((static_cast<unsigned long long>(bf16_key(b)) << 48) |
+                        static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
+                     : 0ull;
+      }
+    }
+  } else {
+    const float* row = static_cast<const float*>(logits) + d * row_stride + c0;
+    if (vec_ok) {
+#pragma unroll
+      for (int j = 0; j < kEPT / 4; ++j) {
+        const int64_t e0 = (static_cast<int64_t>(j) * kThreads + tid) * 4;
+        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e0 < n) q = __ldcs(reinterpret_cast<const float4*>(row + e0));
+        const float w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t idx = e0 + e;
+          const bool ok = idx < n;
+          vals[j * 4 + e] = ok ? w[e] : -INFINITY;
+          comp[j * 4 + e] = ok ? ((static_cast<unsigned long long>(f32_key(w[e])) << 32) |
+                                  static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
+                               : 0ull;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kEPT; ++j) {
+        const int64_t idx = static_cast<int64_t>(j) * kThreads + tid;
+        const bool ok = idx < n;
+        const float x = ok ? row[idx] : -INFINITY;
+        vals[j] = x;
+        comp[j] = ok ? ((static_cast<unsigned long long>(f32_key(x)) << 32) |
+                        static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
+                     : 0ull;
+      }
+    }
+  }
+  // chunk max and sum exp(x - max), both exact-order independent up to double rounding
+  float lm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) lm = fmaxf(lm, vals[j]);
+  const float cm = block_max_f(lm, rs);
+  double ls = 0.0;
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j)
+    if (comp[j] != 0ull) ls += exp(static_cast<double>(vals[j]) - static_cast<double>(cm));
+  const double csum = block_sum_d(ls, rs);
+
+  // exact top-k of the chunk
+  const int kk = static_cast<int>(n < k ? n : k);
+  if (kk < n) {
+    radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(kk), rs);
+  } else if (tid == 0) {
+    rs.prefix = 0ull;
+    rs.mask = 0ull;
+  }
+  if (tid == 0) rs.out_count = 0;
+  __syncthreads();
+  unsigned long long* my_cand = cand + (static_cast<int64_t>(d) * C + c) * k;
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) {
+    if (selected(comp[j], rs)) {
+      const uint32_t pos = atomicAdd(&rs.out_count, 1u);
+      if (pos < static_cast<uint32_t>(k)) my_cand[pos] = comp[j];
+    }
+  }
+  __syncthreads();
+  for (int i = static_cast<int>(rs.out_count) + tid; i < k; i += kThreads) my_cand[i] = 0ull;
+  if (tid == 0) {
+    chunk_max[d * C + c] = cm;
+    chunk_sum[d * C + c] = csum;
+    cand_count[d * C + c] = rs.out_count;
+    __threadfence();
+    const uint32_t prev = atomicAdd(&counters[d], 1u);
+    rs.is_last = (prev == static_cast<uint32_t>(C - 1));
+  }
+  __syncthreads();
+  if (!rs.is_last) return;
+  __threadfence();
+
+  // ------------------------------ phase 2 ----------------------------------------
+  if (tid == 0) counters[d] = 0;  // self-reset for the next launch
+  // log Z from the chunk statistics
+  __shared__ float s_logz;
+  if (tid == 0) {
+    float M = -INFINITY;
+    for (int i = 0; i < C; ++i) M = fmaxf(M, __ldcg(&chunk_max[d * C + i]));
+    double S = 0.0;
+    for (int i = 0; i < C; ++i)
+      S += __ldcg(&chunk_sum[d * C + i]) *
+           exp(static_cast<double>(__ldcg(&chunk_max[d * C + i])) - static_cast<double>(M));
+    s_logz = static_cast<float>(static_cast<double>(M) + log(S));
+  }
+  // candidates of the row: C * k composites, 0 = empty
+  const unsigned long long* row_cand = cand + static_cast<int64_t>(d) * C * k;
+  const int ncand = C * k;
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) {
+    const int i = j * kThreads + tid;
+    comp[j] = i < ncand ? __ldcg(&row_cand[i]) : 0ull;
+  }
+  radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(k), rs);
+  if (tid == 0) rs.out_count = 0;
+  __syncthreads();
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem);
+  int kpad = 1;
+  while (kpad < k) kpad <<= 1;
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) {
+    if (selected(comp[j], rs)) {
+      const uint32_t pos = atomicAdd(&rs.out_count, 1u);
+      if (pos < static_cast<uint32_t>(kpad)) sel[pos] = comp[j];
+    }
+  }
+  __syncthreads();
+  for (int i = k + tid; i < kpad; i += kThreads) sel[i] = 0ull;
+  __syncthreads();
+  // bitonic sort, descending
+  for (int size = 2; size <= kpad; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < kpad; i += kThreads) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const unsigned long long a = sel[i], b = sel[j];
+          const bool desc = (i & size) == 0;
+          if (desc ? (a < b) : (a > b)) {
+            sel[i] = b;
+            sel[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const float lz = s_logz;
+  for (int i = tid; i < k; i += kThreads) {
+    const unsigned long long cv = sel[i];
+    const uint32_t key = static_cast<uint32_t>(cv >> 32);
+    const float value = kBF16 ? key_bf16(key >> 16) : key_f32(key);
+    const uint32_t idx = ~static_cast<uint32_t>(cv);
+    const float lpv = value - lz;  // ddtree.py:109, float subtraction
+    top_lp[d * k + i] = lpv;
+    top_ids[d * k + i] = idx;
+    if (out_top_lp) out_top_lp[static_cast<int64_t>(d) * k + i] = lpv;
+    if (out_top_ids) out_top_ids[static_cast<int64_t>(d) * k + i] = idx;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(&counters[L], 1u);
+    rs.is_last = (prev == static_cast<uint32_t>(L - 1));
+  }
+  __syncthreads();
+  if (!rs.is_last) return;
+  __threadfence();
+
+  // ------------------------------ phase 3 ----------------------------------------
+  if (tid == 0) counters[L] = 0;
+  float* lp_s = reinterpret_cast<float*>(smem);
+  const int fcap = budget + 1;
+  double* f_logw = reinterpret_cast<double*>(
+      smem + align_up(sizeof(float) * static_cast<size_t>(L) * k, 16));
+  unsigned long long* f_r = reinterpret_cast<unsigned long long*>(f_logw + fcap);
+  uint32_t* f_meta = reinterpret_cast<uint32_t*>(f_r + 4 * fcap);
+  uint32_t* node_meta = f_meta + fcap;
+  for (int i = tid; i < L * k; i += kThreads) lp_s[i] = __ldcg(&top_lp[i]);
+  __syncthreads();
+  __shared__ int s_count;
+  if (tid < 32) {
+    Frontier fr{f_logw, f_r, f_meta, fcap};
+    const int cnt = heap_build(lp_s, L, k, budget, fr, node_meta);
+    if (tid == 0) s_count = cnt;
+  }
+  __syncthreads();
+  const int count = s_count;
+  const int nn = count + 1;
+  for (int i = tid; i < count; i += kThreads) {
+    const uint32_t meta = node_meta[i];
+    const int depth = (meta >> 12) & 31;
+    const int rank = static_cast<int>(meta >> 17);
+    const int64_t tok = static_cast<int64_t>(__ldcg(&top_ids[(depth - 1) * k + rank]));
+    node_token_ids[i] = tok;
+    node_depths[i] = depth;
+    parents[i + 1] = static_cast<int32_t>(meta & 0xfffu);
+    if (verify_ids) verify_ids[i + 1] = tok;
+    if (verify_pos) verify_pos[i + 1] = start + depth;
+  }
+  if (tid == 0) {
+    parents[0] = -1;
+    *node_count = count;
+    if (verify_ids) verify_ids[0] = root_token ? *root_token : 0;
+    if (verify_pos) verify_pos[0] = start;
+  }
+  // ancestor bitmasks, one row per thread, written from the highest word down
+  for (int i = tid; i < nn; i += kThreads) {
+    uint32_t* row = anc_bits + static_cast<int64_t>(i) * anc_words;
+    int wcur = anc_words - 1;
+    uint32_t acc = 0;
+    int j = i;
+    for (;;) {
+      const int wj = j >= 0 ? (j >> 5) : -1;
+      while (wcur > wj) {
+        row[wcur] = acc;
+        acc = 0;
+        --wcur;
+      }
+      if (j < 0) break;
+      acc |= 1u << (j & 31);
+      j = (j == 0) ? -1 : static_cast<int>(node_meta[j - 1] & 0xfffu);
+    }
+  }
+}
+
+__global__ void empty_tree_kernel(int32_t* parents, int32_t* node_count, uint32_t* anc_bits,
+                                  int anc_words, const int64_t* root_token, int64_t start,
+                                  int64_t* verify_ids, int64_t* verify_pos) {
+  if (threadIdx.x == 0) {
+    parents[0] = -1;
+    *node_count = 0;
+    for (int w = 0; w < anc_words; ++w) anc_bits[w] = (w == 0) ? 1u : 0u;
+    if (verify_ids) verify_ids[0] = root_token ? *root_token : 0;
+    if (verify_pos) verify_pos[0] = start;
+  }
+}
+
+}  // namespace topk
+}  // namespace ddt
+
+using namespace ddt;
+
+extern "C" size_t ddt_topk_tree_workspace_bytes(int64_t depths, int64_t vocab, int64_t budget) {
+  if (depths <= 0 || vocab <= 0 || budget <= 0) return 256;
+  const int64_t k = budget < vocab ? budget : vocab;
+  return topk::ws_layout(depths, vocab, k).total;
+}
+
+extern "C" int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths, int64_t vocab,
+                             int64_t row_stride, int64_t budget, float* top_log_probs,
+                             int64_t* top_token_ids, int64_t* node_token_ids,
+                             int64_t* node_depths, int32_t* parents, int32_t* node_count,
+                             uint32_t* anc_bits, int64_t anc_words, const int64_t* root_token,
+                             int64_t start, int64_t* verify_ids, int64_t* verify_pos,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype != DDT_F32 && dtype != DDT_BF16) return DDT_ERR_DTYPE;
+  if (!parents || !node_count || !anc_bits || depths < 0 || vocab <= 0) return DDT_ERR_INVALID;
+  if (budget > DDT_MAX_BUDGET || depths > DDT_MAX_DEPTH) return DDT_ERR_CAPACITY;
+  const int64_t nmax = (budget > 0 ? budget : 0) + 1;
+  if (anc_words * 32 < nmax) return DDT_ERR_INVALID;
+  if (budget <= 0 || depths == 0) {
+    topk::empty_tree_kernel<<<1, 32, 0, st>>>(parents, node_count, anc_bits,
+                                              static_cast<int>(anc_words), root_token, start,
+                                              verify_ids, verify_pos);
+    return launch_status();
+  }
+  if (!draft_logits || !node_token_ids || !node_depths || !workspace) return DDT_ERR_INVALID;
+  if (row_stride < vocab || vocab >= (int64_t(1) << 31)) return DDT_ERR_INVALID;
+  const int64_t k = budget < vocab ? budget : vocab;
+  const int C = topk::num_chunks(vocab);
+  if (static_cast<int64_t>(C) * k > topk::kMaxCand) return DDT_ERR_CAPACITY;
+  const topk::WsLayout wl = topk::ws_layout(depths, vocab, k);
+  if (workspace_bytes < wl.total) return DDT_ERR_WORKSPACE;
+  const size_t esz = dtype == DDT_BF16 ? 2 : 4;
+  // 16-byte vectors never cross the end of a row: chunk starts are multiples of 8
+  // elements, and the vocabulary must be a whole number of vectors
+  const int vec_ok = aligned(draft_logits, 16) && ((row_stride * esz) % 16 == 0) &&
+                     ((vocab * esz) % 16 == 0);
+  const size_t smem = topk::smem_bytes(depths, k, budget);
+  const dim3 grid(static_cast<unsigned>(depths * C));
+  if (dtype == DDT_BF16) {
+    auto kern = topk::topk_tree_kernel<true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return DDT_ERR_CUDA;
+    kern<<<grid, topk::kThreads, smem, st>>>(
+        draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(k),
+        static_cast<int>(budget), top_log_probs, top_token_ids, node_token_ids, node_depths,
+        parents, node_count, anc_bits, static_cast<int>(anc_words), root_token, start,
+        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok);
+  } else {
+    auto kern = topk::topk_tree_kernel<false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return DDT_ERR_CUDA;
+    kern<<<grid, topk::kThreads, smem, st>>>(
+        draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(k),
+        static_cast<int>(budget), top_log_probs, top_token_ids, node_token_ids, node_depths,
+        parents, node_count, anc_bits, static_cast<int>(anc_words), root_token, start,
+        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok);
+  }
+  return launch_status();
+}

@@ -1,0 +1,717 @@
+// Tree-masked GQA verify attention on tcgen05 tensor cores (sm_100a).
+//
+// Replaces the verify-forward attention of the reference: transformers'
+// sdpa_attention_forward (integrations/sdpa_attention.py:40-103) calling
+// scaled_dot_product_attention with the dense additive mask built by
+// compile_ddtree_tree (ddtree.py:262-264).  Instead of an [N, P+N] mask the kernel
+// reads per-node ancestor bitmasks: every prefix key is visible, tree key j is visible
+// to node i iff bit j of anc_bits[i] is set.
+//
+// Work unit (one CTA): one KV head, one tile of 128 query rows, one KV split.  Query
+// rows are (node, q head of the GQA group) pairs, node-major, so the whole group shares
+// every K/V tile.  Warp roles:
+//   warp 0     TMA producer: Q once, then K and V tiles (128 keys x 128 dims, 128-byte
+//              swizzle) into a 2-stage ring; never multicast.
+//   warp 1     allocates TMEM; one thread issues tcgen05.mma: S = Q K^T into one of two
+//              TMEM S buffers, O += P V into the TMEM O accumulator.
+//   warps 2-5  softmax: thread t owns query row t (TMEM lane t): loads its S row, masks
+//              it, keeps the running max / sum, rescales O in TMEM only when the max
+//              grew by more than 2^8, writes P (bf16) into swizzled shared memory for
+//              the P V MMA, and finally normalises O.
+// Splits of the key range write fp32 partials (O, m, l) that ddt_attn_merge combines;
+// the same partial format is exchanged between GPUs for sequence-sharded prefixes.
+// Every mbarrier wait is bounded; a timeout sets *status and unwinds the CTA.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace ddt {
+namespace attn {
+
+constexpr int kBlockM = 128;
+constexpr int kBlockN = 128;
+constexpr int kHeadDim = 128;
+constexpr int kStages = 2;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.0f;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr uint32_t kHalfBytes = kBlockM * 64 * 2;   // one 64-dim half of a 128-row tile
+constexpr uint32_t kTileBytes = 2 * kHalfBytes;     // 32 KB
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemK = kSmemQ + kTileBytes;
+constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
+constexpr uint32_t kSmemP = kSmemV + kStages * kTileBytes;
+constexpr uint32_t kSmemBytes = kSmemP + kTileBytes;  // 192 KB
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;    // + alignment slack
+constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kBlockM, kBlockN, false, false);
+constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kBlockM, kHeadDim, false, true);
+constexpr int kStatusTimeout = 1;
+
+struct Params {
+  int n_nodes, past_len, group, q_heads, n_qtiles, n_splits;
+  int key_base;        // global key index of local key 0
+  int key_lo, key_hi;  // global key range covered by this launch
+  const uint32_t* anc;
+  int anc_words, mask_mode;
+  float scale_log2;
+  __nv_bfloat16* out;
+  long long o_node_stride, o_head_stride;
+  float* o_part;  // [n_splits][n_nodes * q_heads][128]
+  float* m_part;  // [n_splits][n_nodes * q_heads]
+  float* l_part;
+  int partial;
+  int* status;
+};
+
+struct Bars {
+  uint64_t q_full, k_full[kStages], v_full[kStages], kv_empty[kStages], s_full[2], p_full, o_ready,
+      mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void raise_abort(Bars& b, int* status) {
+  *reinterpret_cast<volatile int*>(&b.abort) = 1;
+  if (status) atomicOr(status, kStatusTimeout);
+}
+
+// Visibility mask of 32 consecutive keys starting at global key g0 for one node.
+__device__ __forceinline__ uint32_t visible32(const Params& p, int node, int g0, int g_end) {
+  uint32_t m = 0xffffffffu;
+  // keys at or beyond g_end (other shard / past the window) are invisible
+  const int n_ok = g_end - g0;
+  if (n_ok <= 0) return 0u;
+  if (n_ok < 32) m = (1u << n_ok) - 1u;
+  if (p.mask_mode == DDT_MASK_CAUSAL) {
+    const int lim = p.past_len + node + 1 - g0;  // keys < lim visible
+    if (lim <= 0) return 0u;
+    if (lim < 32) m &= (1u << lim) - 1u;
+    return m;
+  }
+  const int o0 = g0 - p.past_len;  // tree offset of the first key
+  if (o0 + 32 <= 0) return m;      // all prefix
+  uint32_t tree;
+  const uint32_t* row = p.anc + static_cast<long long>(node) * p.anc_words;
+  if (o0 >= 0) {
+    const int w = o0 >> 5, b = o0 & 31;
+    const uint32_t lo = (w < p.anc_words) ? __ldg(row + w) : 0u;
+    const uint32_t hi = (b && w + 1 < p.anc_words) ? __ldg(row + w + 1) : 0u;
+    tree = b ? __funnelshift_r(lo, hi, b) : lo;
+  } else {
+    // keys [g0, past) are prefix (visible); tree bits start at bit -o0
+    const int sh = -o0;
+    const uint32_t w0 = p.anc_words > 0 ? __ldg(row) : 0u;
+    tree = (w0 << sh) | ((1u << sh) - 1u);
+  }
+  return m & tree;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ Bars bars;
+  const uint32_t raw = tc::smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- work unit -------------------------------------------------------------------
+  const int unit = blockIdx.x;
+  const int split = unit % p.n_splits;
+  const int tq = unit / p.n_splits;
+  const int qt = tq % p.n_qtiles;
+  const int h = tq / p.n_qtiles;
+  const int row0 = qt * kBlockM;
+  const int node_lo = row0 / p.group;
+  int node_hi = (row0 + kBlockM - 1) / p.group;
+  if (node_hi > p.n_nodes - 1) node_hi = p.n_nodes - 1;
+  // keys beyond past + node_hi are invisible to every row of the tile (both modes)
+  int g_end = p.past_len + node_hi + 1;
+  if (g_end > p.key_hi) g_end = p.key_hi;
+  const int g_begin = p.key_lo;
+  const int ntot = g_end > g_begin ? (g_end - g_begin + kBlockN - 1) / kBlockN : 0;
+  const int tps = (ntot + p.n_splits - 1) / p.n_splits;
+  int t_begin = split * tps;
+  int t_end = t_begin + tps;
+  if (t_end > ntot) t_end = ntot;
+  if (t_begin > t_end) t_begin = t_end;
+  const int nt = t_end - t_begin;
+  const int lk0 = g_begin - p.key_base + t_begin * kBlockN;  // local key of the first tile
+
+  if (tid == 0) {
+    tc::mbar_init(&bars.q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&bars.k_full[s], 1);
+      tc::mbar_init(&bars.v_full[s], 1);
+      tc::mbar_init(&bars.kv_empty[s], 1);
+    }
+    tc::mbar_init(&bars.s_full[0], 1);
+    tc::mbar_init(&bars.s_full[1], 1);
+    tc::mbar_init(&bars.p_full, 128);
+    tc::mbar_init(&bars.o_ready, 1);
+    tc::mbar_init(&bars.mma_done, 1);
+    bars.abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&bars.tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars.tmem_base;
+  volatile int* abort_flag = &bars.abort;
+
+  unsigned char* sQ = smem + kSmemQ;
+  unsigned char* sK = smem + kSmemK;
+  unsigned char* sV = smem + kSmemV;
+  unsigned char* sP = smem + kSmemP;
+
+  if (warp == 0) {
+    // ---------------------------- TMA producer -------------------------------------
+    if (lane == 0 && nt > 0) {
+      tc::tma_prefetch_desc(&tm_q);
+      tc::tma_prefetch_desc(&tm_k);
+      tc::tma_prefetch_desc(&tm_v);
+      tc::mbar_expect_tx(&bars.q_full, kTileBytes);
+      tc::tma_load_3d(sQ, &tm_q, &bars.q_full, 0, h * p.group, node_lo);
+      tc::tma_load_3d(sQ + kHalfBytes, &tm_q, &bars.q_full, 64, h * p.group, node_lo);
+      int issued = 0;
+      for (int j = 0; j < nt; ++j) {
+        const int st = j % kStages;
+        if (j >= kStages &&
+            !tc::mbar_wait(&bars.kv_empty[st], ((j / kStages) - 1) & 1, abort_flag, kTimeoutNs)) {
+          raise_abort(bars, p.status);
+          break;
+        }
+        const int key = lk0 + j * kBlockN;
+        unsigned char* kd = sK + st * kTileBytes;
+        unsigned char* vd = sV + st * kTileBytes;
+        tc::mbar_expect_tx(&bars.k_full[st], kTileBytes);
+        tc::tma_load_3d(kd, &tm_k, &bars.k_full[st], 0, key, h);
+        tc::tma_load_3d(kd + kHalfBytes, &tm_k, &bars.k_full[st], 64, key, h);
+        tc::mbar_expect_tx(&bars.v_full[st], kTileBytes);
+        tc::tma_load_3d(vd, &tm_v, &bars.v_full[st], 0, key, h);
+        tc::tma_load_3d(vd + kHalfBytes, &tm_v, &bars.v_full[st], 64, key, h);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // let the loads already in flight land before the CTA releases its smem
+        tc::mbar_wait_drain(&bars.q_full, 0, kTimeoutNs);
+        for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
+          const int st = j % kStages;
+          tc::mbar_wait_drain(&bars.k_full[st], (j / kStages) & 1, kTimeoutNs);
+          tc::mbar_wait_drain(&bars.v_full[st], (j / kStages) & 1, kTimeoutNs);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------- MMA issuer ---------------------------------------
+    if (lane == 0 && nt > 0) {
+      const uint32_t q_addr = tc::smem_u32(sQ);
+      const uint32_t k_addr = tc::smem_u32(sK);
+      const uint32_t v_addr = tc::smem_u32(sV);
+      const uint32_t p_addr = tc::smem_u32(sP);
+      bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kStages;
+        if (!tc::mbar_wait(&bars.k_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs)) return false;
+        tc::tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>((j & 1) * kBlockN);
+        const uint32_t kb = k_addr + st * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          tc::mma_bf16_ss(d, tc::smem_desc_sw128(q_addr + off, 16, 1024),
+                          tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+        }
+        tc::mma_commit(&bars.s_full[j & 1]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j % kStages;
+        if (!tc::mbar_wait(&bars.p_full, j & 1, abort_flag, kTimeoutNs)) return false;
+        if (!tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs)) return false;
+        tc::tc_fence_after();
+        const uint32_t d = tmem + 2 * kBlockN;
+        const uint32_t vb = v_addr + st * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          tc::mma_bf16_ss(d, tc::smem_desc_sw128(p_addr + aoff, 16, 1024),
+                          tc::smem_desc_sw128(vb + kk * 2048, kHalfBytes, 1024), kIdescPV,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&bars.o_ready);
+        tc::mma_commit(&bars.kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < nt; ++j) {
+        ok = issue_s(j);
+        if (ok && j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok) ok = issue_pv(nt - 1);
+      if (!ok) {
+        raise_abort(bars, p.status);
+        // wait for every MMA issued so far before TMEM is released
+        tc::mma_commit(&bars.mma_done);
+        uint64_t t0 = global_timer_ns();
+        while (!tc::mbar_try_wait(&bars.mma_done, 0) && global_timer_ns() - t0 < kTimeoutNs) {
+        }
+      }
+    }
+  } else {
+    // ---------------------------- softmax warps ------------------------------------
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const int R = row0 + r;
+    const int node = R / p.group;
+    const int qh = h * p.group + (R % p.group);
+    const bool valid = node < p.n_nodes;
+    const int vnode = valid ? node : p.n_nodes - 1;
+    const float sl2 = p.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    unsigned char* prow = sP + r * 128;
+    const int sw = r & 7;
+    for (int j = 0; j < nt; ++j) {
+      if (!tc::mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort_flag, kTimeoutNs)) {
+        ok = false;
+        break;
+      }
+      tc::tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tl + (j & 1) * kBlockN + c * 32, s[c]);
+      tc::tmem_wait_ld();
+      const int gk = p.key_base + lk0 + j * kBlockN;  // global key of column 0
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t vis = visible32(p, vnode, gk + c * 32, g_end);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float x = __uint_as_float(s[c][e]) * sl2;
+          x = ((vis >> e) & 1u) ? x : -INFINITY;
+          s[c][e] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      bool rescale = false;
+      float alpha = 1.f;
+      if (mx > -INFINITY) {
+        if (m_used == -INFINITY) {
+          m_used = mx;  // nothing accumulated yet: O and l are zero
+        } else if (mx > m_used + kRescaleLog2) {
+          alpha = tc::ex2_approx(m_used - mx);
+          m_used = mx;
+          rescale = true;
+        }
+      }
+      const float mref = (m_used == -INFINITY) ? 0.f : m_used;
+      if (j > 0 && !tc::mbar_wait(&bars.o_ready, (j - 1) & 1, abort_flag, kTimeoutNs)) {
+        ok = false;
+        break;
+      }
+      if (rescale) {
+        tc::tc_fence_after();
+        const uint32_t ob = tl + 2 * kBlockN;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tc::tmem_ld32(ob + c * 32, o);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tc::tmem_st32(ob + c * 32, o);
+        }
+        tc::tmem_wait_st();
+        l *= alpha;
+      }
+      float ls = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // 8 keys per 16-byte chunk
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float a = tc::ex2_approx(__uint_as_float(s[c][q * 8 + 2 * e]) - mref);
+            const float b = tc::ex2_approx(__uint_as_float(s[c][q * 8 + 2 * e + 1]) - mref);
+            ls += a + b;
+            pk[e] = tc::pack_bf16x2(a, b);
+          }
+          const int chunk = c * 4 + q;  // 0..15
+          const int half = chunk >> 3, cc = chunk & 7;
+          *reinterpret_cast<uint4*>(prow + half * kHalfBytes + ((cc ^ sw) << 4)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+      l += ls;
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars.p_full);
+    }
+    if (ok && nt > 0 && !tc::mbar_wait(&bars.o_ready, (nt - 1) & 1, abort_flag, kTimeoutNs)) ok = false;
+    if (!ok) raise_abort(bars, p.status);
+    if (valid) {
+      const long long row = static_cast<long long>(node) * p.q_heads + qh;
+      if (p.partial) {
+        float* op = p.o_part + (static_cast<long long>(split) * p.n_nodes * p.q_heads + row) * kHeadDim;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          if (ok && nt > 0) {
+            tc::tc_fence_after();
+            tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
+            tc::tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(op + c * 32 + e) =
+                make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
+                            __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
+        }
+        const long long mi = static_cast<long long>(split) * p.n_nodes * p.q_heads + row;
+        p.m_part[mi] = (ok && nt > 0) ? m_used : -INFINITY;
+        p.l_part[mi] = (ok && nt > 0) ? l : 0.f;
+      } else {
+        const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
+        __nv_bfloat16* orow = p.out + static_cast<long long>(node) * p.o_node_stride +
+                              static_cast<long long>(qh) * p.o_head_stride;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          if (ok && nt > 0) {
+            tc::tc_fence_after();
+            tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
+            tc::tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 v;
+            v.x = tc::pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+            v.y = tc::pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+            v.z = tc::pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+            v.w = tc::pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+          }
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- split merge ---------------------------------------------------------------------
+// One warp per (node, q head) row; lane owns 4 of the 128 dims.
+__global__ void merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ m_parts,
+                             const float* __restrict__ l_parts, int n_parts, long long rows,
+                             int q_heads, __nv_bfloat16* __restrict__ out, long long o_node_stride,
+                             long long o_head_stride, float* __restrict__ o_merged,
+                             float* __restrict__ m_merged, float* __restrict__ l_merged) {
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float M = -INFINITY;
+  for (int i = 0; i < n_parts; ++i) M = fmaxf(M, m_parts[i * rows + row]);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M > -INFINITY) {
+    for (int i = 0; i < n_parts; ++i) {
+      const float mi = m_parts[i * rows + row];
+      if (mi == -INFINITY) continue;
+      const float w = exp2f(mi - M);
+      L += w * l_parts[i * rows + row];
+      const float4 o = *reinterpret_cast<const float4*>(o_parts + (i * rows + row) * kHeadDim + lane * 4);
+      acc.x += w * o.x;
+      acc.y += w * o.y;
+      acc.z += w * o.z;
+      acc.w += w * o.w;
+    }
+  }
+  if (out) {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const long long node = row / q_heads, qh = row % q_heads;
+    __nv_bfloat16* orow = out + node * o_node_stride + qh * o_head_stride + lane * 4;
+    uint2 v;
+    v.x = tc::pack_bf16x2(acc.x * inv, acc.y * inv);
+    v.y = tc::pack_bf16x2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(orow) = v;
+  } else {
+    *reinterpret_cast<float4*>(o_merged + row * kHeadDim + lane * 4) = acc;
+    if (lane == 0) {
+      m_merged[row] = M;
+      l_merged[row] = L;
+    }
+  }
+}
+
+// ---- mask -> bitmask -------------------------------------------------------------------
+template <typename T>
+__global__ void mask_to_bits_kernel(const T* __restrict__ mask, int n, long long row_stride,
+                                    uint32_t* __restrict__ bits, int words) {
+  const int i = blockIdx.x;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) {
+    uint32_t v = 0;
+    for (int b = 0; b < 32; ++b) {
+      const int j = w * 32 + b;
+      if (j < n && static_cast<float>(mask[i * row_stride + j]) == 0.f) v |= 1u << b;
+    }
+    bits[static_cast<long long>(i) * words + w] = v;
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 3-D bf16 tensor map: dims {d0 (contiguous), d1, d2}, byte strides {s1, s2}, box
+// {b0, b1, b2}, 128-byte swizzle, zero fill out of bounds.
+inline int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                    uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return DDT_ERR_CUDA;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DDT_OK : DDT_ERR_ALIGN;
+}
+
+struct Launch {
+  CUtensorMap q, k, v;
+  Params p;
+};
+
+inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                   const void* k, const void* v, int64_t kv_head_stride, int64_t kv_seq_stride,
+                   int64_t kv_len_local, int64_t n_nodes, int64_t past_length, int64_t q_heads,
+                   int64_t kv_heads, int64_t head_dim, const uint32_t* anc_bits,
+                   int64_t anc_words, int mask_mode, float scale) {
+  if (!q || !k || !v) return DDT_ERR_INVALID;
+  if (head_dim != kHeadDim) return DDT_ERR_CAPACITY;
+  if (n_nodes <= 0 || past_length < 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads)
+    return DDT_ERR_INVALID;
+  const int64_t group = q_heads / kv_heads;
+  if (group > kBlockM || kBlockM % group) return DDT_ERR_CAPACITY;
+  if (mask_mode != DDT_MASK_TREE && mask_mode != DDT_MASK_CAUSAL) return DDT_ERR_INVALID;
+  if (mask_mode == DDT_MASK_TREE && (!anc_bits || anc_words * 32 < n_nodes)) return DDT_ERR_INVALID;
+  if (past_length + n_nodes >= (int64_t(1) << 31)) return DDT_ERR_CAPACITY;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16)) return DDT_ERR_ALIGN;
+  if ((q_node_stride * 2) % 16 || (q_head_stride * 2) % 16 || (kv_head_stride * 2) % 16 ||
+      (kv_seq_stride * 2) % 16)
+    return DDT_ERR_ALIGN;
+  int rc = make_map(&L.q, q, kHeadDim, q_heads, n_nodes, q_head_stride * 2, q_node_stride * 2, 64,
+                    static_cast<uint32_t>(group), static_cast<uint32_t>(kBlockM / group));
+  if (rc) return rc;
+  rc = make_map(&L.k, k, kHeadDim, kv_len_local, kv_heads, kv_seq_stride * 2, kv_head_stride * 2,
+                64, kBlockN, 1);
+  if (rc) return rc;
+  rc = make_map(&L.v, v, kHeadDim, kv_len_local, kv_heads, kv_seq_stride * 2, kv_head_stride * 2,
+                64, kBlockN, 1);
+  if (rc) return rc;
+  Params& p = L.p;
+  p.n_nodes = static_cast<int>(n_nodes);
+  p.past_len = static_cast<int>(past_length);
+  p.group = static_cast<int>(group);
+  p.q_heads = static_cast<int>(q_heads);
+  p.n_qtiles = static_cast<int>((n_nodes * group + kBlockM - 1) / kBlockM);
+  p.anc = anc_bits;
+  p.anc_words = static_cast<int>(anc_words);
+  p.mask_mode = mask_mode;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = nullptr;
+  p.o_part = p.m_part = p.l_part = nullptr;
+  p.partial = 0;
+  p.status = nullptr;
+  return DDT_OK;
+}
+
+inline int pick_splits(int64_t units, int64_t kv_tiles) {
+  // One CTA per SM (192 KB of shared memory each): split the key range so the grid
+  // fills at most one wave of 148 SMs, keeping at least 4 key tiles per split.
+  int64_t s = units >= 148 ? 1 : 148 / units;
+  const int64_t cap = kv_tiles / 4 > 1 ? kv_tiles / 4 : 1;
+  if (s > cap) s = cap;
+  if (s < 1) s = 1;
+  if (s > 64) s = 64;
+  return static_cast<int>(s);
+}
+
+inline size_t part_bytes(int64_t rows, int64_t splits) {
+  return static_cast<size_t>(splits) * rows * (kHeadDim + 2) * sizeof(float) + 256;
+}
+
+inline int launch(const Launch& L, int64_t kv_heads, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(tree_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemAlloc) != cudaSuccess)
+      return DDT_ERR_CUDA;
+    attr = true;
+  }
+  const int64_t grid = kv_heads * L.p.n_qtiles * L.p.n_splits;
+  tree_attn_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, st>>>(L.q, L.k, L.v, L.p);
+  return launch_status();
+}
+
+}  // namespace attn
+}  // namespace ddt
+
+using namespace ddt;
+
+extern "C" size_t ddt_tree_attn_workspace_bytes(int64_t n_nodes, int64_t q_heads, int64_t head_dim,
+                                                int64_t kv_splits) {
+  (void)head_dim;
+  const int64_t s = kv_splits > 0 ? kv_splits : 64;
+  return attn::part_bytes(n_nodes * q_heads, s);
+}
+
+extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                             const void* k, const void* v, int64_t kv_head_stride,
+                             int64_t kv_seq_stride, void* out, int64_t o_node_stride,
+                             int64_t o_head_stride, int64_t n_nodes, int64_t past_length,
+                             int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                             const uint32_t* anc_bits, int64_t anc_words, int mask_mode,
+                             float scale, int64_t kv_splits, void* workspace,
+                             size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!out) return DDT_ERR_INVALID;
+  if (!aligned(out, 16) || (o_node_stride * 2) % 16 || (o_head_stride * 2) % 16) return DDT_ERR_ALIGN;
+  attn::Launch L;
+  const int64_t S = past_length + n_nodes;
+  int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride, S,
+                         n_nodes, past_length, q_heads, kv_heads, head_dim, anc_bits, anc_words,
+                         mask_mode, scale);
+  if (rc) return rc;
+  const int64_t units = kv_heads * L.p.n_qtiles;
+  const int64_t kv_tiles = (S + attn::kBlockN - 1) / attn::kBlockN;
+  const int splits = kv_splits > 0 ? static_cast<int>(kv_splits) : attn::pick_splits(units, kv_tiles);
+  if (splits > 64) return DDT_ERR_CAPACITY;
+  L.p.n_splits = splits;
+  L.p.key_base = 0;
+  L.p.key_lo = 0;
+  L.p.key_hi = static_cast<int>(S);
+  L.p.status = status;
+  L.p.out = static_cast<__nv_bfloat16*>(out);
+  L.p.o_node_stride = o_node_stride;
+  L.p.o_head_stride = o_head_stride;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = n_nodes * q_heads;
+  if (splits > 1) {
+    if (!workspace || workspace_bytes < attn::part_bytes(rows, splits)) return DDT_ERR_WORKSPACE;
+    if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
+    float* o_part = static_cast<float*>(workspace);
+    float* m_part = o_part + static_cast<size_t>(splits) * rows * attn::kHeadDim;
+    float* l_part = m_part + static_cast<size_t>(splits) * rows;
+    L.p.o_part = o_part;
+    L.p.m_part = m_part;
+    L.p.l_part = l_part;
+    L.p.partial = 1;
+    rc = attn::launch(L, kv_heads, st);
+    if (rc) return rc;
+    const int wpb = 8;
+    attn::merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+        o_part, m_part, l_part, splits, rows, static_cast<int>(q_heads),
+        static_cast<__nv_bfloat16*>(out), o_node_stride, o_head_stride, nullptr, nullptr, nullptr);
+    return launch_status();
+  }
+  return attn::launch(L, kv_heads, st);
+}
+
+extern "C" int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                                     const void* k, const void* v, int64_t kv_head_stride,
+                                     int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
+                                     float* o_part, float* m_part, float* l_part, int64_t n_nodes,
+                                     int64_t past_length, int64_t q_heads, int64_t kv_heads,
+                                     int64_t head_dim, const uint32_t* anc_bits,
+                                     int64_t anc_words, int mask_mode, float scale,
+                                     int32_t* status, void* stream) {
+  if (!o_part || !m_part || !l_part) return DDT_ERR_INVALID;
+  if (key_begin < 0 || key_end < key_begin || key_end > past_length + n_nodes) return DDT_ERR_INVALID;
+  if (!aligned(o_part, 16)) return DDT_ERR_ALIGN;
+  attn::Launch L;
+  const int64_t local = key_end - key_begin;
+  int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride,
+                         local > 0 ? local : 1, n_nodes, past_length, q_heads, kv_heads, head_dim,
+                         anc_bits, anc_words, mask_mode, scale);
+  if (rc) return rc;
+  L.p.n_splits = 1;
+  L.p.key_base = static_cast<int>(key_begin);
+  L.p.key_lo = static_cast<int>(key_begin);
+  L.p.key_hi = static_cast<int>(key_end);
+  L.p.status = status;
+  L.p.o_part = o_part;
+  L.p.m_part = m_part;
+  L.p.l_part = l_part;
+  L.p.partial = 1;
+  return attn::launch(L, kv_heads, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_parts,
+                              int64_t n_parts, int64_t n_nodes, int64_t q_heads, int64_t head_dim,
+                              void* out, int64_t o_node_stride, int64_t o_head_stride,
+                              void* stream) {
+  if (!o_parts || !m_parts || !l_parts || !out || n_parts <= 0 || n_nodes <= 0 || q_heads <= 0)
+    return DDT_ERR_INVALID;
+  if (head_dim != attn::kHeadDim) return DDT_ERR_CAPACITY;
+  if (!aligned(o_parts, 16) || !aligned(out, 8) || (o_node_stride * 2) % 8 || (o_head_stride * 2) % 8)
+    return DDT_ERR_ALIGN;
+  const int64_t rows = n_nodes * q_heads;
+  const int wpb = 8;
+  attn::merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0,
+                       static_cast<cudaStream_t>(stream)>>>(
+      o_parts, m_parts, l_parts, static_cast<int>(n_parts), rows, static_cast<int>(q_heads),
+      static_cast<__nv_bfloat16*>(out), o_node_stride, o_head_stride, nullptr, nullptr, nullptr);
+  return launch_status();
+}
+
+extern "C" int ddt_mask_to_bits(const void* mask, int dtype, int64_t n_nodes, int64_t row_stride,
+                                uint32_t* anc_bits, int64_t anc_words, void* stream) {
+  if (!mask || !anc_bits || n_nodes <= 0 || anc_words * 32 < n_nodes || row_stride < n_nodes)
+    return DDT_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == DDT_BF16)
+    attn::mask_to_bits_kernel<__nv_bfloat16><<<static_cast<unsigned>(n_nodes), 64, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(mask), static_cast<int>(n_nodes), row_stride, anc_bits,
+        static_cast<int>(anc_words));
+  else if (dtype == DDT_F32)
+    attn::mask_to_bits_kernel<float><<<static_cast<unsigned>(n_nodes), 64, 0, st>>>(
+        static_cast<const float*>(mask), static_cast<int>(n_nodes), row_stride, anc_bits,
+        static_cast<int>(anc_words));
+  else
+    return DDT_ERR_DTYPE;
+  return launch_status();
+}

@@ -1,0 +1,355 @@
+"""Tensor-level wrappers over the C ABI.  PyTorch owns every buffer; the kernels run on
+the current CUDA stream of the tensors' device and never synchronise the host."""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import DDT_BF16, DDT_F32, DDT_MASK_CAUSAL, DDT_MASK_TREE, check
+
+__all__ = [
+    "DeviceTree", "expected_node_count", "topk_tree", "argmax", "accept_compact", "compact_kv",
+    "tree_attention", "tree_attention_partial", "attn_merge", "mask_to_bits", "KvTable",
+    "anc_words_for",
+]
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return DDT_BF16
+    if t.dtype == torch.float32:
+        return DDT_F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("ddtree_b200 kernels need CUDA tensors")
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+class _Workspaces:
+    """Per-device scratch buffers, grown on demand and zero-filled when (re)allocated."""
+
+    def __init__(self):
+        self._bufs: dict[tuple[int, str], torch.Tensor] = {}
+
+    def get(self, device: torch.device, name: str, nbytes: int) -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), name)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            nb = max(nbytes, 256)
+            if buf is not None:
+                nb = max(nb, 2 * buf.numel())
+            buf = torch.zeros(nb, dtype=torch.uint8, device=device)
+            self._bufs[key] = buf
+        return buf
+
+
+WORKSPACES = _Workspaces()
+
+
+def anc_words_for(n_nodes: int) -> int:
+    return max(1, (n_nodes + 31) // 32)
+
+
+def expected_node_count(depths: int, vocab: int, budget: int) -> int:
+    """Nodes (without the root) the best-first expansion produces: the budget, unless
+    the whole tree of sum_{d=1..depths} k^d candidates is smaller (k = min(budget, V))."""
+    if budget <= 0 or depths <= 0:
+        return 0
+    k = min(budget, vocab)
+    total = 0
+    for d in range(1, depths + 1):
+        total += k ** d
+        if total >= budget:
+            return budget
+    return min(budget, total)
+
+
+@dataclass
+class DeviceTree:
+    """Device-resident draft tree (node 0 is the root)."""
+    budget: int
+    depths: int
+    k: int
+    n_nodes: int                   # 1 + node count, known on the host without a sync
+    node_count: torch.Tensor       # i32 [1]
+    node_token_ids: torch.Tensor   # i64 [budget]
+    node_depths: torch.Tensor      # i64 [budget]
+    parents: torch.Tensor          # i32 [budget + 1]
+    anc_bits: torch.Tensor         # i32 (bit pattern of u32) [budget + 1, anc_words]
+    verify_ids: torch.Tensor       # i64 [budget + 1]
+    verify_pos: torch.Tensor       # i64 [budget + 1]
+    top_log_probs: torch.Tensor    # f32 [depths, k]
+    top_token_ids: torch.Tensor    # i64 [depths, k]
+
+    @property
+    def anc_words(self) -> int:
+        return self.anc_bits.shape[1]
+
+    @staticmethod
+    def allocate(device, budget: int, depths: int, vocab: int) -> "DeviceTree":
+        b = max(budget, 0)
+        k = min(b, vocab) if b > 0 else 0
+        n_cap = b + 1
+        i64 = dict(dtype=torch.int64, device=device)
+        return DeviceTree(
+            budget=b, depths=depths, k=k, n_nodes=1 + expected_node_count(depths, vocab, b),
+            node_count=torch.zeros(1, dtype=torch.int32, device=device),
+            node_token_ids=torch.zeros(max(b, 1), **i64),
+            node_depths=torch.zeros(max(b, 1), **i64),
+            parents=torch.zeros(n_cap, dtype=torch.int32, device=device),
+            anc_bits=torch.zeros((n_cap, anc_words_for(n_cap)), dtype=torch.int32, device=device),
+            verify_ids=torch.zeros(n_cap, **i64), verify_pos=torch.zeros(n_cap, **i64),
+            top_log_probs=torch.zeros((max(depths, 1), max(k, 1)), dtype=torch.float32,
+                                      device=device),
+            top_token_ids=torch.zeros((max(depths, 1), max(k, 1)), **i64))
+
+
+def topk_tree(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor | None = None,
+              start: int = 0, out: DeviceTree | None = None) -> DeviceTree:
+    """Per-depth log Z + top-k, best-first tree, ancestor bitmasks and verify ids /
+    positions in one launch (ddtree.py:84-166 and :248-257)."""
+    if draft_logits.dim() != 2:
+        raise ValueError("draft_logits must be [depths, vocab]")
+    dev = _require_cuda(draft_logits)
+    L, V = draft_logits.shape
+    if draft_logits.stride(1) != 1:
+        draft_logits = draft_logits.contiguous()
+    tree = out if out is not None else DeviceTree.allocate(dev, budget, L, V)
+    if tree.budget != max(budget, 0) or tree.depths != L:
+        raise ValueError("output DeviceTree was allocated for another budget / depth")
+    tree.n_nodes = 1 + expected_node_count(L, V, budget)
+    lib = _lib.load()
+    ws_bytes = lib.ddt_topk_tree_workspace_bytes(L, V, budget)
+    ws = WORKSPACES.get(dev, "topk_tree", ws_bytes)
+    if root_token is not None:
+        root_token = root_token.reshape(-1)[:1]
+        if root_token.dtype != torch.int64:
+            root_token = root_token.to(torch.int64)
+    rc = lib.ddt_topk_tree(
+        draft_logits.data_ptr(), _dtype_code(draft_logits), L, V, draft_logits.stride(0), budget,
+        tree.top_log_probs.data_ptr(), tree.top_token_ids.data_ptr(), tree.node_token_ids.data_ptr(),
+        tree.node_depths.data_ptr(), tree.parents.data_ptr(), tree.node_count.data_ptr(),
+        tree.anc_bits.data_ptr(), tree.anc_words,
+        root_token.data_ptr() if root_token is not None else None, int(start),
+        tree.verify_ids.data_ptr(), tree.verify_pos.data_ptr(), ws.data_ptr(), ws.numel(),
+        _stream(dev))
+    check(rc, "ddt_topk_tree")
+    return tree
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row argmax over the last dim (lowest index on ties, NaN largest)."""
+    dev = _require_cuda(logits)
+    x = logits.reshape(-1, logits.shape[-1])
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=dev)
+    check(_lib.load().ddt_argmax(x.data_ptr(), _dtype_code(x), rows, cols, x.stride(0),
+                                 out.data_ptr(), _stream(dev)), "ddt_argmax")
+    return out.view(logits.shape[:-1])
+
+
+class KvTable:
+    """Device table of K/V base pointers ([heads, seq, head_dim] views, head_dim
+    contiguous, identical strides) for the one-launch compaction kernels."""
+
+    def __init__(self, tensors: list[torch.Tensor]):
+        if not tensors:
+            raise ValueError("empty KV table")
+        t0 = tensors[0]
+        self.device = _require_cuda(*tensors)
+        if t0.dim() == 4:
+            if t0.shape[0] != 1:
+                raise ValueError("batch size 1 caches only")
+            tensors = [t[0] for t in tensors]
+            t0 = tensors[0]
+        self.heads, self.seq, self.head_dim = t0.shape
+        self.head_stride, self.seq_stride, inner = t0.stride()
+        for t in tensors:
+            if t.shape[0] != self.heads or t.shape[2] != self.head_dim or \
+                    t.stride() != (self.head_stride, self.seq_stride, 1) or t.dtype != t0.dtype:
+                raise ValueError("KV tensors must share shape, strides and dtype")
+        if inner != 1:
+            raise ValueError("head_dim must be contiguous")
+        self.elem_bytes = t0.element_size()
+        self.n = len(tensors)
+        self.ptrs = torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64,
+                                 device=self.device)
+        self._keep = tensors  # keep storages alive
+
+
+def accept_compact(posterior: torch.Tensor, tree: DeviceTree, kv: KvTable, past_length: int,
+                   accepted: torch.Tensor | None = None, n_accepted: torch.Tensor | None = None,
+                   next_token: torch.Tensor | None = None, n_nodes: int | None = None):
+    """Greedy accept walk + KV compaction in one launch (ddtree.py:270-281, 284-335)."""
+    dev = _require_cuda(posterior)
+    n = tree.n_nodes if n_nodes is None else n_nodes
+    if past_length + n > kv.seq:
+        raise ValueError(f"cache holds {kv.seq} rows, the tree window needs {past_length + n}")
+    if accepted is None:
+        accepted = torch.zeros(n, dtype=torch.int64, device=dev)
+    if n_accepted is None:
+        n_accepted = torch.zeros(1, dtype=torch.int32, device=dev)
+    if next_token is None:
+        next_token = torch.zeros(1, dtype=torch.int64, device=dev)
+    post = posterior.reshape(-1)
+    if post.dtype != torch.int64:
+        post = post.to(torch.int64)
+    check(_lib.load().ddt_accept_compact(
+        post.data_ptr(), tree.parents.data_ptr(), tree.node_token_ids.data_ptr(), n,
+        kv.ptrs.data_ptr(), kv.n, kv.heads, kv.head_dim, kv.head_stride, kv.seq_stride,
+        kv.elem_bytes, past_length, accepted.data_ptr(), n_accepted.data_ptr(),
+        next_token.data_ptr(), _stream(dev)), "ddt_accept_compact")
+    return accepted, n_accepted, next_token
+
+
+def compact_kv(keep, kv: KvTable, past_length: int) -> None:
+    """Moves rows past_length + keep[j] -> past_length + j in every table tensor.  A host
+    list is validated (strictly increasing, inside the cache); a device tensor is trusted."""
+    if not isinstance(keep, torch.Tensor):
+        keep = [int(x) for x in keep]
+        if any(b <= a for a, b in zip(keep, keep[1:])) or (keep and keep[0] < 0):
+            raise ValueError("keep indices must be strictly increasing and non-negative")
+        if keep and past_length + keep[-1] >= kv.seq:
+            raise ValueError("keep index outside the cache window")
+        keep = torch.tensor(keep, dtype=torch.int64, device=kv.device)
+    keep = keep.reshape(-1)
+    if keep.dtype != torch.int64:
+        keep = keep.to(torch.int64)
+    check(_lib.load().ddt_compact_kv(keep.data_ptr(), keep.numel(), kv.ptrs.data_ptr(), kv.n,
+                                     kv.heads, kv.head_dim, kv.head_stride, kv.seq_stride,
+                                     kv.elem_bytes, past_length, _stream(kv.device)),
+          "ddt_compact_kv")
+
+
+def _q_view(q: torch.Tensor):
+    """Accepts [N, Hq, D] or HF's [1, Hq, N, D]; returns (N, Hq, node_stride, head_stride)."""
+    if q.dim() == 4:
+        if q.shape[0] != 1:
+            raise ValueError("batch size 1 only")
+        _, hq, n, d = q.shape
+        return n, hq, q.stride(2), q.stride(1)
+    n, hq, d = q.shape
+    return n, hq, q.stride(0), q.stride(1)
+
+
+def _kv_view(k: torch.Tensor):
+    """Accepts [Hkv, S, D] or [1, Hkv, S, D]; returns (Hkv, S, head_stride, seq_stride)."""
+    if k.dim() == 4:
+        if k.shape[0] != 1:
+            raise ValueError("batch size 1 only")
+        k = k[0]
+    return k.shape[0], k.shape[1], k.stride(0), k.stride(1)
+
+
+def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   anc_bits: torch.Tensor | None, past_length: int, scale: float | None = None,
+                   causal: bool = False, out: torch.Tensor | None = None, kv_splits: int = 0,
+                   status: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(Q K^T * scale, tree / causal mask) V on tcgen05.  q: [N, Hq, D] (or HF
+    [1, Hq, N, D]); k, v: [Hkv, past_length + N, D] (or [1, ...]); returns [N, Hq, D]."""
+    dev = _require_cuda(q, k, v)
+    n, hq, qns, qhs = _q_view(q)
+    hkv, s, khs, kss = _kv_view(k)
+    _, _, vhs, vss = _kv_view(v)
+    if (khs, kss) != (vhs, vss):
+        raise ValueError("k and v must share strides")
+    d = q.shape[-1]
+    if s != past_length + n:
+        raise ValueError(f"key length {s} != past_length + nodes ({past_length} + {n})")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise TypeError("tree attention runs in bf16")
+    if out is None:
+        out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=dev)
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    lib = _lib.load()
+    ws_bytes = lib.ddt_tree_attn_workspace_bytes(n, hq, d, kv_splits)
+    ws = WORKSPACES.get(dev, "tree_attn", ws_bytes)
+    if status is None:
+        status = WORKSPACES.get(dev, "attn_status", 256)[:4].view(torch.int32)
+    mode = DDT_MASK_CAUSAL if causal else DDT_MASK_TREE
+    if not causal and anc_bits is None:
+        raise ValueError("tree mode needs ancestor bitmasks")
+    words = anc_bits.shape[1] if anc_bits is not None else 0
+    rc = lib.ddt_tree_attn(
+        q.data_ptr(), qns, qhs, k.data_ptr(), v.data_ptr(), khs, kss, out.data_ptr(),
+        out.stride(0), out.stride(1), n, past_length, hq, hkv, d,
+        anc_bits.data_ptr() if anc_bits is not None else None, words, mode, float(scale),
+        kv_splits, ws.data_ptr(), ws.numel(), status.data_ptr(), _stream(dev))
+    check(rc, "ddt_tree_attn")
+    return out
+
+
+def tree_attention_partial(q, k_shard, v_shard, key_begin: int, key_end: int, anc_bits,
+                           past_length: int, scale: float | None = None, causal: bool = False,
+                           out=None, status=None):
+    """Partial (O unnormalised fp32, m, l) over global keys [key_begin, key_end), whose
+    K/V rows are k_shard / v_shard ([Hkv, key_end - key_begin, D])."""
+    dev = _require_cuda(q, k_shard, v_shard)
+    n, hq, qns, qhs = _q_view(q)
+    hkv, s_local, khs, kss = _kv_view(k_shard)
+    d = q.shape[-1]
+    if s_local < key_end - key_begin:
+        raise ValueError("shard shorter than its key range")
+    if out is None:
+        out = (torch.empty((n * hq, d), dtype=torch.float32, device=dev),
+               torch.empty(n * hq, dtype=torch.float32, device=dev),
+               torch.empty(n * hq, dtype=torch.float32, device=dev))
+    o, m, l = out
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if status is None:
+        status = WORKSPACES.get(dev, "attn_status", 256)[:4].view(torch.int32)
+    words = anc_bits.shape[1] if anc_bits is not None else 0
+    rc = _lib.load().ddt_tree_attn_partial(
+        q.data_ptr(), qns, qhs, k_shard.data_ptr(), v_shard.data_ptr(), khs, kss, key_begin,
+        key_end, o.data_ptr(), m.data_ptr(), l.data_ptr(), n, past_length, hq, hkv, d,
+        anc_bits.data_ptr() if anc_bits is not None else None, words,
+        DDT_MASK_CAUSAL if causal else DDT_MASK_TREE, float(scale), status.data_ptr(),
+        _stream(dev))
+    check(rc, "ddt_tree_attn_partial")
+    return o, m, l
+
+
+def attn_merge(o_parts: torch.Tensor, m_parts: torch.Tensor, l_parts: torch.Tensor, n_nodes: int,
+               q_heads: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merges [P, rows, D] / [P, rows] partials into bf16 [n_nodes, q_heads, D]."""
+    dev = _require_cuda(o_parts, m_parts, l_parts)
+    d = o_parts.shape[-1]
+    if out is None:
+        out = torch.empty((n_nodes, q_heads, d), dtype=torch.bfloat16, device=dev)
+    check(_lib.load().ddt_attn_merge(o_parts.data_ptr(), m_parts.data_ptr(), l_parts.data_ptr(),
+                                     o_parts.shape[0], n_nodes, q_heads, d, out.data_ptr(),
+                                     out.stride(0), out.stride(1), _stream(dev)), "ddt_attn_merge")
+    return out
+
+
+def mask_to_bits(mask_block: torch.Tensor, words: int | None = None) -> torch.Tensor:
+    """[N, N] additive mask block (0 = visible) -> i32 [N, words] ancestor bitmasks."""
+    dev = _require_cuda(mask_block)
+    n = mask_block.shape[0]
+    words = anc_words_for(n) if words is None else words
+    if mask_block.stride(1) != 1:
+        mask_block = mask_block.contiguous()
+    bits = torch.empty((n, words), dtype=torch.int32, device=dev)
+    check(_lib.load().ddt_mask_to_bits(mask_block.data_ptr(), _dtype_code(mask_block), n,
+                                       mask_block.stride(0), bits.data_ptr(), words, _stream(dev)),
+          "ddt_mask_to_bits")
+    return bits

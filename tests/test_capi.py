@@ -1,0 +1,77 @@
+"""CPU checks of the C-ABI boundary: the library loads and exports every entry point
+declared in include/ddtree_b200.h with the binding's signature; argument validation
+that happens on the host returns the documented error codes without touching a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from mdflash_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "ddtree_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ddt_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_and_binding_agree():
+    assert _declared() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+
+
+def test_error_strings_and_version():
+    lib = _lib.load()
+    assert lib.ddt_version() >= 1
+    for code in (0, -1, -2, -3, -4, -5, -6, -7):
+        assert lib.ddt_error_string(code)
+    assert lib.ddt_error_string(-99) == b"unknown error"
+
+
+def test_host_side_validation_rejects_bad_arguments():
+    lib = _lib.load()
+    # capacity: budget above the compiled limit, before any device work
+    rc = lib.ddt_topk_tree(None, 1, 15, 1000, 1000, 5000, None, None, None, None,
+                           ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 200,
+                           None, 0, None, None, None, 0, None)
+    assert rc == -2
+    rc = lib.ddt_topk_tree(None, 7, 15, 1000, 1000, 8, None, None, None, None,
+                           ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 1,
+                           None, 0, None, None, None, 0, None)
+    assert rc == -3
+    # attention: head_dim other than 128 is a capacity error, odd GQA ratio invalid
+    assert lib.ddt_tree_attn(ctypes.c_void_p(256), 128, 128, ctypes.c_void_p(256),
+                             ctypes.c_void_p(256), 128, 128, ctypes.c_void_p(256), 128, 128, 4,
+                             0, 4, 2, 64, ctypes.c_void_p(256), 1, 0, 1.0, 0, None, 0, None,
+                             None) == -2
+    assert lib.ddt_tree_attn(ctypes.c_void_p(256), 128, 128, ctypes.c_void_p(256),
+                             ctypes.c_void_p(256), 128, 128, ctypes.c_void_p(256), 128, 128, 4,
+                             0, 6, 4, 128, ctypes.c_void_p(256), 1, 0, 1.0, 0, None, 0, None,
+                             None) == -1
+    # compaction: more kept rows than a tree can accept
+    assert lib.ddt_compact_kv(ctypes.c_void_p(256), 64, ctypes.c_void_p(256), 2, 2, 128, 1024,
+                              128, 2, 10, None) == -2
+    assert lib.ddt_argmax(None, 2, 4, 4, 4, None, None) == -3
+
+
+def test_workspace_queries():
+    lib = _lib.load()
+    ws = lib.ddt_topk_tree_workspace_bytes(15, 151936, 256)
+    assert ws > 15 * 10 * 256 * 8
+    assert lib.ddt_tree_attn_workspace_bytes(257, 32, 128, 2) >= 2 * 257 * 32 * 130 * 4
+
+
+@pytest.mark.parametrize("depths,vocab,budget,expect", [
+    (15, 151936, 256, 256), (3, 3, 40, 39), (0, 10, 5, 0), (15, 10, 0, 0), (1, 1000, 8, 8),
+    (2, 4, 100, 20)])
+def test_expected_node_count(depths, vocab, budget, expect):
+    from mdflash_b200.kernels import expected_node_count
+    assert expected_node_count(depths, vocab, budget) == expect
