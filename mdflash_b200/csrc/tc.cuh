@@ -58,6 +58,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-collective bounded wait: every lane of the warp calls it and gets the same
+// answer, so code after it that uses .sync.aligned tcgen05 instructions stays converged.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               uint64_t timeout_ns) {
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    const bool ok = mbar_try_wait(bar, parity);
+    if (__all_sync(DDT_FULL_MASK, ok)) return true;
+    if ((it & 63u) == 63u) {
+      const bool stop = (*abort != 0) || (global_timer_ns() - t0 > timeout_ns);
+      if (__any_sync(DDT_FULL_MASK, stop)) return false;
+    }
+  }
+}
+
 // Bounded wait that ignores the abort flag: used while unwinding to let transfers that
 // are already in flight complete.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {

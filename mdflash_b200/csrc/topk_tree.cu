@@ -117,7 +117,9 @@ __device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, 
     const int sh = pass_shift<kBF16>(p);
     if (tid < 256) s.hist[tid] = 0;
     __syncthreads();
+    // read the pass state before the barrier that precedes its update
     const unsigned long long prefix = s.prefix, mask = s.mask;
+    const uint32_t rem = s.remaining;
 #pragma unroll
     for (int j = 0; j < EPT; ++j) {
       const bool act = comp[j] != 0ull && (comp[j] & mask) == prefix;
@@ -146,7 +148,6 @@ __device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, 
       for (int w = 0; w < (tid >> 5); ++w) base += s.warp_tot[w];
       const uint32_t cum = base + x;
       const uint32_t prev = cum - v;
-      const uint32_t rem = s.remaining;
       if (prev < rem && cum >= rem) {
         const uint32_t b = 255u - tid;
         const uint32_t nrem = rem - prev;
@@ -459,12 +460,17 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
     }
   }
   __syncthreads();
-  for (int i = static_cast<int>(rs.out_count) + tid; i < k; i += kThreads) my_cand[i] = 0ull;
+  const uint32_t n_out = rs.out_count < static_cast<uint32_t>(k) ? rs.out_count : k;
+  for (int i = static_cast<int>(n_out) + tid; i < k; i += kThreads) my_cand[i] = 0ull;
   if (tid == 0) {
     chunk_max[d * C + c] = cm;
     chunk_sum[d * C + c] = csum;
-    cand_count[d * C + c] = rs.out_count;
-    __threadfence();
+    cand_count[d * C + c] = n_out;
+  }
+  // every writer fences its own stores to GPU scope before the CTA signals completion
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
     const uint32_t prev = atomicAdd(&counters[d], 1u);
     rs.is_last = (prev == static_cast<uint32_t>(C - 1));
   }
@@ -538,9 +544,9 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
     if (out_top_lp) out_top_lp[static_cast<int64_t>(d) * k + i] = lpv;
     if (out_top_ids) out_top_ids[static_cast<int64_t>(d) * k + i] = idx;
   }
+  __threadfence();
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
     const uint32_t prev = atomicAdd(&counters[L], 1u);
     rs.is_last = (prev == static_cast<uint32_t>(L - 1));
   }

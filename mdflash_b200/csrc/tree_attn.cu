@@ -266,6 +266,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
   } else {
     // ---------------------------- softmax warps ------------------------------------
+    // tcgen05.ld / tcgen05.st are warp-collective (.sync.aligned): every lane executes
+    // them on every path; per-row conditions only predicate arithmetic and stores.
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
@@ -280,7 +282,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     unsigned char* prow = sP + r * 128;
     const int sw = r & 7;
     for (int j = 0; j < nt; ++j) {
-      if (!tc::mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort_flag, kTimeoutNs)) {
+      if (!tc::mbar_wait_warp(&bars.s_full[j & 1], (j >> 1) & 1, abort_flag, kTimeoutNs)) {
         ok = false;
         break;
       }
@@ -314,11 +316,11 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
       }
       const float mref = (m_used == -INFINITY) ? 0.f : m_used;
-      if (j > 0 && !tc::mbar_wait(&bars.o_ready, (j - 1) & 1, abort_flag, kTimeoutNs)) {
+      if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready, (j - 1) & 1, abort_flag, kTimeoutNs)) {
         ok = false;
         break;
       }
-      if (rescale) {
+      if (__any_sync(DDT_FULL_MASK, rescale)) {  // lanes without a new max scale by 1
         tc::tc_fence_after();
         const uint32_t ob = tl + 2 * kBlockN;
 #pragma unroll
@@ -357,45 +359,50 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc::tc_fence_before();
       tc::mbar_arrive(&bars.p_full);
     }
-    if (ok && nt > 0 && !tc::mbar_wait(&bars.o_ready, (nt - 1) & 1, abort_flag, kTimeoutNs)) ok = false;
-    if (!ok) raise_abort(bars, p.status);
-    if (valid) {
-      const long long row = static_cast<long long>(node) * p.q_heads + qh;
-      if (p.partial) {
-        float* op = p.o_part + (static_cast<long long>(split) * p.n_nodes * p.q_heads + row) * kHeadDim;
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          if (ok && nt > 0) {
-            tc::tc_fence_after();
-            tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
-            tc::tmem_wait_ld();
-          } else {
+    if (ok && nt > 0 && !tc::mbar_wait_warp(&bars.o_ready, (nt - 1) & 1, abort_flag, kTimeoutNs))
+      ok = false;
+    if (!ok && lane == 0) raise_abort(bars, p.status);
+    const bool have = ok && nt > 0;  // warp-uniform
+    const long long row = static_cast<long long>(node) * p.q_heads + qh;
+    if (have) tc::tc_fence_after();
+    if (p.partial) {
+      float* op = p.o_part + (static_cast<long long>(split) * p.n_nodes * p.q_heads + row) * kHeadDim;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        if (have) {
+          tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
+          tc::tmem_wait_ld();
+        } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = 0u;
-          }
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (valid) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
             *reinterpret_cast<float4*>(op + c * 32 + e) =
                 make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
                             __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
         }
+      }
+      if (valid) {
         const long long mi = static_cast<long long>(split) * p.n_nodes * p.q_heads + row;
-        p.m_part[mi] = (ok && nt > 0) ? m_used : -INFINITY;
-        p.l_part[mi] = (ok && nt > 0) ? l : 0.f;
-      } else {
-        const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
-        __nv_bfloat16* orow = p.out + static_cast<long long>(node) * p.o_node_stride +
-                              static_cast<long long>(qh) * p.o_head_stride;
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          if (ok && nt > 0) {
-            tc::tc_fence_after();
-            tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
-            tc::tmem_wait_ld();
-          } else {
+        p.m_part[mi] = have ? m_used : -INFINITY;
+        p.l_part[mi] = have ? l : 0.f;
+      }
+    } else {
+      const float inv = (have && l > 0.f) ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.out + static_cast<long long>(vnode) * p.o_node_stride +
+                            static_cast<long long>(qh) * p.o_head_stride;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        if (have) {
+          tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
+          tc::tmem_wait_ld();
+        } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = 0u;
-          }
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (valid) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             uint4 v;
