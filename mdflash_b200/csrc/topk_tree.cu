@@ -225,110 +225,165 @@ __device__ __forceinline__ bool ranks_less(const unsigned long long (&a)[4],
   return false;
 }
 
-// One warp replays ddtree.py:116-147.  Returns the node count (on every lane).
+// Adds 1 to level `lv` of a packed rank tuple.  The word is chosen with predicated,
+// fully unrolled updates so the tuple stays in registers (a runtime array index would
+// move it to local memory).
+__device__ __forceinline__ void bump_level(unsigned long long (&r)[4], int lv) {
+  const int word = lv / kLevelsPerWord;
+  const unsigned long long inc = 1ull << rank_shift(lv);
+#pragma unroll
+  for (int w = 0; w < 4; ++w) r[w] += (w == word) ? inc : 0ull;
+}
+
+struct Cand {
+  double logw;
+  unsigned long long r[4];
+};
+
+// a pops before b in the reference heap: larger logw, then the smaller rank tuple
+__device__ __forceinline__ bool pops_before(const Cand& a, const Cand& b) {
+  if (a.logw != b.logw) return a.logw > b.logw;
+  return ranks_less(a.r, b.r);
+}
+
+__device__ __forceinline__ Cand load_cand(Frontier& f, int s) {
+  Cand c;
+  c.logw = f.logw[s];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) c.r[w] = f.rw(w, s);
+  return c;
+}
+
+__device__ __forceinline__ void store_cand(Frontier& f, int s, const Cand& c, uint32_t meta) {
+  f.logw[s] = c.logw;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) f.rw(w, s) = c.r[w];
+  f.meta[s] = meta;
+}
+
+// Warp-wide best frontier slot among the slots each lane offers (-1 = none).
+__device__ __forceinline__ int warp_best_slot(Frontier& f, int slot) {
+  const int lane = threadIdx.x & 31;
+  double m = slot >= 0 ? f.logw[slot] : -INFINITY;
+  const bool has = slot >= 0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(DDT_FULL_MASK, m, o));
+  const unsigned tied = __ballot_sync(DDT_FULL_MASK, has && f.logw[has ? slot : 0] == m);
+  if (tied == 0u) return -1;
+  if (__popc(tied) == 1) return __shfl_sync(DDT_FULL_MASK, slot, __ffs(tied) - 1);
+  const bool mine = (tied >> lane) & 1u;
+  unsigned long long r[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) r[w] = mine ? f.rw(w, slot) : ~0ull;
+  int cand = mine ? slot : 0x7fffffff;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long q[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) q[w] = __shfl_xor_sync(DDT_FULL_MASK, r[w], o);
+    const int qc = __shfl_xor_sync(DDT_FULL_MASK, cand, o);
+    const bool qless = ranks_less(q, r) || (!ranks_less(r, q) && qc < cand);
+    if (qless) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) r[w] = q[w];
+      cand = qc;
+    }
+  }
+  return cand;
+}
+
+// One warp replays ddtree.py:116-147 exactly.  The frontier holds one entry per sibling
+// chain (the next unpopped child of some popped node).  Each round the warp finds the
+// best entry W and the best entry S2 among all others; then lane 0 pops along W's chain
+// for as long as the chain's next sibling still pops before S2 and before every child
+// chain pushed during the run (the heap would pop exactly those, in that order), so a
+// full frontier scan is paid once per run instead of once per node.
 __device__ int heap_build(const float* lp, int L, int k, int budget, Frontier f,
                           uint32_t* node_meta) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) {
-    f.logw[0] = static_cast<double>(lp[0]);
-    f.rw(0, 0) = 1ull << rank_shift(0);
-    f.rw(1, 0) = 0ull;
-    f.rw(2, 0) = 0ull;
-    f.rw(3, 0) = 0ull;
-    f.meta[0] = pack_meta(0, 1, 0);
+    Cand c0;
+    c0.logw = static_cast<double>(lp[0]);
+    c0.r[0] = 1ull << rank_shift(0);
+    c0.r[1] = c0.r[2] = c0.r[3] = 0ull;
+    store_cand(f, 0, c0, pack_meta(0, 1, 0));
   }
   __syncwarp();
   int count = 0, fcount = 1;
   while (count < budget && fcount > 0) {
-    // lane-local best among slots lane, lane + 32, ...
-    int bs = -1;
-    double bl = -DBL_MAX;
+    // lane-local best and second best among slots lane, lane + 32, ...
+    int b1 = -1, b2 = -1;
+    Cand c1, c2;
     for (int s = lane; s < fcount; s += 32) {
-      const double x = f.logw[s];
-      bool take = (bs < 0) || (x > bl);
-      if (!take && x == bl) {
-        unsigned long long ra[4] = {f.rw(0, s), f.rw(1, s), f.rw(2, s), f.rw(3, s)};
-        unsigned long long rb[4] = {f.rw(0, bs), f.rw(1, bs), f.rw(2, bs), f.rw(3, bs)};
-        take = ranks_less(ra, rb);
-      }
-      if (take) {
-        bs = s;
-        bl = x;
+      const Cand c = load_cand(f, s);
+      if (b1 < 0 || pops_before(c, c1)) {
+        b2 = b1;
+        c2 = c1;
+        b1 = s;
+        c1 = c;
+      } else if (b2 < 0 || pops_before(c, c2)) {
+        b2 = s;
+        c2 = c;
       }
     }
-    double m = (bs >= 0) ? bl : -INFINITY;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(DDT_FULL_MASK, m, o));
-    const unsigned tied = __ballot_sync(DDT_FULL_MASK, bs >= 0 && bl == m);
-    int wl;
-    if (__popc(tied) == 1) {
-      wl = __ffs(tied) - 1;
-    } else {
-      const bool mine = (tied >> lane) & 1u;
-      unsigned long long r[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) r[w] = mine ? f.rw(w, bs) : ~0ull;
-      int cand = mine ? lane : 32;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        unsigned long long q[4];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) q[w] = __shfl_xor_sync(DDT_FULL_MASK, r[w], o);
-        const int qc = __shfl_xor_sync(DDT_FULL_MASK, cand, o);
-        const bool qless = ranks_less(q, r) || (!ranks_less(r, q) && qc < cand);
-        if (qless) {
-#pragma unroll
-          for (int w = 0; w < 4; ++w) r[w] = q[w];
-          cand = qc;
-        }
-      }
-      wl = cand;
-    }
-    const int slot = __shfl_sync(DDT_FULL_MASK, bs, wl);
-    const double logw = f.logw[slot];
-    unsigned long long rk[4] = {f.rw(0, slot), f.rw(1, slot), f.rw(2, slot), f.rw(3, slot)};
-    const uint32_t meta = f.meta[slot];
-    const int depth = (meta >> 12) & 31;
-    const int rank = static_cast<int>(meta >> 17);
-    const int cur = count + 1;
-    __syncwarp();
+    const int W = warp_best_slot(f, b1);
+    const int S2 = warp_best_slot(f, (b1 == W) ? b2 : b1);
     if (lane == 0) {
-      node_meta[count] = meta;
+      Cand cur = load_cand(f, W);
+      uint32_t meta = f.meta[W];
+      bool have2 = S2 >= 0;
+      Cand k2;
+      if (have2) k2 = load_cand(f, S2);
       int fc = fcount;
-      if (rank + 1 < k) {
-        // ddtree.py:141: logw - lp[d-1, rank] + lp[d-1, rank+1], left to right in double
-        const double sib = (logw - static_cast<double>(lp[(depth - 1) * k + rank])) +
-                           static_cast<double>(lp[(depth - 1) * k + rank + 1]);
-        f.logw[slot] = sib;
-        const int lv = depth - 1;
-        f.rw(0, slot) = rk[0];
-        f.rw(1, slot) = rk[1];
-        f.rw(2, slot) = rk[2];
-        f.rw(3, slot) = rk[3];
-        f.rw(lv / kLevelsPerWord, slot) = rk[lv / kLevelsPerWord] + (1ull << rank_shift(lv));
-        f.meta[slot] = pack_meta(static_cast<int>(meta & 0xfffu), depth, rank + 1);
-      } else {
-        const int last = fc - 1;
-        if (slot != last) {
-          f.logw[slot] = f.logw[last];
-          for (int w = 0; w < 4; ++w) f.rw(w, slot) = f.rw(w, last);
-          f.meta[slot] = f.meta[last];
+      for (;;) {
+        const int depth = (meta >> 12) & 31;
+        const int rank = static_cast<int>(meta >> 17);
+        const int parent = static_cast<int>(meta & 0xfffu);
+        const int cur_index = count + 1;
+        node_meta[count] = meta;
+        ++count;
+        if (depth < L) {  // ddtree.py:144-147: first child, logw + lp[depth, 0]
+          Cand ch;
+          ch.logw = cur.logw + static_cast<double>(lp[depth * k]);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) ch.r[w] = cur.r[w];
+          bump_level(ch.r, depth);
+          store_cand(f, fc, ch, pack_meta(cur_index, depth + 1, 0));
+          ++fc;
+          if (!have2 || pops_before(ch, k2)) {
+            k2 = ch;
+            have2 = true;
+          }
         }
-        fc = last;
-      }
-      if (depth < L) {
-        // ddtree.py:146: logw + lp[depth, 0]
-        const double ch = logw + static_cast<double>(lp[depth * k]);
-        f.logw[fc] = ch;
-        for (int w = 0; w < 4; ++w) f.rw(w, fc) = rk[w];
-        f.rw(depth / kLevelsPerWord, fc) = rk[depth / kLevelsPerWord] + (1ull << rank_shift(depth));
-        f.meta[fc] = pack_meta(cur, depth + 1, 0);
-        fc += 1;
+        if (rank + 1 < k) {  // ddtree.py:139-142: next sibling
+          Cand sib;
+          sib.logw = (cur.logw - static_cast<double>(lp[(depth - 1) * k + rank])) +
+                     static_cast<double>(lp[(depth - 1) * k + rank + 1]);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) sib.r[w] = cur.r[w];
+          const int lv = depth - 1;
+          bump_level(sib.r, lv);
+          const uint32_t smeta = pack_meta(parent, depth, rank + 1);
+          if (count < budget && (!have2 || pops_before(sib, k2))) {
+            cur = sib;
+            meta = smeta;
+            continue;
+          }
+          store_cand(f, W, sib, smeta);
+        } else {
+          const int last = fc - 1;
+          if (W != last) {
+            const Cand lc = load_cand(f, last);
+            store_cand(f, W, lc, f.meta[last]);
+          }
+          fc = last;
+        }
+        break;
       }
       fcount = fc;
     }
     fcount = __shfl_sync(DDT_FULL_MASK, fcount, 0);
-    count += 1;
+    count = __shfl_sync(DDT_FULL_MASK, count, 0);
     __syncwarp();
   }
   return count;

@@ -21,6 +21,28 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+class LaunchStats:
+    """Counts this library's kernel launches, and (when enabled) brackets every tree
+    attention call with CUDA events on its stream so its device time can be measured
+    inside a larger timed region."""
+
+    def __init__(self):
+        self.launches = 0
+        self.time_attention = False
+        self.attn_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+
+    def reset(self, time_attention: bool = False) -> None:
+        self.launches = 0
+        self.time_attention = time_attention
+        self.attn_events = []
+
+    def attention_ms(self) -> list[float]:
+        return [a.elapsed_time(b) for a, b in self.attn_events]
+
+
+STATS = LaunchStats()
+
+
 def _dtype_code(t: torch.Tensor) -> int:
     if t.dtype == torch.bfloat16:
         return DDT_BF16
@@ -148,6 +170,7 @@ def topk_tree(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor 
         tree.verify_ids.data_ptr(), tree.verify_pos.data_ptr(), ws.data_ptr(), ws.numel(),
         _stream(dev))
     check(rc, "ddt_topk_tree")
+    STATS.launches += 1
     return tree
 
 
@@ -162,6 +185,7 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
         out = torch.empty(rows, dtype=torch.int64, device=dev)
     check(_lib.load().ddt_argmax(x.data_ptr(), _dtype_code(x), rows, cols, x.stride(0),
                                  out.data_ptr(), _stream(dev)), "ddt_argmax")
+    STATS.launches += 1
     return out.view(logits.shape[:-1])
 
 
@@ -216,6 +240,7 @@ def accept_compact(posterior: torch.Tensor, tree: DeviceTree, kv: KvTable, past_
         kv.ptrs.data_ptr(), kv.n, kv.heads, kv.head_dim, kv.head_stride, kv.seq_stride,
         kv.elem_bytes, past_length, accepted.data_ptr(), n_accepted.data_ptr(),
         next_token.data_ptr(), _stream(dev)), "ddt_accept_compact")
+    STATS.launches += 1
     return accepted, n_accepted, next_token
 
 
@@ -236,6 +261,7 @@ def compact_kv(keep, kv: KvTable, past_length: int) -> None:
                                      kv.heads, kv.head_dim, kv.head_stride, kv.seq_stride,
                                      kv.elem_bytes, past_length, _stream(kv.device)),
           "ddt_compact_kv")
+    STATS.launches += 1
 
 
 def _q_view(q: torch.Tensor):
@@ -288,13 +314,37 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if not causal and anc_bits is None:
         raise ValueError("tree mode needs ancestor bitmasks")
     words = anc_bits.shape[1] if anc_bits is not None else 0
+    stream = _stream(dev)
+    if STATS.time_attention:
+        # external events are recorded as graph nodes when captured, so they also time
+        # the launch inside a replayed CUDA graph
+        ev = (torch.cuda.Event(enable_timing=True, external=True),
+              torch.cuda.Event(enable_timing=True, external=True))
+        ev[0].record()
     rc = lib.ddt_tree_attn(
         q.data_ptr(), qns, qhs, k.data_ptr(), v.data_ptr(), khs, kss, out.data_ptr(),
         out.stride(0), out.stride(1), n, past_length, hq, hkv, d,
         anc_bits.data_ptr() if anc_bits is not None else None, words, mode, float(scale),
-        kv_splits, ws.data_ptr(), ws.numel(), status.data_ptr(), _stream(dev))
+        kv_splits, ws.data_ptr(), ws.numel(), status.data_ptr(), stream)
     check(rc, "ddt_tree_attn")
+    if STATS.time_attention:
+        ev[1].record()
+        STATS.attn_events.append(ev)
+    STATS.launches += 1 + (1 if attn_splits(n, hq, hkv, past_length, kv_splits) > 1 else 0)
     return out
+
+
+def attn_splits(n_nodes: int, q_heads: int, kv_heads: int, past_length: int,
+                kv_splits: int = 0) -> int:
+    """The key-range split count ddt_tree_attn uses (mirrors pick_splits in the kernel)."""
+    if kv_splits > 0:
+        return kv_splits
+    group = q_heads // kv_heads
+    units = kv_heads * ((n_nodes * group + 127) // 128)
+    tiles = (past_length + n_nodes + 127) // 128
+    s = 1 if units >= 148 else 148 // units
+    cap = max(tiles // 4, 1)
+    return max(1, min(s, cap, 64))
 
 
 def tree_attention_partial(q, k_shard, v_shard, key_begin: int, key_end: int, anc_bits,
@@ -325,6 +375,7 @@ def tree_attention_partial(q, k_shard, v_shard, key_begin: int, key_end: int, an
         DDT_MASK_CAUSAL if causal else DDT_MASK_TREE, float(scale), status.data_ptr(),
         _stream(dev))
     check(rc, "ddt_tree_attn_partial")
+    STATS.launches += 1
     return o, m, l
 
 
@@ -338,6 +389,7 @@ def attn_merge(o_parts: torch.Tensor, m_parts: torch.Tensor, l_parts: torch.Tens
     check(_lib.load().ddt_attn_merge(o_parts.data_ptr(), m_parts.data_ptr(), l_parts.data_ptr(),
                                      o_parts.shape[0], n_nodes, q_heads, d, out.data_ptr(),
                                      out.stride(0), out.stride(1), _stream(dev)), "ddt_attn_merge")
+    STATS.launches += 1
     return out
 
 
@@ -352,4 +404,5 @@ def mask_to_bits(mask_block: torch.Tensor, words: int | None = None) -> torch.Te
     check(_lib.load().ddt_mask_to_bits(mask_block.data_ptr(), _dtype_code(mask_block), n,
                                        mask_block.stride(0), bits.data_ptr(), words, _stream(dev)),
           "ddt_mask_to_bits")
+    STATS.launches += 1
     return bits

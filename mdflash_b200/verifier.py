@@ -1,0 +1,117 @@
+"""Device-resident DDTree verify step (the hot path of ddtree_generate, ddtree.py:439-491,
+without the host round trips of the reference).
+
+    tree build   ddt_topk_tree   draft logits -> tree, ancestor bitmasks, verify ids / pos
+    verify       target forward with attn_implementation="ddtree_tree" (tcgen05 kernel),
+                 new K/V written in place into a TreeKVCache (no torch.cat)
+    posterior    ddt_argmax      [N, V] logits -> [N] tokens
+    commit       ddt_accept_compact   greedy walk + K/V compaction of every layer
+
+Nothing in ``step`` synchronises the host; the caller reads the (small) result when it
+needs it, then calls ``commit`` to set the cache length to past + accepted.
+
+``capture`` records one step for a fixed (prefix length, budget) into a CUDA graph; a
+replay re-runs every kernel of the step (tree build from the current contents of the
+draft-logit buffer, the 36-layer forward, argmax, walk, compaction) with one launch
+from the host, which removes the Python / launch overhead of the forward.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import attention as A
+from . import kernels as K
+from .cache import TreeKVCache
+
+
+@dataclass
+class StepResult:
+    n_nodes: int
+    accepted: torch.Tensor      # i64 [n_nodes] (first n_accepted valid), device
+    n_accepted: torch.Tensor    # i32 [1], device
+    next_token: torch.Tensor    # i64 [1], device
+    posterior: torch.Tensor     # i64 [n_nodes], device
+    logits: torch.Tensor | None = None
+
+
+class TreeVerifier:
+    def __init__(self, target: torch.nn.Module, cache: TreeKVCache, budget: int, depths: int,
+                 vocab: int, device: torch.device | str = "cuda", keep_logits: bool = False):
+        self.target = target
+        self.cache = cache
+        self.budget = budget
+        self.depths = depths
+        self.vocab = vocab
+        self.device = torch.device(device)
+        self.keep_logits = keep_logits
+        self.tree = K.DeviceTree.allocate(self.device, budget, depths, vocab)
+        n_cap = budget + 1
+        self.posterior = torch.zeros(n_cap, dtype=torch.int64, device=self.device)
+        self.accepted = torch.zeros(n_cap, dtype=torch.int64, device=self.device)
+        self.n_accepted = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.next_token = torch.zeros(1, dtype=torch.int64, device=self.device)
+
+    @torch.inference_mode()
+    def step(self, draft_logits: torch.Tensor, root_token: torch.Tensor, start: int) -> StepResult:
+        """One verify step over the prefix of length ``start`` (the cache must hold
+        exactly ``start`` rows).  ``draft_logits`` [depths, vocab] and ``root_token`` [1]
+        are device tensors."""
+        if self.cache.get_seq_length() != start:
+            raise RuntimeError(f"cache holds {self.cache.get_seq_length()} rows, expected {start}")
+        tree = K.topk_tree(draft_logits, self.budget, root_token, start, out=self.tree)
+        n = tree.n_nodes
+        ids = tree.verify_ids[:n].view(1, n)
+        pos = tree.verify_pos[:n].view(1, n)
+        with A.tree_verify(tree, start, n):
+            out = self.target(ids, position_ids=pos, past_key_values=self.cache, use_cache=True)
+        logits = out.logits[0]
+        post = K.argmax(logits, out=self.posterior[:n])
+        K.accept_compact(post, tree, self.cache.kv_table(), start, accepted=self.accepted,
+                         n_accepted=self.n_accepted, next_token=self.next_token, n_nodes=n)
+        return StepResult(n, self.accepted, self.n_accepted, self.next_token, post,
+                          logits if self.keep_logits else None)
+
+    def commit(self, start: int, n_accepted: int) -> None:
+        """Sets the cache length to start + n_accepted after the caller read the count."""
+        self.cache.crop(start + n_accepted)
+
+
+class CapturedStep:
+    """A verify step recorded in a CUDA graph for one prefix length.
+
+    Inputs are read from ``draft_logits`` / ``root_token`` (device buffers owned by this
+    object: copy new values in before ``replay``); outputs land in ``result``."""
+
+    def __init__(self, verifier: TreeVerifier, start: int, warmup: int = 2,
+                 time_attention: bool = False):
+        self.verifier = verifier
+        self.start = start
+        v = verifier
+        self.draft_logits = torch.zeros((v.depths, v.vocab), dtype=torch.bfloat16, device=v.device)
+        self.root_token = torch.zeros(1, dtype=torch.int64, device=v.device)
+        side = torch.cuda.Stream(v.device)
+        side.wait_stream(torch.cuda.current_stream(v.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                v.step(self.draft_logits, self.root_token, start)
+                v.cache.crop(start)
+        torch.cuda.current_stream(v.device).wait_stream(side)
+        torch.cuda.synchronize(v.device)
+        self.graph = torch.cuda.CUDAGraph()
+        K.STATS.reset(time_attention=time_attention)
+        with torch.cuda.graph(self.graph):
+            self.result = v.step(self.draft_logits, self.root_token, start)
+        self.launches_per_replay = K.STATS.launches
+        self.attn_events = list(K.STATS.attn_events)
+        K.STATS.reset()
+        v.cache.crop(start)
+
+    def replay(self) -> StepResult:
+        self.graph.replay()
+        return self.result
+
+    def attention_ms(self) -> list[float]:
+        """Device time of each tree-attention call of the most recent replay."""
+        return [a.elapsed_time(b) for a, b in self.attn_events]
