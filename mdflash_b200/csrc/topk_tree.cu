@@ -165,6 +165,29 @@ __device__ __forceinline__ bool selected(unsigned long long c, const RadixShared
   return c != 0ull && (c & s.mask) >= s.prefix;
 }
 
+// Appends the selected composites of this thread to out[0, cap) in arbitrary order with
+// one shared atomic per warp and element slot (ballot + prefix count), instead of one
+// atomic per element on a single counter.
+template <int EPT>
+__device__ __forceinline__ void append_selected(const unsigned long long (&comp)[EPT],
+                                                RadixShared& s, unsigned long long* out,
+                                                uint32_t cap) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const bool sel = selected(comp[j], s);
+    const unsigned m = __ballot_sync(DDT_FULL_MASK, sel);
+    if (m == 0u) continue;
+    uint32_t base = 0;
+    if (lane == __ffs(m) - 1) base = atomicAdd(&s.out_count, static_cast<uint32_t>(__popc(m)));
+    base = __shfl_sync(DDT_FULL_MASK, base, __ffs(m) - 1);
+    if (sel) {
+      const uint32_t pos = base + __popc(m & ((1u << lane) - 1u));
+      if (pos < cap) out[pos] = comp[j];
+    }
+  }
+}
+
 __device__ __forceinline__ float block_max_f(float v, RadixShared& s) {
   v = warp_max_f(v);
   if ((threadIdx.x & 31) == 0) s.fred[threadIdx.x >> 5] = v;
@@ -507,13 +530,7 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
   if (tid == 0) rs.out_count = 0;
   __syncthreads();
   unsigned long long* my_cand = cand + (static_cast<int64_t>(d) * C + c) * k;
-#pragma unroll
-  for (int j = 0; j < kEPT; ++j) {
-    if (selected(comp[j], rs)) {
-      const uint32_t pos = atomicAdd(&rs.out_count, 1u);
-      if (pos < static_cast<uint32_t>(k)) my_cand[pos] = comp[j];
-    }
-  }
+  append_selected<kEPT>(comp, rs, my_cand, static_cast<uint32_t>(k));
   __syncthreads();
   const uint32_t n_out = rs.out_count < static_cast<uint32_t>(k) ? rs.out_count : k;
   for (int i = static_cast<int>(n_out) + tid; i < k; i += kThreads) my_cand[i] = 0ull;
@@ -560,13 +577,7 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem);
   int kpad = 1;
   while (kpad < k) kpad <<= 1;
-#pragma unroll
-  for (int j = 0; j < kEPT; ++j) {
-    if (selected(comp[j], rs)) {
-      const uint32_t pos = atomicAdd(&rs.out_count, 1u);
-      if (pos < static_cast<uint32_t>(kpad)) sel[pos] = comp[j];
-    }
-  }
+  append_selected<kEPT>(comp, rs, sel, static_cast<uint32_t>(kpad));
   __syncthreads();
   for (int i = k + tid; i < kpad; i += kThreads) sel[i] = 0ull;
   __syncthreads();
