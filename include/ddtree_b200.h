@@ -47,6 +47,7 @@ extern "C" {
 #define DDT_ERR_CUDA (-5)      /* CUDA runtime / launch error */
 #define DDT_ERR_TIMEOUT (-6)   /* a bounded device-side wait expired (status word) */
 #define DDT_ERR_WORKSPACE (-7) /* workspace too small */
+#define DDT_ERR_SCRATCH_LIMIT (-8) /* needs more than the fixed no-alloc scratch array */
 
 /* element types */
 #define DDT_F32 0
@@ -80,6 +81,25 @@ int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths, int64_t v
                   int64_t anc_words, const int64_t* root_token, int64_t start,
                   int64_t* verify_ids, int64_t* verify_pos, void* workspace,
                   size_t workspace_bytes, void* stream);
+
+/* Tree build that allocates nothing and takes no workspace.  No counterpart in the
+ * reference: it serves callers that cannot allocate device memory when they call (a
+ * serving stack that owns all device memory in its own pool after start-up, or a plugin
+ * interface that passes only inputs and outputs).  Arguments and outputs are those of
+ * ddt_topk_tree.  Scratch lives in a DDT_NOALLOC_SCRATCH_BYTES array inside the library's
+ * device image, held by every GPU that loads the library until the process exits; its
+ * address is looked up on a device's first call (make that call before any stream
+ * capture).  Problems whose workspace (ddt_topk_tree_workspace_bytes) exceeds the array
+ * return DDT_ERR_SCRATCH_LIMIT: 15 depths x 151936 vocabulary fit up to budget 1024.
+ * All calls share the array, so calls that overlap on the GPU race. */
+#define DDT_NOALLOC_SCRATCH_BYTES (2u << 20)
+int ddt_topk_tree_noalloc(const void* draft_logits, int dtype, int64_t depths, int64_t vocab,
+                          int64_t row_stride, int64_t budget, float* top_log_probs,
+                          int64_t* top_token_ids, int64_t* node_token_ids,
+                          int64_t* node_depths, int32_t* parents, int32_t* node_count,
+                          uint32_t* anc_bits, int64_t anc_words, const int64_t* root_token,
+                          int64_t start, int64_t* verify_ids, int64_t* verify_pos,
+                          void* stream);
 
 /* ---- greedy posterior ---------------------------------------------------
  * logits [rows, cols] (row stride in elements) -> out i64 [rows]; ties go to the lowest

@@ -33,6 +33,8 @@ SIGNATURES = {
     "ddt_topk_tree_workspace_bytes": (_S, [_I, _I, _I]),
     "ddt_topk_tree": (_i, [_P, _i, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P,
                            _P, _S, _P]),
+    "ddt_topk_tree_noalloc": (_i, [_P, _i, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I,
+                                   _P, _P, _P]),
     "ddt_argmax": (_i, [_P, _i, _I, _I, _I, _P, _P]),
     "ddt_accept_compact": (_i, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "ddt_compact_kv": (_i, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P]),

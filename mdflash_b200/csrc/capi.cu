@@ -11,6 +11,8 @@ extern "C" const char* ddt_error_string(int code) {
     case DDT_ERR_CUDA: return "CUDA runtime or launch error";
     case DDT_ERR_TIMEOUT: return "bounded device wait expired";
     case DDT_ERR_WORKSPACE: return "workspace too small";
+    case DDT_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the fixed no-alloc array holds";
     default: return "unknown error";
   }
 }

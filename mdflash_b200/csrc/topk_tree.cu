@@ -756,3 +756,74 @@ extern "C" int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths
   }
   return launch_status();
 }
+
+// ---------------------------------------------------------------------------------------
+// Tree build without a caller-provided workspace.
+//
+// Some callers of this library cannot allocate device memory at call time: serving stacks
+// that reserve all device memory in their own pool at start-up and forbid any allocation
+// afterwards, and plugin hosts whose interface only carries inputs and outputs, so there is
+// no way to hand a workspace through.  For them the tree build keeps its scratch (chunk
+// statistics, top-k candidates, the merged log-prob table and the atomic tickets) in a
+// fixed array of this library's device image instead.  The array is
+// DDT_NOALLOC_SCRATCH_BYTES long and every GPU that loads the library keeps it until the
+// process exits.  Its device address is looked up once per device, on that device's first
+// call, with cudaGetSymbolAddress (so the first call on a device should happen before any
+// stream capture).  All calls share the one array: calls whose work overlaps on the GPU
+// (different streams, or several host threads) race and must be serialised by the caller.
+// ---------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace ddt {
+namespace topk {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[DDT_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+static void* g_noalloc_addr[kMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+
+// Device address of this device's copy of the scratch array (looked up once per device).
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DDT_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return DDT_ERR_CAPACITY;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return DDT_ERR_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return DDT_OK;
+}
+
+}  // namespace topk
+}  // namespace ddt
+
+extern "C" int ddt_topk_tree_noalloc(const void* draft_logits, int dtype, int64_t depths,
+                                     int64_t vocab, int64_t row_stride, int64_t budget,
+                                     float* top_log_probs, int64_t* top_token_ids,
+                                     int64_t* node_token_ids, int64_t* node_depths,
+                                     int32_t* parents, int32_t* node_count, uint32_t* anc_bits,
+                                     int64_t anc_words, const int64_t* root_token, int64_t start,
+                                     int64_t* verify_ids, int64_t* verify_pos, void* stream) {
+  if (depths > 0 && vocab > 0 && budget > 0 &&
+      ddt_topk_tree_workspace_bytes(depths, vocab, budget) > DDT_NOALLOC_SCRATCH_BYTES)
+    return DDT_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  int rc = topk::noalloc_scratch(&scratch);
+  if (rc != DDT_OK) return rc;
+  if (depths > 0 && vocab > 0 && budget > 0 && depths <= DDT_MAX_DEPTH) {
+    // the array keeps the previous call's contents; the atomic tickets must start at zero
+    const size_t tickets = sizeof(uint32_t) * static_cast<size_t>(depths + 1);
+    if (cudaMemsetAsync(static_cast<unsigned char*>(scratch) +
+                            topk::ws_layout(depths, vocab, budget < vocab ? budget : vocab).counters,
+                        0, tickets, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+      return DDT_ERR_CUDA;
+  }
+  return ddt_topk_tree(draft_logits, dtype, depths, vocab, row_stride, budget, top_log_probs,
+                       top_token_ids, node_token_ids, node_depths, parents, node_count, anc_bits,
+                       anc_words, root_token, start, verify_ids, verify_pos, scratch,
+                       DDT_NOALLOC_SCRATCH_BYTES, stream);
+}
