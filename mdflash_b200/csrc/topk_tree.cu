@@ -27,8 +27,9 @@ namespace ddt {
 namespace topk {
 
 constexpr int kThreads = 512;
-constexpr int kEPT = 32;                    // elements per thread held in registers
-constexpr int kChunk = kThreads * kEPT;     // max elements per chunk (16384)
+constexpr int kEPT = 40;                    // elements per thread held in registers
+constexpr int kChunk = kThreads * kEPT;     // max elements per chunk (20480): 8 chunks of
+                                            // a 151936 vocabulary, 120 CTAs for 15 depths
 constexpr int kMaxCand = kThreads * kEPT;   // max candidates merged per row
 constexpr int kRankBits = 12;               // bits per level in the packed rank tuple
 constexpr int kLevelsPerWord = 5;
@@ -81,10 +82,46 @@ __host__ inline size_t smem_bytes(int64_t L, int64_t k, int64_t budget) {
   while (kpad < k) kpad <<= 1;
   size_t merge = sizeof(unsigned long long) * kpad;
   const int64_t fcap = budget + 1;
-  size_t heap = align_up(sizeof(float) * L * k, 16) + sizeof(double) * fcap +
+  size_t heap = align_up(sizeof(float) * L * k, 16) + sizeof(unsigned long long) * fcap +
+                sizeof(double) * fcap + sizeof(double) * budget +
                 4 * sizeof(unsigned long long) * fcap + sizeof(uint32_t) * fcap +
                 sizeof(uint32_t) * budget;
   return align_up(merge > heap ? merge : heap, 16);
+}
+
+// ---- exp in double for the log-partition sum ------------------------------------------
+// exp(d) for d <= 0 to ~1e-15 relative: Cody-Waite argument reduction d = n ln2 + r with
+// ln2 split into a 32-bit-exact head and a tail (Cody & Waite, Software Manual for the
+// Elementary Functions, 1980), then the Taylor series of e^r on |r| <= ln2 / 2 to degree
+// 13 (truncation < 3e-16), scaled by 2^n through the exponent field.
+__device__ __forceinline__ double exp_neg_d(double d) {
+  if (d < -708.0) return 0.0;
+  const double kLn2Hi = 6.93147180369123816490e-01;  // ln 2 to 32 significant bits
+  const double kLn2Lo = 1.90821492927058770002e-10;  // ln 2 - kLn2Hi
+  const double n = rint(d * 1.44269504088896340736);  // d / ln 2, nearest integer
+  const double r = fma(-n, kLn2Lo, fma(-n, kLn2Hi, d));
+  double p = 1.0 / 6227020800.0;  // 1/13!
+  p = fma(p, r, 1.0 / 479001600.0);
+  p = fma(p, r, 1.0 / 39916800.0);
+  p = fma(p, r, 1.0 / 3628800.0);
+  p = fma(p, r, 1.0 / 362880.0);
+  p = fma(p, r, 1.0 / 40320.0);
+  p = fma(p, r, 1.0 / 5040.0);
+  p = fma(p, r, 1.0 / 720.0);
+  p = fma(p, r, 1.0 / 120.0);
+  p = fma(p, r, 1.0 / 24.0);
+  p = fma(p, r, 1.0 / 6.0);
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  // 2^n for n in [-1022, 0]
+  return p * __longlong_as_double(static_cast<long long>(1023 + static_cast<int>(n)) << 52);
+}
+
+template <bool kBF16>
+__device__ __forceinline__ float composite_value(unsigned long long c) {
+  const uint32_t key = static_cast<uint32_t>(c >> 32);
+  return kBF16 ? key_bf16(key >> 16) : key_f32(key);
 }
 
 // ---- block radix select over register-resident 64-bit composites ----------------
@@ -226,7 +263,27 @@ __device__ __forceinline__ int rank_shift(int level) {
   return (kLevelsPerWord - 1 - level % kLevelsPerWord) * kRankBits + 4;
 }
 
+// Adds v to level `lv` of a packed rank tuple.  The word is chosen with predicated,
+// fully unrolled updates so the tuple stays in registers (a runtime array index would
+// move it to local memory).
+__device__ __forceinline__ void add_level(unsigned long long (&r)[4], int lv, unsigned long long v) {
+  const int word = lv / kLevelsPerWord;
+  const unsigned long long inc = v << rank_shift(lv);
+#pragma unroll
+  for (int w = 0; w < 4; ++w) r[w] += (w == word) ? inc : 0ull;
+}
+
+// Order-preserving unsigned key of a double (larger logw -> larger key); +0 and -0 map to
+// the same key, so key equality is exactly double equality for the finite values here.
+__device__ __forceinline__ unsigned long long dkey(double x) {
+  const unsigned long long u = static_cast<unsigned long long>(__double_as_longlong(x == 0.0 ? 0.0 : x));
+  return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+
+// Frontier slot layout in shared memory (struct of arrays, fcap slots):
+//   key u64 (order key of logw), logw f64, r[4] u64 (packed rank tuple), meta u32
 struct Frontier {
+  unsigned long long* key;
   double* logw;
   unsigned long long* r;  // [4][fcap]
   uint32_t* meta;         // parent | depth << 12 | rank << 17
@@ -248,50 +305,31 @@ __device__ __forceinline__ bool ranks_less(const unsigned long long (&a)[4],
   return false;
 }
 
-// Adds 1 to level `lv` of a packed rank tuple.  The word is chosen with predicated,
-// fully unrolled updates so the tuple stays in registers (a runtime array index would
-// move it to local memory).
-__device__ __forceinline__ void bump_level(unsigned long long (&r)[4], int lv) {
-  const int word = lv / kLevelsPerWord;
-  const unsigned long long inc = 1ull << rank_shift(lv);
+// slot a pops before slot b: larger logw, then the smaller rank tuple
+__device__ __forceinline__ bool slot_before(Frontier& f, int a, unsigned long long ka, int b,
+                                            unsigned long long kb) {
+  if (ka != kb) return ka > kb;
+  unsigned long long ra[4], rb[4];
 #pragma unroll
-  for (int w = 0; w < 4; ++w) r[w] += (w == word) ? inc : 0ull;
+  for (int w = 0; w < 4; ++w) {
+    ra[w] = f.rw(w, a);
+    rb[w] = f.rw(w, b);
+  }
+  return ranks_less(ra, rb);
 }
 
-struct Cand {
-  double logw;
-  unsigned long long r[4];
-};
-
-// a pops before b in the reference heap: larger logw, then the smaller rank tuple
-__device__ __forceinline__ bool pops_before(const Cand& a, const Cand& b) {
-  if (a.logw != b.logw) return a.logw > b.logw;
-  return ranks_less(a.r, b.r);
-}
-
-__device__ __forceinline__ Cand load_cand(Frontier& f, int s) {
-  Cand c;
-  c.logw = f.logw[s];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) c.r[w] = f.rw(w, s);
-  return c;
-}
-
-__device__ __forceinline__ void store_cand(Frontier& f, int s, const Cand& c, uint32_t meta) {
-  f.logw[s] = c.logw;
-#pragma unroll
-  for (int w = 0; w < 4; ++w) f.rw(w, s) = c.r[w];
-  f.meta[s] = meta;
-}
-
-// Warp-wide best frontier slot among the slots each lane offers (-1 = none).
-__device__ __forceinline__ int warp_best_slot(Frontier& f, int slot) {
+// Warp-wide best of the slots the lanes offer (-1 = none); integer keys only, rank tuples
+// are read only when two keys are equal.
+__device__ __forceinline__ int warp_best_slot(Frontier& f, int slot, unsigned long long key) {
   const int lane = threadIdx.x & 31;
-  double m = slot >= 0 ? f.logw[slot] : -INFINITY;
   const bool has = slot >= 0;
+  unsigned long long m = has ? key : 0ull;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(DDT_FULL_MASK, m, o));
-  const unsigned tied = __ballot_sync(DDT_FULL_MASK, has && f.logw[has ? slot : 0] == m);
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long y = __shfl_xor_sync(DDT_FULL_MASK, m, o);
+    m = y > m ? y : m;
+  }
+  const unsigned tied = __ballot_sync(DDT_FULL_MASK, has && key == m);
   if (tied == 0u) return -1;
   if (__popc(tied) == 1) return __shfl_sync(DDT_FULL_MASK, slot, __ffs(tied) - 1);
   const bool mine = (tied >> lane) & 1u;
@@ -316,97 +354,173 @@ __device__ __forceinline__ int warp_best_slot(Frontier& f, int slot) {
 }
 
 // One warp replays ddtree.py:116-147 exactly.  The frontier holds one entry per sibling
-// chain (the next unpopped child of some popped node).  Each round the warp finds the
-// best entry W and the best entry S2 among all others; then lane 0 pops along W's chain
-// for as long as the chain's next sibling still pops before S2 and before every child
-// chain pushed during the run (the heap would pop exactly those, in that order), so a
-// full frontier scan is paid once per run instead of once per node.
+// chain (the next unpopped child of some popped node).  Each round:
+//   1. the warp finds the best entry W and the best entry S2 of all the others;
+//   2. lane 0 walks W's chain: the popped node's child key (logw + lp[d, 0]) joins the
+//      "best of the rest" k2 if it beats it, and the chain's next sibling
+//      ((logw - lp[d-1, r]) + lp[d-1, r+1], the reference's operation order) is popped
+//      next iff it still pops before k2 -- the heap would pop exactly these nodes, in
+//      this order.  Only the keys of the run are kept (run_keys);
+//   3. the whole warp emits the run's nodes and writes their child entries.
+// A frontier scan is paid once per run instead of once per node.
 __device__ int heap_build(const float* lp, int L, int k, int budget, Frontier f,
-                          uint32_t* node_meta) {
+                          uint32_t* node_meta, double* run_keys) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) {
-    Cand c0;
-    c0.logw = static_cast<double>(lp[0]);
-    c0.r[0] = 1ull << rank_shift(0);
-    c0.r[1] = c0.r[2] = c0.r[3] = 0ull;
-    store_cand(f, 0, c0, pack_meta(0, 1, 0));
+    const double l0 = static_cast<double>(lp[0]);
+    f.key[0] = dkey(l0);
+    f.logw[0] = l0;
+    f.rw(0, 0) = 1ull << rank_shift(0);
+    f.rw(1, 0) = 0ull;
+    f.rw(2, 0) = 0ull;
+    f.rw(3, 0) = 0ull;
+    f.meta[0] = pack_meta(0, 1, 0);
   }
   __syncwarp();
   int count = 0, fcount = 1;
   while (count < budget && fcount > 0) {
     // lane-local best and second best among slots lane, lane + 32, ...
     int b1 = -1, b2 = -1;
-    Cand c1, c2;
+    unsigned long long k1 = 0ull, k2v = 0ull;
     for (int s = lane; s < fcount; s += 32) {
-      const Cand c = load_cand(f, s);
-      if (b1 < 0 || pops_before(c, c1)) {
+      const unsigned long long ks = f.key[s];
+      if (b1 < 0 || slot_before(f, s, ks, b1, k1)) {
         b2 = b1;
-        c2 = c1;
+        k2v = k1;
         b1 = s;
-        c1 = c;
-      } else if (b2 < 0 || pops_before(c, c2)) {
+        k1 = ks;
+      } else if (b2 < 0 || slot_before(f, s, ks, b2, k2v)) {
         b2 = s;
-        c2 = c;
+        k2v = ks;
       }
     }
-    const int W = warp_best_slot(f, b1);
-    const int S2 = warp_best_slot(f, (b1 == W) ? b2 : b1);
+    const int W = warp_best_slot(f, b1, k1);
+    const bool w_mine = (b1 == W);
+    const int S2 = warp_best_slot(f, w_mine ? b2 : b1, w_mine ? k2v : k1);
+    // ---- 2. serial walk along W's chain (lane 0) ----
+    int run = 0;
     if (lane == 0) {
-      Cand cur = load_cand(f, W);
-      uint32_t meta = f.meta[W];
+      const uint32_t meta = f.meta[W];
+      const int depth = (meta >> 12) & 31;
+      const int rank = static_cast<int>(meta >> 17);
       bool have2 = S2 >= 0;
-      Cand k2;
-      if (have2) k2 = load_cand(f, S2);
-      int fc = fcount;
+      unsigned long long k2key = have2 ? f.key[S2] : 0ull;
+      unsigned long long k2r[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) k2r[w] = have2 ? f.rw(w, S2) : 0ull;
+      unsigned long long wr[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) wr[w] = f.rw(w, W);
+      const double c0 = depth < L ? static_cast<double>(lp[depth * k]) : 0.0;
+      const float* row = lp + (depth - 1) * k;
+      double logw = f.logw[W];
+      int j = 0;
       for (;;) {
-        const int depth = (meta >> 12) & 31;
-        const int rank = static_cast<int>(meta >> 17);
-        const int parent = static_cast<int>(meta & 0xfffu);
-        const int cur_index = count + 1;
-        node_meta[count] = meta;
-        ++count;
-        if (depth < L) {  // ddtree.py:144-147: first child, logw + lp[depth, 0]
-          Cand ch;
-          ch.logw = cur.logw + static_cast<double>(lp[depth * k]);
+        // pop node (rank + j) with key logw
+        run_keys[j] = logw;
+        ++j;
+        if (depth < L) {
+          const double ch = logw + c0;
+          const unsigned long long chk = dkey(ch);
+          // child ranks: W's tuple with level depth-1 = rank + j (stored + 1) and level depth = 1
+          bool better = !have2 || chk > k2key;
+          if (have2 && chk == k2key) {
+            unsigned long long cr[4];
 #pragma unroll
-          for (int w = 0; w < 4; ++w) ch.r[w] = cur.r[w];
-          bump_level(ch.r, depth);
-          store_cand(f, fc, ch, pack_meta(cur_index, depth + 1, 0));
-          ++fc;
-          if (!have2 || pops_before(ch, k2)) {
-            k2 = ch;
+            for (int w = 0; w < 4; ++w) cr[w] = wr[w];
+            add_level(cr, depth - 1, static_cast<unsigned long long>(j - 1));
+            add_level(cr, depth, 1ull);
+            better = ranks_less(cr, k2r);
+          }
+          if (better) {
             have2 = true;
-          }
-        }
-        if (rank + 1 < k) {  // ddtree.py:139-142: next sibling
-          Cand sib;
-          sib.logw = (cur.logw - static_cast<double>(lp[(depth - 1) * k + rank])) +
-                     static_cast<double>(lp[(depth - 1) * k + rank + 1]);
+            k2key = chk;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) sib.r[w] = cur.r[w];
-          const int lv = depth - 1;
-          bump_level(sib.r, lv);
-          const uint32_t smeta = pack_meta(parent, depth, rank + 1);
-          if (count < budget && (!have2 || pops_before(sib, k2))) {
-            cur = sib;
-            meta = smeta;
-            continue;
+            for (int w = 0; w < 4; ++w) k2r[w] = wr[w];
+            add_level(k2r, depth - 1, static_cast<unsigned long long>(j - 1));
+            add_level(k2r, depth, 1ull);
           }
-          store_cand(f, W, sib, smeta);
-        } else {
-          const int last = fc - 1;
-          if (W != last) {
-            const Cand lc = load_cand(f, last);
-            store_cand(f, W, lc, f.meta[last]);
-          }
-          fc = last;
         }
-        break;
+        const int r = rank + j - 1;  // rank just popped
+        if (r + 1 >= k || count + j >= budget) break;
+        const double sib = (logw - static_cast<double>(row[r])) + static_cast<double>(row[r + 1]);
+        const unsigned long long sk = dkey(sib);
+        bool next = !have2 || sk > k2key;
+        if (have2 && sk == k2key) {
+          unsigned long long sr[4];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) sr[w] = wr[w];
+          add_level(sr, depth - 1, static_cast<unsigned long long>(j));
+          next = ranks_less(sr, k2r);
+        }
+        if (!next) break;
+        logw = sib;
       }
-      fcount = fc;
+      run = j;
     }
-    fcount = __shfl_sync(DDT_FULL_MASK, fcount, 0);
-    count = __shfl_sync(DDT_FULL_MASK, count, 0);
+    run = __shfl_sync(DDT_FULL_MASK, run, 0);
+    __syncwarp();
+    // ---- 3. the warp emits the run and its child entries ----
+    const uint32_t meta = f.meta[W];
+    const int depth = (meta >> 12) & 31;
+    const int rank = static_cast<int>(meta >> 17);
+    const int parent = static_cast<int>(meta & 0xfffu);
+    unsigned long long wr[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) wr[w] = f.rw(w, W);
+    const double logw_w = f.logw[W];
+    const bool kids = depth < L;
+    const double c0 = kids ? static_cast<double>(lp[depth * k]) : 0.0;
+    for (int j = lane; j < run; j += 32) {
+      node_meta[count + j] = pack_meta(parent, depth, rank + j);
+      if (kids) {
+        const int s = fcount + j;
+        const double ch = run_keys[j] + c0;
+        f.logw[s] = ch;
+        f.key[s] = dkey(ch);
+        unsigned long long cr[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) cr[w] = wr[w];
+        add_level(cr, depth - 1, static_cast<unsigned long long>(j));
+        add_level(cr, depth, 1ull);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) f.rw(w, s) = cr[w];
+        f.meta[s] = pack_meta(count + j + 1, depth + 1, 0);
+      }
+    }
+    __syncwarp();
+    int fc = fcount + (kids ? run : 0);
+    const int last_rank = rank + run - 1;
+    if (lane == 0) {
+      if (last_rank + 1 < k) {  // W now holds the chain's next sibling
+        const double lw = run_keys[run - 1];
+        const float* row = lp + (depth - 1) * k;
+        const double sib = (lw - static_cast<double>(row[last_rank])) +
+                           static_cast<double>(row[last_rank + 1]);
+        f.logw[W] = sib;
+        f.key[W] = dkey(sib);
+        unsigned long long sr[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) sr[w] = wr[w];
+        add_level(sr, depth - 1, static_cast<unsigned long long>(run));
+#pragma unroll
+        for (int w = 0; w < 4; ++w) f.rw(w, W) = sr[w];
+        f.meta[W] = pack_meta(parent, depth, last_rank + 1);
+      } else {  // chain exhausted: move the last entry into W
+        const int last = fc - 1;
+        if (W != last) {
+          f.logw[W] = f.logw[last];
+          f.key[W] = f.key[last];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) f.rw(w, W) = f.rw(w, last);
+          f.meta[W] = f.meta[last];
+        }
+      }
+    }
+    if (last_rank + 1 >= k) fc -= 1;
+    (void)logw_w;
+    count += run;
+    fcount = fc;
     __syncwarp();
   }
   return count;
@@ -443,7 +557,6 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
   const int64_t c1 = (c0 + CH < V) ? c0 + CH : V;
   const int64_t n = c1 > c0 ? c1 - c0 : 0;
   unsigned long long comp[kEPT];
-  float vals[kEPT];
   if constexpr (kBF16) {
     const uint16_t* row = static_cast<const uint16_t*>(logits) + d * row_stride + c0;
     if (vec_ok) {
@@ -458,7 +571,6 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
           const int64_t idx = e0 + e;
           const uint16_t b = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
           const bool ok = idx < n;
-          vals[j * 8 + e] = ok ? bf16_bits_to_f32(b) : -INFINITY;
           comp[j * 8 + e] = ok ? ((static_cast<unsigned long long>(bf16_key(b)) << 48) |
                                   static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
                                : 0ull;
@@ -470,7 +582,6 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
         const int64_t idx = static_cast<int64_t>(j) * kThreads + tid;
         const bool ok = idx < n;
         const uint16_t b = ok ? row[idx] : 0;
-        vals[j] = ok ? bf16_bits_to_f32(b) : -INFINITY;
         comp[j] = ok ? ((static_cast<unsigned long long>(bf16_key(b)) << 48) |
                         static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
                      : 0ull;
@@ -489,7 +600,6 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
         for (int e = 0; e < 4; ++e) {
           const int64_t idx = e0 + e;
           const bool ok = idx < n;
-          vals[j * 4 + e] = ok ? w[e] : -INFINITY;
           comp[j * 4 + e] = ok ? ((static_cast<unsigned long long>(f32_key(w[e])) << 32) |
                                   static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
                                : 0ull;
@@ -501,7 +611,6 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
         const int64_t idx = static_cast<int64_t>(j) * kThreads + tid;
         const bool ok = idx < n;
         const float x = ok ? row[idx] : -INFINITY;
-        vals[j] = x;
         comp[j] = ok ? ((static_cast<unsigned long long>(f32_key(x)) << 32) |
                         static_cast<uint32_t>(~static_cast<uint32_t>(c0 + idx)))
                      : 0ull;
@@ -509,14 +618,17 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
     }
   }
   // chunk max and sum exp(x - max), both exact-order independent up to double rounding
-  float lm = -INFINITY;
+  // values are decoded from the composites (keeps the register footprint to one array)
+  unsigned long long top = 0ull;
 #pragma unroll
-  for (int j = 0; j < kEPT; ++j) lm = fmaxf(lm, vals[j]);
+  for (int j = 0; j < kEPT; ++j) top = comp[j] > top ? comp[j] : top;
+  const float lm = top ? composite_value<kBF16>(top) : -INFINITY;
   const float cm = block_max_f(lm, rs);
   double ls = 0.0;
 #pragma unroll
   for (int j = 0; j < kEPT; ++j)
-    if (comp[j] != 0ull) ls += exp(static_cast<double>(vals[j]) - static_cast<double>(cm));
+    if (comp[j] != 0ull)
+      ls += exp_neg_d(static_cast<double>(composite_value<kBF16>(comp[j])) - static_cast<double>(cm));
   const double csum = block_sum_d(ls, rs);
 
   // exact top-k of the chunk
@@ -560,7 +672,7 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
     double S = 0.0;
     for (int i = 0; i < C; ++i)
       S += __ldcg(&chunk_sum[d * C + i]) *
-           exp(static_cast<double>(__ldcg(&chunk_max[d * C + i])) - static_cast<double>(M));
+           exp_neg_d(static_cast<double>(__ldcg(&chunk_max[d * C + i])) - static_cast<double>(M));
     s_logz = static_cast<float>(static_cast<double>(M) + log(S));
   }
   // candidates of the row: C * k composites, 0 = empty
@@ -624,17 +736,19 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
   if (tid == 0) counters[L] = 0;
   float* lp_s = reinterpret_cast<float*>(smem);
   const int fcap = budget + 1;
-  double* f_logw = reinterpret_cast<double*>(
+  unsigned long long* f_key = reinterpret_cast<unsigned long long*>(
       smem + align_up(sizeof(float) * static_cast<size_t>(L) * k, 16));
-  unsigned long long* f_r = reinterpret_cast<unsigned long long*>(f_logw + fcap);
+  double* f_logw = reinterpret_cast<double*>(f_key + fcap);
+  double* run_keys = f_logw + fcap;
+  unsigned long long* f_r = reinterpret_cast<unsigned long long*>(run_keys + budget);
   uint32_t* f_meta = reinterpret_cast<uint32_t*>(f_r + 4 * fcap);
   uint32_t* node_meta = f_meta + fcap;
   for (int i = tid; i < L * k; i += kThreads) lp_s[i] = __ldcg(&top_lp[i]);
   __syncthreads();
   __shared__ int s_count;
   if (tid < 32) {
-    Frontier fr{f_logw, f_r, f_meta, fcap};
-    const int cnt = heap_build(lp_s, L, k, budget, fr, node_meta);
+    Frontier fr{f_key, f_logw, f_r, f_meta, fcap};
+    const int cnt = heap_build(lp_s, L, k, budget, fr, node_meta, run_keys);
     if (tid == 0) s_count = cnt;
   }
   __syncthreads();
