@@ -65,7 +65,8 @@ def test_host_side_validation_rejects_bad_arguments():
 def test_workspace_queries():
     lib = _lib.load()
     ws = lib.ddt_topk_tree_workspace_bytes(15, 151936, 256)
-    assert ws > 15 * 10 * 256 * 8
+    chunks = -(-151936 // 20480)  # 20480-element chunks per depth row
+    assert ws > 15 * chunks * 256 * 8  # candidates of every chunk
     assert lib.ddt_tree_attn_workspace_bytes(257, 32, 128, 2) >= 2 * 257 * 32 * 130 * 4
 
 
