@@ -7,20 +7,26 @@
 // reads per-node ancestor bitmasks: every prefix key is visible, tree key j is visible
 // to node i iff bit j of anc_bits[i] is set.
 //
-// Work unit (one CTA): one KV head, one tile of 128 query rows, one KV split.  Query
-// rows are (node, q head of the GQA group) pairs, node-major, so the whole group shares
-// every K/V tile.  Warp roles:
-//   warp 0     TMA producer: Q once, then K and V tiles (128 keys x 128 dims, 128-byte
-//              swizzle) into a 2-stage ring; never multicast.
-//   warp 1     allocates TMEM; one thread issues tcgen05.mma: S = Q K^T into one of two
-//              TMEM S buffers, O += P V into the TMEM O accumulator.
-//   warps 2-5  softmax: thread t owns query row t (TMEM lane t): loads its S row, masks
-//              it, keeps the running max / sum, rescales O in TMEM only when the max
-//              grew by more than 2^8, writes P (bf16) into swizzled shared memory for
-//              the P V MMA, and finally normalises O.
+// Work unit (one CTA): one KV head, two tiles of 128 query rows (256 rows), one key
+// split.  Query rows are (node, q head of the GQA group) pairs, node-major, so the whole
+// group shares every K/V tile.  Warp roles (12 warps, 3 warpgroups):
+//   warp 0      TMA producer: both Q tiles once, then K and V tiles (128 keys x 128 dims,
+//               128-byte swizzle) into a 2-stage ring; never multicast.
+//   warp 1      allocates all 512 TMEM columns; one thread issues tcgen05.mma:
+//               S_q = Q_q K^T (SMEM x SMEM) and O_q += P_q V with P_q read from TMEM.
+//   warps 2-3   idle (they complete warpgroup 0, which gives its registers away)
+//   warps 4-7   softmax of query tile 0, warps 8-11 of query tile 1: thread t of a warp
+//               owns row 32 * (warp % 4) + t (the TMEM lane quarter of the warp).  Pass 1 loads the S row and takes the masked max; pass 2
+//               reloads it, computes P = exp2(S * scale - m) and writes P back as packed
+//               bf16 into the first 64 columns of the tile's S region, where the P V MMA
+//               reads it.  O is rescaled in TMEM only when the row max grew by > 2^8.
+// The two softmax warpgroups work on different query tiles, so while one computes
+// exponentials the tensor pipe runs the other's MMAs.
+// TMEM columns: S0/P0 [0,128) O0 [128,256) S1/P1 [256,384) O1 [384,512).
 // Splits of the key range write fp32 partials (O, m, l) that ddt_attn_merge combines;
 // the same partial format is exchanged between GPUs for sequence-sharded prefixes.
-// Every mbarrier wait is bounded; a timeout sets *status and unwinds the CTA.
+// Every mbarrier wait is bounded; a timeout sets *status and unwinds the CTA.  Every
+// tcgen05.ld / st / wait is executed by whole warps.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -34,24 +40,36 @@ constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
 constexpr int kHeadDim = 128;
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 384;
+// Register split (setmaxnreg): the launch gives every thread 168 registers (3 warps per SM
+// sub-partition share its 16K-entry file); warpgroup 0 (TMA, MMA, 2 idle warps) gives
+// back down to 56 and the two softmax warpgroups take 224:
+// 128 * 56 + 256 * 224 = 64512 = 384 * 168.
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsControl = 56;
+constexpr int kRegsSoftmax = 224;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch,
+              "register split exceeds the launch's registers");
+constexpr int kRowsPerCta = 2 * kBlockM;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr uint32_t kHalfBytes = kBlockM * 64 * 2;   // one 64-dim half of a 128-row tile
 constexpr uint32_t kTileBytes = 2 * kHalfBytes;     // 32 KB
-constexpr uint32_t kSmemQ = 0;
-constexpr uint32_t kSmemK = kSmemQ + kTileBytes;
+constexpr uint32_t kSmemQ = 0;                      // Q0, Q1
+constexpr uint32_t kSmemK = kSmemQ + 2 * kTileBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
-constexpr uint32_t kSmemP = kSmemV + kStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kSmemP + kTileBytes;  // 192 KB
-constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;    // + alignment slack
+constexpr uint32_t kSmemBytes = kSmemV + kStages * kTileBytes;  // 192 KB
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;               // + alignment slack
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kBlockM, kBlockN, false, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kBlockM, kHeadDim, false, true);
 constexpr int kStatusTimeout = 1;
+// TMEM column of query tile q's S/P region and O accumulator
+__device__ __forceinline__ uint32_t col_s(int q) { return q ? 256u : 0u; }
+__device__ __forceinline__ uint32_t col_o(int q) { return q ? 384u : 128u; }
 
 struct Params {
-  int n_nodes, past_len, group, q_heads, n_qtiles, n_splits;
+  int n_nodes, past_len, group, q_heads, n_pairs, n_splits;
   int key_base;        // global key index of local key 0
   int key_lo, key_hi;  // global key range covered by this launch
   const uint32_t* anc;
@@ -67,8 +85,8 @@ struct Params {
 };
 
 struct Bars {
-  uint64_t q_full, k_full[kStages], v_full[kStages], kv_empty[kStages], s_full[2], p_full, o_ready,
-      mma_done;
+  uint64_t q_full, k_full[kStages], v_full[kStages], kv_empty[kStages], s_full[2], p_full[2],
+      o_ready[2], mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -122,13 +140,14 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   const int unit = blockIdx.x;
   const int split = unit % p.n_splits;
   const int tq = unit / p.n_splits;
-  const int qt = tq % p.n_qtiles;
-  const int h = tq / p.n_qtiles;
-  const int row0 = qt * kBlockM;
-  const int node_lo = row0 / p.group;
-  int node_hi = (row0 + kBlockM - 1) / p.group;
+  const int pair = tq % p.n_pairs;
+  const int h = tq / p.n_pairs;
+  const int rows = p.n_nodes * p.group;
+  const int row0 = pair * kRowsPerCta;
+  const bool q1_active = row0 + kBlockM < rows;
+  int node_hi = (row0 + kRowsPerCta - 1) / p.group;
   if (node_hi > p.n_nodes - 1) node_hi = p.n_nodes - 1;
-  // keys beyond past + node_hi are invisible to every row of the tile (both modes)
+  // keys beyond past + node_hi are invisible to every row of the CTA (both modes)
   int g_end = p.past_len + node_hi + 1;
   if (g_end > p.key_hi) g_end = p.key_hi;
   const int g_begin = p.key_lo;
@@ -148,10 +167,11 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc::mbar_init(&bars.v_full[s], 1);
       tc::mbar_init(&bars.kv_empty[s], 1);
     }
-    tc::mbar_init(&bars.s_full[0], 1);
-    tc::mbar_init(&bars.s_full[1], 1);
-    tc::mbar_init(&bars.p_full, 128);
-    tc::mbar_init(&bars.o_ready, 1);
+    for (int q = 0; q < 2; ++q) {
+      tc::mbar_init(&bars.s_full[q], 1);
+      tc::mbar_init(&bars.p_full[q], 128);
+      tc::mbar_init(&bars.o_ready[q], 1);
+    }
     tc::mbar_init(&bars.mma_done, 1);
     bars.abort = 0;
     tc::fence_mbar_init();
@@ -169,248 +189,281 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   unsigned char* sQ = smem + kSmemQ;
   unsigned char* sK = smem + kSmemK;
   unsigned char* sV = smem + kSmemV;
-  unsigned char* sP = smem + kSmemP;
 
-  if (warp == 0) {
-    // ---------------------------- TMA producer -------------------------------------
-    if (lane == 0 && nt > 0) {
-      tc::tma_prefetch_desc(&tm_q);
-      tc::tma_prefetch_desc(&tm_k);
-      tc::tma_prefetch_desc(&tm_v);
-      tc::mbar_expect_tx(&bars.q_full, kTileBytes);
-      tc::tma_load_3d(sQ, &tm_q, &bars.q_full, 0, h * p.group, node_lo);
-      tc::tma_load_3d(sQ + kHalfBytes, &tm_q, &bars.q_full, 64, h * p.group, node_lo);
-      int issued = 0;
-      for (int j = 0; j < nt; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages &&
-            !tc::mbar_wait(&bars.kv_empty[st], ((j / kStages) - 1) & 1, abort_flag, kTimeoutNs)) {
-          raise_abort(bars, p.status);
-          break;
+  if (warp < 4) {
+    tc::reg_dealloc<kRegsControl>();
+    if (warp == 0) {
+      // ---------------------------- TMA producer -------------------------------------
+      if (lane == 0 && nt > 0) {
+        tc::tma_prefetch_desc(&tm_q);
+        tc::tma_prefetch_desc(&tm_k);
+        tc::tma_prefetch_desc(&tm_v);
+        tc::mbar_expect_tx(&bars.q_full, (q1_active ? 2 : 1) * kTileBytes);
+        for (int q = 0; q < (q1_active ? 2 : 1); ++q) {
+          const int node0 = (row0 + q * kBlockM) / p.group;
+          tc::tma_load_3d(sQ + q * kTileBytes, &tm_q, &bars.q_full, 0, h * p.group, node0);
+          tc::tma_load_3d(sQ + q * kTileBytes + kHalfBytes, &tm_q, &bars.q_full, 64, h * p.group,
+                          node0);
         }
-        const int key = lk0 + j * kBlockN;
-        unsigned char* kd = sK + st * kTileBytes;
-        unsigned char* vd = sV + st * kTileBytes;
-        tc::mbar_expect_tx(&bars.k_full[st], kTileBytes);
-        tc::tma_load_3d(kd, &tm_k, &bars.k_full[st], 0, key, h);
-        tc::tma_load_3d(kd + kHalfBytes, &tm_k, &bars.k_full[st], 64, key, h);
-        tc::mbar_expect_tx(&bars.v_full[st], kTileBytes);
-        tc::tma_load_3d(vd, &tm_v, &bars.v_full[st], 0, key, h);
-        tc::tma_load_3d(vd + kHalfBytes, &tm_v, &bars.v_full[st], 64, key, h);
-        issued = j + 1;
-      }
-      if (*abort_flag) {
-        // let the loads already in flight land before the CTA releases its smem
-        tc::mbar_wait_drain(&bars.q_full, 0, kTimeoutNs);
-        for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
+        int issued = 0;
+        for (int j = 0; j < nt; ++j) {
           const int st = j % kStages;
-          tc::mbar_wait_drain(&bars.k_full[st], (j / kStages) & 1, kTimeoutNs);
-          tc::mbar_wait_drain(&bars.v_full[st], (j / kStages) & 1, kTimeoutNs);
+          if (j >= kStages &&
+              !tc::mbar_wait(&bars.kv_empty[st], ((j / kStages) - 1) & 1, abort_flag, kTimeoutNs)) {
+            raise_abort(bars, p.status);
+            break;
+          }
+          const int key = lk0 + j * kBlockN;
+          unsigned char* kd = sK + st * kTileBytes;
+          unsigned char* vd = sV + st * kTileBytes;
+          tc::mbar_expect_tx(&bars.k_full[st], kTileBytes);
+          tc::tma_load_3d(kd, &tm_k, &bars.k_full[st], 0, key, h);
+          tc::tma_load_3d(kd + kHalfBytes, &tm_k, &bars.k_full[st], 64, key, h);
+          tc::mbar_expect_tx(&bars.v_full[st], kTileBytes);
+          tc::tma_load_3d(vd, &tm_v, &bars.v_full[st], 0, key, h);
+          tc::tma_load_3d(vd + kHalfBytes, &tm_v, &bars.v_full[st], 64, key, h);
+          issued = j + 1;
+        }
+        if (*abort_flag) {
+          // let the loads already in flight land before the CTA releases its smem
+          tc::mbar_wait_drain(&bars.q_full, 0, kTimeoutNs);
+          for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
+            const int st = j % kStages;
+            tc::mbar_wait_drain(&bars.k_full[st], (j / kStages) & 1, kTimeoutNs);
+            tc::mbar_wait_drain(&bars.v_full[st], (j / kStages) & 1, kTimeoutNs);
+          }
         }
       }
-    }
-  } else if (warp == 1) {
-    // ---------------------------- MMA issuer ---------------------------------------
-    if (lane == 0 && nt > 0) {
-      const uint32_t q_addr = tc::smem_u32(sQ);
-      const uint32_t k_addr = tc::smem_u32(sK);
-      const uint32_t v_addr = tc::smem_u32(sV);
-      const uint32_t p_addr = tc::smem_u32(sP);
-      bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % kStages;
-        if (!tc::mbar_wait(&bars.k_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs)) return false;
-        tc::tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>((j & 1) * kBlockN);
-        const uint32_t kb = k_addr + st * kTileBytes;
+    } else if (warp == 1) {
+      // ---------------------------- MMA issuer ---------------------------------------
+      if (lane == 0 && nt > 0) {
+        const uint32_t q_addr = tc::smem_u32(sQ);
+        const uint32_t k_addr = tc::smem_u32(sK);
+        const uint32_t v_addr = tc::smem_u32(sV);
+        const int nq = q1_active ? 2 : 1;
+        bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
+        // S_q = Q_q K_j^T into the S region of query tile q
+        auto issue_s = [&](int q, int j) {
+          const uint32_t kb = k_addr + (j % kStages) * kTileBytes;
+          const uint32_t qb = q_addr + q * kTileBytes;
 #pragma unroll
-        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          tc::mma_bf16_ss(d, tc::smem_desc_sw128(q_addr + off, 16, 1024),
-                          tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
-        }
-        tc::mma_commit(&bars.s_full[j & 1]);
-        return true;
-      };
-      auto issue_pv = [&](int j) -> bool {
-        const int st = j % kStages;
-        if (!tc::mbar_wait(&bars.p_full, j & 1, abort_flag, kTimeoutNs)) return false;
-        if (!tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs)) return false;
-        tc::tc_fence_after();
-        const uint32_t d = tmem + 2 * kBlockN;
-        const uint32_t vb = v_addr + st * kTileBytes;
+          for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+            tc::mma_bf16_ss(tmem + col_s(q), tc::smem_desc_sw128(qb + off, 16, 1024),
+                            tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+          }
+          tc::mma_commit(&bars.s_full[q]);
+        };
+        // O_q += P_q V_j, P_q in TMEM (first 64 columns of the S region, 8 per K step)
+        auto issue_pv = [&](int q, int j) {
+          const uint32_t vb = v_addr + (j % kStages) * kTileBytes;
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          tc::mma_bf16_ss(d, tc::smem_desc_sw128(p_addr + aoff, 16, 1024),
-                          tc::smem_desc_sw128(vb + kk * 2048, kHalfBytes, 1024), kIdescPV,
-                          (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBlockN / 16; ++kk)
+            tc::mma_bf16_ts(tmem + col_o(q), tmem + col_s(q) + kk * 8,
+                            tc::smem_desc_sw128(vb + kk * 2048, kHalfBytes, 1024), kIdescPV,
+                            (j > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_commit(&bars.o_ready[q]);
+        };
+        if (ok) ok = tc::mbar_wait(&bars.k_full[0], 0, abort_flag, kTimeoutNs);
+        if (ok) {
+          tc::tc_fence_after();
+          for (int q = 0; q < nq; ++q) issue_s(q, 0);
         }
-        tc::mma_commit(&bars.o_ready);
-        tc::mma_commit(&bars.kv_empty[st]);
-        return true;
-      };
-      for (int j = 0; ok && j < nt; ++j) {
-        ok = issue_s(j);
-        if (ok && j >= 1) ok = issue_pv(j - 1);
-      }
-      if (ok) ok = issue_pv(nt - 1);
-      if (!ok) {
-        raise_abort(bars, p.status);
-        // wait for every MMA issued so far before TMEM is released
-        tc::mma_commit(&bars.mma_done);
-        uint64_t t0 = global_timer_ns();
-        while (!tc::mbar_try_wait(&bars.mma_done, 0) && global_timer_ns() - t0 < kTimeoutNs) {
+        for (int j = 0; ok && j < nt; ++j) {
+          const int st = j % kStages;
+          ok = tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs);
+          const bool more = j + 1 < nt;
+          if (ok && more)
+            ok = tc::mbar_wait(&bars.k_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort_flag,
+                               kTimeoutNs);
+          for (int q = 0; ok && q < nq; ++q) {
+            ok = tc::mbar_wait(&bars.p_full[q], j & 1, abort_flag, kTimeoutNs);
+            if (!ok) break;
+            tc::tc_fence_after();
+            issue_pv(q, j);
+            if (q == nq - 1) tc::mma_commit(&bars.kv_empty[st]);
+            if (more) issue_s(q, j + 1);  // reuses S_q / P_q: runs after the P V MMA above
+          }
+        }
+        if (!ok) {
+          raise_abort(bars, p.status);
+          // wait for every MMA issued so far before TMEM is released
+          tc::mma_commit(&bars.mma_done);
+          tc::mbar_wait_drain(&bars.mma_done, 0, kTimeoutNs);
         }
       }
     }
   } else {
-    // ---------------------------- softmax warps ------------------------------------
-    // tcgen05.ld / tcgen05.st are warp-collective (.sync.aligned): every lane executes
-    // them on every path; per-row conditions only predicate arithmetic and stores.
-    const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;
-    const uint32_t tl = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    const int R = row0 + r;
+    tc::reg_alloc<kRegsSoftmax>();
+    // ---------------------------- softmax warpgroups -------------------------------
+    const int q = (warp - 4) >> 2;  // query tile of this warpgroup (warps 4-7 / 8-11)
+    const int wq = warp & 3;        // TMEM lane quarter a warp may access: warp id % 4
+    const int r = wq * 32 + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    const uint32_t tS = tl + col_s(q);
+    const uint32_t tO = tl + col_o(q);
+    const int R = row0 + q * kBlockM + r;
     const int node = R / p.group;
     const int qh = h * p.group + (R % p.group);
-    const bool valid = node < p.n_nodes;
+    const bool valid = R < rows;
     const int vnode = valid ? node : p.n_nodes - 1;
+    const bool active = (q == 0) || q1_active;
     const float sl2 = p.scale_log2;
+    // the whole key range of the tile is visible to this row (no mask needed) when it
+    // ends before the tree window / the launch's last key
+    const int full_end = p.mask_mode == DDT_MASK_CAUSAL
+                             ? (g_end < p.past_len + node + 1 ? g_end : p.past_len + node + 1)
+                             : (g_end < p.past_len ? g_end : p.past_len);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    unsigned char* prow = sP + r * 128;
-    const int sw = r & 7;
-    for (int j = 0; j < nt; ++j) {
-      if (!tc::mbar_wait_warp(&bars.s_full[j & 1], (j >> 1) & 1, abort_flag, kTimeoutNs)) {
+    for (int j = 0; active && j < nt; ++j) {
+      if (!tc::mbar_wait_warp(&bars.s_full[q], j & 1, abort_flag, kTimeoutNs)) {
         ok = false;
         break;
       }
       tc::tc_fence_after();
-      uint32_t s[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tl + (j & 1) * kBlockN + c * 32, s[c]);
-      tc::tmem_wait_ld();
       const int gk = p.key_base + lk0 + j * kBlockN;  // global key of column 0
-      float mx = -INFINITY;
+      const bool masked = __any_sync(DDT_FULL_MASK, gk + kBlockN > full_end);
+      uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
+      if (masked) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint32_t vis = visible32(p, vnode, gk + c * 32, g_end);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float x = __uint_as_float(s[c][e]) * sl2;
-          x = ((vis >> e) & 1u) ? x : -INFINITY;
-          s[c][e] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
+        for (int c = 0; c < 4; ++c) vis[c] = visible32(p, vnode, gk + c * 32, g_end);
       }
+      // the whole S row (128 fp32) comes out of TMEM in one round trip
+      uint32_t sv[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + c * 32, sv[c]);
+      tc::tmem_wait_ld();
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (!((vis[c] >> e) & 1u)) sv[c][e] = __float_as_uint(-INFINITY);
+      }
+      // masked row max of the raw scores, 8 independent chains
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sv[c][e]));
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       bool rescale = false;
       float alpha = 1.f;
       if (mx > -INFINITY) {
+        const float ms = mx * sl2;
         if (m_used == -INFINITY) {
-          m_used = mx;  // nothing accumulated yet: O and l are zero
-        } else if (mx > m_used + kRescaleLog2) {
-          alpha = tc::ex2_approx(m_used - mx);
-          m_used = mx;
+          m_used = ms;  // nothing accumulated yet: O and l are zero
+        } else if (ms > m_used + kRescaleLog2) {
+          alpha = tc::ex2_approx(m_used - ms);
+          m_used = ms;
           rescale = true;
         }
       }
-      const float mref = (m_used == -INFINITY) ? 0.f : m_used;
-      if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready, (j - 1) & 1, abort_flag, kTimeoutNs)) {
-        ok = false;
-        break;
-      }
-      if (__any_sync(DDT_FULL_MASK, rescale)) {  // lanes without a new max scale by 1
+      if (__any_sync(DDT_FULL_MASK, rescale)) {
+        // O_q is stable once the previous P V MMA of this tile completed
+        if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready[q], (j - 1) & 1, abort_flag, kTimeoutNs)) {
+          ok = false;
+          break;
+        }
         tc::tc_fence_after();
-        const uint32_t ob = tl + 2 * kBlockN;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tc::tmem_ld32(ob + c * 32, o);
+          tc::tmem_ld32(tO + c * 32, o);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tc::tmem_st32(ob + c * 32, o);
+          tc::tmem_st32(tO + c * 32, o);
         }
-        tc::tmem_wait_st();
         l *= alpha;
       }
-      float ls = 0.f;
+      const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
+      // P = exp2(S * scale - m), packed bf16 into columns [0, 64) of S_q (masked keys hold
+      // -inf and give 0); 8 independent partial sums
+      float ls8[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int i = 0; i < 8; ++i) ls8[i] = 0.f;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {  // 8 keys per 16-byte chunk
-          uint32_t pk[4];
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pk[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float a = tc::ex2_approx(__uint_as_float(s[c][q * 8 + 2 * e]) - mref);
-            const float b = tc::ex2_approx(__uint_as_float(s[c][q * 8 + 2 * e + 1]) - mref);
-            ls += a + b;
-            pk[e] = tc::pack_bf16x2(a, b);
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float a = tc::ex2_approx(fmaf(__uint_as_float(sv[hf * 2 + c][e]), sl2, nm));
+            const float b = tc::ex2_approx(fmaf(__uint_as_float(sv[hf * 2 + c][e + 1]), sl2, nm));
+            ls8[(e >> 1) & 7] += a + b;
+            pk[c * 16 + e / 2] = tc::pack_bf16x2(a, b);
           }
-          const int chunk = c * 4 + q;  // 0..15
-          const int half = chunk >> 3, cc = chunk & 7;
-          *reinterpret_cast<uint4*>(prow + half * kHalfBytes + ((cc ^ sw) << 4)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        tc::tmem_st32(tS + hf * 32, pk);
       }
+      const float ls = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       l += ls;
-      tc::fence_proxy_async_smem();
+      tc::tmem_wait_st();
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars.p_full);
+      tc::mbar_arrive(&bars.p_full[q]);
     }
-    if (ok && nt > 0 && !tc::mbar_wait_warp(&bars.o_ready, (nt - 1) & 1, abort_flag, kTimeoutNs))
+    if (active && ok && nt > 0 &&
+        !tc::mbar_wait_warp(&bars.o_ready[q], (nt - 1) & 1, abort_flag, kTimeoutNs))
       ok = false;
     if (!ok && lane == 0) raise_abort(bars, p.status);
-    const bool have = ok && nt > 0;  // warp-uniform
-    const long long row = static_cast<long long>(node) * p.q_heads + qh;
+    const bool have = active && ok && nt > 0;  // warp-uniform
+    const long long orow_idx = static_cast<long long>(node) * p.q_heads + qh;
     if (have) tc::tc_fence_after();
-    if (p.partial) {
-      float* op = p.o_part + (static_cast<long long>(split) * p.n_nodes * p.q_heads + row) * kHeadDim;
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        if (have) {
-          tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
-          tc::tmem_wait_ld();
-        } else {
+    if (active) {
+      if (p.partial) {
+        float* op = p.o_part +
+                    (static_cast<long long>(split) * p.n_nodes * p.q_heads + orow_idx) * kHeadDim;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          if (have) {
+            tc::tmem_ld32(tO + c * 32, o);
+            tc::tmem_wait_ld();
+          } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0u;
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+          if (valid) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(op + c * 32 + e) =
+                  make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
+                              __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
+          }
         }
         if (valid) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4*>(op + c * 32 + e) =
-                make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
-                            __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
+          const long long mi = static_cast<long long>(split) * p.n_nodes * p.q_heads + orow_idx;
+          p.m_part[mi] = have ? m_used : -INFINITY;
+          p.l_part[mi] = have ? l : 0.f;
         }
-      }
-      if (valid) {
-        const long long mi = static_cast<long long>(split) * p.n_nodes * p.q_heads + row;
-        p.m_part[mi] = have ? m_used : -INFINITY;
-        p.l_part[mi] = have ? l : 0.f;
-      }
-    } else {
-      const float inv = (have && l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.out + static_cast<long long>(vnode) * p.o_node_stride +
-                            static_cast<long long>(qh) * p.o_head_stride;
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        if (have) {
-          tc::tmem_ld32(tl + 2 * kBlockN + c * 32, o);
-          tc::tmem_wait_ld();
-        } else {
+      } else {
+        const float inv = (have && l > 0.f) ? 1.f / l : 0.f;
+        __nv_bfloat16* orow = p.out + static_cast<long long>(vnode) * p.o_node_stride +
+                              static_cast<long long>(qh) * p.o_head_stride;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          if (have) {
+            tc::tmem_ld32(tO + c * 32, o);
+            tc::tmem_wait_ld();
+          } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0u;
-        }
-        if (valid) {
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+          if (valid) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 v;
-            v.x = tc::pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
-            v.y = tc::pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
-            v.z = tc::pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
-            v.w = tc::pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+            for (int e = 0; e < 32; e += 8) {
+              uint4 v;
+              v.x = tc::pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+              v.y = tc::pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+              v.z = tc::pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+              v.w = tc::pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
+            }
           }
         }
       }
@@ -555,7 +608,7 @@ inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_he
   p.past_len = static_cast<int>(past_length);
   p.group = static_cast<int>(group);
   p.q_heads = static_cast<int>(q_heads);
-  p.n_qtiles = static_cast<int>((n_nodes * group + kBlockM - 1) / kBlockM);
+  p.n_pairs = static_cast<int>((n_nodes * group + kRowsPerCta - 1) / kRowsPerCta);
   p.anc = anc_bits;
   p.anc_words = static_cast<int>(anc_words);
   p.mask_mode = mask_mode;
@@ -590,7 +643,7 @@ inline int launch(const Launch& L, int64_t kv_heads, cudaStream_t st) {
       return DDT_ERR_CUDA;
     attr = true;
   }
-  const int64_t grid = kv_heads * L.p.n_qtiles * L.p.n_splits;
+  const int64_t grid = kv_heads * L.p.n_pairs * L.p.n_splits;
   tree_attn_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, st>>>(L.q, L.k, L.v, L.p);
   return launch_status();
 }
@@ -623,7 +676,7 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
                          n_nodes, past_length, q_heads, kv_heads, head_dim, anc_bits, anc_words,
                          mask_mode, scale);
   if (rc) return rc;
-  const int64_t units = kv_heads * L.p.n_qtiles;
+  const int64_t units = kv_heads * L.p.n_pairs;
   const int64_t kv_tiles = (S + attn::kBlockN - 1) / attn::kBlockN;
   const int splits = kv_splits > 0 ? static_cast<int>(kv_splits) : attn::pick_splits(units, kv_tiles);
   if (splits > 64) return DDT_ERR_CAPACITY;
