@@ -60,6 +60,9 @@ def parse_args():
     ap.add_argument("--budget", type=int, default=256)
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fused", type=int, default=1,
+                    help="1: verify forward through the fused Qwen3 runner (default); 0: through "
+                         "transformers' Qwen3 with the ddtree_tree attention plug-in")
     return ap.parse_args()
 
 
@@ -286,13 +289,20 @@ def run_ours(args):
     torch.set_default_dtype(prev_dtype)
     ids, logits = request_inputs(rank, args.prefix)
     P, B = args.prefix, args.budget
-    cache = TreeKVCache(QWEN3_8B["layers"], P + B + 1 + 64)
+    cache = TreeKVCache(QWEN3_8B["layers"], P + B + 1 + 64).allocate(
+        QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
+    verifier = TreeVerifier(model, cache, B, DEPTHS, V, dev, fused=args.fused)
     with torch.inference_mode():
-        out = model(ids.to(dev), position_ids=torch.arange(P, device=dev)[None],
-                    past_key_values=cache, use_cache=True, logits_to_keep=1)
-        root_dev = K.argmax(out.logits[0, -1:]).view(1).clone()
-    del out
-    verifier = TreeVerifier(model, cache, B, DEPTHS, V, dev)
+        if verifier.runner is not None:  # causal prefill on the same kernels
+            out_logits = verifier.runner.forward(ids[0].to(dev), torch.arange(P, device=dev),
+                                                 cache, 0, None, causal=True)
+            root_dev = K.argmax(out_logits[-1:]).view(1).clone()
+            del out_logits
+        else:
+            out = model(ids.to(dev), position_ids=torch.arange(P, device=dev)[None],
+                        past_key_values=cache, use_cache=True, logits_to_keep=1)
+            root_dev = K.argmax(out.logits[0, -1:]).view(1).clone()
+            del out
     draft_dev = logits.to(torch.bfloat16).to(dev)
     n_nodes = 1 + K.expected_node_count(DEPTHS, V, B)
     for _ in range(args.warmup):  # eager steps: allocations, kernel attributes, TMA encode
@@ -399,7 +409,9 @@ def run_ours(args):
         "launches_per_step": launches / args.steps,
         "execution": "each step is one CUDA-graph replay of the full verify step (tree build, "
                      "36-layer forward, argmax, accept walk + compaction) at prefix length "
-                     f"{P}; eager warm-up steps precede the capture",
+                     f"{P}; eager warm-up steps precede the capture; forward: "
+                     + ("fused Qwen3 runner (cuBLAS GEMMs + fused norm/rope/silu kernels)"
+                        if args.fused else "transformers Qwen3 + ddtree_tree attention"),
         "accepted_per_step": n_acc, "verified_per_step": n_nodes,
         "attention_share": (attn_mean_ms * QWEN3_8B["layers"]) / ms,
     }

@@ -169,6 +169,28 @@ int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_pa
                    int64_t n_parts, int64_t n_nodes, int64_t q_heads, int64_t head_dim,
                    void* out, int64_t o_node_stride, int64_t o_head_stride, void* stream);
 
+/* ---- fused elementwise stages of the Qwen3 verify forward (bf16) ----------
+ * ddt_add_rmsnorm: r = x + delta (delta may be NULL), writes r to residual_out (may be
+ *   NULL, may alias x) and weight * rmsnorm(r) to norm_out; rows x hidden, hidden a
+ *   multiple of 8 up to 8192.  Replaces the residual add of Qwen3DecoderLayer and
+ *   Qwen3RMSNorm.forward (transformers/models/qwen3/modeling_qwen3.py:59-64).
+ * ddt_qk_norm_rope_cache: from the fused projection qkv [n_tokens, (q_heads + 2 kv_heads),
+ *   head_dim], applies q_norm / k_norm and the rotary embedding at positions (device i64),
+ *   writes q to q_out [n_tokens, q_heads, head_dim] and k / v to rows past_length + i of the
+ *   caches ([kv_heads, seq, head_dim] at the given strides).  Replaces
+ *   modeling_qwen3.py:263-271 (q/k norm, apply_rotary_pos_emb :151-181, cos / sin of
+ *   Qwen3RotaryEmbedding :137-147) and DynamicLayer.update (cache_utils.py:102-121).
+ * ddt_silu_mul: out[r, i] = silu(gate_up[r, i]) * gate_up[r, inter + i]; Qwen3MLP.forward
+ *   (modeling_qwen3.py:81-83) between its projections. */
+int ddt_add_rmsnorm(const void* x, const void* delta, const void* weight, int64_t rows,
+                    int64_t hidden, float eps, void* residual_out, void* norm_out, void* stream);
+int ddt_qk_norm_rope_cache(const void* qkv, int64_t n_tokens, int64_t q_heads, int64_t kv_heads,
+                           int64_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                           const int64_t* positions, const float* inv_freq, float rope_scale,
+                           void* q_out, void* k_cache, void* v_cache, int64_t head_stride,
+                           int64_t seq_stride, int64_t past_length, void* stream);
+int ddt_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* out, void* stream);
+
 /* additive mask block [n_nodes, n_nodes] (row stride in elements; 0 = visible) ->
  * anc_bits [n_nodes, anc_words]. */
 int ddt_mask_to_bits(const void* mask, int dtype, int64_t n_nodes, int64_t row_stride,

@@ -45,6 +45,10 @@ SIGNATURES = {
                                    _I, _P, _I, _i, _F, _P, _P]),
     "ddt_attn_merge": (_i, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P]),
     "ddt_mask_to_bits": (_i, [_P, _i, _I, _I, _P, _I, _P]),
+    "ddt_add_rmsnorm": (_i, [_P, _P, _P, _I, _I, _F, _P, _P, _P]),
+    "ddt_qk_norm_rope_cache": (_i, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _F, _P, _P, _P, _I, _I,
+                                    _I, _P]),
+    "ddt_silu_mul": (_i, [_P, _I, _I, _P, _P]),
 }
 
 

@@ -80,6 +80,15 @@ class TreeKVCache(DynamicCache):
         self.layer_class_to_replicate = None
         self._table: K.KvTable | None = None
 
+    def allocate(self, kv_heads: int, head_dim: int, dtype: torch.dtype, device,
+                 batch: int = 1) -> "TreeKVCache":
+        """Allocates every layer's buffers up front (instead of on the first update)."""
+        proto = torch.empty((batch, kv_heads, 0, head_dim), dtype=dtype, device=device)
+        for layer in self.layers:
+            if not layer.is_initialized:
+                layer.lazy_initialization(proto, proto)
+        return self
+
     def kv_table(self) -> K.KvTable:
         """Pointer table of every layer's K and V buffers (stable across steps)."""
         if self._table is None:

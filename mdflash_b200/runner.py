@@ -1,0 +1,112 @@
+"""Lean Qwen3 verify forward over the weights of a transformers Qwen3ForCausalLM.
+
+transformers' Qwen3 decoder layer (models/qwen3/modeling_qwen3.py:294-330 with
+Qwen3Attention :252-291 and Qwen3MLP :70-83) launches about 55 kernels per layer at verify
+size, most of them small elementwise ops.  This runner keeps the model's parameters and
+its bf16 rounding points but runs each layer as
+
+    ddt_add_rmsnorm          residual add + input_layernorm
+    GEMM                     q/k/v projections (one cuBLAS GEMM on the concatenated weight)
+    ddt_qk_norm_rope_cache   q_norm / k_norm, rotary embedding, K/V written into the cache
+    ddt_tree_attn            tree attention (tcgen05)
+    GEMM                     o_proj
+    ddt_add_rmsnorm          residual add + post_attention_layernorm
+    GEMM                     gate/up projections (one GEMM on the concatenated weight)
+    ddt_silu_mul             SiLU(gate) * up
+    GEMM                     down_proj
+
+followed by the final norm and lm_head.  It is used by TreeVerifier(fused=True).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from . import kernels as K
+from ._lib import check
+
+
+class Qwen3VerifyRunner:
+    def __init__(self, model):
+        cfg = model.config
+        self.cfg = cfg
+        self.hidden = cfg.hidden_size
+        self.q_heads = cfg.num_attention_heads
+        self.kv_heads = cfg.num_key_value_heads
+        self.head_dim = getattr(cfg, "head_dim", self.hidden // self.q_heads)
+        self.inter = cfg.intermediate_size
+        self.eps = float(cfg.rms_norm_eps)
+        inner = model.model
+        self.embed = inner.embed_tokens.weight
+        self.final_norm = inner.norm.weight
+        self.lm_head = model.lm_head.weight
+        rot = inner.rotary_emb
+        self.inv_freq = rot.inv_freq.to(torch.float32).contiguous()
+        self.rope_scale = float(getattr(rot, "attention_scaling", 1.0))
+        self.scaling = self.head_dim ** -0.5
+        self.layers = []
+        with torch.no_grad():
+            for layer in inner.layers:
+                a, m = layer.self_attn, layer.mlp
+                for lin in (a.q_proj, a.k_proj, a.v_proj, a.o_proj):
+                    if lin.bias is not None:
+                        raise ValueError("attention projections with bias are not supported")
+                self.layers.append(dict(
+                    w_qkv=torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0),
+                    w_o=a.o_proj.weight,
+                    w_gu=torch.cat([m.gate_proj.weight, m.up_proj.weight], 0),
+                    w_down=m.down_proj.weight,
+                    ln1=layer.input_layernorm.weight, ln2=layer.post_attention_layernorm.weight,
+                    qn=a.q_norm.weight, kn=a.k_norm.weight))
+        self.device = self.embed.device
+
+    def _stream(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def forward(self, ids: torch.Tensor, positions: torch.Tensor, cache, past_length: int,
+                anc_bits: torch.Tensor | None, causal: bool = False) -> torch.Tensor:
+        """ids, positions: i64 [N] (device).  Writes the N new K/V rows into `cache`
+        (a TreeKVCache) at [past_length, past_length + N) and returns logits [N, V] (bf16).
+        Tree mode attends with anc_bits; causal=True attends causally (prefill)."""
+        lib = _lib.load()
+        st = self._stream()
+        n = ids.numel()
+        H, hq, hkv, d = self.hidden, self.q_heads, self.kv_heads, self.head_dim
+        x = torch.nn.functional.embedding(ids.view(-1), self.embed)  # [N, H] bf16
+        h = torch.empty_like(x)
+        q = torch.empty((n, hq, d), dtype=x.dtype, device=x.device)
+        act = torch.empty((n, self.inter), dtype=x.dtype, device=x.device)
+        delta = None
+        for li, w in enumerate(self.layers):
+            layer = cache.layers[li]
+            kbuf, vbuf = layer.k_buf[0], layer.v_buf[0]  # [Hkv, cap, D]
+            check(lib.ddt_add_rmsnorm(x.data_ptr(), delta.data_ptr() if delta is not None else None,
+                                      w["ln1"].data_ptr(), n, H, self.eps, x.data_ptr(),
+                                      h.data_ptr(), st), "ddt_add_rmsnorm")
+            qkv = torch.matmul(h, w["w_qkv"].t())
+            check(lib.ddt_qk_norm_rope_cache(qkv.data_ptr(), n, hq, hkv, d, w["qn"].data_ptr(),
+                                             w["kn"].data_ptr(), self.eps, positions.data_ptr(),
+                                             self.inv_freq.data_ptr(), self.rope_scale,
+                                             q.data_ptr(), kbuf.data_ptr(), vbuf.data_ptr(),
+                                             kbuf.stride(0), kbuf.stride(1), past_length, st),
+                  "ddt_qk_norm_rope_cache")
+            K.STATS.launches += 3
+            s = past_length + n
+            attn = K.tree_attention(q, kbuf[:, :s], vbuf[:, :s], anc_bits, past_length,
+                                    scale=self.scaling, causal=causal)
+            o = torch.matmul(attn.view(n, hq * d), w["w_o"].t())
+            check(lib.ddt_add_rmsnorm(x.data_ptr(), o.data_ptr(), w["ln2"].data_ptr(), n, H,
+                                      self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")
+            gu = torch.matmul(h, w["w_gu"].t())
+            check(lib.ddt_silu_mul(gu.data_ptr(), n, self.inter, act.data_ptr(), st),
+                  "ddt_silu_mul")
+            delta = torch.matmul(act, w["w_down"].t())
+            K.STATS.launches += 2
+        check(lib.ddt_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.final_norm.data_ptr(), n, H,
+                                  self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")
+        K.STATS.launches += 1
+        for layer in cache.layers:
+            layer.length = past_length + n
+            layer.keys = layer.k_buf[..., :layer.length, :]
+            layer.values = layer.v_buf[..., :layer.length, :]
+        return torch.matmul(h, self.lm_head.t())

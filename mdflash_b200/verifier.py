@@ -38,8 +38,15 @@ class StepResult:
 
 class TreeVerifier:
     def __init__(self, target: torch.nn.Module, cache: TreeKVCache, budget: int, depths: int,
-                 vocab: int, device: torch.device | str = "cuda", keep_logits: bool = False):
+                 vocab: int, device: torch.device | str = "cuda", keep_logits: bool = False,
+                 fused: bool = False):
+        """fused=False runs the transformers model with attn_implementation="ddtree_tree";
+        fused=True runs its weights through Qwen3VerifyRunner (fused elementwise stages)."""
         self.target = target
+        self.runner = None
+        if fused:
+            from .runner import Qwen3VerifyRunner
+            self.runner = Qwen3VerifyRunner(target)
         self.cache = cache
         self.budget = budget
         self.depths = depths
@@ -64,9 +71,14 @@ class TreeVerifier:
         n = tree.n_nodes
         ids = tree.verify_ids[:n].view(1, n)
         pos = tree.verify_pos[:n].view(1, n)
-        with A.tree_verify(tree, start, n):
-            out = self.target(ids, position_ids=pos, past_key_values=self.cache, use_cache=True)
-        logits = out.logits[0]
+        if self.runner is not None:
+            logits = self.runner.forward(tree.verify_ids[:n], tree.verify_pos[:n], self.cache,
+                                         start, tree.anc_bits)
+        else:
+            with A.tree_verify(tree, start, n):
+                out = self.target(ids, position_ids=pos, past_key_values=self.cache,
+                                  use_cache=True)
+            logits = out.logits[0]
         post = K.argmax(logits, out=self.posterior[:n])
         K.accept_compact(post, tree, self.cache.kv_table(), start, accepted=self.accepted,
                          n_accepted=self.n_accepted, next_token=self.next_token, n_nodes=n)

@@ -1,0 +1,176 @@
+"""End-to-end GPU parity of the drop-in path against the reference path.
+
+Reference path: transformers Qwen3 with attn_implementation="sdpa", a DynamicCache, and the
+oracle's build_ddtree_tree / compile_ddtree_tree (the reference functions restated), exactly
+as ddtree_generate calls them (ddtree.py:440-486).  Our paths: (1) the drop-in functions of
+mdflash_b200.ddtree with the "ddtree_tree" attention plug-in, (2) TreeVerifier (device
+resident) over transformers, (3) TreeVerifier over the fused runner.  Tree topology,
+accepted paths and compaction are bit-exact; logits / KV rows are within bf16 tolerance
+(max |err| / max |ref| <= 2e-2) and the greedy posteriors agree.
+"""
+import numpy as np
+import pytest
+import torch
+
+import inputs as gin
+import oracle
+from mdflash_b200 import attention as A
+from mdflash_b200 import ddtree as D
+from mdflash_b200 import kernels as K
+from mdflash_b200.cache import TreeKVCache
+from mdflash_b200.verifier import TreeVerifier
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+V, P, BUDGET, DEPTHS = 2048, 96, 24, 4
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-30)).item()
+
+
+@pytest.fixture(scope="module")
+def setup(cuda_device):
+    from transformers import DynamicCache, Qwen3Config, Qwen3ForCausalLM
+    A.register()
+    cfg = Qwen3Config(vocab_size=V, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+                      rope_theta=1e6, max_position_embeddings=4096, rms_norm_eps=1e-6,
+                      tie_word_embeddings=False, initializer_range=0.2,
+                      attn_implementation="sdpa")
+    torch.manual_seed(0)
+    model = Qwen3ForCausalLM(cfg).to(cuda_device, torch.bfloat16).eval()
+    rng = np.random.default_rng(7)
+    ids = torch.from_numpy(rng.integers(0, V, (1, P))).to(cuda_device)
+    logits = torch.from_numpy(rng.standard_normal((DEPTHS, V)).astype(np.float32) * 3).to(
+        torch.bfloat16)
+    # ---- reference path ----
+    model.config._attn_implementation = "sdpa"
+    ref_cache = DynamicCache()
+    with torch.inference_mode():
+        out = model(ids, position_ids=torch.arange(P, device=cuda_device)[None],
+                    past_key_values=ref_cache, use_cache=True)
+        root = out.logits[0, -1].argmax()
+        tree = oracle.build_ddtree_tree(logits, BUDGET)
+        node_ids, depths, parents, child_maps, vis, _ = tree
+        n = 1 + node_ids.numel()
+        vib = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        vpb = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        amb = torch.zeros((1, 1, n, P + n), dtype=torch.bfloat16, device=cuda_device)
+        tvb = torch.empty((n, n), dtype=torch.bool, device=cuda_device)
+        vi, vp, am, _, _ = oracle.compile_ddtree_tree(root, P, node_ids, depths, vis, P,
+                                                      torch.bfloat16, cuda_device, vib, vpb, amb,
+                                                      tvb, 0, 0)
+        ref_logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=ref_cache,
+                           use_cache=True).logits[0]
+    ref_post = ref_logits.argmax(-1)
+    ref_acc, ref_next = oracle.follow_verified_tree(child_maps, ref_post.cpu())
+    return dict(model=model, ids=ids, logits=logits, root=root, tree=tree, n=n,
+                ref_logits=ref_logits, ref_post=ref_post, ref_cache=ref_cache, ref_acc=ref_acc,
+                ref_next=ref_next, vi=vi, vp=vp)
+
+
+def test_dropin_functions_and_plugin(setup, cuda_device):
+    from transformers import DynamicCache
+    s = setup
+    model = s["model"]
+    model.config._attn_implementation = A.ATTN_IMPLEMENTATION
+    cache = DynamicCache()
+    with torch.inference_mode():
+        out = model(s["ids"], position_ids=torch.arange(P, device=cuda_device)[None],
+                    past_key_values=cache, use_cache=True)  # causal prefill on our kernel
+        for lo, lr in zip(cache.layers, s["ref_cache"].layers):
+            assert _rel(lo.keys, lr.keys[..., :P, :]) <= TOL
+            assert _rel(lo.values, lr.values[..., :P, :]) <= TOL
+        root = out.logits[0, -1].argmax()
+        node_ids, depths, parents, child_maps, vis, sub = D.build_ddtree_tree(
+            s["logits"].to(cuda_device), BUDGET)
+        o_ids, o_depths, o_par, o_cm, o_vis, _ = s["tree"]
+        assert torch.equal(node_ids, o_ids) and torch.equal(depths, o_depths)
+        assert parents == o_par and child_maps == o_cm and torch.equal(vis, o_vis)
+        assert set(sub) == set(D.DDTREE_TREE_BUILD_STAGE_ORDER)
+        n = s["n"]
+        vib = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        vpb = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        amb = torch.zeros((1, 1, n, P + n), dtype=torch.bfloat16, device=cuda_device)
+        tvb = torch.empty((n, n), dtype=torch.bool, device=cuda_device)
+        vi, vp, am, pl, cl = D.compile_ddtree_tree(root, P, node_ids, depths, vis, P,
+                                                   torch.bfloat16, cuda_device, vib, vpb, amb, tvb,
+                                                   0, 0)
+        assert torch.equal(vi, s["vi"]) and torch.equal(vp, s["vp"]) and (pl, cl) == (P, n)
+        logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=cache,
+                       use_cache=True).logits[0]
+        assert _rel(logits, s["ref_logits"]) <= TOL
+        post = logits.argmax(-1)
+        agree = (post == s["ref_post"]).float().mean().item()
+        assert agree >= 0.95, agree
+        acc, nxt = D.follow_verified_tree(child_maps, post[None])
+        acc_host, nxt_host = oracle.follow_verified_tree(child_maps, post.cpu())
+        assert (acc, nxt) == (acc_host, nxt_host)
+        # forced deep path: compaction through the drop-in on both caches, bit-exact
+        forced = gin.follow_posterior(dict(kind="path", target=-1, seed=3, V=V),
+                                      node_ids.numpy(), np.asarray(parents, np.int32))
+        f_acc, f_next = D.follow_verified_tree(child_maps, torch.from_numpy(forced).to(cuda_device)[None])
+        assert (f_acc, f_next) == oracle.follow_verified_tree(child_maps, forced)
+        before = [(l.keys.float().cpu().numpy().copy(), l.values.float().cpu().numpy().copy())
+                  for l in cache.layers]
+        D.compact_dynamic_cache(cache, P, f_acc)
+        for layer, (kb, vb) in zip(cache.layers, before):
+            assert layer.keys.shape[-2] == P + len(f_acc)
+            np.testing.assert_array_equal(layer.keys.float().cpu().numpy(),
+                                          oracle.compact_rows(kb, P, f_acc))
+            np.testing.assert_array_equal(layer.values.float().cpu().numpy(),
+                                          oracle.compact_rows(vb, P, f_acc))
+    A.clear_tree_context()
+
+
+def test_compact_tail_inplace_mirrors_reference_checks(cuda_device):
+    mod = D.load_cpp_compact_module()
+    t = torch.randn((1, 2, 12, 128), device=cuda_device).to(torch.bfloat16)
+    before = t.float().cpu().numpy().copy()
+    keep = torch.tensor([0, 2, 5], device=cuda_device)
+    mod.compact_tail_inplace(t, 4, keep)
+    np.testing.assert_array_equal(t.float().cpu().numpy()[..., :7, :],
+                                  oracle.compact_rows(before, 4, [0, 2, 5]))
+    with pytest.raises(RuntimeError, match="keep_count exceeds"):
+        mod.compact_tail_inplace(t, 10, torch.tensor([0, 1, 2], device=cuda_device))
+    with pytest.raises(RuntimeError, match="dtype torch.long"):
+        mod.compact_tail_inplace(t, 4, keep.to(torch.int32))
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_tree_verifier_matches_reference(setup, cuda_device, fused):
+    s = setup
+    model = s["model"]
+    model.config._attn_implementation = A.ATTN_IMPLEMENTATION
+    cache = TreeKVCache(2, P + BUDGET + 8).allocate(2, 128, torch.bfloat16, cuda_device)
+    verifier = TreeVerifier(model, cache, BUDGET, DEPTHS, V, cuda_device, keep_logits=True,
+                            fused=fused)
+    with torch.inference_mode():
+        if fused:
+            pos = torch.arange(P, device=cuda_device)
+            verifier.runner.forward(s["ids"][0], pos, cache, 0, None, causal=True)
+        else:
+            model(s["ids"], position_ids=torch.arange(P, device=cuda_device)[None],
+                  past_key_values=cache, use_cache=True)
+        for lo, lr in zip(cache.layers, s["ref_cache"].layers):
+            assert _rel(lo.keys, lr.keys[..., :P, :]) <= TOL
+        res = verifier.step(s["logits"].to(cuda_device), s["root"].view(1), P)
+        torch.cuda.synchronize()
+    o_ids, o_depths, o_par, _, _, _ = s["tree"]
+    n = s["n"]
+    assert res.n_nodes == n
+    assert verifier.tree.parents[:n].tolist() == o_par
+    assert torch.equal(verifier.tree.node_token_ids[:n - 1].cpu(), o_ids)
+    assert _rel(res.logits, s["ref_logits"]) <= TOL
+    agree = (res.posterior == s["ref_post"]).float().mean().item()
+    assert agree >= 0.95, agree
+    k = int(res.n_accepted.item())
+    acc = res.accepted[:k].tolist()
+    o_acc, o_next = oracle.follow_verified_tree((np.asarray(o_par, np.int32), o_ids.numpy()),
+                                                res.posterior.cpu())
+    assert acc == o_acc and int(res.next_token.item()) == o_next
+    if torch.equal(res.posterior, s["ref_post"]):
+        assert acc == s["ref_acc"]
+    verifier.commit(P, k)
+    assert cache.get_seq_length() == P + k
