@@ -53,17 +53,28 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["verify", "attn", "tree"], default="verify",
-                    help="verify: the full verify step (default); attn: the tree-attention "
-                         "op alone at the given prefix / budget")
-    ap.add_argument("--prefix", type=int, default=8192)
-    ap.add_argument("--budget", type=int, default=256)
+    ap.add_argument("--workload", choices=["verify", "attn", "tree", "requests", "splitkv"],
+                    default="verify",
+                    help="verify: the single-request verify step (default); attn / tree: one op "
+                         "alone; requests: 64 requests sharded over the GPUs; splitkv: "
+                         "attention over a prefix sharded along the sequence")
+    ap.add_argument("--prefix", type=int, default=None,
+                    help="prefix length (default 8192; 131072 for --workload splitkv)")
+    ap.add_argument("--budget", type=int, default=None,
+                    help="tree budget (default 256; 512 for --workload splitkv)")
+    ap.add_argument("--requests", type=int, default=64)
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--fused", type=int, default=1,
                     help="1: verify forward through the fused Qwen3 runner (default); 0: through "
                          "transformers' Qwen3 with the ddtree_tree attention plug-in")
-    return ap.parse_args()
+    args = ap.parse_args()
+    long_ctx = args.workload == "splitkv"
+    if args.prefix is None:
+        args.prefix = 131072 if long_ctx else 8192
+    if args.budget is None:
+        args.budget = 512 if long_ctx else 256
+    return args
 
 
 def qwen3_config(attn: str, layers: int | None = None):
@@ -549,8 +560,197 @@ def run_tree(args):
     }), flush=True)
 
 
+# ------------------------------------------------------------- multi-GPU workloads
+def _dist_setup():
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    return world, rank, dev
+
+
+def run_requests(args):
+    """64 independent requests (prefix log-uniform 1k..32k, budget in {64,128,256,512},
+    per-request drafter seeds) assigned to ranks by longest-processing-time; each rank
+    verifies its requests one after another (one CUDA-graph replay each), then the result
+    records are all-gathered.  Prefix K/V are random bf16 (the verify work does not depend
+    on their values); the step for each request is the full verify step."""
+    import torch.distributed as dist
+    from transformers import Qwen3ForCausalLM
+
+    from mdflash_b200 import attention as A
+    from mdflash_b200 import kernels as K
+    from mdflash_b200 import sharding as S
+    from mdflash_b200.cache import TreeKVCache
+    from mdflash_b200.runner import Qwen3VerifyRunner
+    from mdflash_b200.verifier import CapturedStep, TreeVerifier
+
+    world, rank, dev = _dist_setup()
+    K._lib.load(build_if_missing=False)
+    attn = A.register()
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev), torch.inference_mode():
+        model = Qwen3ForCausalLM(qwen3_config(attn)).eval()
+    torch.set_default_dtype(prev)
+    runner = Qwen3VerifyRunner(model)
+    specs = S.request_specs(args.requests, seed=0)
+    mine = S.assign_requests([S.request_cost(s) for s in specs], world)[rank]
+    pool = torch.cuda.graph_pool_handle()
+    caps = []
+    g = torch.Generator(device=dev).manual_seed(rank)
+    for i in mine:
+        sp = specs[i]
+        cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
+            QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
+        for layer in cache.layers:
+            layer.k_buf.normal_(0.0, 1.0, generator=g)
+            layer.v_buf.normal_(0.0, 1.0, generator=g)
+            layer.length = sp.prefix
+            layer.keys = layer.k_buf[..., :sp.prefix, :]
+            layer.values = layer.v_buf[..., :sp.prefix, :]
+        ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
+        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pool)
+        rng = np.random.default_rng(sp.seed)
+        cap.draft_logits.copy_(torch.from_numpy(
+            rng.standard_normal((DEPTHS, V)).astype(np.float32) * np.float32(3.0)).to(torch.bfloat16))
+        cap.root_token.fill_(int(rng.integers(0, V)))
+        caps.append((sp, cap))
+    for _ in range(args.warmup):
+        for _, cap in caps:
+            cap.replay()
+    local = torch.full((len(caps), S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
+    for j, (sp, cap) in enumerate(caps):
+        local[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
+        local[j, 5] = 0
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    allrec = None
+    for _ in range(args.steps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0.record()
+        for j, (sp, cap) in enumerate(caps):
+            r = cap.replay()
+            # record on the device: [index, rank, n_nodes | n_accepted, next | 0 | path]
+            local[j, 3] = r.n_accepted[0]
+            local[j, 4] = r.next_token[0]
+            m = min(S.MAX_PATH, r.n_nodes)
+            local[j, 6:6 + m] = r.accepted[:m]
+        allrec = S.gather_results(local)
+        ev1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times.append(t.item())
+    ms = float(np.mean(times))
+    host = allrec.cpu()
+    tokens = int((host[:, 2] + host[:, 3]).sum())
+    value = tokens / (ms / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded request mix, random prefix K/V, N(0,1)*3 drafter logits, "
+                "random-init Qwen3-8B-shaped weights",
+        "config": {"workload": f"{args.requests} requests, prefix log-uniform 1k-32k, budget "
+                               "{64,128,256,512}, Qwen3-8B shape, one verify step each",
+                   "parallelism": f"request-dp{world} (longest-processing-time assignment)",
+                   "requests_per_rank": [len(x) for x in S.assign_requests(
+                       [S.request_cost(s) for s in specs], world)],
+                   "step": "every request's verify step once + all-gather of result records"},
+        "tokens_per_step": tokens,
+    }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_splitkv(args):
+    """Tree attention over one 131072-key prefix (Hq 32 / Hkv 8, D 128, 513 tree rows of a
+    seeded random tree) whose K/V are sharded along the sequence across the GPUs: each rank
+    computes the partial (O, m, l) of its shard, one NCCL all-gather exchanges them and
+    ddt_attn_merge combines them (the last rank also holds the tree rows)."""
+    import torch.distributed as dist
+
+    from mdflash_b200 import kernels as K
+    from mdflash_b200 import sharding as S
+
+    world, rank, dev = _dist_setup()
+    K._lib.load(build_if_missing=False)
+    P, B = args.prefix, args.budget
+    n = B + 1
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import inputs as gin
+    parents = gin.random_tree(n, 5)
+    bits = torch.from_numpy(anc_bits_host(parents).view(np.int32)).to(dev)
+    kb, ke = S.shard_range(P, n, world, rank)
+    g = torch.Generator(device=dev).manual_seed(11)
+    sc = 1.0 / math.sqrt(128)
+    q = (torch.randn((n, 32, 128), generator=g, device=dev) * sc).to(torch.bfloat16)
+    gk = torch.Generator(device=dev).manual_seed(100 + rank)
+    k = (torch.randn((8, ke - kb, 128), generator=gk, device=dev) * sc).to(torch.bfloat16)
+    v = torch.randn((8, ke - kb, 128), generator=gk, device=dev).to(torch.bfloat16)
+    out = torch.empty((n, 32, 128), dtype=torch.bfloat16, device=dev)
+    for _ in range(args.warmup):
+        S.splitkv_attention(q, k, v, kb, ke, bits, P, out=out)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        S.splitkv_attention(q, k, v, kb, ke, bits, P, out=out)
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times.append(t.item())
+    ms = float(np.mean(times))
+    flops = attn_flops(parents, P)
+    peaks, kind = measured_peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    link_bytes = (world - 1) * n * 32 * (128 + 2) * 4  # partials each rank receives
+    line = {
+        "metric": "tree-attn TFLOP/s", "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"split-KV tree attention: prefix {P} sharded over {world} GPUs, "
+                               f"{n} tree rows, Hq 32 / Hkv 8, D 128",
+                   "exchange": "NCCL all-gather of fp32 (O, m, l) partials + ddt_attn_merge",
+                   "partial_bytes_received_per_rank": link_bytes},
+        "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s per GPU", "frac": tflops / world / peaks["bf16_tflops"],
+                     "peak_source": f"{kind} bf16 burst", "flops_per_step": flops},
+    }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.workload == "requests":
+        return run_requests(args)
+    if args.workload == "splitkv":
+        return run_splitkv(args)
     if args.workload == "attn":
         run_attn(args)
     elif args.workload == "tree":

@@ -150,17 +150,22 @@ int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride, c
                   int64_t kv_splits, void* workspace, size_t workspace_bytes, int32_t* status,
                   void* stream);
 
-/* Partial-result attention: like ddt_tree_attn but writes un-normalised fp32 partials
- * (o_part [n_nodes, q_heads, head_dim], row max m and row sum l [n_nodes, q_heads]) over
- * the key range [key_begin, key_end) of this shard, for a cross-GPU split-KV merge.
+/* Partial-result attention: like ddt_tree_attn but writes un-normalised fp32 partials over
+ * the key range [key_begin, key_end) of this shard, for a cross-GPU split-KV merge, split
+ * in-GPU into kv_splits key ranges (0 picks one; query ddt_tree_attn_partial_splits):
+ * o_part [kv_splits, n_nodes * q_heads, head_dim], row max m and row sum l
+ * [kv_splits, n_nodes * q_heads] (m in log2 units of the scaled scores).
  * Keys are indexed globally: this shard's k/v pointers address key key_begin. */
+int64_t ddt_tree_attn_partial_splits(int64_t n_nodes, int64_t key_count, int64_t q_heads,
+                                     int64_t kv_heads);
 int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64_t q_head_stride,
                           const void* k, const void* v, int64_t kv_head_stride,
                           int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
                           float* o_part, float* m_part, float* l_part, int64_t n_nodes,
                           int64_t past_length, int64_t q_heads, int64_t kv_heads,
                           int64_t head_dim, const uint32_t* anc_bits, int64_t anc_words,
-                          int mask_mode, float scale, int32_t* status, void* stream);
+                          int mask_mode, float scale, int64_t kv_splits, int32_t* status,
+                          void* stream);
 
 /* Merge n_parts partials laid out [n_parts, rows, head_dim] / [n_parts, rows]
  * (rows = n_nodes * q_heads) into out (bf16, [n_nodes, q_heads, head_dim] at the given

@@ -711,6 +711,14 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
   return attn::launch(L, kv_heads, st);
 }
 
+extern "C" int64_t ddt_tree_attn_partial_splits(int64_t n_nodes, int64_t key_count,
+                                                int64_t q_heads, int64_t kv_heads) {
+  if (n_nodes <= 0 || key_count <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads)
+    return 1;
+  const int64_t pairs = (n_nodes * (q_heads / kv_heads) + attn::kRowsPerCta - 1) / attn::kRowsPerCta;
+  return attn::pick_splits(kv_heads * pairs, (key_count + attn::kBlockN - 1) / attn::kBlockN);
+}
+
 extern "C" int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64_t q_head_stride,
                                      const void* k, const void* v, int64_t kv_head_stride,
                                      int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
@@ -718,7 +726,7 @@ extern "C" int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64
                                      int64_t past_length, int64_t q_heads, int64_t kv_heads,
                                      int64_t head_dim, const uint32_t* anc_bits,
                                      int64_t anc_words, int mask_mode, float scale,
-                                     int32_t* status, void* stream) {
+                                     int64_t kv_splits, int32_t* status, void* stream) {
   if (!o_part || !m_part || !l_part) return DDT_ERR_INVALID;
   if (key_begin < 0 || key_end < key_begin || key_end > past_length + n_nodes) return DDT_ERR_INVALID;
   if (!aligned(o_part, 16)) return DDT_ERR_ALIGN;
@@ -728,7 +736,12 @@ extern "C" int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64
                          local > 0 ? local : 1, n_nodes, past_length, q_heads, kv_heads, head_dim,
                          anc_bits, anc_words, mask_mode, scale);
   if (rc) return rc;
-  L.p.n_splits = 1;
+  if (kv_splits <= 0) {
+    const int64_t kv_tiles = (local + attn::kBlockN - 1) / attn::kBlockN;
+    kv_splits = attn::pick_splits(kv_heads * L.p.n_pairs, kv_tiles);
+  }
+  if (kv_splits > 64) return DDT_ERR_CAPACITY;
+  L.p.n_splits = static_cast<int>(kv_splits);
   L.p.key_base = static_cast<int>(key_begin);
   L.p.key_lo = static_cast<int>(key_begin);
   L.p.key_hi = static_cast<int>(key_end);

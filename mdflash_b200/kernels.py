@@ -349,30 +349,34 @@ def attn_splits(n_nodes: int, q_heads: int, kv_heads: int, past_length: int,
 
 def tree_attention_partial(q, k_shard, v_shard, key_begin: int, key_end: int, anc_bits,
                            past_length: int, scale: float | None = None, causal: bool = False,
-                           out=None, status=None):
-    """Partial (O unnormalised fp32, m, l) over global keys [key_begin, key_end), whose
-    K/V rows are k_shard / v_shard ([Hkv, key_end - key_begin, D])."""
+                           out=None, status=None, kv_splits: int = 0):
+    """Partials (O unnormalised fp32 [S, N*Hq, D], m [S, N*Hq], l [S, N*Hq]) over global keys
+    [key_begin, key_end), whose K/V rows are k_shard / v_shard ([Hkv, key_end - key_begin,
+    D]); S = kv_splits in-GPU key splits (0 picks enough to fill the GPU)."""
     dev = _require_cuda(q, k_shard, v_shard)
     n, hq, qns, qhs = _q_view(q)
     hkv, s_local, khs, kss = _kv_view(k_shard)
     d = q.shape[-1]
     if s_local < key_end - key_begin:
         raise ValueError("shard shorter than its key range")
+    lib = _lib.load()
+    if kv_splits <= 0:
+        kv_splits = int(lib.ddt_tree_attn_partial_splits(n, key_end - key_begin, hq, hkv))
     if out is None:
-        out = (torch.empty((n * hq, d), dtype=torch.float32, device=dev),
-               torch.empty(n * hq, dtype=torch.float32, device=dev),
-               torch.empty(n * hq, dtype=torch.float32, device=dev))
+        out = (torch.empty((kv_splits, n * hq, d), dtype=torch.float32, device=dev),
+               torch.empty((kv_splits, n * hq), dtype=torch.float32, device=dev),
+               torch.empty((kv_splits, n * hq), dtype=torch.float32, device=dev))
     o, m, l = out
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     if status is None:
         status = WORKSPACES.get(dev, "attn_status", 256)[:4].view(torch.int32)
     words = anc_bits.shape[1] if anc_bits is not None else 0
-    rc = _lib.load().ddt_tree_attn_partial(
+    rc = lib.ddt_tree_attn_partial(
         q.data_ptr(), qns, qhs, k_shard.data_ptr(), v_shard.data_ptr(), khs, kss, key_begin,
         key_end, o.data_ptr(), m.data_ptr(), l.data_ptr(), n, past_length, hq, hkv, d,
         anc_bits.data_ptr() if anc_bits is not None else None, words,
-        DDT_MASK_CAUSAL if causal else DDT_MASK_TREE, float(scale), status.data_ptr(),
+        DDT_MASK_CAUSAL if causal else DDT_MASK_TREE, float(scale), kv_splits, status.data_ptr(),
         _stream(dev))
     check(rc, "ddt_tree_attn_partial")
     STATS.launches += 1

@@ -1,0 +1,167 @@
+"""Multi-GPU partitioning of the DDTree verify path (one process per GPU).
+
+Two modes, both without any data-path collective inside the verify step except the one
+split-KV exchange:
+
+* Request data parallelism.  The reference shards its dataset rank-strided
+  (benchmark.py:436, ``indices = range(rank, len, world)``) and gathers pickled per-request
+  results to rank 0 with ``gather_object`` (distributed.py:55-64).  Here requests are
+  assigned by longest-processing-time first on a cost model of the verify step (attention
+  grows with prefix x tree rows, the GEMMs with tree rows), and results travel as
+  fixed-size int64 records in one ``all_gather`` (NCCL on GPUs, gloo on CPUs).
+* Sequence-sharded split-KV for one long prefix.  The prefix keys are split into
+  contiguous, 128-key-aligned shards; the last rank also owns the tree rows (so it is the
+  rank that runs the compaction).  Every rank computes the partial (O, m, l) of its keys
+  with ``ddt_tree_attn_partial``; one ``all_gather`` of the partials and ``ddt_attn_merge``
+  give every rank the full attention output.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+MAX_PATH = 21          # root + one node per drafted depth (DDT_MAX_DEPTH = 20)
+RECORD_LEN = 6 + MAX_PATH
+
+
+@dataclass(frozen=True)
+class RequestSpec:
+    index: int
+    prefix: int
+    budget: int
+    seed: int
+
+
+def request_specs(n: int = 64, seed: int = 0, lo: int = 1024, hi: int = 32768,
+                  budgets=(64, 128, 256, 512)) -> list[RequestSpec]:
+    """Seeded request mix: prefix lengths log-uniform in [lo, hi], budgets uniform over
+    `budgets`, one drafter-logit seed per request."""
+    rng = np.random.default_rng(seed)
+    prefixes = np.exp(rng.uniform(math.log(lo), math.log(hi), n)).round().astype(np.int64)
+    bud = rng.choice(np.asarray(budgets), n)
+    return [RequestSpec(i, int(prefixes[i]), int(bud[i]), seed * 100003 + i) for i in range(n)]
+
+
+def request_cost(spec: RequestSpec, layers: int = 36, q_heads: int = 32, head_dim: int = 128,
+                 params: float = 8.2e9) -> float:
+    """FLOPs of one verify step: tree attention 4 Hq D N P per layer plus 2 W N for the
+    projections and lm_head (W = weight count), N = budget + 1 rows."""
+    n = spec.budget + 1
+    return n * (4.0 * q_heads * head_dim * spec.prefix * layers + 2.0 * params)
+
+
+def assign_requests(costs, world: int) -> list[list[int]]:
+    """Longest-processing-time first: requests in decreasing cost go to the least loaded
+    rank (ties to the lower rank, then the lower request index).  Deterministic, so every
+    rank computes the same assignment without communication."""
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    load = [0.0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda x: (load[x], x))
+        out[r].append(i)
+        load[r] += costs[i]
+    return [sorted(o) for o in out]
+
+
+def pack_result(index: int, n_nodes: int, accepted, next_token: int, time_ns: int = 0,
+                rank: int = 0) -> torch.Tensor:
+    """One int64 record: [index, rank, n_nodes, n_accepted, next_token, time_ns,
+    accepted[0..MAX_PATH) padded with -1]."""
+    rec = torch.full((RECORD_LEN,), -1, dtype=torch.int64)
+    acc = list(accepted)
+    if len(acc) > MAX_PATH:
+        raise ValueError("accepted path longer than the record holds")
+    rec[:6] = torch.tensor([index, rank, n_nodes, len(acc), next_token, time_ns])
+    if acc:
+        rec[6:6 + len(acc)] = torch.tensor(acc, dtype=torch.int64)
+    return rec
+
+
+def unpack_result(rec: torch.Tensor) -> dict:
+    r = rec.tolist()
+    k = r[3]
+    return dict(index=r[0], rank=r[1], n_nodes=r[2], n_accepted=k, next_token=r[4], time_ns=r[5],
+                accepted=r[6:6 + k])
+
+
+def gather_results(records: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gathers variable numbers of [k, RECORD_LEN] records from every rank; returns all
+    records sorted by request index (identical on every rank).  Works on NCCL (CUDA tensors)
+    and gloo (CPU tensors)."""
+    if not dist.is_initialized():
+        return records[records[:, 0].argsort()]
+    world = dist.get_world_size(group)
+    dev = records.device
+    cnt = torch.tensor([records.shape[0]], dtype=torch.int64, device=dev)
+    counts = [torch.zeros_like(cnt) for _ in range(world)]
+    dist.all_gather(counts, cnt, group=group)
+    mx = int(max(c.item() for c in counts))
+    pad = torch.full((mx, RECORD_LEN), -1, dtype=torch.int64, device=dev)
+    pad[:records.shape[0]] = records
+    bufs = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(bufs, pad, group=group)
+    allr = torch.cat([b[:int(c.item())] for b, c in zip(bufs, counts)])
+    return allr[allr[:, 0].argsort()]
+
+
+def shard_range(prefix: int, n_nodes: int, world: int, rank: int, align: int = 128):
+    """Global key range [begin, end) of `rank`: the prefix [0, prefix) split into
+    `align`-aligned contiguous shards, the last rank also owning the tree keys
+    [prefix, prefix + n_nodes).  Shards are non-empty as long as prefix >= world * align."""
+    per = -(-prefix // world)
+    per = -(-per // align) * align
+    begin = min(rank * per, prefix)
+    end = min((rank + 1) * per, prefix)
+    if rank == world - 1:
+        end = prefix + n_nodes
+    return begin, end
+
+
+def owner_rank(world: int) -> int:
+    """The rank that holds the tree rows (and compacts them)."""
+    return world - 1
+
+
+def exchange_partials(o: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=None):
+    """All-gathers this rank's partials (O [S, rows, D], m [S, rows], l [S, rows]; a single
+    partial may drop the leading S) into ([world * S, rows, D], [world * S, rows] x 2).
+    Every rank must hold the same S."""
+    if o.dim() == 2:
+        o, m, l = o[None], m[None], l[None]
+    if not dist.is_initialized():
+        return o, m, l
+    world = dist.get_world_size(group)
+    s, rows, d = o.shape
+    packed = torch.cat([o.reshape(-1), m.reshape(-1), l.reshape(-1)])
+    bufs = [torch.empty_like(packed) for _ in range(world)]
+    dist.all_gather(bufs, packed, group=group)
+    allp = torch.stack(bufs)
+    og = allp[:, :s * rows * d].reshape(world * s, rows, d)
+    mg = allp[:, s * rows * d:s * rows * (d + 1)].reshape(world * s, rows)
+    lg = allp[:, s * rows * (d + 1):].reshape(world * s, rows)
+    return og, mg, lg
+
+
+def splitkv_attention(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
+                      key_begin: int, key_end: int, anc_bits: torch.Tensor | None,
+                      past_length: int, scale: float | None = None, group=None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tree attention over a sequence-sharded prefix: partial on this rank's keys, one
+    all-gather of the partials, merge.  Returns the bf16 output [N, Hq, D] on every rank."""
+    from . import kernels as K
+    n, hq = q.shape[0], q.shape[1]
+    # the in-GPU split count must be the same on every rank (the exchanged partials have one
+    # shape): derive it from quantities every rank shares, not from this rank's shard size
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    per_rank_keys = -(-(past_length + n) // world)
+    splits = int(K._lib.load().ddt_tree_attn_partial_splits(n, per_rank_keys, hq,
+                                                           k_shard.shape[-3]))
+    o, m, l = K.tree_attention_partial(q, k_shard, v_shard, key_begin, key_end, anc_bits,
+                                       past_length, scale=scale, kv_splits=splits)
+    og, mg, lg = exchange_partials(o, m, l, group)
+    return K.attn_merge(og, mg, lg, n, hq, out=out)

@@ -39,12 +39,13 @@ class StepResult:
 class TreeVerifier:
     def __init__(self, target: torch.nn.Module, cache: TreeKVCache, budget: int, depths: int,
                  vocab: int, device: torch.device | str = "cuda", keep_logits: bool = False,
-                 fused: bool = False):
+                 fused: bool = False, runner=None):
         """fused=False runs the transformers model with attn_implementation="ddtree_tree";
-        fused=True runs its weights through Qwen3VerifyRunner (fused elementwise stages)."""
+        fused=True runs its weights through Qwen3VerifyRunner (fused elementwise stages); a
+        runner can be shared between verifiers of the same model (runner=...)."""
         self.target = target
-        self.runner = None
-        if fused:
+        self.runner = runner
+        if fused and runner is None:
             from .runner import Qwen3VerifyRunner
             self.runner = Qwen3VerifyRunner(target)
         self.cache = cache
@@ -97,7 +98,7 @@ class CapturedStep:
     object: copy new values in before ``replay``); outputs land in ``result``."""
 
     def __init__(self, verifier: TreeVerifier, start: int, warmup: int = 2,
-                 time_attention: bool = False):
+                 time_attention: bool = False, pool=None):
         self.verifier = verifier
         self.start = start
         v = verifier
@@ -113,7 +114,7 @@ class CapturedStep:
         torch.cuda.synchronize(v.device)
         self.graph = torch.cuda.CUDAGraph()
         K.STATS.reset(time_attention=time_attention)
-        with torch.cuda.graph(self.graph):
+        with torch.cuda.graph(self.graph, pool=pool):
             self.result = v.step(self.draft_logits, self.root_token, start)
         self.launches_per_replay = K.STATS.launches
         self.attn_events = list(K.STATS.attn_events)
