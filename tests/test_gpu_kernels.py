@@ -237,9 +237,9 @@ def test_tree_attention_partial_merge_equals_full(cuda_device):
     parts = []
     for a, b in zip(bounds[:-1], bounds[1:]):
         parts.append(K.tree_attention_partial(q, k[:, a:b], v[:, a:b], a, b, bits, past))
-    o = torch.stack([p[0] for p in parts])
-    m = torch.stack([p[1] for p in parts])
-    l = torch.stack([p[2] for p in parts])
+    o = torch.cat([p[0] for p in parts])  # each shard: [S, rows, D] partials
+    m = torch.cat([p[1] for p in parts])
+    l = torch.cat([p[2] for p in parts])
     merged = K.attn_merge(o, m, l, n, hq)
     torch.cuda.synchronize()
     assert _rel_err(merged, full) <= 1e-2

@@ -43,8 +43,9 @@ def test_splitkv_shards_in_one_process(cuda_device, world):
         kb, ke = S.shard_range(P, N, world, r)
         parts.append(K.tree_attention_partial(q, k[:, kb:ke].contiguous(), v[:, kb:ke].contiguous(),
                                               kb, ke, bits, P))
-    merged = K.attn_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]),
-                          torch.stack([p[2] for p in parts]), N, 32)
+    # each shard yields [S, rows, ...] partials (S in-GPU key splits)
+    merged = K.attn_merge(torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts]),
+                          torch.cat([p[2] for p in parts]), N, 32)
     torch.cuda.synchronize()
     assert _rel(merged, full) <= 1e-2
     assert _rel(S.splitkv_attention(q, k, v, 0, P + N, bits, P), full) <= 1e-2
