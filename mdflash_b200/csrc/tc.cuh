@@ -196,6 +196,42 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   d |= 2ull << 61;
   return d;
 }
+// The same descriptor split into its two 32-bit words.  The low word (start address and
+// leading byte offset) is the only part that changes between the MMAs of a tile, and it is
+// linear in the address while the address stays below 256 KB: desc_lo(a + off) =
+// desc_lo(a) + off / 16.  Building each descriptor as one 32-bit add keeps the single MMA
+// issuing thread at the tensor pipe's rate (one 128x128x16 MMA per 64 cycles); computing
+// the full 64-bit value per MMA made the issue loop, not the pipe, the bound.
+__host__ __device__ constexpr uint32_t desc_sw128_hi(uint32_t sbo_bytes) {
+  return ((sbo_bytes >> 4) & 0x3fffu) | (1u << 14) | (2u << 29);
+}
+__device__ __forceinline__ uint32_t desc_sw128_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3fffu) | (((lbo_bytes >> 4) & 0x3fffu) << 16);
+}
+// SS MMA from descriptor words; ACC (0/1) is a compile-time accumulate flag.
+template <uint32_t ACC>
+__device__ __forceinline__ void mma_bf16_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                              uint32_t hi, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "n"(ACC)
+      : "memory");
+}
+// TS MMA (A from TMEM) from a B descriptor's words; accumulate flag at run time.
+__device__ __forceinline__ void mma_bf16_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                              uint32_t hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 D:
 // D format [4,6) = 1 (f32), A format [7,10) = 1 (bf16), B format [10,13) = 1 (bf16),
 // A major bit 15, B major bit 16 (1 = MN-major), N >> 3 in [17,23), M >> 4 in [24,29).

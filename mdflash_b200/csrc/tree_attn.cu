@@ -85,8 +85,10 @@ struct Params {
 };
 
 struct Bars {
-  uint64_t q_full, k_full[kStages], v_full[kStages], kv_empty[kStages], s_full[2], p_full[2],
-      o_ready[2], mma_done;
+  // K and V stages are released separately: K_j once both S_q(j) MMAs completed, V_j once
+  // both P V MMAs of tile j completed, so the next K load starts a full tile earlier
+  uint64_t q_full, k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages],
+      s_full[2], p_full[2], o_ready[2], mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -165,7 +167,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&bars.k_full[s], 1);
       tc::mbar_init(&bars.v_full[s], 1);
-      tc::mbar_init(&bars.kv_empty[s], 1);
+      tc::mbar_init(&bars.k_empty[s], 1);
+      tc::mbar_init(&bars.v_empty[s], 1);
     }
     for (int q = 0; q < 2; ++q) {
       tc::mbar_init(&bars.s_full[q], 1);
@@ -205,84 +208,100 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           tc::tma_load_3d(sQ + q * kTileBytes + kHalfBytes, &tm_q, &bars.q_full, 64, h * p.group,
                           node0);
         }
-        int issued = 0;
+        int issued_k = 0, issued_v = 0;
         for (int j = 0; j < nt; ++j) {
           const int st = j % kStages;
-          if (j >= kStages &&
-              !tc::mbar_wait(&bars.kv_empty[st], ((j / kStages) - 1) & 1, abort_flag, kTimeoutNs)) {
+          const uint32_t ph = ((j / kStages) - 1) & 1;  // release phase of tile j - kStages
+          const int key = lk0 + j * kBlockN;
+          if (j >= kStages && !tc::mbar_wait(&bars.k_empty[st], ph, abort_flag, kTimeoutNs)) {
             raise_abort(bars, p.status);
             break;
           }
-          const int key = lk0 + j * kBlockN;
           unsigned char* kd = sK + st * kTileBytes;
-          unsigned char* vd = sV + st * kTileBytes;
           tc::mbar_expect_tx(&bars.k_full[st], kTileBytes);
           tc::tma_load_3d(kd, &tm_k, &bars.k_full[st], 0, key, h);
           tc::tma_load_3d(kd + kHalfBytes, &tm_k, &bars.k_full[st], 64, key, h);
+          issued_k = j + 1;
+          if (j >= kStages && !tc::mbar_wait(&bars.v_empty[st], ph, abort_flag, kTimeoutNs)) {
+            raise_abort(bars, p.status);
+            break;
+          }
+          unsigned char* vd = sV + st * kTileBytes;
           tc::mbar_expect_tx(&bars.v_full[st], kTileBytes);
           tc::tma_load_3d(vd, &tm_v, &bars.v_full[st], 0, key, h);
           tc::tma_load_3d(vd + kHalfBytes, &tm_v, &bars.v_full[st], 64, key, h);
-          issued = j + 1;
+          issued_v = j + 1;
         }
         if (*abort_flag) {
           // let the loads already in flight land before the CTA releases its smem
           tc::mbar_wait_drain(&bars.q_full, 0, kTimeoutNs);
-          for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
-            const int st = j % kStages;
-            tc::mbar_wait_drain(&bars.k_full[st], (j / kStages) & 1, kTimeoutNs);
-            tc::mbar_wait_drain(&bars.v_full[st], (j / kStages) & 1, kTimeoutNs);
-          }
+          for (int j = issued_k > kStages ? issued_k - kStages : 0; j < issued_k; ++j)
+            tc::mbar_wait_drain(&bars.k_full[j % kStages], (j / kStages) & 1, kTimeoutNs);
+          for (int j = issued_v > kStages ? issued_v - kStages : 0; j < issued_v; ++j)
+            tc::mbar_wait_drain(&bars.v_full[j % kStages], (j / kStages) & 1, kTimeoutNs);
         }
       }
     } else if (warp == 1) {
       // ---------------------------- MMA issuer ---------------------------------------
       if (lane == 0 && nt > 0) {
-        const uint32_t q_addr = tc::smem_u32(sQ);
-        const uint32_t k_addr = tc::smem_u32(sK);
-        const uint32_t v_addr = tc::smem_u32(sV);
+        // descriptor low words of the Q, K and V tiles; every MMA adds a constant to them
+        constexpr uint32_t kDescHi = tc::desc_sw128_hi(1024);
+        const uint32_t q_lo = tc::desc_sw128_lo(tc::smem_u32(sQ), 16);
+        const uint32_t k_lo = tc::desc_sw128_lo(tc::smem_u32(sK), 16);
+        const uint32_t v_lo = tc::desc_sw128_lo(tc::smem_u32(sV), kHalfBytes);
         const int nq = q1_active ? 2 : 1;
         bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
         // S_q = Q_q K_j^T into the S region of query tile q
         auto issue_s = [&](int q, int j) {
-          const uint32_t kb = k_addr + (j % kStages) * kTileBytes;
-          const uint32_t qb = q_addr + q * kTileBytes;
+          const uint32_t a = q_lo + q * (kTileBytes >> 4);
+          const uint32_t b = k_lo + (j % kStages) * (kTileBytes >> 4);
+          const uint32_t d = tmem + col_s(q);
+          tc::mma_bf16_ss_w<0>(d, a, b, kDescHi, kIdescS);
 #pragma unroll
-          for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-            tc::mma_bf16_ss(tmem + col_s(q), tc::smem_desc_sw128(qb + off, 16, 1024),
-                            tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+          for (int kk = 1; kk < kHeadDim / 16; ++kk) {
+            const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+            tc::mma_bf16_ss_w<1>(d, a + off, b + off, kDescHi, kIdescS);
           }
           tc::mma_commit(&bars.s_full[q]);
         };
         // O_q += P_q V_j, P_q in TMEM (first 64 columns of the S region, 8 per K step)
         auto issue_pv = [&](int q, int j) {
-          const uint32_t vb = v_addr + (j % kStages) * kTileBytes;
+          const uint32_t b = v_lo + (j % kStages) * (kTileBytes >> 4);
+          const uint32_t d = tmem + col_o(q);
+          const uint32_t a = tmem + col_s(q);
 #pragma unroll
           for (int kk = 0; kk < kBlockN / 16; ++kk)
-            tc::mma_bf16_ts(tmem + col_o(q), tmem + col_s(q) + kk * 8,
-                            tc::smem_desc_sw128(vb + kk * 2048, kHalfBytes, 1024), kIdescPV,
-                            (j > 0 || kk > 0) ? 1u : 0u);
+            tc::mma_bf16_ts_w(d, a + kk * 8, b + ((kk * 2048) >> 4), kDescHi, kIdescPV,
+                              (j > 0 || kk > 0) ? 1u : 0u);
           tc::mma_commit(&bars.o_ready[q]);
         };
+        // stage releases are committed only where the producer will wait for them
         if (ok) ok = tc::mbar_wait(&bars.k_full[0], 0, abort_flag, kTimeoutNs);
         if (ok) {
           tc::tc_fence_after();
           for (int q = 0; q < nq; ++q) issue_s(q, 0);
+          if (kStages < nt) tc::mma_commit(&bars.k_empty[0]);
         }
         for (int j = 0; ok && j < nt; ++j) {
           const int st = j % kStages;
-          ok = tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs);
+          const int sn = (j + 1) % kStages;
           const bool more = j + 1 < nt;
-          if (ok && more)
-            ok = tc::mbar_wait(&bars.k_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, abort_flag,
-                               kTimeoutNs);
+          ok = tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs);
           for (int q = 0; ok && q < nq; ++q) {
             ok = tc::mbar_wait(&bars.p_full[q], j & 1, abort_flag, kTimeoutNs);
             if (!ok) break;
             tc::tc_fence_after();
             issue_pv(q, j);
-            if (q == nq - 1) tc::mma_commit(&bars.kv_empty[st]);
-            if (more) issue_s(q, j + 1);  // reuses S_q / P_q: runs after the P V MMA above
+            if (q == nq - 1 && j + kStages < nt) tc::mma_commit(&bars.v_empty[st]);
+            if (more) {
+              // K of the next tile is only needed here, not before the P V MMAs above
+              if (q == 0 &&
+                  !(ok = tc::mbar_wait(&bars.k_full[sn], ((j + 1) / kStages) & 1, abort_flag,
+                                       kTimeoutNs)))
+                break;
+              issue_s(q, j + 1);  // reuses S_q / P_q: runs after the P V MMA above
+              if (q == nq - 1 && j + 1 + kStages < nt) tc::mma_commit(&bars.k_empty[sn]);
+            }
           }
         }
         if (!ok) {
