@@ -83,6 +83,36 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   return true;
 }
 
+// ---- shared-memory counters with acquire/release ordering ----------------------------
+// The MMA-issuing thread waits on these rather than on mbarriers: an mbarrier try_wait
+// issued while that thread has tcgen05.mma in flight stalls until they drain (measured
+// ~180 cycles per wait, during which the tensor pipe idles), a plain acquire load does not.
+__device__ __forceinline__ uint32_t ld_acquire_shared(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_shared(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_add_shared(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v)
+               : "memory");
+}
+// Bounded spin until the monotonic counter *p reaches `target`; false on abort or timeout.
+__device__ __forceinline__ bool counter_wait(const uint32_t* p, uint32_t target,
+                                             volatile int* abort, uint64_t timeout_ns) {
+  if (ld_acquire_shared(p) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ld_acquire_shared(p) >= target) return true;
+    if ((it & 255u) == 0) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > timeout_ns) return false;
+    }
+  }
+}
+
 // ---- TMA ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -255,6 +285,68 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes per instruction) -----------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// three-input maximum (one instruction on sm_100); NaN operands are ignored like fmaxf
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of lanes on the FMA pipe, to take part of the exponentials off the
+// 16-per-cycle MUFU unit.  Method: Cody-Waite style range reduction, j = round(x) by adding
+// and subtracting the shifter 1.5 * 2^23 (exact for |x| < 2^22), f = x - j in [-1/2, 1/2];
+// 2^f by a degree-3 polynomial whose coefficients were fitted for relative error over
+// [-1/2, 1/2] (iteratively reweighted least squares; max relative error 1.1e-4, a twentieth
+// of the bf16 rounding step of P); 2^j is added into the exponent field, which is what the
+// low mantissa bits of the shifted value shifted left by 23 hold.  x is clamped at -126
+// first: -inf (masked keys) gives 2^-126 rather than 0, and the exponent cannot wrap.
+struct Exp2Poly {
+  uint64_t shift, neg_shift, minus1, c0, c1, c2, c3;
+  __device__ __forceinline__ Exp2Poly() {
+    shift = f2_pack(12582912.f, 12582912.f);
+    neg_shift = f2_pack(-12582912.f, -12582912.f);
+    minus1 = f2_pack(-1.f, -1.f);
+    c0 = f2_pack(0.99994176626f, 0.99994176626f);
+    c1 = f2_pack(0.69325703382f, 0.69325703382f);
+    c2 = f2_pack(0.24241356552f, 0.24241356552f);
+    c3 = f2_pack(0.05509214476f, 0.05509214476f);
+  }
+  __device__ __forceinline__ void operator()(uint64_t x2, float& y0, float& y1) const {
+    float x0, x1;
+    f2_unpack(x2, x0, x1);
+    const uint64_t x = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+    const uint64_t t = f2_add(x, shift);
+    const uint64_t f = f2_fma(f2_add(t, neg_shift), minus1, x);
+    uint64_t p = f2_fma(c3, f, c2);
+    p = f2_fma(p, f, c1);
+    p = f2_fma(p, f, c0);
+    float p0, p1, t0, t1;
+    f2_unpack(p, p0, p1);
+    f2_unpack(t, t0, t1);
+    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  }
+};
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;

@@ -64,6 +64,13 @@ constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;               // + alignment 
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kBlockM, kBlockN, false, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kBlockM, kHeadDim, false, true);
 constexpr int kStatusTimeout = 1;
+// Pairs (of the 16 in each 32-column chunk of an S row) whose exponentials are computed by
+// the FMA-pipe polynomial instead of MUFU (0: none; the extra instructions slowed the
+// MMA-issuing warp that shares their SM sub-partition more than the MUFU time they saved).
+#ifndef DDT_POLY_PAIRS
+#define DDT_POLY_PAIRS 0u
+#endif
+constexpr uint32_t kPolyPairs = DDT_POLY_PAIRS;
 // TMEM column of query tile q's S/P region and O accumulator
 __device__ __forceinline__ uint32_t col_s(int q) { return q ? 256u : 0u; }
 __device__ __forceinline__ uint32_t col_o(int q) { return q ? 384u : 128u; }
@@ -88,7 +95,14 @@ struct Bars {
   // K and V stages are released separately: K_j once both S_q(j) MMAs completed, V_j once
   // both P V MMAs of tile j completed, so the next K load starts a full tile earlier
   uint64_t q_full, k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages],
-      s_full[2], p_full[2], o_ready[2], mma_done;
+      s_full[2], o_ready[2], mma_done[2];
+  // counters the MMA thread polls instead of mbarriers: tiles whose K / V landed (set by the
+  // relay warp from k_full / v_full) and softmax warps done with P of query tile q
+  uint32_t k_ready, v_ready, p_count[2];
+  // MMA blocks issued per query tile (S_q(0), then P V(j) + S(j + 1) per tile): the two
+  // issuers take turns, tile 0 then tile 1, so the two softmax warpgroups stay half a
+  // period apart instead of competing for the same SM sub-partitions
+  uint32_t issued[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -167,15 +181,18 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&bars.k_full[s], 1);
       tc::mbar_init(&bars.v_full[s], 1);
-      tc::mbar_init(&bars.k_empty[s], 1);
-      tc::mbar_init(&bars.v_empty[s], 1);
+      tc::mbar_init(&bars.k_empty[s], q1_active ? 2 : 1);
+      tc::mbar_init(&bars.v_empty[s], q1_active ? 2 : 1);
     }
     for (int q = 0; q < 2; ++q) {
       tc::mbar_init(&bars.s_full[q], 1);
-      tc::mbar_init(&bars.p_full[q], 128);
+      bars.p_count[q] = 0;
+      bars.issued[q] = 0;
       tc::mbar_init(&bars.o_ready[q], 1);
     }
-    tc::mbar_init(&bars.mma_done, 1);
+    tc::mbar_init(&bars.mma_done[0], 1);
+    tc::mbar_init(&bars.mma_done[1], 1);
+    bars.k_ready = bars.v_ready = 0;
     bars.abort = 0;
     tc::fence_mbar_init();
   }
@@ -241,74 +258,111 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             tc::mbar_wait_drain(&bars.v_full[j % kStages], (j / kStages) & 1, kTimeoutNs);
         }
       }
-    } else if (warp == 1) {
-      // ---------------------------- MMA issuer ---------------------------------------
+    } else if (warp == 2) {
+      // ---------------------------- TMA completion relay -----------------------------
+      // turns k_full / v_full phases into the k_ready / v_ready tile counts
       if (lane == 0 && nt > 0) {
+        for (int j = 0; j < nt; ++j) {
+          const int st = j % kStages;
+          const uint32_t ph = (j / kStages) & 1;
+          if (!tc::mbar_wait(&bars.k_full[st], ph, abort_flag, kTimeoutNs)) {
+            raise_abort(bars, p.status);
+            break;
+          }
+          tc::st_release_shared(&bars.k_ready, j + 1);
+          if (!tc::mbar_wait(&bars.v_full[st], ph, abort_flag, kTimeoutNs)) {
+            raise_abort(bars, p.status);
+            break;
+          }
+          tc::st_release_shared(&bars.v_ready, j + 1);
+        }
+      }
+    } else if (warp == 1 || warp == 3) {
+      // ---------------------------- MMA issuers, one per query tile ------------------
+      // Query tile 0's MMAs come from warp 1, tile 1's from warp 3.  A wait with acquire
+      // semantics holds the waiting thread until its own MMAs in flight have drained; with
+      // one issuer per tile every wait falls where that tile's previous MMAs are already
+      // complete (P_q(j) ready implies S_q(j) done), while the other tile's MMAs keep the
+      // tensor pipe busy.
+      const int q = warp == 1 ? 0 : 1;
+      if (lane == 0 && nt > 0 && (q == 0 || q1_active)) {
         // descriptor low words of the Q, K and V tiles; every MMA adds a constant to them
         constexpr uint32_t kDescHi = tc::desc_sw128_hi(1024);
-        const uint32_t q_lo = tc::desc_sw128_lo(tc::smem_u32(sQ), 16);
+        const uint32_t a_q = tc::desc_sw128_lo(tc::smem_u32(sQ), 16) + q * (kTileBytes >> 4);
         const uint32_t k_lo = tc::desc_sw128_lo(tc::smem_u32(sK), 16);
         const uint32_t v_lo = tc::desc_sw128_lo(tc::smem_u32(sV), kHalfBytes);
-        const int nq = q1_active ? 2 : 1;
-        bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
+        const uint32_t d_s = tmem + col_s(q), d_o = tmem + col_o(q);
         // S_q = Q_q K_j^T into the S region of query tile q
-        auto issue_s = [&](int q, int j) {
-          const uint32_t a = q_lo + q * (kTileBytes >> 4);
+        auto issue_s = [&](int j) {
           const uint32_t b = k_lo + (j % kStages) * (kTileBytes >> 4);
-          const uint32_t d = tmem + col_s(q);
-          tc::mma_bf16_ss_w<0>(d, a, b, kDescHi, kIdescS);
+          tc::mma_bf16_ss_w<0>(d_s, a_q, b, kDescHi, kIdescS);
 #pragma unroll
           for (int kk = 1; kk < kHeadDim / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
-            tc::mma_bf16_ss_w<1>(d, a + off, b + off, kDescHi, kIdescS);
+            tc::mma_bf16_ss_w<1>(d_s, a_q + off, b + off, kDescHi, kIdescS);
           }
           tc::mma_commit(&bars.s_full[q]);
         };
         // O_q += P_q V_j, P_q in TMEM (first 64 columns of the S region, 8 per K step)
-        auto issue_pv = [&](int q, int j) {
+        auto issue_pv = [&](int j) {
           const uint32_t b = v_lo + (j % kStages) * (kTileBytes >> 4);
-          const uint32_t d = tmem + col_o(q);
-          const uint32_t a = tmem + col_s(q);
 #pragma unroll
           for (int kk = 0; kk < kBlockN / 16; ++kk)
-            tc::mma_bf16_ts_w(d, a + kk * 8, b + ((kk * 2048) >> 4), kDescHi, kIdescPV,
+            tc::mma_bf16_ts_w(d_o, d_s + kk * 8, b + ((kk * 2048) >> 4), kDescHi, kIdescPV,
                               (j > 0 || kk > 0) ? 1u : 0u);
           tc::mma_commit(&bars.o_ready[q]);
         };
-        // stage releases are committed only where the producer will wait for them
-        if (ok) ok = tc::mbar_wait(&bars.k_full[0], 0, abort_flag, kTimeoutNs);
+        // stage releases (k_empty / v_empty count one commit per active tile) are committed
+        // only where the producer will wait for them
+        // turn-taking on plain (volatile) loads and stores: an acquire or release here
+        // would wait for this thread's MMAs in flight, and the turns order only the issue
+        // of the two tiles' MMAs, no data
+        volatile uint32_t* my_turns = &bars.issued[q];
+        const volatile uint32_t* other_turns = &bars.issued[q ^ 1];
+        const bool alternate = q1_active;
+        auto wait_turn = [&](uint32_t target) {
+          if (!alternate) return true;
+          const uint64_t t0 = global_timer_ns();
+          for (uint32_t it = 0; *other_turns < target; ++it) {
+            if ((it & 255u) == 255u && (*abort_flag || global_timer_ns() - t0 > kTimeoutNs))
+              return false;
+          }
+          return true;
+        };
+        bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
+        if (ok) ok = tc::counter_wait(&bars.k_ready, 1, abort_flag, kTimeoutNs);
+        if (ok && q == 1) ok = wait_turn(1);
         if (ok) {
           tc::tc_fence_after();
-          for (int q = 0; q < nq; ++q) issue_s(q, 0);
+          issue_s(0);
           if (kStages < nt) tc::mma_commit(&bars.k_empty[0]);
+          *my_turns = 1;
         }
         for (int j = 0; ok && j < nt; ++j) {
           const int st = j % kStages;
           const int sn = (j + 1) % kStages;
           const bool more = j + 1 < nt;
-          ok = tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs);
-          for (int q = 0; ok && q < nq; ++q) {
-            ok = tc::mbar_wait(&bars.p_full[q], j & 1, abort_flag, kTimeoutNs);
-            if (!ok) break;
-            tc::tc_fence_after();
-            issue_pv(q, j);
-            if (q == nq - 1 && j + kStages < nt) tc::mma_commit(&bars.v_empty[st]);
-            if (more) {
-              // K of the next tile is only needed here, not before the P V MMAs above
-              if (q == 0 &&
-                  !(ok = tc::mbar_wait(&bars.k_full[sn], ((j + 1) / kStages) & 1, abort_flag,
-                                       kTimeoutNs)))
-                break;
-              issue_s(q, j + 1);  // reuses S_q / P_q: runs after the P V MMA above
-              if (q == nq - 1 && j + 1 + kStages < nt) tc::mma_commit(&bars.k_empty[sn]);
-            }
+          // every wait of the tile before any of its MMAs: nothing of this thread in flight
+          if (!(ok = tc::counter_wait(&bars.p_count[q], 4u * (j + 1), abort_flag, kTimeoutNs)))
+            break;
+          if (!(ok = tc::counter_wait(&bars.v_ready, j + 1, abort_flag, kTimeoutNs))) break;
+          if (more && !(ok = tc::counter_wait(&bars.k_ready, j + 2, abort_flag, kTimeoutNs)))
+            break;
+          if (!(ok = wait_turn(q == 0 ? j + 1 : j + 2))) break;
+          tc::tc_fence_after();
+          issue_pv(j);
+          if (j + kStages < nt) tc::mma_commit(&bars.v_empty[st]);
+          if (more) {
+            issue_s(j + 1);  // reuses S_q / P_q: runs after the P V MMA above
+            if (j + 1 + kStages < nt) tc::mma_commit(&bars.k_empty[sn]);
           }
+          *my_turns = j + 2;
         }
         if (!ok) {
           raise_abort(bars, p.status);
-          // wait for every MMA issued so far before TMEM is released
-          tc::mma_commit(&bars.mma_done);
-          tc::mbar_wait_drain(&bars.mma_done, 0, kTimeoutNs);
+          // wait for every MMA this thread issued before TMEM is released
+          tc::mma_commit(&bars.mma_done[q]);
+          tc::mbar_wait_drain(&bars.mma_done[q], 0, kTimeoutNs);
         }
       }
     }
@@ -333,6 +387,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int full_end = p.mask_mode == DDT_MASK_CAUSAL
                              ? (g_end < p.past_len + node + 1 ? g_end : p.past_len + node + 1)
                              : (g_end < p.past_len ? g_end : p.past_len);
+    const tc::Exp2Poly exp2_poly;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; active && j < nt; ++j) {
@@ -360,16 +415,18 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           for (int e = 0; e < 32; ++e)
             if (!((vis[c] >> e) & 1u)) sv[c][e] = __float_as_uint(-INFINITY);
       }
-      // masked row max of the raw scores, 8 independent chains
+      // masked row max of the raw scores: three-input maxima in 8 independent chains
       float mx8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sv[c][e]));
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int e = 0; e < 32; e += 2)
+          mx8[(e >> 1) & 7] = tc::fmax3(mx8[(e >> 1) & 7], __uint_as_float(sv[c][e]),
+                                        __uint_as_float(sv[c][e + 1]));
+      const float mx = tc::fmax3(tc::fmax3(mx8[0], mx8[1], mx8[2]), tc::fmax3(mx8[3], mx8[4], mx8[5]),
+                                 fmaxf(mx8[6], mx8[7]));
       bool rescale = false;
       float alpha = 1.f;
       if (mx > -INFINITY) {
@@ -402,10 +459,11 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
       // P = exp2(S * scale - m), packed bf16 into columns [0, 64) of S_q (masked keys hold
-      // -inf and give 0); 8 independent partial sums
-      float ls8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ls8[i] = 0.f;
+      // -inf and give 0, or 2^-126 on the polynomial lanes).  Scale and row sum run on
+      // packed fp32 pairs; the pairs selected by kPolyPairs take the polynomial exponential,
+      // the rest the MUFU one.
+      const uint64_t sl2x2 = tc::f2_pack(sl2, sl2), nmx2 = tc::f2_pack(nm, nm);
+      uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t pk[32];
@@ -413,19 +471,32 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int c = 0; c < 2; ++c) {
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float a = tc::ex2_approx(fmaf(__uint_as_float(sv[hf * 2 + c][e]), sl2, nm));
-            const float b = tc::ex2_approx(fmaf(__uint_as_float(sv[hf * 2 + c][e + 1]), sl2, nm));
-            ls8[(e >> 1) & 7] += a + b;
+            const uint64_t x = tc::f2_fma(tc::f2_pack(__uint_as_float(sv[hf * 2 + c][e]),
+                                                      __uint_as_float(sv[hf * 2 + c][e + 1])),
+                                          sl2x2, nmx2);
+            float a, b;
+            if ((kPolyPairs >> (e >> 1)) & 1u) {
+              exp2_poly(x, a, b);
+            } else {
+              float x0, x1;
+              tc::f2_unpack(x, x0, x1);
+              a = tc::ex2_approx(x0);
+              b = tc::ex2_approx(x1);
+            }
+            ls2[(e >> 1) & 3] = tc::f2_add(ls2[(e >> 1) & 3], tc::f2_pack(a, b));
             pk[c * 16 + e / 2] = tc::pack_bf16x2(a, b);
           }
         }
         tc::tmem_st32(tS + hf * 32, pk);
       }
-      const float ls = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
-      l += ls;
+      float l0, l1, l2, l3;
+      tc::f2_unpack(tc::f2_add(ls2[0], ls2[1]), l0, l1);
+      tc::f2_unpack(tc::f2_add(ls2[2], ls2[3]), l2, l3);
+      l += (l0 + l1) + (l2 + l3);
       tc::tmem_wait_st();
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars.p_full[q]);
+      __syncwarp();
+      if (lane == 0) tc::red_release_add_shared(&bars.p_count[q], 1u);
     }
     if (active && ok && nt > 0 &&
         !tc::mbar_wait_warp(&bars.o_ready[q], (nt - 1) & 1, abort_flag, kTimeoutNs))
