@@ -95,10 +95,7 @@ struct Bars {
   // K and V stages are released separately: K_j once both S_q(j) MMAs completed, V_j once
   // both P V MMAs of tile j completed, so the next K load starts a full tile earlier
   uint64_t q_full, k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages],
-      s_full[2], o_ready[2], mma_done[2];
-  // counters the MMA thread polls instead of mbarriers: tiles whose K / V landed (set by the
-  // relay warp from k_full / v_full) and softmax warps done with P of query tile q
-  uint32_t k_ready, v_ready, p_count[2];
+      s_full[2], p_half[2], p_full[2], o_ready[2], mma_done[2];
   // MMA blocks issued per query tile (S_q(0), then P V(j) + S(j + 1) per tile): the two
   // issuers take turns, tile 0 then tile 1, so the two softmax warpgroups stay half a
   // period apart instead of competing for the same SM sub-partitions
@@ -186,13 +183,13 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     }
     for (int q = 0; q < 2; ++q) {
       tc::mbar_init(&bars.s_full[q], 1);
-      bars.p_count[q] = 0;
+      tc::mbar_init(&bars.p_half[q], 4);  // one arrive per softmax warp
+      tc::mbar_init(&bars.p_full[q], 4);
       bars.issued[q] = 0;
       tc::mbar_init(&bars.o_ready[q], 1);
     }
     tc::mbar_init(&bars.mma_done[0], 1);
     tc::mbar_init(&bars.mma_done[1], 1);
-    bars.k_ready = bars.v_ready = 0;
     bars.abort = 0;
     tc::fence_mbar_init();
   }
@@ -258,32 +255,13 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             tc::mbar_wait_drain(&bars.v_full[j % kStages], (j / kStages) & 1, kTimeoutNs);
         }
       }
-    } else if (warp == 2) {
-      // ---------------------------- TMA completion relay -----------------------------
-      // turns k_full / v_full phases into the k_ready / v_ready tile counts
-      if (lane == 0 && nt > 0) {
-        for (int j = 0; j < nt; ++j) {
-          const int st = j % kStages;
-          const uint32_t ph = (j / kStages) & 1;
-          if (!tc::mbar_wait(&bars.k_full[st], ph, abort_flag, kTimeoutNs)) {
-            raise_abort(bars, p.status);
-            break;
-          }
-          tc::st_release_shared(&bars.k_ready, j + 1);
-          if (!tc::mbar_wait(&bars.v_full[st], ph, abort_flag, kTimeoutNs)) {
-            raise_abort(bars, p.status);
-            break;
-          }
-          tc::st_release_shared(&bars.v_ready, j + 1);
-        }
-      }
     } else if (warp == 1 || warp == 3) {
       // ---------------------------- MMA issuers, one per query tile ------------------
-      // Query tile 0's MMAs come from warp 1, tile 1's from warp 3.  A wait with acquire
-      // semantics holds the waiting thread until its own MMAs in flight have drained; with
-      // one issuer per tile every wait falls where that tile's previous MMAs are already
-      // complete (P_q(j) ready implies S_q(j) done), while the other tile's MMAs keep the
-      // tensor pipe busy.
+      // Query tile 0's MMAs come from warp 1, tile 1's from warp 3.  An mbarrier wait (or
+      // any acquire) holds the waiting thread until its own MMAs in flight have drained
+      // (measured ~180 cycles of idle tensor pipe per wait with a single issuer).  With one
+      // issuer per tile every wait falls where that tile's previous MMAs are complete anyway
+      // (P_q(j) ready implies S_q(j) done), while the other tile's MMAs keep the pipe busy.
       const int q = warp == 1 ? 0 : 1;
       if (lane == 0 && nt > 0 && (q == 0 || q1_active)) {
         // descriptor low words of the Q, K and V tiles; every MMA adds a constant to them
@@ -303,14 +281,17 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
           tc::mma_commit(&bars.s_full[q]);
         };
-        // O_q += P_q V_j, P_q in TMEM (first 64 columns of the S region, 8 per K step)
-        auto issue_pv = [&](int j) {
+        // O_q += P_q V_j, P_q in TMEM (first 64 columns of the S region, 8 per K step), in
+        // two halves of 64 keys: the first runs while the softmax computes the second
+        auto issue_pv = [&](int j, int half) {
           const uint32_t b = v_lo + (j % kStages) * (kTileBytes >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kBlockN / 16; ++kk)
+          for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
+            const int kk = half * (kBlockN / 32) + k4;
             tc::mma_bf16_ts_w(d_o, d_s + kk * 8, b + ((kk * 2048) >> 4), kDescHi, kIdescPV,
                               (j > 0 || kk > 0) ? 1u : 0u);
-          tc::mma_commit(&bars.o_ready[q]);
+          }
+          if (half) tc::mma_commit(&bars.o_ready[q]);
         };
         // stage releases (k_empty / v_empty count one commit per active tile) are committed
         // only where the producer will wait for them
@@ -330,7 +311,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           return true;
         };
         bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
-        if (ok) ok = tc::counter_wait(&bars.k_ready, 1, abort_flag, kTimeoutNs);
+        if (ok) ok = tc::mbar_wait(&bars.k_full[0], 0, abort_flag, kTimeoutNs);
         if (ok && q == 1) ok = wait_turn(1);
         if (ok) {
           tc::tc_fence_after();
@@ -342,15 +323,19 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           const int st = j % kStages;
           const int sn = (j + 1) % kStages;
           const bool more = j + 1 < nt;
-          // every wait of the tile before any of its MMAs: nothing of this thread in flight
-          if (!(ok = tc::counter_wait(&bars.p_count[q], 4u * (j + 1), abort_flag, kTimeoutNs)))
+          // K / V of the tile landed long before P_q(j): waited first, while the softmax runs
+          if (!(ok = tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs)))
             break;
-          if (!(ok = tc::counter_wait(&bars.v_ready, j + 1, abort_flag, kTimeoutNs))) break;
-          if (more && !(ok = tc::counter_wait(&bars.k_ready, j + 2, abort_flag, kTimeoutNs)))
+          if (more && !(ok = tc::mbar_wait(&bars.k_full[sn], ((j + 1) / kStages) & 1, abort_flag,
+                                           kTimeoutNs)))
             break;
+          if (!(ok = tc::mbar_wait(&bars.p_half[q], j & 1, abort_flag, kTimeoutNs))) break;
           if (!(ok = wait_turn(q == 0 ? j + 1 : j + 2))) break;
           tc::tc_fence_after();
-          issue_pv(j);
+          issue_pv(j, 0);
+          if (!(ok = tc::mbar_wait(&bars.p_full[q], j & 1, abort_flag, kTimeoutNs))) break;
+          tc::tc_fence_after();
+          issue_pv(j, 1);
           if (j + kStages < nt) tc::mma_commit(&bars.v_empty[st]);
           if (more) {
             issue_s(j + 1);  // reuses S_q / P_q: runs after the P V MMA above
@@ -464,9 +449,11 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // the rest the MUFU one.
       const uint64_t sl2x2 = tc::f2_pack(sl2, sl2), nmx2 = tc::f2_pack(nm, nm);
       uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
+      // keys [0, 64) first: their P columns are stored and signalled (p_half) while the
+      // second half is computed, so the first four P V MMAs overlap it
+      uint32_t pk[2][32];
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
 #pragma unroll
@@ -484,11 +471,16 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
               b = tc::ex2_approx(x1);
             }
             ls2[(e >> 1) & 3] = tc::f2_add(ls2[(e >> 1) & 3], tc::f2_pack(a, b));
-            pk[c * 16 + e / 2] = tc::pack_bf16x2(a, b);
+            pk[hf][c * 16 + e / 2] = tc::pack_bf16x2(a, b);
           }
         }
-        tc::tmem_st32(tS + hf * 32, pk);
+        if (hf == 0) tc::tmem_st32(tS, pk[0]);
       }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars.p_half[q]);
+      tc::tmem_st32(tS + 32, pk[1]);
       float l0, l1, l2, l3;
       tc::f2_unpack(tc::f2_add(ls2[0], ls2[1]), l0, l1);
       tc::f2_unpack(tc::f2_add(ls2[2], ls2[3]), l2, l3);
@@ -496,7 +488,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc::tmem_wait_st();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::red_release_add_shared(&bars.p_count[q], 1u);
+      if (lane == 0) tc::mbar_arrive(&bars.p_full[q]);
     }
     if (active && ok && nt > 0 &&
         !tc::mbar_wait_warp(&bars.o_ready[q], (nt - 1) & 1, abort_flag, kTimeoutNs))
