@@ -83,36 +83,6 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   return true;
 }
 
-// ---- shared-memory counters with acquire/release ordering ----------------------------
-// The MMA-issuing thread waits on these rather than on mbarriers: an mbarrier try_wait
-// issued while that thread has tcgen05.mma in flight stalls until they drain (measured
-// ~180 cycles per wait, during which the tensor pipe idles), a plain acquire load does not.
-__device__ __forceinline__ uint32_t ld_acquire_shared(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_shared(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
-}
-__device__ __forceinline__ void red_release_add_shared(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v)
-               : "memory");
-}
-// Bounded spin until the monotonic counter *p reaches `target`; false on abort or timeout.
-__device__ __forceinline__ bool counter_wait(const uint32_t* p, uint32_t target,
-                                             volatile int* abort, uint64_t timeout_ns) {
-  if (ld_acquire_shared(p) >= target) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (ld_acquire_shared(p) >= target) return true;
-    if ((it & 255u) == 0) {
-      if (*abort) return false;
-      if (global_timer_ns() - t0 > timeout_ns) return false;
-    }
-  }
-}
-
 // ---- TMA ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -312,14 +282,16 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair of lanes on the FMA pipe, to take part of the exponentials off the
-// 16-per-cycle MUFU unit.  Method: Cody-Waite style range reduction, j = round(x) by adding
-// and subtracting the shifter 1.5 * 2^23 (exact for |x| < 2^22), f = x - j in [-1/2, 1/2];
-// 2^f by a degree-3 polynomial whose coefficients were fitted for relative error over
-// [-1/2, 1/2] (iteratively reweighted least squares; max relative error 1.1e-4, a twentieth
-// of the bf16 rounding step of P); 2^j is added into the exponent field, which is what the
-// low mantissa bits of the shifted value shifted left by 23 hold.  x is clamped at -126
-// first: -inf (masked keys) gives 2^-126 rather than 0, and the exponent cannot wrap.
+// 2^x for a pair of lanes on the FMA pipe, an alternative to the MUFU ex2 for part of the
+// exponentials.  Method: Cody-Waite style range reduction, j = round(x) by adding and
+// subtracting the shifter 1.5 * 2^23 (exact for |x| < 2^22), f = x - j in [-1/2, 1/2]; 2^f by
+// a degree-3 polynomial whose coefficients were fitted for relative error over [-1/2, 1/2]
+// (iteratively reweighted least squares; max relative error 1.1e-4, a twentieth of the bf16
+// rounding step of P); 2^j is added into the exponent field, which is what the low mantissa
+// bits of the shifted value shifted left by 23 hold.  x is clamped at -126 first: -inf
+// (masked keys) gives 2^-126 rather than 0, and the exponent cannot wrap.  Measured on B200:
+// ~9 cycles per element per SM sub-partition against 8 for MUFU ex2 (f32x2 FMAs issue at half
+// rate), so offloading to it does not pay there; the tree-attention kernel selects no pairs.
 struct Exp2Poly {
   uint64_t shift, neg_shift, minus1, c0, c1, c2, c3;
   __device__ __forceinline__ Exp2Poly() {

@@ -336,15 +336,11 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 def attn_splits(n_nodes: int, q_heads: int, kv_heads: int, past_length: int,
                 kv_splits: int = 0) -> int:
-    """The key-range split count ddt_tree_attn uses (mirrors pick_splits in the kernel)."""
+    """The key-range split count ddt_tree_attn uses (asked of the library, which picks it)."""
     if kv_splits > 0:
         return kv_splits
-    group = q_heads // kv_heads
-    units = kv_heads * ((n_nodes * group + 127) // 128)
-    tiles = (past_length + n_nodes + 127) // 128
-    s = 1 if units >= 148 else 148 // units
-    cap = max(tiles // 4, 1)
-    return max(1, min(s, cap, 64))
+    return int(_lib.load().ddt_tree_attn_partial_splits(n_nodes, past_length + n_nodes, q_heads,
+                                                        kv_heads))
 
 
 def tree_attention_partial(q, k_shard, v_shard, key_begin: int, key_end: int, anc_bits,

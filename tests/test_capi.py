@@ -70,6 +70,20 @@ def test_workspace_queries():
     assert lib.ddt_tree_attn_workspace_bytes(257, 32, 128, 2) >= 2 * 257 * 32 * 130 * 4
 
 
+@pytest.mark.parametrize("n,past,expect", [
+    # 256 query rows (64 nodes x 4 grouped heads) per CTA: 8 heads x 5 row pairs = 40 CTAs
+    # per split, 148 // 40 = 3 splits of the 66 key tiles
+    (257, 8192, 3),
+    # 8 x 9 = 72 CTAs per split -> 2 splits
+    (513, 131072, 2),
+    # key range too short for more than one split of >= 4 tiles
+    (65, 300, 1)])
+def test_attention_split_count(n, past, expect):
+    from mdflash_b200.kernels import attn_splits
+    assert attn_splits(n, 32, 8, past) == expect
+    assert attn_splits(n, 32, 8, past, kv_splits=5) == 5
+
+
 @pytest.mark.parametrize("depths,vocab,budget,expect", [
     (15, 151936, 256, 256), (3, 3, 40, 39), (0, 10, 5, 0), (15, 10, 0, 0), (1, 1000, 8, 8),
     (2, 4, 100, 20)])
