@@ -53,11 +53,12 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["verify", "attn", "tree", "requests", "splitkv"],
+    ap.add_argument("--workload", choices=["verify", "attn", "tree", "argmax", "compact",
+                                           "requests", "splitkv"],
                     default="verify",
-                    help="verify: the single-request verify step (default); attn / tree: one op "
-                         "alone; requests: 64 requests sharded over the GPUs; splitkv: "
-                         "attention over a prefix sharded along the sequence")
+                    help="verify: the single-request verify step (default); attn / tree / argmax "
+                         "/ compact: one op alone; requests: 64 requests sharded over the GPUs; "
+                         "splitkv: attention over a prefix sharded along the sequence")
     ap.add_argument("--prefix", type=int, default=None,
                     help="prefix length (default 8192; 131072 for --workload splitkv)")
     ap.add_argument("--budget", type=int, default=None,
@@ -560,6 +561,128 @@ def run_tree(args):
     }), flush=True)
 
 
+def _timed_launches(fn, steps: int, warmup: int, dev) -> float:
+    """Mean device time (ms) of `fn` over `steps` launches, each bracketed by CUDA events,
+    with a 256 MB buffer written before each launch (L2 flushed)."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    torch.cuda.nvtx.range_push("timed")
+    for _ in range(steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        times.append((a, b))
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in times]))
+
+
+def run_argmax(args):
+    """Greedy posterior (model/utils.py:28-30 at T=0) alone: argmax over [N, 151936] bf16
+    verify logits, N = budget + 1.  GB/s of the algorithmic bytes (one read of the logits)."""
+    from mdflash_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = args.budget + 1
+    g = torch.Generator(device=dev).manual_seed(0)
+    logits = torch.randn((n, V), generator=g, device=dev).mul_(3).to(torch.bfloat16)
+    out = torch.empty(n, dtype=torch.int64, device=dev)
+    ms = _timed_launches(lambda: K.argmax(logits, out=out), args.steps, args.warmup, dev)
+    nbytes = logits.numel() * logits.element_size()
+    peaks, kind = measured_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "argmax GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"argmax over [{n}, {V}] bf16 verify logits (N(0,1)*3)",
+                   "l2": "256 MB buffer written between launches (L2 flushed)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
+                     "bytes_per_launch": nbytes},
+    }), flush=True)
+
+
+def run_compact(args):
+    """Accept walk + KV compaction alone on the Qwen3-8B cache shape (36 layers x K, V
+    [1, 8, P + N, 128] bf16) with a forced accepted path: the posterior follows the tree
+    from the root to its deepest node (the drafter logits make the tree reach all 15
+    depths), so a 16-row path is accepted and each layer's K and V move one row per
+    accepted node not already in place.  GB/s of the algorithmic
+    bytes (read + write of every moved row) over the launch time."""
+    from mdflash_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers, hkv, d = 36, 8, 128
+    _, logits = request_inputs(0, 16)
+    # one token per depth lifted to about the log-sum-exp of the rest (log-prob ~ -0.7), so
+    # the best-first tree reaches every drafted depth while its siblings interleave with the
+    # path in node order (the moved rows are then the path's nodes past their slots)
+    rng = np.random.default_rng(7)
+    lg = logits.clone()
+    for dep in range(lg.shape[0]):
+        lg[dep, int(rng.integers(V))] = 16.4
+    x = lg.to(torch.bfloat16).to(dev)
+    root = torch.zeros(1, dtype=torch.int64, device=dev)
+    tree = K.topk_tree(x, args.budget, root, args.prefix)
+    n = int(tree.node_count.item()) + 1
+    parents = tree.parents[:n].cpu().numpy()
+    tokens = tree.verify_ids[:n].cpu().numpy()
+    depth = np.zeros(n, np.int64)
+    for i in range(1, n):
+        depth[i] = depth[parents[i]] + 1
+    target = int(np.flatnonzero(depth == depth.max())[-1])  # deepest, last in node order
+    path = [target]
+    while path[-1] != 0:
+        path.append(int(parents[path[-1]]))
+    path = path[::-1]
+    post = np.zeros(n, np.int64)
+    for a, b in zip(path[:-1], path[1:]):
+        post[a] = tokens[b]
+    child_tokens = {int(tokens[c]) for c in range(1, n) if parents[c] == target}
+    t = 0
+    while t in child_tokens:
+        t += 1
+    post[target] = t
+    posterior = torch.from_numpy(post).to(dev)
+    seq = args.prefix + n
+    cache = [torch.randn((1, hkv, seq, d), device=dev).to(torch.bfloat16)
+             for _ in range(2 * layers)]
+    table = K.KvTable(cache)
+    accepted = torch.zeros(n, dtype=torch.int64, device=dev)
+    n_acc = torch.zeros(1, dtype=torch.int32, device=dev)
+    nxt = torch.zeros(1, dtype=torch.int64, device=dev)
+
+    def step():
+        K.accept_compact(posterior, tree, table, args.prefix, accepted, n_acc, nxt, n_nodes=n)
+
+    ms = _timed_launches(step, args.steps, args.warmup, dev)
+    acc = accepted[:int(n_acc.item())].cpu().tolist()
+    assert acc == path, (acc, path)
+    moved = sum(1 for i, a in enumerate(acc) if a != i)
+    nbytes = 2 * layers * hkv * moved * d * 2 * 2
+    peaks, kind = measured_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "compaction GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"accept walk + KV compaction, Qwen3-8B cache (36 layers x K/V "
+                               f"[1, 8, {seq}, 128] bf16), forced path of {len(acc)} accepted "
+                               f"rows, {moved} moved per tensor",
+                   "l2": "256 MB buffer written between launches (L2 flushed)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
+                     "bytes_per_launch": nbytes},
+        "accepted": len(acc),
+    }), flush=True)
+
+
 # ------------------------------------------------------------- multi-GPU workloads
 def _dist_setup():
     import torch.distributed as dist
@@ -755,6 +878,10 @@ def main():
         run_attn(args)
     elif args.workload == "tree":
         run_tree(args)
+    elif args.workload == "argmax":
+        run_argmax(args)
+    elif args.workload == "compact":
+        run_compact(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

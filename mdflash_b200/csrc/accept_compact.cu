@@ -1,9 +1,10 @@
 // Greedy posterior (row argmax), accept walk and KV-cache compaction.
 //
 // ddt_argmax replaces sample() at temperature 0 (model/utils.py:28-30), i.e.
-// torch.argmax over the verify logits (ddtree.py:478): one CTA per row streams the row
-// with 16-byte loads and reduces (order key, ~index) composites, so ties resolve to
-// the lowest index and NaN (canonicalised to the largest key) wins like in torch.
+// torch.argmax over the verify logits (ddtree.py:478): a cluster of 4 CTAs per row
+// streams the row with 16-byte loads and reduces (order key, ~index) composites, so ties
+// resolve to the lowest index and NaN (canonicalised to the largest key) wins like in
+// torch.
 //
 // ddt_accept_compact fuses follow_verified_tree (ddtree.py:270-281) with
 // compact_dynamic_cache (ddtree.py:284-335): every CTA replays the short walk from
@@ -12,77 +13,155 @@
 // before writing; rows may overlap (row past+j is the source of an earlier row when
 // accepted[j'] == j), so a warp loads every row of its slice into registers before it
 // stores any.  Rows already in place (accepted[j] == j) are skipped.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace ddt {
 namespace accept {
 
-constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxThreads = 256;
+constexpr int kArgmaxCluster = 4;  // CTAs per row (rows * 4 CTAs fit in one wave at N = 257)
 constexpr int kCompactWarps = 8;
 constexpr int kMaxRows = DDT_MAX_DEPTH + 1;  // accepted rows: root + one per depth
 constexpr int kMaxVecPerLane = 24;           // rows * (row bytes / 16) / 32
+
+// Order keys of the two bf16 in a 32-bit word, per 16-bit half: 0x8000 + |b| for positive
+// values and 0x8000 - |b| for negative ones, so -0 and +0 share 0x8000 and the order is that
+// of argmax_comp on the fp32 value for all numbers; NaNs land above +inf's key (0xff80) when
+// positive and below -inf's (0x0080) when negative, which the caller checks for.
+// prmt replicates each half's sign bit over the half (0xffff in negative halves); the add
+// (x ^ neg) + 0x8000 - neg stays within each half, so one 32-bit add serves both.
+__device__ __forceinline__ uint32_t bf16x2_order_keys(uint32_t w) {
+  uint32_t neg;
+  asm("prmt.b32 %0, %1, 0, 0xbb99;" : "=r"(neg) : "r"(w));
+  return ((w & 0x7fff7fffu) ^ neg) + 0x80008000u - neg;
+}
 
 __device__ __forceinline__ unsigned long long argmax_comp(float x, uint32_t idx) {
   const uint32_t key = isnan(x) ? 0xffffffffu : f32_key(x);
   return (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(~idx);
 }
 
+// One thread-block cluster of kArgmaxCluster CTAs per row: CTA c streams the c-th
+// contiguous chunk of the row (four 16-byte loads in flight per thread), reduces it to one
+// composite, and cluster rank 0 combines the cluster's composites through distributed
+// shared memory.  Rows are spread over rows * 8 CTAs instead of one CTA per row, which
+// left SMs idle and each thread with a single load in flight.
 template <bool kBF16>
-__global__ void __launch_bounds__(kArgmaxThreads)
+__global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmaxThreads)
 argmax_kernel(const void* __restrict__ logits, int64_t cols, int64_t row_stride,
               int64_t* __restrict__ out, int vec_ok) {
-  const int64_t r = blockIdx.x;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int part = static_cast<int>(cluster.block_rank());
+  const int64_t r = blockIdx.x / kArgmaxCluster;
   const int tid = threadIdx.x;
+  constexpr int kPer = kBF16 ? 8 : 4;  // elements per 16-byte vector
+  constexpr int kUnroll = 8;  // 16-byte loads in flight per thread
   unsigned long long best = 0ull;
-  if constexpr (kBF16) {
-    const uint16_t* row = static_cast<const uint16_t*>(logits) + r * row_stride;
-    if (vec_ok) {
-      const int64_t nvec = cols / 8;
-      const uint4* rv = reinterpret_cast<const uint4*>(row);
-      for (int64_t v = tid; v < nvec; v += kArgmaxThreads) {
-        const uint4 q = __ldcs(rv + v);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  auto take = [&](float x, int64_t i) {
+    const unsigned long long c = argmax_comp(x, static_cast<uint32_t>(i));
+    best = c > best ? c : best;
+  };
+  auto elem = [&](int64_t i) -> float {
+    if constexpr (kBF16)
+      return bf16_bits_to_f32(static_cast<const uint16_t*>(logits)[r * row_stride + i]);
+    else
+      return static_cast<const float*>(logits)[r * row_stride + i];
+  };
+  // element range [e0, e1) of this CTA; with 16-byte loads the split is in whole vectors
+  // and the last CTA also takes the ragged tail
+  const int64_t unit = vec_ok ? kPer : 1;
+  const int64_t units = cols / unit;
+  const int64_t per = (units + kArgmaxCluster - 1) / kArgmaxCluster;
+  const int64_t u0 = part * per < units ? part * per : units;
+  const int64_t u1 = (part + 1) * per < units ? (part + 1) * per : units;
+  if (vec_ok) {
+    const uint4* rv = reinterpret_cast<const uint4*>(static_cast<const char*>(logits) +
+                                                     r * row_stride * (kBF16 ? 2 : 4));
+    // bf16: order keys on packed 16-bit halves (bf16x2_order_keys: three instructions per
+    // pair) and packed 16-bit max / min trees per 16-byte vector; a thread keeps
+    // (best vector key << 16 | 0xffff - vector ordinal) and only re-reads its winning vector
+    // to find the first element holding that key.  NaNs (positive: keys above +inf's, negative:
+    // keys below -inf's) send the thread to the exact per-element path.  About three
+    // instructions per element; a 64-bit composite per element made the kernel issue-bound.
+    if (kBF16 && per <= static_cast<int64_t>(kArgmaxThreads) * 0xfff0) {
+      uint32_t bestc = 0u, kmin = 0xffffffffu, m = 0u;
+      for (int64_t v = u0 + tid; v < u1; v += kUnroll * kArgmaxThreads) {
+        uint4 q[kUnroll];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const uint16_t b = static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16));
-          const unsigned long long c = argmax_comp(bf16_bits_to_f32(b), static_cast<uint32_t>(v * 8 + e));
-          best = c > best ? c : best;
+        for (int k = 0; k < kUnroll; ++k) {
+          const int64_t vi = v + k * kArgmaxThreads;
+          q[k] = vi < u1 ? __ldcs(rv + vi) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+          if (v + k * kArgmaxThreads >= u1) break;
+          const uint32_t k0 = bf16x2_order_keys(q[k].x), k1 = bf16x2_order_keys(q[k].y);
+          const uint32_t k2 = bf16x2_order_keys(q[k].z), k3 = bf16x2_order_keys(q[k].w);
+          const uint32_t kx = __vmaxu2(__vmaxu2(k0, k1), __vmaxu2(k2, k3));
+          kmin = __vminu2(kmin, __vminu2(__vminu2(k0, k1), __vminu2(k2, k3)));
+          const uint32_t vk = max(kx >> 16, kx & 0xffffu);
+          bestc = max(bestc, (vk << 16) | (0xffffu - m));
+          ++m;
         }
       }
-      for (int64_t i = nvec * 8 + tid; i < cols; i += kArgmaxThreads) {
-        const unsigned long long c = argmax_comp(bf16_bits_to_f32(row[i]), static_cast<uint32_t>(i));
-        best = c > best ? c : best;
+      const bool has_nan = (bestc >> 16) > 0xff80u || (kmin & 0xffffu) < 0x0080u ||
+                           (kmin >> 16) < 0x0080u;
+      if (has_nan) {
+        for (int64_t vi = u0 + tid; vi < u1; vi += kArgmaxThreads) {
+          const uint4 q = rv[vi];
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            take(bf16_bits_to_f32(static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16))), vi * 8 + e);
+        }
+      } else if (bestc) {
+        const uint32_t kbest = bestc >> 16;
+        const int64_t vi = u0 + tid + static_cast<int64_t>(0xffffu - (bestc & 0xffffu)) * kArgmaxThreads;
+        const uint4 q = rv[vi];
+        const uint32_t kw[4] = {bf16x2_order_keys(q.x), bf16x2_order_keys(q.y),
+                                bf16x2_order_keys(q.z), bf16x2_order_keys(q.w)};
+        int e = 7;
+#pragma unroll
+        for (int x = 7; x >= 0; --x)
+          if (((kw[x >> 1] >> ((x & 1) * 16)) & 0xffffu) == kbest) e = x;
+        // the 32-bit key of the same value as argmax_comp builds it from the fp32 value
+        const uint32_t key32 = kbest >= 0x8000u ? kbest << 16 : ((kbest - 1u) << 16) | 0xffffu;
+        best = (static_cast<unsigned long long>(key32) << 32) |
+               static_cast<uint32_t>(~static_cast<uint32_t>(vi * 8 + e));
       }
     } else {
-      for (int64_t i = tid; i < cols; i += kArgmaxThreads) {
-        const unsigned long long c = argmax_comp(bf16_bits_to_f32(row[i]), static_cast<uint32_t>(i));
-        best = c > best ? c : best;
+      // fp32 (and very long bf16 rows): a 64-bit composite per element
+      for (int64_t v = u0 + tid; v < u1; v += kUnroll * kArgmaxThreads) {
+        uint4 q[kUnroll];
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+          const int64_t vi = v + k * kArgmaxThreads;
+          q[k] = vi < u1 ? __ldcs(rv + vi) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+          const int64_t vi = v + k * kArgmaxThreads;
+          if (vi >= u1) break;
+          const uint32_t w[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
+          if constexpr (kBF16) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              take(bf16_bits_to_f32(static_cast<uint16_t>(w[e >> 1] >> ((e & 1) * 16))),
+                   vi * 8 + e);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) take(__uint_as_float(w[e]), vi * 4 + e);
+          }
+        }
       }
     }
+    if (part == kArgmaxCluster - 1)
+      for (int64_t i = units * kPer + tid; i < cols; i += kArgmaxThreads) take(elem(i), i);
   } else {
-    const float* row = static_cast<const float*>(logits) + r * row_stride;
-    if (vec_ok) {
-      const int64_t nvec = cols / 4;
-      const float4* rv = reinterpret_cast<const float4*>(row);
-      for (int64_t v = tid; v < nvec; v += kArgmaxThreads) {
-        const float4 q = __ldcs(rv + v);
-        const float w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const unsigned long long c = argmax_comp(w[e], static_cast<uint32_t>(v * 4 + e));
-          best = c > best ? c : best;
-        }
-      }
-      for (int64_t i = nvec * 4 + tid; i < cols; i += kArgmaxThreads) {
-        const unsigned long long c = argmax_comp(row[i], static_cast<uint32_t>(i));
-        best = c > best ? c : best;
-      }
-    } else {
-      for (int64_t i = tid; i < cols; i += kArgmaxThreads) {
-        const unsigned long long c = argmax_comp(row[i], static_cast<uint32_t>(i));
-        best = c > best ? c : best;
-      }
-    }
+    for (int64_t i = u0 + tid; i < u1; i += kArgmaxThreads) take(elem(i), i);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -90,6 +169,7 @@ argmax_kernel(const void* __restrict__ logits, int64_t cols, int64_t row_stride,
     best = y > best ? y : best;
   }
   __shared__ unsigned long long wbest[kArgmaxThreads / 32];
+  __shared__ unsigned long long cta_best;
   if ((tid & 31) == 0) wbest[tid >> 5] = best;
   __syncthreads();
   if (tid < 32) {
@@ -99,8 +179,19 @@ argmax_kernel(const void* __restrict__ logits, int64_t cols, int64_t row_stride,
       const unsigned long long y = __shfl_xor_sync(DDT_FULL_MASK, b, o);
       b = y > b ? y : b;
     }
+    if (tid == 0) cta_best = b;
+  }
+  cluster.sync();
+  if (part == 0 && tid < 32) {
+    unsigned long long b = tid < kArgmaxCluster ? *cluster.map_shared_rank(&cta_best, tid) : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(DDT_FULL_MASK, b, o);
+      b = y > b ? y : b;
+    }
     if (tid == 0) out[r] = static_cast<int64_t>(~static_cast<uint32_t>(b));
   }
+  cluster.sync();  // every CTA's shared memory stays live until rank 0 has read it
 }
 
 struct KvDesc {
@@ -251,16 +342,19 @@ extern "C" int ddt_argmax(const void* logits, int dtype, int64_t rows, int64_t c
   if (dtype != DDT_F32 && dtype != DDT_BF16) return DDT_ERR_DTYPE;
   if (rows < 0 || cols <= 0 || row_stride < cols || (rows > 0 && (!logits || !out)))
     return DDT_ERR_INVALID;
-  if (cols >= (int64_t(1) << 32) - 1 || rows > 0x7fffffff) return DDT_ERR_CAPACITY;
+  if (cols >= (int64_t(1) << 32) - 1 || rows > 0x7fffffff / accept::kArgmaxCluster)
+    return DDT_ERR_CAPACITY;
   if (rows == 0) return DDT_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t esz = dtype == DDT_BF16 ? 2 : 4;
   const int vec_ok = aligned(logits, 16) && (row_stride * esz) % 16 == 0;
   if (dtype == DDT_BF16)
-    accept::argmax_kernel<true><<<static_cast<unsigned>(rows), accept::kArgmaxThreads, 0, st>>>(
+    accept::argmax_kernel<true><<<static_cast<unsigned>(rows * accept::kArgmaxCluster),
+                                  accept::kArgmaxThreads, 0, st>>>(
         logits, cols, row_stride, out, vec_ok);
   else
-    accept::argmax_kernel<false><<<static_cast<unsigned>(rows), accept::kArgmaxThreads, 0, st>>>(
+    accept::argmax_kernel<false><<<static_cast<unsigned>(rows * accept::kArgmaxCluster),
+                                   accept::kArgmaxThreads, 0, st>>>(
         logits, cols, row_stride, out, vec_ok);
   return launch_status();
 }

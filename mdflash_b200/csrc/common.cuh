@@ -22,9 +22,11 @@ inline int launch_status() {
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // ---- order-preserving keys ------------------------------------------------
-// key(x) grows with x; positive NaN maps above +inf.
+// key(x) grows with x; positive NaN maps above +inf.  -0 and +0 get the same key (they
+// compare equal, so ties between them resolve by index as torch's do).
 __device__ __forceinline__ uint32_t f32_key(float x) {
   uint32_t u = __float_as_uint(x);
+  if ((u << 1) == 0u) u = 0u;
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 __device__ __forceinline__ float key_f32(uint32_t k) {
@@ -32,6 +34,7 @@ __device__ __forceinline__ float key_f32(uint32_t k) {
   return __uint_as_float(u);
 }
 __device__ __forceinline__ uint32_t bf16_key(uint16_t b) {
+  if ((b & 0x7fffu) == 0u) b = 0u;
   return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
 }
 __device__ __forceinline__ float key_bf16(uint32_t k) {

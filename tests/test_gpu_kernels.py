@@ -102,6 +102,34 @@ def test_argmax_nan_and_strided(cuda_device):
     assert got.cpu().tolist() == oracle.argmax(x).tolist()
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_argmax_signed_zero_ties_and_chunk_edges(cuda_device, dtype):
+    """-0 and +0 are equal (lowest index wins); maxima placed on the edges of the per-CTA
+    chunks, in the ragged tail, at both ends of the row; negative-only and NaN rows."""
+    cols = 151936 + 5
+    vec = 8 if dtype == torch.bfloat16 else 4       # elements per 16-byte load
+    # edges of the per-CTA chunks for 4- and 8-way row splits, the ragged tail, both ends
+    edges = sorted({c for parts in (4, 8) for j in (1, 2, 3)
+                    for per in [-(-(cols // vec) // parts) * vec] for c in (j * per - 1, j * per)}
+                   | {cols - 1, cols - 3, 0})
+    x = torch.full((4 + len(edges), cols), -3.0)
+    x[0, 100] = -0.0
+    x[0, 90000] = 0.0                     # +0 after -0: the -0 index wins
+    x[1, 5] = 0.0
+    x[1, 7] = -0.0
+    x[2] = -torch.arange(cols, dtype=torch.float32) - 1.0   # all negative, max at index 0
+    x[3, 123] = float("nan")
+    x[3, 77777] = float("inf")
+    for r, c in enumerate(edges, start=4):
+        x[r, c] = 2.0
+    got = K.argmax(x.to(dtype).to(cuda_device))
+    torch.cuda.synchronize()
+    ref = oracle.argmax(x.to(dtype))
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+    assert ref[0] == 100 and ref[1] == 5 and ref[2] == 0 and ref[3] == 123
+    assert ref[4:].tolist() == edges
+
+
 # ------------------------------------------------------------- accept walk + compaction
 def _kv_cache(layers, heads, seq, dim, dtype, device, seed):
     g = torch.Generator().manual_seed(seed)
