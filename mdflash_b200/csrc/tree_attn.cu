@@ -77,6 +77,7 @@ __device__ __forceinline__ uint32_t col_o(int q) { return q ? 384u : 128u; }
 
 struct Params {
   int n_nodes, past_len, group, q_heads, n_pairs, n_splits;
+  int balanced;        // 1: work items from the Sched table, partials in per-part slots
   int key_base;        // global key index of local key 0
   int key_lo, key_hi;  // global key range covered by this launch
   const uint32_t* anc;
@@ -91,11 +92,51 @@ struct Params {
   int* status;
 };
 
+// Balanced schedule ("stream-K" over the key tiles): the flattened (work unit, key tile)
+// space is cut into equal contiguous ranges, one per CTA, so every SM runs the same number of
+// tiles whatever the number of work units.  A CTA's range may cover the end of one unit and
+// the start of the next: each such piece is one item, whose fp32 partial goes to its own
+// slot; the parts of a unit have consecutive slots, starting at unit_slot[unit].  Built on
+// the host and passed by value (kernel parameter space).
+constexpr int kMaxCtas = 148;
+constexpr int kMaxItems = 320;
+constexpr int kMaxUnits = 256;
+constexpr int kMaxPartsPerUnit = 32;  // merge_slots_kernel keeps one weight per part
+struct SchedItem {
+  uint16_t unit, t0, nt, slot;  // work unit, first key tile of the unit, tiles, partial slot
+};
+struct Sched {
+  uint16_t cta_first[kMaxCtas + 1];  // items of CTA c: [cta_first[c], cta_first[c + 1])
+  SchedItem items[kMaxItems];
+};
+struct SlotTable {
+  uint16_t unit_slot[kMaxUnits + 1];  // parts of unit u: slots [unit_slot[u], unit_slot[u + 1])
+};
+
+// Rows, key range and tile count of work unit u (one KV head, 256 query rows); shared by
+// the host schedule and the kernel.
+struct UnitGeo {
+  int h, row0, g_end, ntot;
+};
+__host__ __device__ inline UnitGeo unit_geo(const Params& p, int u) {
+  UnitGeo g;
+  g.h = u / p.n_pairs;
+  g.row0 = (u % p.n_pairs) * kRowsPerCta;
+  int node_hi = (g.row0 + kRowsPerCta - 1) / p.group;
+  if (node_hi > p.n_nodes - 1) node_hi = p.n_nodes - 1;
+  // keys beyond past + node_hi are invisible to every row of the unit (both mask modes)
+  g.g_end = p.past_len + node_hi + 1;
+  if (g.g_end > p.key_hi) g.g_end = p.key_hi;
+  g.ntot = g.g_end > p.key_lo ? (g.g_end - p.key_lo + kBlockN - 1) / kBlockN : 0;
+  return g;
+}
+
 struct Bars {
   // K and V stages are released separately: K_j once both S_q(j) MMAs completed, V_j once
-  // both P V MMAs of tile j completed, so the next K load starts a full tile earlier
-  uint64_t q_full, k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages],
-      s_full[2], p_half[2], p_full[2], o_ready[2], mma_done[2];
+  // both P V MMAs of tile j completed, so the next K load starts a full tile earlier.
+  // q_empty: both S MMAs of an item's last tile are done, Q may be replaced.
+  uint64_t q_full, q_empty, k_full[kStages], v_full[kStages], k_empty[kStages],
+      v_empty[kStages], s_full[2], p_half[2], p_full[2], o_ready[2], mma_done[2];
   // MMA blocks issued per query tile (S_q(0), then P V(j) + S(j + 1) per tile): the two
   // issuers take turns, tile 0 then tile 1, so the two softmax warpgroups stay half a
   // period apart instead of competing for the same SM sub-partitions
@@ -142,44 +183,52 @@ __device__ __forceinline__ uint32_t visible32(const Params& p, int node, int g0,
 
 __global__ void __launch_bounds__(kThreads, 1)
 tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                 const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params p,
+                 const __grid_constant__ Sched sched) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ Bars bars;
   const uint32_t raw = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  // ---- work unit -------------------------------------------------------------------
-  const int unit = blockIdx.x;
-  const int split = unit % p.n_splits;
-  const int tq = unit / p.n_splits;
-  const int pair = tq % p.n_pairs;
-  const int h = tq / p.n_pairs;
   const int rows = p.n_nodes * p.group;
-  const int row0 = pair * kRowsPerCta;
-  const bool q1_active = row0 + kBlockM < rows;
-  int node_hi = (row0 + kRowsPerCta - 1) / p.group;
-  if (node_hi > p.n_nodes - 1) node_hi = p.n_nodes - 1;
-  // keys beyond past + node_hi are invisible to every row of the CTA (both modes)
-  int g_end = p.past_len + node_hi + 1;
-  if (g_end > p.key_hi) g_end = p.key_hi;
-  const int g_begin = p.key_lo;
-  const int ntot = g_end > g_begin ? (g_end - g_begin + kBlockN - 1) / kBlockN : 0;
-  const int tps = (ntot + p.n_splits - 1) / p.n_splits;
-  int t_begin = split * tps;
-  int t_end = t_begin + tps;
-  if (t_end > ntot) t_end = ntot;
-  if (t_begin > t_end) t_begin = t_end;
-  const int nt = t_end - t_begin;
-  const int lk0 = g_begin - p.key_base + t_begin * kBlockN;  // local key of the first tile
+
+  // ---- work items of this CTA ----------------------------------------------------------
+  // uniform splits: one item, (unit, split) from blockIdx.x; balanced: the Sched table.
+  // Barrier phases run on the CTA-wide tile count, across items.
+  const int item_lo = p.balanced ? sched.cta_first[blockIdx.x] : 0;
+  const int n_items = p.balanced ? sched.cta_first[blockIdx.x + 1] - item_lo : 1;
+  auto item = [&](int i, int& u, int& t0, int& nt, int& slot) {
+    if (p.balanced) {
+      const SchedItem it = sched.items[item_lo + i];
+      u = it.unit;
+      t0 = it.t0;
+      nt = it.nt;
+      slot = it.slot;
+    } else {
+      const int split = blockIdx.x % p.n_splits;
+      u = blockIdx.x / p.n_splits;
+      slot = split;
+      const int ntot = unit_geo(p, u).ntot;
+      const int tps = (ntot + p.n_splits - 1) / p.n_splits;
+      t0 = split * tps < ntot ? split * tps : ntot;
+      nt = (t0 + tps < ntot ? t0 + tps : ntot) - t0;
+    }
+  };
+  int total = 0;
+  for (int i = 0; i < n_items; ++i) {
+    int u, t0, nt, sl;
+    item(i, u, t0, nt, sl);
+    total += nt;
+  }
 
   if (tid == 0) {
     tc::mbar_init(&bars.q_full, 1);
+    tc::mbar_init(&bars.q_empty, 2);  // one commit per MMA issuer
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&bars.k_full[s], 1);
       tc::mbar_init(&bars.v_full[s], 1);
-      tc::mbar_init(&bars.k_empty[s], q1_active ? 2 : 1);
-      tc::mbar_init(&bars.v_empty[s], q1_active ? 2 : 1);
+      tc::mbar_init(&bars.k_empty[s], 2);
+      tc::mbar_init(&bars.v_empty[s], 2);
     }
     for (int q = 0; q < 2; ++q) {
       tc::mbar_init(&bars.s_full[q], 1);
@@ -187,9 +236,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc::mbar_init(&bars.p_full[q], 4);
       bars.issued[q] = 0;
       tc::mbar_init(&bars.o_ready[q], 1);
+      tc::mbar_init(&bars.mma_done[q], 1);
     }
-    tc::mbar_init(&bars.mma_done[0], 1);
-    tc::mbar_init(&bars.mma_done[1], 1);
     bars.abort = 0;
     tc::fence_mbar_init();
   }
@@ -211,44 +259,63 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     tc::reg_dealloc<kRegsControl>();
     if (warp == 0) {
       // ---------------------------- TMA producer -------------------------------------
-      if (lane == 0 && nt > 0) {
+      if (lane == 0 && total > 0) {
         tc::tma_prefetch_desc(&tm_q);
         tc::tma_prefetch_desc(&tm_k);
         tc::tma_prefetch_desc(&tm_v);
-        tc::mbar_expect_tx(&bars.q_full, (q1_active ? 2 : 1) * kTileBytes);
-        for (int q = 0; q < (q1_active ? 2 : 1); ++q) {
-          const int node0 = (row0 + q * kBlockM) / p.group;
-          tc::tma_load_3d(sQ + q * kTileBytes, &tm_q, &bars.q_full, 0, h * p.group, node0);
-          tc::tma_load_3d(sQ + q * kTileBytes + kHalfBytes, &tm_q, &bars.q_full, 64, h * p.group,
-                          node0);
-        }
-        int issued_k = 0, issued_v = 0;
-        for (int j = 0; j < nt; ++j) {
-          const int st = j % kStages;
-          const uint32_t ph = ((j / kStages) - 1) & 1;  // release phase of tile j - kStages
-          const int key = lk0 + j * kBlockN;
-          if (j >= kStages && !tc::mbar_wait(&bars.k_empty[st], ph, abort_flag, kTimeoutNs)) {
-            raise_abort(bars, p.status);
-            break;
+        // both query tiles of a unit; the second one of a unit's last row pair may lie
+        // past the last node, where the load reads zeros and its rows are not stored
+        int q_loads = 0;
+        auto load_q = [&](const UnitGeo& g) {
+          tc::mbar_expect_tx(&bars.q_full, 2 * kTileBytes);
+          for (int q = 0; q < 2; ++q) {
+            const int node0 = (g.row0 + q * kBlockM) / p.group;
+            tc::tma_load_3d(sQ + q * kTileBytes, &tm_q, &bars.q_full, 0, g.h * p.group, node0);
+            tc::tma_load_3d(sQ + q * kTileBytes + kHalfBytes, &tm_q, &bars.q_full, 64,
+                            g.h * p.group, node0);
           }
-          unsigned char* kd = sK + st * kTileBytes;
-          tc::mbar_expect_tx(&bars.k_full[st], kTileBytes);
-          tc::tma_load_3d(kd, &tm_k, &bars.k_full[st], 0, key, h);
-          tc::tma_load_3d(kd + kHalfBytes, &tm_k, &bars.k_full[st], 64, key, h);
-          issued_k = j + 1;
-          if (j >= kStages && !tc::mbar_wait(&bars.v_empty[st], ph, abort_flag, kTimeoutNs)) {
-            raise_abort(bars, p.status);
-            break;
+          ++q_loads;
+        };
+        int issued_k = 0, issued_v = 0, J = 0;
+        bool ok = true;
+        for (int i = 0; ok && i < n_items; ++i) {
+          int u, t0, nt, sl;
+          item(i, u, t0, nt, sl);
+          const UnitGeo g = unit_geo(p, u);
+          const int lk0 = p.key_lo - p.key_base + t0 * kBlockN;  // local key of the first tile
+          if (i == 0) load_q(g);
+          for (int j = 0; j < nt; ++j) {
+            const int jg = J + j;
+            const int st = jg % kStages;
+            const uint32_t ph = ((jg / kStages) - 1) & 1;  // release phase of tile jg - kStages
+            const int key = lk0 + j * kBlockN;
+            if (jg >= kStages && !(ok = tc::mbar_wait(&bars.k_empty[st], ph, abort_flag, kTimeoutNs)))
+              break;
+            unsigned char* kd = sK + st * kTileBytes;
+            tc::mbar_expect_tx(&bars.k_full[st], kTileBytes);
+            tc::tma_load_3d(kd, &tm_k, &bars.k_full[st], 0, key, g.h);
+            tc::tma_load_3d(kd + kHalfBytes, &tm_k, &bars.k_full[st], 64, key, g.h);
+            issued_k = jg + 1;
+            if (jg >= kStages && !(ok = tc::mbar_wait(&bars.v_empty[st], ph, abort_flag, kTimeoutNs)))
+              break;
+            unsigned char* vd = sV + st * kTileBytes;
+            tc::mbar_expect_tx(&bars.v_full[st], kTileBytes);
+            tc::tma_load_3d(vd, &tm_v, &bars.v_full[st], 0, key, g.h);
+            tc::tma_load_3d(vd + kHalfBytes, &tm_v, &bars.v_full[st], 64, key, g.h);
+            issued_v = jg + 1;
+            if (j == 0 && i > 0) {
+              // the item's Q replaces the previous item's once both its S MMAs are done;
+              // the first K / V tile of the item is already on its way
+              if (!(ok = tc::mbar_wait(&bars.q_empty, (i - 1) & 1, abort_flag, kTimeoutNs))) break;
+              load_q(g);
+            }
           }
-          unsigned char* vd = sV + st * kTileBytes;
-          tc::mbar_expect_tx(&bars.v_full[st], kTileBytes);
-          tc::tma_load_3d(vd, &tm_v, &bars.v_full[st], 0, key, h);
-          tc::tma_load_3d(vd + kHalfBytes, &tm_v, &bars.v_full[st], 64, key, h);
-          issued_v = j + 1;
+          J += nt;
         }
+        if (!ok) raise_abort(bars, p.status);
         if (*abort_flag) {
           // let the loads already in flight land before the CTA releases its smem
-          tc::mbar_wait_drain(&bars.q_full, 0, kTimeoutNs);
+          if (q_loads > 0) tc::mbar_wait_drain(&bars.q_full, (q_loads - 1) & 1, kTimeoutNs);
           for (int j = issued_k > kStages ? issued_k - kStages : 0; j < issued_k; ++j)
             tc::mbar_wait_drain(&bars.k_full[j % kStages], (j / kStages) & 1, kTimeoutNs);
           for (int j = issued_v > kStages ? issued_v - kStages : 0; j < issued_v; ++j)
@@ -263,16 +330,16 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // issuer per tile every wait falls where that tile's previous MMAs are complete anyway
       // (P_q(j) ready implies S_q(j) done), while the other tile's MMAs keep the pipe busy.
       const int q = warp == 1 ? 0 : 1;
-      if (lane == 0 && nt > 0 && (q == 0 || q1_active)) {
+      if (lane == 0 && total > 0) {
         // descriptor low words of the Q, K and V tiles; every MMA adds a constant to them
         constexpr uint32_t kDescHi = tc::desc_sw128_hi(1024);
         const uint32_t a_q = tc::desc_sw128_lo(tc::smem_u32(sQ), 16) + q * (kTileBytes >> 4);
         const uint32_t k_lo = tc::desc_sw128_lo(tc::smem_u32(sK), 16);
         const uint32_t v_lo = tc::desc_sw128_lo(tc::smem_u32(sV), kHalfBytes);
         const uint32_t d_s = tmem + col_s(q), d_o = tmem + col_o(q);
-        // S_q = Q_q K_j^T into the S region of query tile q
-        auto issue_s = [&](int j) {
-          const uint32_t b = k_lo + (j % kStages) * (kTileBytes >> 4);
+        // S_q = Q_q K^T of CTA tile jg into the S region of query tile q
+        auto issue_s = [&](int jg) {
+          const uint32_t b = k_lo + (jg % kStages) * (kTileBytes >> 4);
           tc::mma_bf16_ss_w<0>(d_s, a_q, b, kDescHi, kIdescS);
 #pragma unroll
           for (int kk = 1; kk < kHeadDim / 16; ++kk) {
@@ -281,10 +348,11 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
           tc::mma_commit(&bars.s_full[q]);
         };
-        // O_q += P_q V_j, P_q in TMEM (first 64 columns of the S region, 8 per K step), in
-        // two halves of 64 keys: the first runs while the softmax computes the second
-        auto issue_pv = [&](int j, int half) {
-          const uint32_t b = v_lo + (j % kStages) * (kTileBytes >> 4);
+        // O_q += P_q V of tile jg (item tile j; j == 0 starts the item's O), P_q in TMEM
+        // (first 64 columns of the S region, 8 per K step), in two halves of 64 keys: the
+        // first runs while the softmax computes the second
+        auto issue_pv = [&](int jg, int j, int half) {
+          const uint32_t b = v_lo + (jg % kStages) * (kTileBytes >> 4);
 #pragma unroll
           for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
             const int kk = half * (kBlockN / 32) + k4;
@@ -293,16 +361,13 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
           if (half) tc::mma_commit(&bars.o_ready[q]);
         };
-        // stage releases (k_empty / v_empty count one commit per active tile) are committed
-        // only where the producer will wait for them
-        // turn-taking on plain (volatile) loads and stores: an acquire or release here
+        // Turn-taking on plain (volatile) loads and stores: an acquire or release here
         // would wait for this thread's MMAs in flight, and the turns order only the issue
-        // of the two tiles' MMAs, no data
+        // of the two tiles' MMAs, no data.  Blocks per item: S of its first tile, then one
+        // per tile (P V(j) + S(j + 1)); `base` counts the blocks of earlier items.
         volatile uint32_t* my_turns = &bars.issued[q];
         const volatile uint32_t* other_turns = &bars.issued[q ^ 1];
-        const bool alternate = q1_active;
         auto wait_turn = [&](uint32_t target) {
-          if (!alternate) return true;
           const uint64_t t0 = global_timer_ns();
           for (uint32_t it = 0; *other_turns < target; ++it) {
             if ((it & 255u) == 255u && (*abort_flag || global_timer_ns() - t0 > kTimeoutNs))
@@ -310,38 +375,52 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
           return true;
         };
-        bool ok = tc::mbar_wait(&bars.q_full, 0, abort_flag, kTimeoutNs);
-        if (ok) ok = tc::mbar_wait(&bars.k_full[0], 0, abort_flag, kTimeoutNs);
-        if (ok && q == 1) ok = wait_turn(1);
-        if (ok) {
-          tc::tc_fence_after();
-          issue_s(0);
-          if (kStages < nt) tc::mma_commit(&bars.k_empty[0]);
-          *my_turns = 1;
-        }
-        for (int j = 0; ok && j < nt; ++j) {
-          const int st = j % kStages;
-          const int sn = (j + 1) % kStages;
-          const bool more = j + 1 < nt;
-          // K / V of the tile landed long before P_q(j): waited first, while the softmax runs
-          if (!(ok = tc::mbar_wait(&bars.v_full[st], (j / kStages) & 1, abort_flag, kTimeoutNs)))
+        // stage releases (k_empty / v_empty count one commit per issuer) are committed
+        // only where the producer will wait for them
+        bool ok = true;
+        uint32_t base = 0;
+        int J = 0;
+        for (int i = 0; ok && i < n_items; ++i) {
+          int u, t0, nt, sl;
+          item(i, u, t0, nt, sl);
+          if (!(ok = tc::mbar_wait(&bars.q_full, i & 1, abort_flag, kTimeoutNs))) break;
+          if (!(ok = tc::mbar_wait(&bars.k_full[J % kStages], (J / kStages) & 1, abort_flag,
+                                   kTimeoutNs)))
             break;
-          if (more && !(ok = tc::mbar_wait(&bars.k_full[sn], ((j + 1) / kStages) & 1, abort_flag,
-                                           kTimeoutNs)))
-            break;
-          if (!(ok = tc::mbar_wait(&bars.p_half[q], j & 1, abort_flag, kTimeoutNs))) break;
-          if (!(ok = wait_turn(q == 0 ? j + 1 : j + 2))) break;
+          if (!(ok = wait_turn(q == 0 ? base : base + 1))) break;
           tc::tc_fence_after();
-          issue_pv(j, 0);
-          if (!(ok = tc::mbar_wait(&bars.p_full[q], j & 1, abort_flag, kTimeoutNs))) break;
-          tc::tc_fence_after();
-          issue_pv(j, 1);
-          if (j + kStages < nt) tc::mma_commit(&bars.v_empty[st]);
-          if (more) {
-            issue_s(j + 1);  // reuses S_q / P_q: runs after the P V MMA above
-            if (j + 1 + kStages < nt) tc::mma_commit(&bars.k_empty[sn]);
+          issue_s(J);
+          if (J + kStages < total) tc::mma_commit(&bars.k_empty[J % kStages]);
+          *my_turns = base + 1;
+          for (int j = 0; j < nt; ++j) {
+            const int jg = J + j;
+            const int st = jg % kStages;
+            const int sn = (jg + 1) % kStages;
+            const bool more = j + 1 < nt;
+            // K / V of the tile landed long before P_q(j): waited first, while the softmax runs
+            if (!(ok = tc::mbar_wait(&bars.v_full[st], (jg / kStages) & 1, abort_flag, kTimeoutNs)))
+              break;
+            if (more && !(ok = tc::mbar_wait(&bars.k_full[sn], ((jg + 1) / kStages) & 1,
+                                             abort_flag, kTimeoutNs)))
+              break;
+            if (!(ok = tc::mbar_wait(&bars.p_half[q], jg & 1, abort_flag, kTimeoutNs))) break;
+            if (!(ok = wait_turn(q == 0 ? base + j + 1 : base + j + 2))) break;
+            tc::tc_fence_after();
+            issue_pv(jg, j, 0);
+            if (!(ok = tc::mbar_wait(&bars.p_full[q], jg & 1, abort_flag, kTimeoutNs))) break;
+            tc::tc_fence_after();
+            issue_pv(jg, j, 1);
+            if (jg + kStages < total) tc::mma_commit(&bars.v_empty[st]);
+            if (more) {
+              issue_s(jg + 1);  // reuses S_q / P_q: runs after the P V MMA above
+              if (jg + 1 + kStages < total) tc::mma_commit(&bars.k_empty[sn]);
+            }
+            *my_turns = base + j + 2;
           }
-          *my_turns = j + 2;
+          // the item's S MMAs are all issued: Q may be replaced once they are done
+          if (ok && i + 1 < n_items) tc::mma_commit(&bars.q_empty);
+          base += nt + 1;
+          J += nt;
         }
         if (!ok) {
           raise_abort(bars, p.status);
@@ -360,147 +439,181 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     const uint32_t tS = tl + col_s(q);
     const uint32_t tO = tl + col_o(q);
-    const int R = row0 + q * kBlockM + r;
-    const int node = R / p.group;
-    const int qh = h * p.group + (R % p.group);
-    const bool valid = R < rows;
-    const int vnode = valid ? node : p.n_nodes - 1;
-    const bool active = (q == 0) || q1_active;
     const float sl2 = p.scale_log2;
-    // the whole key range of the tile is visible to this row (no mask needed) when it
-    // ends before the tree window / the launch's last key
-    const int full_end = p.mask_mode == DDT_MASK_CAUSAL
-                             ? (g_end < p.past_len + node + 1 ? g_end : p.past_len + node + 1)
-                             : (g_end < p.past_len ? g_end : p.past_len);
     const tc::Exp2Poly exp2_poly;
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; active && j < nt; ++j) {
-      if (!tc::mbar_wait_warp(&bars.s_full[q], j & 1, abort_flag, kTimeoutNs)) {
-        ok = false;
-        break;
-      }
-      tc::tc_fence_after();
-      const int gk = p.key_base + lk0 + j * kBlockN;  // global key of column 0
-      const bool masked = __any_sync(DDT_FULL_MASK, gk + kBlockN > full_end);
-      uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) vis[c] = visible32(p, vnode, gk + c * 32, g_end);
-      }
-      // the whole S row (128 fp32) comes out of TMEM in one round trip
-      uint32_t sv[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + c * 32, sv[c]);
-      tc::tmem_wait_ld();
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (!((vis[c] >> e) & 1u)) sv[c][e] = __float_as_uint(-INFINITY);
-      }
-      // masked row max of the raw scores: three-input maxima in 8 independent chains
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; e += 2)
-          mx8[(e >> 1) & 7] = tc::fmax3(mx8[(e >> 1) & 7], __uint_as_float(sv[c][e]),
-                                        __uint_as_float(sv[c][e + 1]));
-      const float mx = tc::fmax3(tc::fmax3(mx8[0], mx8[1], mx8[2]), tc::fmax3(mx8[3], mx8[4], mx8[5]),
-                                 fmaxf(mx8[6], mx8[7]));
-      bool rescale = false;
-      float alpha = 1.f;
-      if (mx > -INFINITY) {
-        const float ms = mx * sl2;
-        if (m_used == -INFINITY) {
-          m_used = ms;  // nothing accumulated yet: O and l are zero
-        } else if (ms > m_used + kRescaleLog2) {
-          alpha = tc::ex2_approx(m_used - ms);
-          m_used = ms;
-          rescale = true;
-        }
-      }
-      if (__any_sync(DDT_FULL_MASK, rescale)) {
-        // O_q is stable once the previous P V MMA of this tile completed
-        if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready[q], (j - 1) & 1, abort_flag, kTimeoutNs)) {
+    int J = 0;
+    for (int i = 0; i < n_items; ++i) {
+      int u, t0, nt, slot;
+      item(i, u, t0, nt, slot);
+      const UnitGeo g = unit_geo(p, u);
+      const int R = g.row0 + q * kBlockM + r;
+      const int node = R / p.group;
+      const int qh = g.h * p.group + (R % p.group);
+      const bool valid = R < rows;
+      const int vnode = valid ? node : p.n_nodes - 1;
+      const int g_end = g.g_end;
+      // the whole key range of the tile is visible to this row (no mask needed) when it
+      // ends before the tree window / the launch's last key
+      const int full_end = p.mask_mode == DDT_MASK_CAUSAL
+                               ? (g_end < p.past_len + vnode + 1 ? g_end : p.past_len + vnode + 1)
+                               : (g_end < p.past_len ? g_end : p.past_len);
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; ok && j < nt; ++j) {
+        const int jg = J + j;
+        if (!tc::mbar_wait_warp(&bars.s_full[q], jg & 1, abort_flag, kTimeoutNs)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
+        const int gk = p.key_lo + (t0 + j) * kBlockN;  // global key of column 0
+        const bool masked = __any_sync(DDT_FULL_MASK, gk + kBlockN > full_end);
+        uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
+        if (masked) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tc::tmem_ld32(tO + c * 32, o);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tc::tmem_st32(tO + c * 32, o);
+          for (int c = 0; c < 4; ++c) vis[c] = visible32(p, vnode, gk + c * 32, g_end);
         }
-        l *= alpha;
-      }
-      const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
-      // P = exp2(S * scale - m), packed bf16 into columns [0, 64) of S_q (masked keys hold
-      // -inf and give 0, or 2^-126 on the polynomial lanes).  Scale and row sum run on
-      // packed fp32 pairs; the pairs selected by kPolyPairs take the polynomial exponential,
-      // the rest the MUFU one.
-      const uint64_t sl2x2 = tc::f2_pack(sl2, sl2), nmx2 = tc::f2_pack(nm, nm);
-      uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
-      // keys [0, 64) first: their P columns are stored and signalled (p_half) while the
-      // second half is computed, so the first four P V MMAs overlap it
-      uint32_t pk[2][32];
+        // the whole S row (128 fp32) comes out of TMEM in one round trip
+        uint32_t sv[4][32];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
+        for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + c * 32, sv[c]);
+        tc::tmem_wait_ld();
+        if (masked) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const uint64_t x = tc::f2_fma(tc::f2_pack(__uint_as_float(sv[hf * 2 + c][e]),
-                                                      __uint_as_float(sv[hf * 2 + c][e + 1])),
-                                          sl2x2, nmx2);
-            float a, b;
-            if ((kPolyPairs >> (e >> 1)) & 1u) {
-              exp2_poly(x, a, b);
-            } else {
-              float x0, x1;
-              tc::f2_unpack(x, x0, x1);
-              a = tc::ex2_approx(x0);
-              b = tc::ex2_approx(x1);
-            }
-            ls2[(e >> 1) & 3] = tc::f2_add(ls2[(e >> 1) & 3], tc::f2_pack(a, b));
-            pk[hf][c * 16 + e / 2] = tc::pack_bf16x2(a, b);
+            for (int e = 0; e < 32; ++e)
+              if (!((vis[c] >> e) & 1u)) sv[c][e] = __float_as_uint(-INFINITY);
+        }
+        // masked row max of the raw scores: three-input maxima in 8 independent chains
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            mx8[(e >> 1) & 7] = tc::fmax3(mx8[(e >> 1) & 7], __uint_as_float(sv[c][e]),
+                                          __uint_as_float(sv[c][e + 1]));
+        const float mx = tc::fmax3(tc::fmax3(mx8[0], mx8[1], mx8[2]),
+                                   tc::fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        bool rescale = false;
+        float alpha = 1.f;
+        if (mx > -INFINITY) {
+          const float ms = mx * sl2;
+          if (m_used == -INFINITY) {
+            m_used = ms;  // nothing accumulated yet: O and l are zero
+          } else if (ms > m_used + kRescaleLog2) {
+            alpha = tc::ex2_approx(m_used - ms);
+            m_used = ms;
+            rescale = true;
           }
         }
-        if (hf == 0) tc::tmem_st32(tS, pk[0]);
+        if (__any_sync(DDT_FULL_MASK, rescale)) {
+          // O_q is stable once the previous P V MMA of this item completed
+          if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready[q], (jg - 1) & 1, abort_flag, kTimeoutNs)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tc::tmem_ld32(tO + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tc::tmem_st32(tO + c * 32, o);
+          }
+          l *= alpha;
+        }
+        const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
+        // P = exp2(S * scale - m), packed bf16 into columns [0, 64) of S_q (masked keys hold
+        // -inf and give 0, or 2^-126 on the polynomial lanes).  Scale and row sum run on
+        // packed fp32 pairs; the pairs selected by kPolyPairs take the polynomial
+        // exponential, the rest the MUFU one.
+        const uint64_t sl2x2 = tc::f2_pack(sl2, sl2), nmx2 = tc::f2_pack(nm, nm);
+        uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
+        // keys [0, 64) first: their P columns are stored and signalled (p_half) while the
+        // second half is computed, so the first four P V MMAs overlap it
+        uint32_t pk[2][32];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const uint64_t x = tc::f2_fma(tc::f2_pack(__uint_as_float(sv[hf * 2 + c][e]),
+                                                        __uint_as_float(sv[hf * 2 + c][e + 1])),
+                                            sl2x2, nmx2);
+              float a, b;
+              if ((kPolyPairs >> (e >> 1)) & 1u) {
+                exp2_poly(x, a, b);
+              } else {
+                float x0, x1;
+                tc::f2_unpack(x, x0, x1);
+                a = tc::ex2_approx(x0);
+                b = tc::ex2_approx(x1);
+              }
+              ls2[(e >> 1) & 3] = tc::f2_add(ls2[(e >> 1) & 3], tc::f2_pack(a, b));
+              pk[hf][c * 16 + e / 2] = tc::pack_bf16x2(a, b);
+            }
+          }
+          if (hf == 0) tc::tmem_st32(tS, pk[0]);
+        }
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars.p_half[q]);
+        tc::tmem_st32(tS + 32, pk[1]);
+        float l0, l1, l2, l3;
+        tc::f2_unpack(tc::f2_add(ls2[0], ls2[1]), l0, l1);
+        tc::f2_unpack(tc::f2_add(ls2[2], ls2[3]), l2, l3);
+        l += (l0 + l1) + (l2 + l3);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars.p_full[q]);
       }
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars.p_half[q]);
-      tc::tmem_st32(tS + 32, pk[1]);
-      float l0, l1, l2, l3;
-      tc::f2_unpack(tc::f2_add(ls2[0], ls2[1]), l0, l1);
-      tc::f2_unpack(tc::f2_add(ls2[2], ls2[3]), l2, l3);
-      l += (l0 + l1) + (l2 + l3);
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars.p_full[q]);
-    }
-    if (active && ok && nt > 0 &&
-        !tc::mbar_wait_warp(&bars.o_ready[q], (nt - 1) & 1, abort_flag, kTimeoutNs))
-      ok = false;
-    if (!ok && lane == 0) raise_abort(bars, p.status);
-    const bool have = active && ok && nt > 0;  // warp-uniform
-    const long long orow_idx = static_cast<long long>(node) * p.q_heads + qh;
-    if (have) tc::tc_fence_after();
-    if (active) {
-      if (p.partial) {
-        float* op = p.o_part +
-                    (static_cast<long long>(split) * p.n_nodes * p.q_heads + orow_idx) * kHeadDim;
+      if (ok && nt > 0 &&
+          !tc::mbar_wait_warp(&bars.o_ready[q], (J + nt - 1) & 1, abort_flag, kTimeoutNs))
+        ok = false;
+      const bool have = ok && nt > 0;  // warp-uniform
+      if (have) tc::tc_fence_after();
+      // ---- epilogue of the item ----------------------------------------------------------
+      if (p.partial && p.balanced) {
+        // the part's own slot, laid out [dim / 4][unit row][4]: the 32 lanes of a warp
+        // (consecutive rows) store 512 contiguous bytes per instruction
+        const int lr = q * kBlockM + r;
+        float* op = p.o_part + static_cast<long long>(slot) * kRowsPerCta * kHeadDim + lr * 4;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          if (have) {
+            tc::tmem_ld32(tO + c * 32, o);
+            tc::tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+          if (valid) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(op + ((c * 32 + e) / 4) * kRowsPerCta * 4) =
+                  make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
+                              __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
+          }
+        }
+        if (valid) {
+          const long long mi = static_cast<long long>(slot) * kRowsPerCta + lr;
+          p.m_part[mi] = have ? m_used : -INFINITY;
+          p.l_part[mi] = have ? l : 0.f;
+        }
+      } else if (p.partial) {
+        // uniform splits: split-major rows in (node, q head) order, the layout the
+        // cross-GPU merge exchanges
+        const long long orow_idx = static_cast<long long>(node) * p.q_heads + qh;
+        const long long pi = static_cast<long long>(slot) * p.n_nodes * p.q_heads + orow_idx;
+        float* op = p.o_part + pi * kHeadDim;
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
           if (have) {
@@ -519,9 +632,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
         }
         if (valid) {
-          const long long mi = static_cast<long long>(split) * p.n_nodes * p.q_heads + orow_idx;
-          p.m_part[mi] = have ? m_used : -INFINITY;
-          p.l_part[mi] = have ? l : 0.f;
+          p.m_part[pi] = have ? m_used : -INFINITY;
+          p.l_part[pi] = have ? l : 0.f;
         }
       } else {
         const float inv = (have && l > 0.f) ? 1.f / l : 0.f;
@@ -549,7 +661,13 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
         }
       }
+      // the O columns are read: the next item's first P V MMA may overwrite them (it waits
+      // for this warpgroup's p_half of that item, which comes after this point)
+      tc::tc_fence_before();
+      J += nt;
+      if (!ok) break;
     }
+    if (!ok && lane == 0) raise_abort(bars, p.status);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -560,7 +678,97 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 }
 
 // ---- split merge ---------------------------------------------------------------------
-// One warp per (node, q head) row; lane owns 4 of the 128 dims.
+// One warp per (node, q head) row.  Lane i < parts loads part i's (m, l); the row max M
+// and the weights exp2(m_i - M) come from warp shuffles, then every lane accumulates 4 of the
+// 128 dims with all parts' loads in flight (a serial walk over the parts made the merge
+// latency-bound).  Up to 32 parts per pass.
+template <typename PartIndex>
+__device__ __forceinline__ void merge_row(const float* __restrict__ o_parts,
+                                          const float* __restrict__ m_parts,
+                                          const float* __restrict__ l_parts, int n_parts,
+                                          PartIndex part_index, int lane, float4& acc, float& M,
+                                          float& L) {
+  M = -INFINITY;
+  L = 0.f;
+  acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  constexpr int kFast = 8;
+  if (n_parts <= kFast) {
+    // one round trip: every part's (m, l) and O issued before any is used
+    const long long pi = lane < n_parts ? part_index(lane) : 0;
+    float4 ov[kFast];
+#pragma unroll
+    for (int k = 0; k < kFast; ++k) {
+      const long long pk = __shfl_sync(DDT_FULL_MASK, pi, k);
+      ov[k] = k < n_parts ? *reinterpret_cast<const float4*>(o_parts + pk * kHeadDim + lane * 4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float mi = lane < n_parts ? m_parts[pi] : -INFINITY;
+    const float li = lane < n_parts ? l_parts[pi] : 0.f;
+    float mx = mi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(DDT_FULL_MASK, mx, o));
+    M = mx;
+    if (M == -INFINITY) return;
+    const float wi = mi == -INFINITY ? 0.f : exp2f(mi - M);
+    float lw = wi * li;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(DDT_FULL_MASK, lw, o);
+    L = lw;
+#pragma unroll
+    for (int k = 0; k < kFast; ++k) {
+      const float w = __shfl_sync(DDT_FULL_MASK, wi, k);  // 0 for k >= n_parts
+      acc.x += w * ov[k].x;
+      acc.y += w * ov[k].y;
+      acc.z += w * ov[k].z;
+      acc.w += w * ov[k].w;
+    }
+    return;
+  }
+  for (int base = 0; base < n_parts; base += 32) {
+    const int cnt = n_parts - base < 32 ? n_parts - base : 32;
+    const long long pi = lane < cnt ? part_index(base + lane) : 0;
+    const float mi = lane < cnt ? m_parts[pi] : -INFINITY;
+    const float li = lane < cnt ? l_parts[pi] : 0.f;
+    float mx = mi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(DDT_FULL_MASK, mx, o));
+    const float Mn = fmaxf(M, mx);
+    if (Mn == -INFINITY) continue;  // warp-uniform: nothing visible yet
+    const float cs = M == -INFINITY ? 0.f : exp2f(M - Mn);  // rescale of the earlier passes
+    acc.x *= cs;
+    acc.y *= cs;
+    acc.z *= cs;
+    acc.w *= cs;
+    L *= cs;
+    M = Mn;
+    const float wi = mi == -INFINITY ? 0.f : exp2f(mi - M);
+    float lw = wi * li;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(DDT_FULL_MASK, lw, o);
+    L += lw;
+    constexpr int kBatch = 8;
+    for (int k0 = 0; k0 < cnt; k0 += kBatch) {
+      float4 ov[kBatch];
+      float wv[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int kk = k0 + k < cnt ? k0 + k : cnt - 1;
+        wv[k] = __shfl_sync(DDT_FULL_MASK, wi, kk);
+        const long long pk = __shfl_sync(DDT_FULL_MASK, pi, kk);
+        ov[k] = *reinterpret_cast<const float4*>(o_parts + pk * kHeadDim + lane * 4);
+        if (k0 + k >= cnt) wv[k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        acc.x += wv[k] * ov[k].x;
+        acc.y += wv[k] * ov[k].y;
+        acc.z += wv[k] * ov[k].z;
+        acc.w += wv[k] * ov[k].w;
+      }
+    }
+  }
+}
+
 __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ m_parts,
                              const float* __restrict__ l_parts, int n_parts, long long rows,
                              int q_heads, __nv_bfloat16* __restrict__ out, long long o_node_stride,
@@ -569,23 +777,10 @@ __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __r
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  float M = -INFINITY;
-  for (int i = 0; i < n_parts; ++i) M = fmaxf(M, m_parts[i * rows + row]);
-  float L = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (M > -INFINITY) {
-    for (int i = 0; i < n_parts; ++i) {
-      const float mi = m_parts[i * rows + row];
-      if (mi == -INFINITY) continue;
-      const float w = exp2f(mi - M);
-      L += w * l_parts[i * rows + row];
-      const float4 o = *reinterpret_cast<const float4*>(o_parts + (i * rows + row) * kHeadDim + lane * 4);
-      acc.x += w * o.x;
-      acc.y += w * o.y;
-      acc.z += w * o.z;
-      acc.w += w * o.w;
-    }
-  }
+  float4 acc;
+  float M, L;
+  merge_row(o_parts, m_parts, l_parts, n_parts,
+            [&](int i) { return static_cast<long long>(i) * rows + row; }, lane, acc, M, L);
   if (out) {
     const float inv = L > 0.f ? 1.f / L : 0.f;
     const long long node = row / q_heads, qh = row % q_heads;
@@ -601,6 +796,76 @@ __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __r
       l_merged[row] = L;
     }
   }
+}
+
+// ---- merge of balanced parts -------------------------------------------------------------
+// One warp per (work unit, 32 consecutive unit rows, 4 of the 128 dims), one lane per row;
+// the unit's parts are slots [unit_slot[u], unit_slot[u + 1]), each holding that part's O
+// laid out [dim / 4][unit row][4] and its m, l per unit row, so a warp's loads are 512 (O)
+// or 128 (m, l) contiguous bytes.  Two passes over the parts, each with all of its loads in
+// flight (batches of 8): the row max, then the weighted sums.  Many small warps keep enough
+// loads outstanding to hide the L2 latency.
+constexpr int kMergeBatch = 8;
+__global__ void __launch_bounds__(256)
+merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ m_parts,
+                   const float* __restrict__ l_parts, const __grid_constant__ SlotTable tab,
+                   const Params p, __nv_bfloat16* __restrict__ out, long long o_node_stride,
+                   long long o_head_stride) {
+  constexpr int kRowGroups = kRowsPerCta / 32, kDimGroups = kHeadDim / 4;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int u = gw / (kRowGroups * kDimGroups);
+  if (u >= p.n_pairs * (p.q_heads / p.group)) return;
+  const int rg = (gw / kDimGroups) % kRowGroups, d4 = gw % kDimGroups;
+  const int lr = rg * 32 + lane;
+  const int R = (u % p.n_pairs) * kRowsPerCta + lr;
+  const int rows = p.n_nodes * p.group;
+  if (R >= rows) return;
+  const int s0 = tab.unit_slot[u], n = tab.unit_slot[u + 1] - s0;
+  float M = -INFINITY;
+  for (int k0 = 0; k0 < n; k0 += kMergeBatch) {
+    float mv[kMergeBatch];
+#pragma unroll
+    for (int k = 0; k < kMergeBatch; ++k)
+      mv[k] = k0 + k < n ? m_parts[static_cast<long long>(s0 + k0 + k) * kRowsPerCta + lr] : -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kMergeBatch; ++k) M = fmaxf(M, mv[k]);
+  }
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M > -INFINITY) {
+    for (int k0 = 0; k0 < n; k0 += kMergeBatch) {
+      float mv[kMergeBatch], lv[kMergeBatch];
+      float4 ov[kMergeBatch];
+#pragma unroll
+      for (int k = 0; k < kMergeBatch; ++k) {
+        const bool in = k0 + k < n;
+        const long long pi = static_cast<long long>(s0 + k0 + (in ? k : 0)) * kRowsPerCta + lr;
+        mv[k] = in ? m_parts[pi] : -INFINITY;
+        lv[k] = in ? l_parts[pi] : 0.f;
+        ov[k] = in ? *reinterpret_cast<const float4*>(
+                         o_parts + static_cast<long long>(s0 + k0 + k) * kRowsPerCta * kHeadDim +
+                         static_cast<long long>(d4) * kRowsPerCta * 4 + lr * 4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < kMergeBatch; ++k) {
+        const float w = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - M);
+        L += w * lv[k];
+        acc.x += w * ov[k].x;
+        acc.y += w * ov[k].y;
+        acc.z += w * ov[k].z;
+        acc.w += w * ov[k].w;
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int h = u / p.n_pairs;
+  const long long node = R / p.group, qh = h * p.group + R % p.group;
+  uint2 v;
+  v.x = tc::pack_bf16x2(acc.x * inv, acc.y * inv);
+  v.y = tc::pack_bf16x2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(out + node * o_node_stride + qh * o_head_stride + d4 * 4) = v;
 }
 
 // ---- mask -> bitmask -------------------------------------------------------------------
@@ -656,6 +921,10 @@ inline int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 struct Launch {
   CUtensorMap q, k, v;
   Params p;
+  Sched sched;
+  SlotTable slots;
+  int grid;
+  int n_parts;
 };
 
 inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_head_stride,
@@ -698,8 +967,63 @@ inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_he
   p.out = nullptr;
   p.o_part = p.m_part = p.l_part = nullptr;
   p.partial = 0;
+  p.balanced = 0;
+  p.n_splits = 1;
   p.status = nullptr;
   return DDT_OK;
+}
+
+// Balanced schedule: the flattened (unit, key tile) range cut into G equal pieces (CTA c:
+// [c W / G, (c + 1) W / G)).  Each unit is preceded by kItemCost virtual tiles, the cost of
+// starting an item (Q load, pipeline refill, the partial's epilogue), so a CTA whose range
+// reaches into a second unit gets correspondingly fewer real tiles.  Returns false (and
+// leaves the launch on uniform splits) when a limit of the tables is exceeded or a unit has
+// no key tile.
+#ifndef DDT_ITEM_COST
+#define DDT_ITEM_COST 1
+#endif
+constexpr int kItemCost = DDT_ITEM_COST;
+
+inline bool build_balanced(Launch& L, int64_t units) {
+  Params& p = L.p;
+  if (units <= 0 || units > kMaxUnits) return false;
+  int64_t W = 0, real = 0;
+  int ntot[kMaxUnits];
+  for (int u = 0; u < units; ++u) {
+    ntot[u] = unit_geo(p, u).ntot;
+    if (ntot[u] <= 0 || ntot[u] > 0xffff) return false;
+    W += kItemCost + ntot[u];
+    real += ntot[u];
+  }
+  const int64_t G = real < kMaxCtas ? real : kMaxCtas;
+  auto cta_of = [&](int64_t x) { return ((x + 1) * G - 1) / W; };  // CTA holding position x
+  // items in unit order (slots of a unit consecutive); CTA lists follow since units and
+  // CTAs both advance monotonically along the flattened range
+  int n = 0;
+  int64_t T = 0;  // first real tile of unit u in the flattened range
+  int cur_cta = -1;
+  for (int u = 0; u < units; ++u) {
+    T += kItemCost;
+    L.slots.unit_slot[u] = static_cast<uint16_t>(n);
+    const int64_t cf = cta_of(T), cl = cta_of(T + ntot[u] - 1);
+    if (cl - cf + 1 > kMaxPartsPerUnit) return false;
+    for (int64_t c = cf; c <= cl; ++c) {
+      if (n >= kMaxItems) return false;
+      const int64_t b = c * W / G, e = (c + 1) * W / G;
+      const int64_t lo = b > T ? b : T, hi = e < T + ntot[u] ? e : T + ntot[u];
+      while (cur_cta < c) L.sched.cta_first[++cur_cta] = static_cast<uint16_t>(n);
+      L.sched.items[n] = SchedItem{static_cast<uint16_t>(u), static_cast<uint16_t>(lo - T),
+                                   static_cast<uint16_t>(hi - lo), static_cast<uint16_t>(n)};
+      ++n;
+    }
+    T += ntot[u];
+  }
+  while (cur_cta < G) L.sched.cta_first[++cur_cta] = static_cast<uint16_t>(n);
+  L.slots.unit_slot[units] = static_cast<uint16_t>(n);
+  L.grid = static_cast<int>(G);
+  L.n_parts = n;
+  p.balanced = 1;
+  return true;
 }
 
 inline int pick_splits(int64_t units, int64_t kv_tiles) {
@@ -717,6 +1041,11 @@ inline size_t part_bytes(int64_t rows, int64_t splits) {
   return static_cast<size_t>(splits) * rows * (kHeadDim + 2) * sizeof(float) + 256;
 }
 
+// bytes of `parts` balanced partials of 256 rows each (O, m, l in fp32)
+inline size_t slot_bytes(int64_t parts) {
+  return static_cast<size_t>(parts) * kRowsPerCta * (kHeadDim + 2) * sizeof(float) + 256;
+}
+
 inline int launch(const Launch& L, int64_t kv_heads, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
@@ -725,8 +1054,9 @@ inline int launch(const Launch& L, int64_t kv_heads, cudaStream_t st) {
       return DDT_ERR_CUDA;
     attr = true;
   }
-  const int64_t grid = kv_heads * L.p.n_pairs * L.p.n_splits;
-  tree_attn_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, st>>>(L.q, L.k, L.v, L.p);
+  const int64_t grid = L.p.balanced ? L.grid : kv_heads * L.p.n_pairs * L.p.n_splits;
+  tree_attn_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, st>>>(L.q, L.k, L.v, L.p,
+                                                                             L.sched);
   return launch_status();
 }
 
@@ -738,8 +1068,14 @@ using namespace ddt;
 extern "C" size_t ddt_tree_attn_workspace_bytes(int64_t n_nodes, int64_t q_heads, int64_t head_dim,
                                                 int64_t kv_splits) {
   (void)head_dim;
-  const int64_t s = kv_splits > 0 ? kv_splits : 64;
-  return attn::part_bytes(n_nodes * q_heads, s);
+  const int64_t rows = n_nodes * q_heads;
+  if (kv_splits > 0) return attn::part_bytes(rows, kv_splits);
+  // automatic: balanced parts (at most one per CTA plus one per work unit; units <=
+  // rows / 256 + q_heads), or uniform splits, whose rows * splits stay below 148 * 256
+  const int64_t parts = attn::kMaxCtas + (rows + attn::kRowsPerCta - 1) / attn::kRowsPerCta + q_heads;
+  const size_t a = attn::slot_bytes(parts);
+  const size_t b = attn::part_bytes(rows, 64);
+  return a > b ? a : b;
 }
 
 extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride,
@@ -772,6 +1108,28 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
   L.p.o_head_stride = o_head_stride;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t rows = n_nodes * q_heads;
+  // automatic split with fewer work units than SMs: balanced parts (every SM the same
+  // number of key tiles), merged per unit
+  if (kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::build_balanced(L, units)) {
+    const size_t need = attn::slot_bytes(L.n_parts);
+    if (!workspace || workspace_bytes < need) return DDT_ERR_WORKSPACE;
+    if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
+    float* o_part = static_cast<float*>(workspace);
+    float* m_part = o_part + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta * attn::kHeadDim;
+    float* l_part = m_part + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta;
+    L.p.o_part = o_part;
+    L.p.m_part = m_part;
+    L.p.l_part = l_part;
+    L.p.partial = 1;
+    rc = attn::launch(L, kv_heads, st);
+    if (rc) return rc;
+    const int wpb = 8;
+    const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / 4);
+    attn::merge_slots_kernel<<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+        o_part, m_part, l_part, L.slots, L.p, static_cast<__nv_bfloat16*>(out), o_node_stride,
+        o_head_stride);
+    return launch_status();
+  }
   if (splits > 1) {
     if (!workspace || workspace_bytes < attn::part_bytes(rows, splits)) return DDT_ERR_WORKSPACE;
     if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
