@@ -799,73 +799,74 @@ __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __r
 }
 
 // ---- merge of balanced parts -------------------------------------------------------------
-// One warp per (work unit, 32 consecutive unit rows, 4 of the 128 dims), one lane per row;
+// One warp per (work unit, 32 consecutive unit rows, 8 of the 128 dims), one lane per row;
 // the unit's parts are slots [unit_slot[u], unit_slot[u + 1]), each holding that part's O
 // laid out [dim / 4][unit row][4] and its m, l per unit row, so a warp's loads are 512 (O)
-// or 128 (m, l) contiguous bytes.  Two passes over the parts, each with all of its loads in
-// flight (batches of 8): the row max, then the weighted sums.  Many small warps keep enough
-// loads outstanding to hide the L2 latency.
+// or 128 (m, l) contiguous bytes.  One pass over the parts in batches of 8 with every load
+// of a batch in flight and an online maximum (earlier batches rescaled when it grows): one
+// L2 round trip for up to 8 parts.
 constexpr int kMergeBatch = 8;
+constexpr int kMergeDims = 8;
 __global__ void __launch_bounds__(256)
 merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ m_parts,
                    const float* __restrict__ l_parts, const __grid_constant__ SlotTable tab,
                    const Params p, __nv_bfloat16* __restrict__ out, long long o_node_stride,
                    long long o_head_stride) {
-  constexpr int kRowGroups = kRowsPerCta / 32, kDimGroups = kHeadDim / 4;
+  constexpr int kRowGroups = kRowsPerCta / 32, kDimGroups = kHeadDim / kMergeDims;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int u = gw / (kRowGroups * kDimGroups);
   if (u >= p.n_pairs * (p.q_heads / p.group)) return;
-  const int rg = (gw / kDimGroups) % kRowGroups, d4 = gw % kDimGroups;
+  const int rg = (gw / kDimGroups) % kRowGroups, dg = gw % kDimGroups;
   const int lr = rg * 32 + lane;
   const int R = (u % p.n_pairs) * kRowsPerCta + lr;
   const int rows = p.n_nodes * p.group;
   if (R >= rows) return;
   const int s0 = tab.unit_slot[u], n = tab.unit_slot[u + 1] - s0;
-  float M = -INFINITY;
+  float M = -INFINITY, L = 0.f;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
   for (int k0 = 0; k0 < n; k0 += kMergeBatch) {
-    float mv[kMergeBatch];
+    float mv[kMergeBatch], lv[kMergeBatch];
+    float4 ov[kMergeBatch][2];
 #pragma unroll
-    for (int k = 0; k < kMergeBatch; ++k)
-      mv[k] = k0 + k < n ? m_parts[static_cast<long long>(s0 + k0 + k) * kRowsPerCta + lr] : -INFINITY;
+    for (int k = 0; k < kMergeBatch; ++k) {
+      const bool in = k0 + k < n;
+      const long long sl = s0 + k0 + (in ? k : 0);
+      const long long pi = sl * kRowsPerCta + lr;
+      const float* op = o_parts + sl * kRowsPerCta * kHeadDim +
+                        static_cast<long long>(dg * 2) * kRowsPerCta * 4 + lr * 4;
+      mv[k] = in ? m_parts[pi] : -INFINITY;
+      lv[k] = in ? l_parts[pi] : 0.f;
+      ov[k][0] = in ? *reinterpret_cast<const float4*>(op) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ov[k][1] = in ? *reinterpret_cast<const float4*>(op + kRowsPerCta * 4)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float Mb = M;
 #pragma unroll
-    for (int k = 0; k < kMergeBatch; ++k) M = fmaxf(M, mv[k]);
-  }
-  float L = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (M > -INFINITY) {
-    for (int k0 = 0; k0 < n; k0 += kMergeBatch) {
-      float mv[kMergeBatch], lv[kMergeBatch];
-      float4 ov[kMergeBatch];
+    for (int k = 0; k < kMergeBatch; ++k) Mb = fmaxf(Mb, mv[k]);
+    if (Mb == -INFINITY) continue;
+    const float cs = M == -INFINITY ? 0.f : exp2f(M - Mb);
+    M = Mb;
+    L *= cs;
+    a.x *= cs; a.y *= cs; a.z *= cs; a.w *= cs;
+    b.x *= cs; b.y *= cs; b.z *= cs; b.w *= cs;
 #pragma unroll
-      for (int k = 0; k < kMergeBatch; ++k) {
-        const bool in = k0 + k < n;
-        const long long pi = static_cast<long long>(s0 + k0 + (in ? k : 0)) * kRowsPerCta + lr;
-        mv[k] = in ? m_parts[pi] : -INFINITY;
-        lv[k] = in ? l_parts[pi] : 0.f;
-        ov[k] = in ? *reinterpret_cast<const float4*>(
-                         o_parts + static_cast<long long>(s0 + k0 + k) * kRowsPerCta * kHeadDim +
-                         static_cast<long long>(d4) * kRowsPerCta * 4 + lr * 4)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int k = 0; k < kMergeBatch; ++k) {
-        const float w = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - M);
-        L += w * lv[k];
-        acc.x += w * ov[k].x;
-        acc.y += w * ov[k].y;
-        acc.z += w * ov[k].z;
-        acc.w += w * ov[k].w;
-      }
+    for (int k = 0; k < kMergeBatch; ++k) {
+      const float w = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - M);
+      L += w * lv[k];
+      a.x += w * ov[k][0].x; a.y += w * ov[k][0].y; a.z += w * ov[k][0].z; a.w += w * ov[k][0].w;
+      b.x += w * ov[k][1].x; b.y += w * ov[k][1].y; b.z += w * ov[k][1].z; b.w += w * ov[k][1].w;
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
   const int h = u / p.n_pairs;
   const long long node = R / p.group, qh = h * p.group + R % p.group;
-  uint2 v;
-  v.x = tc::pack_bf16x2(acc.x * inv, acc.y * inv);
-  v.y = tc::pack_bf16x2(acc.z * inv, acc.w * inv);
-  *reinterpret_cast<uint2*>(out + node * o_node_stride + qh * o_head_stride + d4 * 4) = v;
+  uint4 v;
+  v.x = tc::pack_bf16x2(a.x * inv, a.y * inv);
+  v.y = tc::pack_bf16x2(a.z * inv, a.w * inv);
+  v.z = tc::pack_bf16x2(b.x * inv, b.y * inv);
+  v.w = tc::pack_bf16x2(b.z * inv, b.w * inv);
+  *reinterpret_cast<uint4*>(out + node * o_node_stride + qh * o_head_stride + dg * kMergeDims) = v;
 }
 
 // ---- mask -> bitmask -------------------------------------------------------------------
@@ -1124,7 +1125,7 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
     rc = attn::launch(L, kv_heads, st);
     if (rc) return rc;
     const int wpb = 8;
-    const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / 4);
+    const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
     attn::merge_slots_kernel<<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
         o_part, m_part, l_part, L.slots, L.p, static_cast<__nv_bfloat16*>(out), o_node_stride,
         o_head_stride);
