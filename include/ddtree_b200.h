@@ -167,6 +167,24 @@ int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64_t q_head_s
                           int mask_mode, float scale, int64_t kv_splits, int32_t* status,
                           void* stream);
 
+/* Like ddt_tree_attn_partial, but the shard's key tiles are spread evenly over the SMs
+ * (balanced work items) and merged in-GPU, so the result is one partial per row:
+ * o_part [n_nodes * q_heads, head_dim], m_part / l_part [n_nodes * q_heads].  Halves the
+ * bytes a cross-GPU exchange moves against two in-GPU splits.  Needs a workspace of
+ * ddt_tree_attn_partial_merged_workspace_bytes bytes (16-byte aligned).  Replaces, like
+ * ddt_tree_attn_partial, one key shard of the verify attention of
+ * integrations/sdpa_attention.py:40-103. */
+size_t ddt_tree_attn_partial_merged_workspace_bytes(int64_t n_nodes, int64_t q_heads,
+                                                    int64_t head_dim);
+int ddt_tree_attn_partial_merged(const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                                 const void* k, const void* v, int64_t kv_head_stride,
+                                 int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
+                                 float* o_part, float* m_part, float* l_part, int64_t n_nodes,
+                                 int64_t past_length, int64_t q_heads, int64_t kv_heads,
+                                 int64_t head_dim, const uint32_t* anc_bits, int64_t anc_words,
+                                 int mask_mode, float scale, void* workspace,
+                                 size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Merge n_parts partials laid out [n_parts, rows, head_dim] / [n_parts, rows]
  * (rows = n_nodes * q_heads) into out (bf16, [n_nodes, q_heads, head_dim] at the given
  * strides). */

@@ -44,6 +44,9 @@ SIGNATURES = {
     "ddt_tree_attn_partial_splits": (_I, [_I, _I, _I, _I]),
     "ddt_tree_attn_partial": (_i, [_P, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I,
                                    _I, _P, _I, _i, _F, _I, _P, _P]),
+    "ddt_tree_attn_partial_merged_workspace_bytes": (_S, [_I, _I, _I]),
+    "ddt_tree_attn_partial_merged": (_i, [_P, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I,
+                                          _I, _I, _I, _P, _I, _i, _F, _P, _S, _P, _P]),
     "ddt_attn_merge": (_i, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P]),
     "ddt_mask_to_bits": (_i, [_P, _i, _I, _I, _P, _I, _P]),
     "ddt_add_rmsnorm": (_i, [_P, _P, _P, _I, _I, _F, _P, _P, _P]),

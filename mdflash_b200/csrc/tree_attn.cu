@@ -102,6 +102,14 @@ constexpr int kMaxCtas = 148;
 constexpr int kMaxItems = 320;
 constexpr int kMaxUnits = 256;
 constexpr int kMaxPartsPerUnit = 32;  // merge_slots_kernel keeps one weight per part
+// The balanced cut staggers the key positions that the row pairs of a head read at a time.
+// That costs nothing while the launch's K / V stay in L2, but K / V much larger than L2 are
+// then read from HBM once per row pair; uniform splits keep the pairs in step (each K / V
+// tile read once and shared through L2).  Balanced only below this many K / V bytes.
+constexpr int64_t kBalancedMaxKvBytes = 64ll << 20;
+inline bool kv_fits_l2(int64_t keys, int64_t kv_heads) {
+  return 2 * kv_heads * keys * kHeadDim * 2 <= kBalancedMaxKvBytes;
+}
 struct SchedItem {
   uint16_t unit, t0, nt, slot;  // work unit, first key tile of the unit, tiles, partial slot
 };
@@ -805,13 +813,17 @@ __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __r
 // or 128 (m, l) contiguous bytes.  One pass over the parts in batches of 8 with every load
 // of a batch in flight and an online maximum (earlier batches rescaled when it grows): one
 // L2 round trip for up to 8 parts.
+// kFp32: write the merged partial (O un-normalised, m, l) in (node, q head) row order, the
+// cross-GPU exchange format, instead of the bf16 output.
 constexpr int kMergeBatch = 8;
 constexpr int kMergeDims = 8;
+template <bool kFp32>
 __global__ void __launch_bounds__(256)
 merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ m_parts,
                    const float* __restrict__ l_parts, const __grid_constant__ SlotTable tab,
                    const Params p, __nv_bfloat16* __restrict__ out, long long o_node_stride,
-                   long long o_head_stride) {
+                   long long o_head_stride, float* __restrict__ o_merged,
+                   float* __restrict__ m_merged, float* __restrict__ l_merged) {
   constexpr int kRowGroups = kRowsPerCta / 32, kDimGroups = kHeadDim / kMergeDims;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -858,15 +870,26 @@ merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ 
       b.x += w * ov[k][1].x; b.y += w * ov[k][1].y; b.z += w * ov[k][1].z; b.w += w * ov[k][1].w;
     }
   }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
   const int h = u / p.n_pairs;
   const long long node = R / p.group, qh = h * p.group + R % p.group;
-  uint4 v;
-  v.x = tc::pack_bf16x2(a.x * inv, a.y * inv);
-  v.y = tc::pack_bf16x2(a.z * inv, a.w * inv);
-  v.z = tc::pack_bf16x2(b.x * inv, b.y * inv);
-  v.w = tc::pack_bf16x2(b.z * inv, b.w * inv);
-  *reinterpret_cast<uint4*>(out + node * o_node_stride + qh * o_head_stride + dg * kMergeDims) = v;
+  if constexpr (kFp32) {
+    const long long row = node * p.q_heads + qh;
+    float* o = o_merged + row * kHeadDim + dg * kMergeDims;
+    *reinterpret_cast<float4*>(o) = a;
+    *reinterpret_cast<float4*>(o + 4) = b;
+    if (dg == 0) {
+      m_merged[row] = M;
+      l_merged[row] = L;
+    }
+  } else {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    uint4 v;
+    v.x = tc::pack_bf16x2(a.x * inv, a.y * inv);
+    v.y = tc::pack_bf16x2(a.z * inv, a.w * inv);
+    v.z = tc::pack_bf16x2(b.x * inv, b.y * inv);
+    v.w = tc::pack_bf16x2(b.z * inv, b.w * inv);
+    *reinterpret_cast<uint4*>(out + node * o_node_stride + qh * o_head_stride + dg * kMergeDims) = v;
+  }
 }
 
 // ---- mask -> bitmask -------------------------------------------------------------------
@@ -1072,10 +1095,11 @@ extern "C" size_t ddt_tree_attn_workspace_bytes(int64_t n_nodes, int64_t q_heads
   const int64_t rows = n_nodes * q_heads;
   if (kv_splits > 0) return attn::part_bytes(rows, kv_splits);
   // automatic: balanced parts (at most one per CTA plus one per work unit; units <=
-  // rows / 256 + q_heads), or uniform splits, whose rows * splits stay below 148 * 256
+  // rows / 256 + q_heads), or, when the schedule tables do not fit, uniform splits, whose
+  // splits * rows stay below 148 * 256 (splits <= 148 / units, rows <= 256 units)
   const int64_t parts = attn::kMaxCtas + (rows + attn::kRowsPerCta - 1) / attn::kRowsPerCta + q_heads;
   const size_t a = attn::slot_bytes(parts);
-  const size_t b = attn::part_bytes(rows, 64);
+  const size_t b = attn::part_bytes(attn::kMaxCtas * attn::kRowsPerCta, 1);
   return a > b ? a : b;
 }
 
@@ -1111,7 +1135,8 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
   const int64_t rows = n_nodes * q_heads;
   // automatic split with fewer work units than SMs: balanced parts (every SM the same
   // number of key tiles), merged per unit
-  if (kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::build_balanced(L, units)) {
+  if (kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::kv_fits_l2(S, kv_heads) &&
+      attn::build_balanced(L, units)) {
     const size_t need = attn::slot_bytes(L.n_parts);
     if (!workspace || workspace_bytes < need) return DDT_ERR_WORKSPACE;
     if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
@@ -1126,9 +1151,9 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
     if (rc) return rc;
     const int wpb = 8;
     const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
-    attn::merge_slots_kernel<<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+    attn::merge_slots_kernel<false><<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
         o_part, m_part, l_part, L.slots, L.p, static_cast<__nv_bfloat16*>(out), o_node_stride,
-        o_head_stride);
+        o_head_stride, nullptr, nullptr, nullptr);
     return launch_status();
   }
   if (splits > 1) {
@@ -1192,6 +1217,72 @@ extern "C" int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64
   L.p.l_part = l_part;
   L.p.partial = 1;
   return attn::launch(L, kv_heads, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t ddt_tree_attn_partial_merged_workspace_bytes(int64_t n_nodes, int64_t q_heads,
+                                                               int64_t head_dim) {
+  return ddt_tree_attn_workspace_bytes(n_nodes, q_heads, head_dim, 0);
+}
+
+extern "C" int ddt_tree_attn_partial_merged(
+    const void* q, int64_t q_node_stride, int64_t q_head_stride, const void* k, const void* v,
+    int64_t kv_head_stride, int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
+    float* o_part, float* m_part, float* l_part, int64_t n_nodes, int64_t past_length,
+    int64_t q_heads, int64_t kv_heads, int64_t head_dim, const uint32_t* anc_bits,
+    int64_t anc_words, int mask_mode, float scale, void* workspace, size_t workspace_bytes,
+    int32_t* status, void* stream) {
+  if (!o_part || !m_part || !l_part) return DDT_ERR_INVALID;
+  if (key_begin < 0 || key_end < key_begin || key_end > past_length + n_nodes) return DDT_ERR_INVALID;
+  if (!aligned(o_part, 16)) return DDT_ERR_ALIGN;
+  attn::Launch L;
+  const int64_t local = key_end - key_begin;
+  int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride,
+                         local > 0 ? local : 1, n_nodes, past_length, q_heads, kv_heads, head_dim,
+                         anc_bits, anc_words, mask_mode, scale);
+  if (rc) return rc;
+  L.p.key_base = static_cast<int>(key_begin);
+  L.p.key_lo = static_cast<int>(key_begin);
+  L.p.key_hi = static_cast<int>(key_end);
+  L.p.status = status;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t units = kv_heads * L.p.n_pairs;
+  const int64_t rows = n_nodes * q_heads;
+  if (!workspace || !aligned(workspace, 16)) return DDT_ERR_WORKSPACE;
+  const int wpb = 8;
+  if (attn::kv_fits_l2(local, kv_heads) && attn::build_balanced(L, units)) {
+    if (workspace_bytes < attn::slot_bytes(L.n_parts)) return DDT_ERR_WORKSPACE;
+    float* op = static_cast<float*>(workspace);
+    float* mp = op + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta * attn::kHeadDim;
+    float* lp = mp + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta;
+    L.p.o_part = op;
+    L.p.m_part = mp;
+    L.p.l_part = lp;
+    L.p.partial = 1;
+    rc = attn::launch(L, kv_heads, st);
+    if (rc) return rc;
+    const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
+    attn::merge_slots_kernel<true><<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+        op, mp, lp, L.slots, L.p, nullptr, 0, 0, o_part, m_part, l_part);
+    return launch_status();
+  }
+  // large shards (K / V beyond L2), units with no key in this shard, or tables too small:
+  // uniform splits, merged
+  const int64_t kv_tiles = (local + attn::kBlockN - 1) / attn::kBlockN;
+  const int splits = attn::pick_splits(units, kv_tiles > 0 ? kv_tiles : 1);
+  if (workspace_bytes < attn::part_bytes(rows, splits)) return DDT_ERR_WORKSPACE;
+  float* op = static_cast<float*>(workspace);
+  float* mp = op + static_cast<size_t>(splits) * rows * attn::kHeadDim;
+  float* lp = mp + static_cast<size_t>(splits) * rows;
+  L.p.n_splits = splits;
+  L.p.o_part = op;
+  L.p.m_part = mp;
+  L.p.l_part = lp;
+  L.p.partial = 1;
+  rc = attn::launch(L, kv_heads, st);
+  if (rc) return rc;
+  attn::merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+      op, mp, lp, splits, rows, static_cast<int>(q_heads), nullptr, 0, 0, o_part, m_part, l_part);
+  return launch_status();
 }
 
 extern "C" int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_parts,

@@ -379,6 +379,43 @@ def tree_attention_partial(q, k_shard, v_shard, key_begin: int, key_end: int, an
     return o, m, l
 
 
+def tree_attention_partial_merged(q, k_shard, v_shard, key_begin: int, key_end: int, anc_bits,
+                                  past_length: int, scale: float | None = None,
+                                  causal: bool = False, out=None, status=None):
+    """One partial per row over global keys [key_begin, key_end): (O unnormalised fp32
+    [N*Hq, D], m [N*Hq], l [N*Hq]).  The shard's key tiles are spread over all SMs and merged
+    in-GPU (ddt_tree_attn_partial_merged), so a cross-GPU exchange moves one partial per
+    row and rank."""
+    dev = _require_cuda(q, k_shard, v_shard)
+    n, hq, qns, qhs = _q_view(q)
+    hkv, s_local, khs, kss = _kv_view(k_shard)
+    d = q.shape[-1]
+    if s_local < key_end - key_begin:
+        raise ValueError("shard shorter than its key range")
+    lib = _lib.load()
+    if out is None:
+        out = (torch.empty((n * hq, d), dtype=torch.float32, device=dev),
+               torch.empty((n * hq,), dtype=torch.float32, device=dev),
+               torch.empty((n * hq,), dtype=torch.float32, device=dev))
+    o, m, l = out
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if status is None:
+        status = WORKSPACES.get(dev, "attn_status", 256)[:4].view(torch.int32)
+    ws_bytes = lib.ddt_tree_attn_partial_merged_workspace_bytes(n, hq, d)
+    ws = WORKSPACES.get(dev, "attn_partial_merged", ws_bytes)
+    words = anc_bits.shape[1] if anc_bits is not None else 0
+    rc = lib.ddt_tree_attn_partial_merged(
+        q.data_ptr(), qns, qhs, k_shard.data_ptr(), v_shard.data_ptr(), khs, kss, key_begin,
+        key_end, o.data_ptr(), m.data_ptr(), l.data_ptr(), n, past_length, hq, hkv, d,
+        anc_bits.data_ptr() if anc_bits is not None else None, words,
+        DDT_MASK_CAUSAL if causal else DDT_MASK_TREE, float(scale), ws.data_ptr(), ws.numel(),
+        status.data_ptr(), _stream(dev))
+    check(rc, "ddt_tree_attn_partial_merged")
+    STATS.launches += 2
+    return o, m, l
+
+
 def attn_merge(o_parts: torch.Tensor, m_parts: torch.Tensor, l_parts: torch.Tensor, n_nodes: int,
                q_heads: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Merges [P, rows, D] / [P, rows] partials into bf16 [n_nodes, q_heads, D]."""

@@ -11,9 +11,10 @@ split-KV exchange:
   fixed-size int64 records in one ``all_gather`` (NCCL on GPUs, gloo on CPUs).
 * Sequence-sharded split-KV for one long prefix.  The prefix keys are split into
   contiguous, 128-key-aligned shards; the last rank also owns the tree rows (so it is the
-  rank that runs the compaction).  Every rank computes the partial (O, m, l) of its keys
-  with ``ddt_tree_attn_partial``; one ``all_gather`` of the partials and ``ddt_attn_merge``
-  give every rank the full attention output.
+  rank that runs the compaction).  Every rank computes one partial (O, m, l) per row over
+  its keys with ``ddt_tree_attn_partial_merged`` (the shard's tiles spread over all SMs and
+  merged in-GPU); all-gathers straight into the merge layout and ``ddt_attn_merge`` give
+  every rank the full attention output.
 """
 from __future__ import annotations
 
@@ -147,21 +148,33 @@ def exchange_partials(o: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=N
     return og, mg, lg
 
 
+def gather_partials(o: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=None):
+    """All-gathers one partial per row and rank (O [rows, D], m [rows], l [rows]) straight
+    into contiguous [world, rows, D] / [world, rows] tensors, the layout ddt_attn_merge
+    reads (no packing copies)."""
+    if not dist.is_initialized():
+        return o[None], m[None], l[None]
+    world = dist.get_world_size(group)
+    out = []
+    for t in (o, m, l):
+        # gathered as the concatenation along dim 0 (the form every backend accepts), which
+        # is the [world, ...] stack in memory
+        g = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(g, t.contiguous(), group=group)
+        out.append(g.view((world,) + tuple(t.shape)))
+    return tuple(out)
+
+
 def splitkv_attention(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
                       key_begin: int, key_end: int, anc_bits: torch.Tensor | None,
                       past_length: int, scale: float | None = None, group=None,
                       out: torch.Tensor | None = None) -> torch.Tensor:
-    """Tree attention over a sequence-sharded prefix: partial on this rank's keys, one
-    all-gather of the partials, merge.  Returns the bf16 output [N, Hq, D] on every rank."""
+    """Tree attention over a sequence-sharded prefix: this rank's keys spread over all of its
+    SMs and merged in-GPU to one partial per row, one all-gather of the partials, merge.
+    Returns the bf16 output [N, Hq, D] on every rank."""
     from . import kernels as K
     n, hq = q.shape[0], q.shape[1]
-    # the in-GPU split count must be the same on every rank (the exchanged partials have one
-    # shape): derive it from quantities every rank shares, not from this rank's shard size
-    world = dist.get_world_size(group) if dist.is_initialized() else 1
-    per_rank_keys = -(-(past_length + n) // world)
-    splits = int(K._lib.load().ddt_tree_attn_partial_splits(n, per_rank_keys, hq,
-                                                           k_shard.shape[-3]))
-    o, m, l = K.tree_attention_partial(q, k_shard, v_shard, key_begin, key_end, anc_bits,
-                                       past_length, scale=scale, kv_splits=splits)
-    og, mg, lg = exchange_partials(o, m, l, group)
+    o, m, l = K.tree_attention_partial_merged(q, k_shard, v_shard, key_begin, key_end, anc_bits,
+                                              past_length, scale=scale)
+    og, mg, lg = gather_partials(o, m, l, group)
     return K.attn_merge(og, mg, lg, n, hq, out=out)

@@ -51,6 +51,21 @@ def test_splitkv_shards_in_one_process(cuda_device, world):
     assert _rel(S.splitkv_attention(q, k, v, 0, P + N, bits, P), full) <= 1e-2
 
 
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_merged_partials_per_shard(cuda_device, world):
+    """One in-GPU-merged partial per row and shard (balanced work items inside each shard),
+    then the cross-shard merge."""
+    q, k, v, bits = _data(cuda_device)
+    full = K.tree_attention(q, k, v, bits, P)
+    parts = [K.tree_attention_partial_merged(q, k[:, kb:ke].contiguous(), v[:, kb:ke].contiguous(),
+                                             kb, ke, bits, P)
+             for kb, ke in (S.shard_range(P, N, world, r) for r in range(world))]
+    merged = K.attn_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]),
+                          torch.stack([p[2] for p in parts]), N, 32)
+    torch.cuda.synchronize()
+    assert _rel(merged, full) <= 1e-2
+
+
 def _port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

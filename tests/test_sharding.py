@@ -114,6 +114,11 @@ def _worker(rank, world, port, q):
         merged = _merge_reference(og, mg, lg).view(n, qq.shape[0], -1)
         full = oracle.tree_attention(qq, kk, vv, vis, past)
         err = ((merged - full).abs().max() / full.abs().max()).item()
+        # the same partials, one per row, through the no-copy gather
+        og2, mg2, lg2 = S.gather_partials(o, m, l)
+        assert og2.shape == (world,) + tuple(o.shape) and mg2.shape == (world, m.shape[0])
+        merged2 = _merge_reference(og2, mg2, lg2).view(n, qq.shape[0], -1)
+        err = max(err, ((merged2 - full).abs().max() / full.abs().max()).item())
         q.put((rank, err))
     finally:
         dist.destroy_process_group()
