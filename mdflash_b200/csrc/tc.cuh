@@ -60,17 +60,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // Warp-collective bounded wait: every lane of the warp calls it and gets the same
 // answer, so code after it that uses .sync.aligned tcgen05 instructions stays converged.
+// The clock is first read after 64 polls, so a wait that is already satisfied costs one
+// try_wait.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
                                                uint64_t timeout_ns) {
-  const uint64_t t0 = global_timer_ns();
+  uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     const bool ok = mbar_try_wait(bar, parity);
     if (__all_sync(DDT_FULL_MASK, ok)) return true;
     if ((it & 63u) == 63u) {
-      const bool stop = (*abort != 0) || (global_timer_ns() - t0 > timeout_ns);
+      const uint64_t now = global_timer_ns();
+      if (t0 == 0) t0 = now;
+      const bool stop = (*abort != 0) || (now - t0 > timeout_ns);
       if (__any_sync(DDT_FULL_MASK, stop)) return false;
     }
   }
+}
+
+// True on one lane of the calling warp (all 32 lanes must call it).  For the same set of
+// active lanes it elects the same lane every time, so MMAs and the commits that track them
+// can be issued from separate elect_one() blocks.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e != 0;
 }
 
 // Bounded wait that ignores the abort flag: used while unwinding to let transfers that
@@ -291,7 +308,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // bits of the shifted value shifted left by 23 hold.  x is clamped at -126 first: -inf
 // (masked keys) gives 2^-126 rather than 0, and the exponent cannot wrap.  Measured on B200:
 // ~9 cycles per element per SM sub-partition against 8 for MUFU ex2 (f32x2 FMAs issue at half
-// rate), so offloading to it does not pay there; the tree-attention kernel selects no pairs.
+// rate), so it pays only as a share of the exponentials that runs beside MUFU; the
+// tree-attention kernel gives it 10 of every 32.
 struct Exp2Poly {
   uint64_t shift, neg_shift, minus1, c0, c1, c2, c3;
   __device__ __forceinline__ Exp2Poly() {

@@ -65,10 +65,12 @@ constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kBlockM, kBlockN, false, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kBlockM, kHeadDim, false, true);
 constexpr int kStatusTimeout = 1;
 // Pairs (of the 16 in each 32-column chunk of an S row) whose exponentials are computed by
-// the FMA-pipe polynomial instead of MUFU (0: none; the extra instructions slowed the
-// MMA-issuing warp that shares their SM sub-partition more than the MUFU time they saved).
+// the FMA-pipe polynomial instead of MUFU: pairs 0, 3, 6, 9 and 12, 10 of every 32
+// exponentials.  Measured per-CTA cycles against MUFU alone: -10% (prefix 8192, 257 rows),
+// -14% (prefix 131072); 3, 4, 6 and 8 pairs were slower than 5.  (With the MMAs issued from a
+// lone lane this offload did not pay: the FMA-bound softmax warps starved that lane.)
 #ifndef DDT_POLY_PAIRS
-#define DDT_POLY_PAIRS 0u
+#define DDT_POLY_PAIRS 0x1249u
 #endif
 constexpr uint32_t kPolyPairs = DDT_POLY_PAIRS;
 // TMEM column of query tile q's S/P region and O accumulator
@@ -337,22 +339,32 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // (measured ~180 cycles of idle tensor pipe per wait with a single issuer).  With one
       // issuer per tile every wait falls where that tile's previous MMAs are complete anyway
       // (P_q(j) ready implies S_q(j) done), while the other tile's MMAs keep the pipe busy.
+      // The whole warp runs the loop (uniform control flow, warp-collective waits) and one
+      // elected lane issues: a lone lane in a divergent branch issued one MMA per ~130
+      // cycles next to FMA-bound softmax warps on its sub-partition (measured), against
+      // the pipe's 64.
       const int q = warp == 1 ? 0 : 1;
-      if (lane == 0 && total > 0) {
+      if (total > 0) {
         // descriptor low words of the Q, K and V tiles; every MMA adds a constant to them
         constexpr uint32_t kDescHi = tc::desc_sw128_hi(1024);
         const uint32_t a_q = tc::desc_sw128_lo(tc::smem_u32(sQ), 16) + q * (kTileBytes >> 4);
         const uint32_t k_lo = tc::desc_sw128_lo(tc::smem_u32(sK), 16);
         const uint32_t v_lo = tc::desc_sw128_lo(tc::smem_u32(sV), kHalfBytes);
         const uint32_t d_s = tmem + col_s(q), d_o = tmem + col_o(q);
-        // S_q = Q_q K^T of CTA tile jg into the S region of query tile q
-        auto issue_s = [&](int jg) {
+        volatile uint32_t* my_turns = &bars.issued[q];
+        const volatile uint32_t* other_turns = &bars.issued[q ^ 1];
+        // S_q = Q_q K^T of CTA tile jg into the S region of query tile q; the block's turn
+        // count `turn` is published right after its last MMA.  (Publishing it after half of
+        // the S MMAs, so the other issuer's block would queue behind this one, measured
+        // 5% slower: the two softmax warpgroups drift into each other.)
+        auto issue_s = [&](int jg, uint32_t turn) {
           const uint32_t b = k_lo + (jg % kStages) * (kTileBytes >> 4);
           tc::mma_bf16_ss_w<0>(d_s, a_q, b, kDescHi, kIdescS);
 #pragma unroll
           for (int kk = 1; kk < kHeadDim / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
             tc::mma_bf16_ss_w<1>(d_s, a_q + off, b + off, kDescHi, kIdescS);
+            if (kk == kHeadDim / 16 - 1) *my_turns = turn;
           }
           tc::mma_commit(&bars.s_full[q]);
         };
@@ -373,15 +385,17 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // would wait for this thread's MMAs in flight, and the turns order only the issue
         // of the two tiles' MMAs, no data.  Blocks per item: S of its first tile, then one
         // per tile (P V(j) + S(j + 1)); `base` counts the blocks of earlier items.
-        volatile uint32_t* my_turns = &bars.issued[q];
-        const volatile uint32_t* other_turns = &bars.issued[q ^ 1];
         auto wait_turn = [&](uint32_t target) {
-          const uint64_t t0 = global_timer_ns();
-          for (uint32_t it = 0; *other_turns < target; ++it) {
-            if ((it & 255u) == 255u && (*abort_flag || global_timer_ns() - t0 > kTimeoutNs))
-              return false;
+          uint64_t t0 = 0;
+          for (uint32_t it = 0;; ++it) {
+            if (__all_sync(DDT_FULL_MASK, *other_turns >= target)) return true;
+            if ((it & 255u) == 255u) {
+              const uint64_t now = global_timer_ns();
+              if (t0 == 0) t0 = now;
+              if (__any_sync(DDT_FULL_MASK, *abort_flag != 0 || now - t0 > kTimeoutNs))
+                return false;
+            }
           }
-          return true;
         };
         // stage releases (k_empty / v_empty count one commit per issuer) are committed
         // only where the producer will wait for them
@@ -391,49 +405,59 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int i = 0; ok && i < n_items; ++i) {
           int u, t0, nt, sl;
           item(i, u, t0, nt, sl);
-          if (!(ok = tc::mbar_wait(&bars.q_full, i & 1, abort_flag, kTimeoutNs))) break;
-          if (!(ok = tc::mbar_wait(&bars.k_full[J % kStages], (J / kStages) & 1, abort_flag,
-                                   kTimeoutNs)))
+          if (!(ok = tc::mbar_wait_warp(&bars.q_full, i & 1, abort_flag, kTimeoutNs))) break;
+          if (!(ok = tc::mbar_wait_warp(&bars.k_full[J % kStages], (J / kStages) & 1, abort_flag,
+                                        kTimeoutNs)))
             break;
           if (!(ok = wait_turn(q == 0 ? base : base + 1))) break;
           tc::tc_fence_after();
-          issue_s(J);
-          if (J + kStages < total) tc::mma_commit(&bars.k_empty[J % kStages]);
-          *my_turns = base + 1;
+          if (tc::elect_one()) {
+            issue_s(J, base + 1);
+            if (J + kStages < total) tc::mma_commit(&bars.k_empty[J % kStages]);
+          }
+          __syncwarp();
           for (int j = 0; j < nt; ++j) {
             const int jg = J + j;
             const int st = jg % kStages;
             const int sn = (jg + 1) % kStages;
             const bool more = j + 1 < nt;
             // K / V of the tile landed long before P_q(j): waited first, while the softmax runs
-            if (!(ok = tc::mbar_wait(&bars.v_full[st], (jg / kStages) & 1, abort_flag, kTimeoutNs)))
+            if (!(ok = tc::mbar_wait_warp(&bars.v_full[st], (jg / kStages) & 1, abort_flag,
+                                          kTimeoutNs)))
               break;
-            if (more && !(ok = tc::mbar_wait(&bars.k_full[sn], ((jg + 1) / kStages) & 1,
-                                             abort_flag, kTimeoutNs)))
+            if (more && !(ok = tc::mbar_wait_warp(&bars.k_full[sn], ((jg + 1) / kStages) & 1,
+                                                  abort_flag, kTimeoutNs)))
               break;
-            if (!(ok = tc::mbar_wait(&bars.p_half[q], jg & 1, abort_flag, kTimeoutNs))) break;
+            if (!(ok = tc::mbar_wait_warp(&bars.p_half[q], jg & 1, abort_flag, kTimeoutNs))) break;
             if (!(ok = wait_turn(q == 0 ? base + j + 1 : base + j + 2))) break;
             tc::tc_fence_after();
-            issue_pv(jg, j, 0);
-            if (!(ok = tc::mbar_wait(&bars.p_full[q], jg & 1, abort_flag, kTimeoutNs))) break;
+            if (tc::elect_one()) issue_pv(jg, j, 0);
+            __syncwarp();
+            if (!(ok = tc::mbar_wait_warp(&bars.p_full[q], jg & 1, abort_flag, kTimeoutNs))) break;
             tc::tc_fence_after();
-            issue_pv(jg, j, 1);
-            if (jg + kStages < total) tc::mma_commit(&bars.v_empty[st]);
-            if (more) {
-              issue_s(jg + 1);  // reuses S_q / P_q: runs after the P V MMA above
-              if (jg + 1 + kStages < total) tc::mma_commit(&bars.k_empty[sn]);
+            if (tc::elect_one()) {
+              issue_pv(jg, j, 1);
+              if (jg + kStages < total) tc::mma_commit(&bars.v_empty[st]);
+              if (more) {
+                issue_s(jg + 1, base + j + 2);  // reuses S_q / P_q: runs after the P V above
+                if (jg + 1 + kStages < total) tc::mma_commit(&bars.k_empty[sn]);
+              } else {
+                *my_turns = base + j + 2;
+              }
             }
-            *my_turns = base + j + 2;
+            __syncwarp();
           }
           // the item's S MMAs are all issued: Q may be replaced once they are done
-          if (ok && i + 1 < n_items) tc::mma_commit(&bars.q_empty);
+          if (ok && i + 1 < n_items && tc::elect_one()) tc::mma_commit(&bars.q_empty);
+          __syncwarp();
           base += nt + 1;
           J += nt;
         }
         if (!ok) {
-          raise_abort(bars, p.status);
-          // wait for every MMA this thread issued before TMEM is released
-          tc::mma_commit(&bars.mma_done[q]);
+          if (lane == 0) raise_abort(bars, p.status);
+          // wait for every MMA this warp issued before TMEM is released
+          if (tc::elect_one()) tc::mma_commit(&bars.mma_done[q]);
+          __syncwarp();
           tc::mbar_wait_drain(&bars.mma_done[q], 0, kTimeoutNs);
         }
       }
