@@ -87,8 +87,10 @@ struct Params {
   float scale_log2;
   __nv_bfloat16* out;
   long long o_node_stride, o_head_stride;
-  float* o_part;  // [n_splits][n_nodes * q_heads][128]
-  float* m_part;  // [n_splits][n_nodes * q_heads]
+  float* o_part;  // uniform splits: [n_splits][n_nodes * q_heads][128]
+  // balanced parts: O / l of each part in bf16, [slot][dim / 8][unit row][8]
+  __nv_bfloat16* o_slot;
+  float* m_part;  // [n_splits][n_nodes * q_heads] or [slot][unit row]
   float* l_part;
   int partial;
   int* status;
@@ -97,9 +99,9 @@ struct Params {
 // Balanced schedule ("stream-K" over the key tiles): the flattened (work unit, key tile)
 // space is cut into equal contiguous ranges, one per CTA, so every SM runs the same number of
 // tiles whatever the number of work units.  A CTA's range may cover the end of one unit and
-// the start of the next: each such piece is one item, whose fp32 partial goes to its own
-// slot; the parts of a unit have consecutive slots, starting at unit_slot[unit].  Built on
-// the host and passed by value (kernel parameter space).
+// the start of the next: each such piece is one item, whose partial (O / l in bf16, m and l
+// in fp32) goes to its own slot; the parts of a unit have consecutive slots, starting at
+// unit_slot[unit].  Built on the host and passed by value (kernel parameter space).
 constexpr int kMaxCtas = 148;
 constexpr int kMaxItems = 320;
 constexpr int kMaxUnits = 256;
@@ -614,10 +616,14 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       if (have) tc::tc_fence_after();
       // ---- epilogue of the item ----------------------------------------------------------
       if (p.partial && p.balanced) {
-        // the part's own slot, laid out [dim / 4][unit row][4]: the 32 lanes of a warp
-        // (consecutive rows) store 512 contiguous bytes per instruction
+        // the part's own slot: O / l in bf16 (a convex combination of V rows, so in V's
+        // range), laid out [dim / 8][unit row][8]: the 32 lanes of a warp (consecutive rows)
+        // store 512 contiguous bytes per instruction.  Half the bytes of fp32 O for the
+        // merge to read; the merge weights each part by 2^(m - M) l.
         const int lr = q * kBlockM + r;
-        float* op = p.o_part + static_cast<long long>(slot) * kRowsPerCta * kHeadDim + lr * 4;
+        const float inv = (have && l > 0.f) ? 1.f / l : 0.f;
+        __nv_bfloat16* op =
+            p.o_slot + static_cast<long long>(slot) * kRowsPerCta * kHeadDim + lr * 8;
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
           if (have) {
@@ -629,10 +635,14 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
           if (valid) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 4)
-              *reinterpret_cast<float4*>(op + ((c * 32 + e) / 4) * kRowsPerCta * 4) =
-                  make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
-                              __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
+            for (int e = 0; e < 32; e += 8) {
+              uint4 v;
+              v.x = tc::pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+              v.y = tc::pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+              v.z = tc::pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+              v.w = tc::pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+              *reinterpret_cast<uint4*>(op + ((c * 32 + e) / 8) * kRowsPerCta * 8) = v;
+            }
           }
         }
         if (valid) {
@@ -832,9 +842,9 @@ __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __r
 
 // ---- merge of balanced parts -------------------------------------------------------------
 // One warp per (work unit, 32 consecutive unit rows, 8 of the 128 dims), one lane per row;
-// the unit's parts are slots [unit_slot[u], unit_slot[u + 1]), each holding that part's O
-// laid out [dim / 4][unit row][4] and its m, l per unit row, so a warp's loads are 512 (O)
-// or 128 (m, l) contiguous bytes.  One pass over the parts in batches of 8 with every load
+// the unit's parts are slots [unit_slot[u], unit_slot[u + 1]), each holding that part's
+// O / l in bf16 laid out [dim / 8][unit row][8] and its m, l per unit row, so a warp's loads
+// are 512 (O) or 128 (m, l) contiguous bytes.  Part i has weight 2^(m_i - M) l_i.  One pass over the parts in batches of 8 with every load
 // of a batch in flight and an online maximum (earlier batches rescaled when it grows): one
 // L2 round trip for up to 8 parts.
 // kFp32: write the merged partial (O un-normalised, m, l) in (node, q head) row order, the
@@ -843,7 +853,7 @@ constexpr int kMergeBatch = 8;
 constexpr int kMergeDims = 8;
 template <bool kFp32>
 __global__ void __launch_bounds__(256)
-merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ m_parts,
+merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __restrict__ m_parts,
                    const float* __restrict__ l_parts, const __grid_constant__ SlotTable tab,
                    const Params p, __nv_bfloat16* __restrict__ out, long long o_node_stride,
                    long long o_head_stride, float* __restrict__ o_merged,
@@ -860,22 +870,22 @@ merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ 
   if (R >= rows) return;
   const int s0 = tab.unit_slot[u], n = tab.unit_slot[u + 1] - s0;
   float M = -INFINITY, L = 0.f;
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+  float a[kMergeDims];
+#pragma unroll
+  for (int d = 0; d < kMergeDims; ++d) a[d] = 0.f;
   for (int k0 = 0; k0 < n; k0 += kMergeBatch) {
     float mv[kMergeBatch], lv[kMergeBatch];
-    float4 ov[kMergeBatch][2];
+    uint4 ov[kMergeBatch];
 #pragma unroll
     for (int k = 0; k < kMergeBatch; ++k) {
       const bool in = k0 + k < n;
       const long long sl = s0 + k0 + (in ? k : 0);
       const long long pi = sl * kRowsPerCta + lr;
-      const float* op = o_parts + sl * kRowsPerCta * kHeadDim +
-                        static_cast<long long>(dg * 2) * kRowsPerCta * 4 + lr * 4;
+      const __nv_bfloat16* op = o_parts + sl * kRowsPerCta * kHeadDim +
+                                static_cast<long long>(dg) * kRowsPerCta * 8 + lr * 8;
       mv[k] = in ? m_parts[pi] : -INFINITY;
       lv[k] = in ? l_parts[pi] : 0.f;
-      ov[k][0] = in ? *reinterpret_cast<const float4*>(op) : make_float4(0.f, 0.f, 0.f, 0.f);
-      ov[k][1] = in ? *reinterpret_cast<const float4*>(op + kRowsPerCta * 4)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      ov[k] = in ? *reinterpret_cast<const uint4*>(op) : make_uint4(0u, 0u, 0u, 0u);
     }
     float Mb = M;
 #pragma unroll
@@ -884,14 +894,18 @@ merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ 
     const float cs = M == -INFINITY ? 0.f : exp2f(M - Mb);
     M = Mb;
     L *= cs;
-    a.x *= cs; a.y *= cs; a.z *= cs; a.w *= cs;
-    b.x *= cs; b.y *= cs; b.z *= cs; b.w *= cs;
+#pragma unroll
+    for (int d = 0; d < kMergeDims; ++d) a[d] *= cs;
 #pragma unroll
     for (int k = 0; k < kMergeBatch; ++k) {
-      const float w = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - M);
-      L += w * lv[k];
-      a.x += w * ov[k][0].x; a.y += w * ov[k][0].y; a.z += w * ov[k][0].z; a.w += w * ov[k][0].w;
-      b.x += w * ov[k][1].x; b.y += w * ov[k][1].y; b.z += w * ov[k][1].z; b.w += w * ov[k][1].w;
+      const float w = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - M) * lv[k];
+      L += w;
+      const uint32_t wd[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
+#pragma unroll
+      for (int d = 0; d < 4; ++d) {
+        a[2 * d] += w * __uint_as_float(wd[d] << 16);
+        a[2 * d + 1] += w * __uint_as_float(wd[d] & 0xffff0000u);
+      }
     }
   }
   const int h = u / p.n_pairs;
@@ -899,8 +913,8 @@ merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ 
   if constexpr (kFp32) {
     const long long row = node * p.q_heads + qh;
     float* o = o_merged + row * kHeadDim + dg * kMergeDims;
-    *reinterpret_cast<float4*>(o) = a;
-    *reinterpret_cast<float4*>(o + 4) = b;
+    *reinterpret_cast<float4*>(o) = make_float4(a[0], a[1], a[2], a[3]);
+    *reinterpret_cast<float4*>(o + 4) = make_float4(a[4], a[5], a[6], a[7]);
     if (dg == 0) {
       m_merged[row] = M;
       l_merged[row] = L;
@@ -908,10 +922,10 @@ merge_slots_kernel(const float* __restrict__ o_parts, const float* __restrict__ 
   } else {
     const float inv = L > 0.f ? 1.f / L : 0.f;
     uint4 v;
-    v.x = tc::pack_bf16x2(a.x * inv, a.y * inv);
-    v.y = tc::pack_bf16x2(a.z * inv, a.w * inv);
-    v.z = tc::pack_bf16x2(b.x * inv, b.y * inv);
-    v.w = tc::pack_bf16x2(b.z * inv, b.w * inv);
+    v.x = tc::pack_bf16x2(a[0] * inv, a[1] * inv);
+    v.y = tc::pack_bf16x2(a[2] * inv, a[3] * inv);
+    v.z = tc::pack_bf16x2(a[4] * inv, a[5] * inv);
+    v.w = tc::pack_bf16x2(a[6] * inv, a[7] * inv);
     *reinterpret_cast<uint4*>(out + node * o_node_stride + qh * o_head_stride + dg * kMergeDims) = v;
   }
 }
@@ -1014,6 +1028,7 @@ inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_he
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = nullptr;
   p.o_part = p.m_part = p.l_part = nullptr;
+  p.o_slot = nullptr;
   p.partial = 0;
   p.balanced = 0;
   p.n_splits = 1;
@@ -1089,9 +1104,24 @@ inline size_t part_bytes(int64_t rows, int64_t splits) {
   return static_cast<size_t>(splits) * rows * (kHeadDim + 2) * sizeof(float) + 256;
 }
 
-// bytes of `parts` balanced partials of 256 rows each (O, m, l in fp32)
+// bytes of `parts` balanced partials of 256 rows each (O / l in bf16, m and l in fp32)
 inline size_t slot_bytes(int64_t parts) {
-  return static_cast<size_t>(parts) * kRowsPerCta * (kHeadDim + 2) * sizeof(float) + 256;
+  return static_cast<size_t>(parts) * kRowsPerCta *
+             (kHeadDim * sizeof(__nv_bfloat16) + 2 * sizeof(float)) +
+         256;
+}
+// workspace carve-up of balanced parts: O slots, then m, then l (16-byte aligned)
+struct SlotPtrs {
+  __nv_bfloat16* o;
+  float* m;
+  float* l;
+};
+inline SlotPtrs slot_ptrs(void* ws, int64_t parts) {
+  SlotPtrs sp;
+  sp.o = static_cast<__nv_bfloat16*>(ws);
+  sp.m = reinterpret_cast<float*>(sp.o + static_cast<size_t>(parts) * kRowsPerCta * kHeadDim);
+  sp.l = sp.m + static_cast<size_t>(parts) * kRowsPerCta;
+  return sp;
 }
 
 inline int launch(const Launch& L, int64_t kv_heads, cudaStream_t st) {
@@ -1164,19 +1194,17 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
     const size_t need = attn::slot_bytes(L.n_parts);
     if (!workspace || workspace_bytes < need) return DDT_ERR_WORKSPACE;
     if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
-    float* o_part = static_cast<float*>(workspace);
-    float* m_part = o_part + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta * attn::kHeadDim;
-    float* l_part = m_part + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta;
-    L.p.o_part = o_part;
-    L.p.m_part = m_part;
-    L.p.l_part = l_part;
+    const attn::SlotPtrs sp = attn::slot_ptrs(workspace, L.n_parts);
+    L.p.o_slot = sp.o;
+    L.p.m_part = sp.m;
+    L.p.l_part = sp.l;
     L.p.partial = 1;
     rc = attn::launch(L, kv_heads, st);
     if (rc) return rc;
     const int wpb = 8;
     const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
     attn::merge_slots_kernel<false><<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
-        o_part, m_part, l_part, L.slots, L.p, static_cast<__nv_bfloat16*>(out), o_node_stride,
+        sp.o, sp.m, sp.l, L.slots, L.p, static_cast<__nv_bfloat16*>(out), o_node_stride,
         o_head_stride, nullptr, nullptr, nullptr);
     return launch_status();
   }
@@ -1275,18 +1303,16 @@ extern "C" int ddt_tree_attn_partial_merged(
   const int wpb = 8;
   if (attn::kv_fits_l2(local, kv_heads) && attn::build_balanced(L, units)) {
     if (workspace_bytes < attn::slot_bytes(L.n_parts)) return DDT_ERR_WORKSPACE;
-    float* op = static_cast<float*>(workspace);
-    float* mp = op + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta * attn::kHeadDim;
-    float* lp = mp + static_cast<size_t>(L.n_parts) * attn::kRowsPerCta;
-    L.p.o_part = op;
-    L.p.m_part = mp;
-    L.p.l_part = lp;
+    const attn::SlotPtrs sp = attn::slot_ptrs(workspace, L.n_parts);
+    L.p.o_slot = sp.o;
+    L.p.m_part = sp.m;
+    L.p.l_part = sp.l;
     L.p.partial = 1;
     rc = attn::launch(L, kv_heads, st);
     if (rc) return rc;
     const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
     attn::merge_slots_kernel<true><<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
-        op, mp, lp, L.slots, L.p, nullptr, 0, 0, o_part, m_part, l_part);
+        sp.o, sp.m, sp.l, L.slots, L.p, nullptr, 0, 0, o_part, m_part, l_part);
     return launch_status();
   }
   // large shards (K / V beyond L2), units with no key in this shard, or tables too small:
