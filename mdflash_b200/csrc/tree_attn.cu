@@ -841,70 +841,83 @@ __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __r
 }
 
 // ---- merge of balanced parts -------------------------------------------------------------
-// One warp per (work unit, 32 consecutive unit rows, 8 of the 128 dims), one lane per row;
+// One warp per (work unit, 32 consecutive unit rows, 32 of the 128 dims), one lane per row;
 // the unit's parts are slots [unit_slot[u], unit_slot[u + 1]), each holding that part's
 // O / l in bf16 laid out [dim / 8][unit row][8] and its m, l per unit row, so a warp's loads
-// are 512 (O) or 128 (m, l) contiguous bytes.  Part i has weight 2^(m_i - M) l_i.  One pass over the parts in batches of 8 with every load
-// of a batch in flight and an online maximum (earlier batches rescaled when it grows): one
-// L2 round trip for up to 8 parts.
+// are 512 (O) or 128 (m, l) contiguous bytes.  Part i has weight 2^(m_i - M) l_i, computed
+// once for the lane's 32 dims.  Batches of 4 parts with every load in flight and an online
+// maximum (earlier batches rescaled when it grows).  (One warp per 8 dims with full-precision
+// exp2f issued 2.8 M instructions at the Qwen3-8B verify shape and was instruction-bound:
+// 7.7 us, measured.)
 // kFp32: write the merged partial (O un-normalised, m, l) in (node, q head) row order, the
 // cross-GPU exchange format, instead of the bf16 output.
-constexpr int kMergeBatch = 8;
-constexpr int kMergeDims = 8;
+constexpr int kMergeBatch = 4;
+constexpr int kMergeDims = 32;
+constexpr int kMergeWarps = 4;  // warps per block
 template <bool kFp32>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kMergeWarps * 32)
 merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __restrict__ m_parts,
                    const float* __restrict__ l_parts, const __grid_constant__ SlotTable tab,
                    const Params p, __nv_bfloat16* __restrict__ out, long long o_node_stride,
                    long long o_head_stride, float* __restrict__ o_merged,
                    float* __restrict__ m_merged, float* __restrict__ l_merged) {
   constexpr int kRowGroups = kRowsPerCta / 32, kDimGroups = kHeadDim / kMergeDims;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int gw = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int u = gw / (kRowGroups * kDimGroups);
   if (u >= p.n_pairs * (p.q_heads / p.group)) return;
-  const int rg = (gw / kDimGroups) % kRowGroups, dg = gw % kDimGroups;
+  const int rg = (gw / kDimGroups) % kRowGroups, dq = gw % kDimGroups;
   const int lr = rg * 32 + lane;
   const int R = (u % p.n_pairs) * kRowsPerCta + lr;
   const int rows = p.n_nodes * p.group;
   if (R >= rows) return;
   const int s0 = tab.unit_slot[u], n = tab.unit_slot[u + 1] - s0;
+  // the lane's 32 dims of part slot sl: 4 loads of 8 dims, kRowsPerCta * 8 elements apart
+  const __nv_bfloat16* obase = o_parts + static_cast<long long>(dq) * 4 * kRowsPerCta * 8 + lr * 8;
+  constexpr long long kSlotElems = static_cast<long long>(kRowsPerCta) * kHeadDim;
   float M = -INFINITY, L = 0.f;
   float a[kMergeDims];
 #pragma unroll
   for (int d = 0; d < kMergeDims; ++d) a[d] = 0.f;
   for (int k0 = 0; k0 < n; k0 += kMergeBatch) {
     float mv[kMergeBatch], lv[kMergeBatch];
-    uint4 ov[kMergeBatch];
+    uint4 ov[kMergeBatch][4];
 #pragma unroll
     for (int k = 0; k < kMergeBatch; ++k) {
       const bool in = k0 + k < n;
-      const long long sl = s0 + k0 + (in ? k : 0);
-      const long long pi = sl * kRowsPerCta + lr;
-      const __nv_bfloat16* op = o_parts + sl * kRowsPerCta * kHeadDim +
-                                static_cast<long long>(dg) * kRowsPerCta * 8 + lr * 8;
+      const int sl = s0 + k0 + (in ? k : 0);
+      const int pi = sl * kRowsPerCta + lr;
+      const __nv_bfloat16* op = obase + sl * kSlotElems;
       mv[k] = in ? m_parts[pi] : -INFINITY;
       lv[k] = in ? l_parts[pi] : 0.f;
-      ov[k] = in ? *reinterpret_cast<const uint4*>(op) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int d = 0; d < 4; ++d)
+        ov[k][d] = in ? *reinterpret_cast<const uint4*>(op + d * kRowsPerCta * 8)
+                      : make_uint4(0u, 0u, 0u, 0u);
     }
     float Mb = M;
 #pragma unroll
     for (int k = 0; k < kMergeBatch; ++k) Mb = fmaxf(Mb, mv[k]);
     if (Mb == -INFINITY) continue;
-    const float cs = M == -INFINITY ? 0.f : exp2f(M - Mb);
-    M = Mb;
-    L *= cs;
+    if (Mb > M) {
+      const float cs = M == -INFINITY ? 0.f : tc::ex2_approx(M - Mb);
+      M = Mb;
+      L *= cs;
 #pragma unroll
-    for (int d = 0; d < kMergeDims; ++d) a[d] *= cs;
+      for (int d = 0; d < kMergeDims; ++d) a[d] *= cs;
+    }
 #pragma unroll
     for (int k = 0; k < kMergeBatch; ++k) {
-      const float w = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - M) * lv[k];
+      const float w = mv[k] == -INFINITY ? 0.f : tc::ex2_approx(mv[k] - M) * lv[k];
       L += w;
-      const uint32_t wd[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w};
 #pragma unroll
       for (int d = 0; d < 4; ++d) {
-        a[2 * d] += w * __uint_as_float(wd[d] << 16);
-        a[2 * d + 1] += w * __uint_as_float(wd[d] & 0xffff0000u);
+        const uint32_t wd[4] = {ov[k][d].x, ov[k][d].y, ov[k][d].z, ov[k][d].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          a[d * 8 + 2 * e] = fmaf(w, __uint_as_float(wd[e] << 16), a[d * 8 + 2 * e]);
+          a[d * 8 + 2 * e + 1] = fmaf(w, __uint_as_float(wd[e] & 0xffff0000u), a[d * 8 + 2 * e + 1]);
+        }
       }
     }
   }
@@ -912,21 +925,26 @@ merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __res
   const long long node = R / p.group, qh = h * p.group + R % p.group;
   if constexpr (kFp32) {
     const long long row = node * p.q_heads + qh;
-    float* o = o_merged + row * kHeadDim + dg * kMergeDims;
-    *reinterpret_cast<float4*>(o) = make_float4(a[0], a[1], a[2], a[3]);
-    *reinterpret_cast<float4*>(o + 4) = make_float4(a[4], a[5], a[6], a[7]);
-    if (dg == 0) {
+    float* o = o_merged + row * kHeadDim + dq * kMergeDims;
+#pragma unroll
+    for (int d = 0; d < kMergeDims; d += 4)
+      *reinterpret_cast<float4*>(o + d) = make_float4(a[d], a[d + 1], a[d + 2], a[d + 3]);
+    if (dq == 0) {
       m_merged[row] = M;
       l_merged[row] = L;
     }
   } else {
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    uint4 v;
-    v.x = tc::pack_bf16x2(a[0] * inv, a[1] * inv);
-    v.y = tc::pack_bf16x2(a[2] * inv, a[3] * inv);
-    v.z = tc::pack_bf16x2(a[4] * inv, a[5] * inv);
-    v.w = tc::pack_bf16x2(a[6] * inv, a[7] * inv);
-    *reinterpret_cast<uint4*>(out + node * o_node_stride + qh * o_head_stride + dg * kMergeDims) = v;
+    __nv_bfloat16* o = out + node * o_node_stride + qh * o_head_stride + dq * kMergeDims;
+#pragma unroll
+    for (int d = 0; d < kMergeDims; d += 8) {
+      uint4 v;
+      v.x = tc::pack_bf16x2(a[d] * inv, a[d + 1] * inv);
+      v.y = tc::pack_bf16x2(a[d + 2] * inv, a[d + 3] * inv);
+      v.z = tc::pack_bf16x2(a[d + 4] * inv, a[d + 5] * inv);
+      v.w = tc::pack_bf16x2(a[d + 6] * inv, a[d + 7] * inv);
+      *reinterpret_cast<uint4*>(o + d) = v;
+    }
   }
 }
 
@@ -1201,7 +1219,7 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
     L.p.partial = 1;
     rc = attn::launch(L, kv_heads, st);
     if (rc) return rc;
-    const int wpb = 8;
+    const int wpb = attn::kMergeWarps;
     const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
     attn::merge_slots_kernel<false><<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
         sp.o, sp.m, sp.l, L.slots, L.p, static_cast<__nv_bfloat16*>(out), o_node_stride,
@@ -1311,7 +1329,9 @@ extern "C" int ddt_tree_attn_partial_merged(
     rc = attn::launch(L, kv_heads, st);
     if (rc) return rc;
     const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
-    attn::merge_slots_kernel<true><<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+    attn::merge_slots_kernel<true><<<static_cast<unsigned>((warps + attn::kMergeWarps - 1) /
+                                                          attn::kMergeWarps),
+                                    attn::kMergeWarps * 32, 0, st>>>(
         sp.o, sp.m, sp.l, L.slots, L.p, nullptr, 0, 0, o_part, m_part, l_part);
     return launch_status();
   }
