@@ -841,21 +841,23 @@ __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __r
 }
 
 // ---- merge of balanced parts -------------------------------------------------------------
-// One warp per (work unit, 32 consecutive unit rows, 32 of the 128 dims), one lane per row;
+// One warp per (work unit, 32 consecutive unit rows, 16 of the 128 dims), one lane per row;
 // the unit's parts are slots [unit_slot[u], unit_slot[u + 1]), each holding that part's
 // O / l in bf16 laid out [dim / 8][unit row][8] and its m, l per unit row, so a warp's loads
 // are 512 (O) or 128 (m, l) contiguous bytes.  Part i has weight 2^(m_i - M) l_i, computed
-// once for the lane's 32 dims.  Batches of 4 parts with every load in flight and an online
-// maximum (earlier batches rescaled when it grows).  (One warp per 8 dims with full-precision
-// exp2f issued 2.8 M instructions at the Qwen3-8B verify shape and was instruction-bound:
-// 7.7 us, measured.)
+// once for the lane's 16 dims.  Batches of 6 parts with every load in flight and an online
+// maximum (earlier batches rescaled when it grows): one L2 round trip for the ~5 parts of a
+// unit at the Qwen3-8B verify shape.  96 registers and 2-warp blocks keep the grid one wave.
+// (One warp per 8 dims with full-precision exp2f issued 2.8 M instructions at that shape and
+// was instruction-bound: 7.7 us, measured; 32 dims per warp in batches of 4 took 5.2 us.)
 // kFp32: write the merged partial (O un-normalised, m, l) in (node, q head) row order, the
 // cross-GPU exchange format, instead of the bf16 output.
-constexpr int kMergeBatch = 4;
-constexpr int kMergeDims = 32;
-constexpr int kMergeWarps = 4;  // warps per block
+constexpr int kMergeBatch = 6;
+constexpr int kMergeDims = 16;
+constexpr int kMergeVecs = kMergeDims / 8;  // 16-byte loads per part and lane
+constexpr int kMergeWarps = 2;              // warps per block
 template <bool kFp32>
-__global__ void __launch_bounds__(kMergeWarps * 32)
+__global__ void __launch_bounds__(kMergeWarps * 32, 9)
 merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __restrict__ m_parts,
                    const float* __restrict__ l_parts, const __grid_constant__ SlotTable tab,
                    const Params p, __nv_bfloat16* __restrict__ out, long long o_node_stride,
@@ -872,8 +874,9 @@ merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __res
   const int rows = p.n_nodes * p.group;
   if (R >= rows) return;
   const int s0 = tab.unit_slot[u], n = tab.unit_slot[u + 1] - s0;
-  // the lane's 32 dims of part slot sl: 4 loads of 8 dims, kRowsPerCta * 8 elements apart
-  const __nv_bfloat16* obase = o_parts + static_cast<long long>(dq) * 4 * kRowsPerCta * 8 + lr * 8;
+  // the lane's dims of part slot sl: loads of 8 dims, kRowsPerCta * 8 elements apart
+  const __nv_bfloat16* obase =
+      o_parts + static_cast<long long>(dq) * kMergeVecs * kRowsPerCta * 8 + lr * 8;
   constexpr long long kSlotElems = static_cast<long long>(kRowsPerCta) * kHeadDim;
   float M = -INFINITY, L = 0.f;
   float a[kMergeDims];
@@ -881,7 +884,7 @@ merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __res
   for (int d = 0; d < kMergeDims; ++d) a[d] = 0.f;
   for (int k0 = 0; k0 < n; k0 += kMergeBatch) {
     float mv[kMergeBatch], lv[kMergeBatch];
-    uint4 ov[kMergeBatch][4];
+    uint4 ov[kMergeBatch][kMergeVecs];
 #pragma unroll
     for (int k = 0; k < kMergeBatch; ++k) {
       const bool in = k0 + k < n;
@@ -891,7 +894,7 @@ merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __res
       mv[k] = in ? m_parts[pi] : -INFINITY;
       lv[k] = in ? l_parts[pi] : 0.f;
 #pragma unroll
-      for (int d = 0; d < 4; ++d)
+      for (int d = 0; d < kMergeVecs; ++d)
         ov[k][d] = in ? *reinterpret_cast<const uint4*>(op + d * kRowsPerCta * 8)
                       : make_uint4(0u, 0u, 0u, 0u);
     }
@@ -911,7 +914,7 @@ merge_slots_kernel(const __nv_bfloat16* __restrict__ o_parts, const float* __res
       const float w = mv[k] == -INFINITY ? 0.f : tc::ex2_approx(mv[k] - M) * lv[k];
       L += w;
 #pragma unroll
-      for (int d = 0; d < 4; ++d) {
+      for (int d = 0; d < kMergeVecs; ++d) {
         const uint32_t wd[4] = {ov[k][d].x, ov[k][d].y, ov[k][d].z, ov[k][d].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
