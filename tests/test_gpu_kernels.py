@@ -219,6 +219,8 @@ def test_tree_attention_matches_reference(golden, cuda_device, spec, splits):
     (16, 8, 512, 33, 2),       # Qwen3-0.6B-shaped verify
     (32, 8, 1000, 513, 3),     # prefix not a tile multiple, many tree tiles
     (8, 8, 300, 100, 4),       # no GQA sharing (group 1)
+    (8, 8, 2048, 40, 5),       # 8 units x 17 key tiles over 136 CTAs: 16 parts per unit,
+                               # merged in three batches
 ])
 def test_tree_attention_shapes(cuda_device, hq, hkv, past, n, seed):
     g = torch.Generator().manual_seed(seed)
