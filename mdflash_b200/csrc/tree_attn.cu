@@ -1057,26 +1057,38 @@ inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_he
   return DDT_OK;
 }
 
-// Balanced schedule: the flattened (unit, key tile) range cut into G equal pieces (CTA c:
-// [c W / G, (c + 1) W / G)).  Each unit is preceded by kItemCost virtual tiles, the cost of
-// starting an item (Q load, pipeline refill, the partial's epilogue), so a CTA whose range
-// reaches into a second unit gets correspondingly fewer real tiles.  Returns false (and
-// leaves the launch on uniform splits) when a limit of the tables is exceeded or a unit has
-// no key tile.
-#ifndef DDT_ITEM_COST
-#define DDT_ITEM_COST 1
-#endif
-constexpr int kItemCost = DDT_ITEM_COST;
+// Balanced schedule: the flattened (unit, key tile) cost range cut into G equal pieces (CTA
+// c: [c W / G, (c + 1) W / G)).  Costs are in eighths of a key tile and follow per-CTA cycle
+// counts measured at the Qwen3-8B verify shape, fitted as cycles = 2494 per key tile + 1527
+// per tile that ends past the prefix (the tree window: masked, for some rows, in the
+// softmax) + 4918 per item (Q load, pipeline refill, the partial's epilogue):
+//   kCostTile = 8, kCostMasked = 13 (1.6 tiles), kCostItem = 16 (2 tiles, paid at the start
+//   of each unit's range, so a CTA whose range reaches into a second unit gets
+//   correspondingly fewer tiles).
+// A CTA's cost range maps to whole tiles of a unit by the unit's cumulative cost (a tile goes
+// to the CTA whose range holds the tile's start); a CTA may get no tile of a unit it touches,
+// and then has no item for it.  Returns false (and leaves the launch on uniform splits) when
+// a limit of the tables is exceeded or a unit has no key tile.
+constexpr int kCostTile = 8;
+constexpr int kCostMasked = 13;
+constexpr int kCostItem = 16;
 
 inline bool build_balanced(Launch& L, int64_t units) {
   Params& p = L.p;
   if (units <= 0 || units > kMaxUnits) return false;
   int64_t W = 0, real = 0;
-  int ntot[kMaxUnits];
+  int ntot[kMaxUnits], nfull[kMaxUnits];
+  int64_t cost[kMaxUnits];
+  // tiles of a unit that end at or before the prefix end (unmasked in the tree window sense)
+  int64_t before = (static_cast<int64_t>(p.past_len) - p.key_lo) / kBlockN;
+  if (p.past_len < p.key_lo) before = 0;
   for (int u = 0; u < units; ++u) {
     ntot[u] = unit_geo(p, u).ntot;
     if (ntot[u] <= 0 || ntot[u] > 0xffff) return false;
-    W += kItemCost + ntot[u];
+    nfull[u] = static_cast<int>(before < ntot[u] ? before : ntot[u]);
+    cost[u] = static_cast<int64_t>(nfull[u]) * kCostTile +
+              static_cast<int64_t>(ntot[u] - nfull[u]) * kCostMasked;
+    W += kCostItem + cost[u];
     real += ntot[u];
   }
   const int64_t G = real < kMaxCtas ? real : kMaxCtas;
@@ -1084,23 +1096,33 @@ inline bool build_balanced(Launch& L, int64_t units) {
   // items in unit order (slots of a unit consecutive); CTA lists follow since units and
   // CTAs both advance monotonically along the flattened range
   int n = 0;
-  int64_t T = 0;  // first real tile of unit u in the flattened range
+  int64_t T = 0;  // cost position of unit u's first tile
   int cur_cta = -1;
   for (int u = 0; u < units; ++u) {
-    T += kItemCost;
+    T += kCostItem;
     L.slots.unit_slot[u] = static_cast<uint16_t>(n);
-    const int64_t cf = cta_of(T), cl = cta_of(T + ntot[u] - 1);
+    // tile boundary at cost offset x of this unit (the first tile not started before x)
+    const int64_t fcost = static_cast<int64_t>(nfull[u]) * kCostTile;
+    auto tile_at = [&](int64_t x) -> int64_t {
+      if (x >= cost[u]) return ntot[u];
+      if (x <= fcost) return (x + kCostTile - 1) / kCostTile;
+      const int64_t t = nfull[u] + (x - fcost + kCostMasked - 1) / kCostMasked;
+      return t < ntot[u] ? t : ntot[u];
+    };
+    const int64_t cf = cta_of(T), cl = cta_of(T + cost[u] - 1);
     if (cl - cf + 1 > kMaxPartsPerUnit) return false;
     for (int64_t c = cf; c <= cl; ++c) {
-      if (n >= kMaxItems) return false;
       const int64_t b = c * W / G, e = (c + 1) * W / G;
-      const int64_t lo = b > T ? b : T, hi = e < T + ntot[u] ? e : T + ntot[u];
+      const int64_t lo = b > T ? b : T, hi = e < T + cost[u] ? e : T + cost[u];
+      const int64_t tlo = tile_at(lo - T), thi = tile_at(hi - T);
+      if (thi <= tlo) continue;
+      if (n >= kMaxItems) return false;
       while (cur_cta < c) L.sched.cta_first[++cur_cta] = static_cast<uint16_t>(n);
-      L.sched.items[n] = SchedItem{static_cast<uint16_t>(u), static_cast<uint16_t>(lo - T),
-                                   static_cast<uint16_t>(hi - lo), static_cast<uint16_t>(n)};
+      L.sched.items[n] = SchedItem{static_cast<uint16_t>(u), static_cast<uint16_t>(tlo),
+                                   static_cast<uint16_t>(thi - tlo), static_cast<uint16_t>(n)};
       ++n;
     }
-    T += ntot[u];
+    T += cost[u];
   }
   while (cur_cta < G) L.sched.cta_first[++cur_cta] = static_cast<uint16_t>(n);
   L.slots.unit_slot[units] = static_cast<uint16_t>(n);
