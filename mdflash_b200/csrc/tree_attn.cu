@@ -1280,6 +1280,65 @@ extern "C" int64_t ddt_tree_attn_partial_splits(int64_t n_nodes, int64_t key_cou
   return attn::pick_splits(kv_heads * pairs, (key_count + attn::kBlockN - 1) / attn::kBlockN);
 }
 
+// The launch plan ddt_tree_attn would use for these sizes, computed on the host only, and a
+// check of the balanced table: every key tile of every work unit in exactly one item, the
+// items of a unit in key order with consecutive slots, every item in one CTA's list.
+extern "C" int ddt_tree_attn_plan(int64_t n_nodes, int64_t past_length, int64_t q_heads,
+                                  int64_t kv_heads, int64_t kv_splits, int64_t* plan) {
+  if (!plan || n_nodes <= 0 || past_length < 0 || q_heads <= 0 || kv_heads <= 0 ||
+      q_heads % kv_heads || kv_splits < 0)
+    return DDT_ERR_INVALID;
+  const int64_t group = q_heads / kv_heads;
+  if (group > attn::kBlockM || attn::kBlockM % group) return DDT_ERR_CAPACITY;
+  const int64_t S = past_length + n_nodes;
+  if (S >= (int64_t(1) << 31)) return DDT_ERR_CAPACITY;
+  attn::Launch L;
+  attn::Params& p = L.p;
+  p.n_nodes = static_cast<int>(n_nodes);
+  p.past_len = static_cast<int>(past_length);
+  p.group = static_cast<int>(group);
+  p.q_heads = static_cast<int>(q_heads);
+  p.n_pairs = static_cast<int>((n_nodes * group + attn::kRowsPerCta - 1) / attn::kRowsPerCta);
+  p.key_base = p.key_lo = 0;
+  p.key_hi = static_cast<int>(S);
+  p.balanced = 0;
+  const int64_t units = kv_heads * p.n_pairs;
+  const int64_t kv_tiles = (S + attn::kBlockN - 1) / attn::kBlockN;
+  const int splits = kv_splits > 0 ? static_cast<int>(kv_splits) : attn::pick_splits(units, kv_tiles);
+  if (splits > 64) return DDT_ERR_CAPACITY;
+  if (kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::kv_fits_l2(S, kv_heads) &&
+      attn::build_balanced(L, units)) {
+    int64_t max_items = 0;
+    for (int c = 0; c < L.grid; ++c) {
+      const int64_t k = L.sched.cta_first[c + 1] - L.sched.cta_first[c];
+      if (k < 0) return 1;
+      if (k > max_items) max_items = k;
+    }
+    if (L.sched.cta_first[0] != 0 || L.sched.cta_first[L.grid] != L.n_parts) return 1;
+    for (int64_t u = 0; u < units; ++u) {
+      const int s0 = L.slots.unit_slot[u], s1 = L.slots.unit_slot[u + 1];
+      if (s1 <= s0 || s1 - s0 > attn::kMaxPartsPerUnit) return 1;
+      int next = 0;
+      for (int sl = s0; sl < s1; ++sl) {
+        const attn::SchedItem& it = L.sched.items[sl];
+        if (it.unit != u || it.slot != sl || it.t0 != next || it.nt == 0) return 1;
+        next += it.nt;
+      }
+      if (next != attn::unit_geo(p, static_cast<int>(u)).ntot) return 1;
+    }
+    plan[0] = 1;
+    plan[1] = L.grid;
+    plan[2] = L.n_parts;
+    plan[3] = max_items;
+    return DDT_OK;
+  }
+  plan[0] = 0;
+  plan[1] = units * splits;
+  plan[2] = splits > 1 ? splits : 0;
+  plan[3] = 1;
+  return DDT_OK;
+}
+
 extern "C" int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64_t q_head_stride,
                                      const void* k, const void* v, int64_t kv_head_stride,
                                      int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,

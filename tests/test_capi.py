@@ -84,6 +84,46 @@ def test_attention_split_count(n, past, expect):
     assert attn_splits(n, 32, 8, past, kv_splits=5) == 5
 
 
+def _plan(n, past, hq, hkv, splits=0):
+    import ctypes
+    from mdflash_b200 import _lib
+    out = (ctypes.c_int64 * 4)()
+    rc = _lib.load().ddt_tree_attn_plan(n, past, hq, hkv, splits, ctypes.cast(out, ctypes.c_void_p))
+    return rc, list(out)
+
+
+def test_attention_plan_known_shapes():
+    # Qwen3-8B verify shape: 40 units of 256 rows, balanced over all 148 SMs, merged
+    rc, plan = _plan(257, 8192, 32, 8)
+    assert rc == 0 and plan[0] == 1 and plan[1] == 148 and plan[2] >= 148
+    # 131072-key prefix: K / V beyond L2, uniform key splits
+    rc, plan = _plan(513, 131072, 32, 8)
+    assert rc == 0 and plan[0] == 0 and plan[2] > 1 and plan[1] <= 148
+    # explicit splits stay uniform
+    rc, plan = _plan(257, 8192, 32, 8, 3)
+    assert rc == 0 and plan == [0, 40 * 3, 3, 1]
+    # sizes the kernel rejects
+    assert _plan(0, 8192, 32, 8)[0] == -1
+    assert _plan(257, 8192, 32, 7)[0] == -1
+
+
+def test_attention_balanced_tables_cover_every_tile():
+    """The balanced scheduler (fitted cost model) checks its own table: each key tile of each
+    work unit in exactly one item, a unit's items in key order.  Swept over tree sizes,
+    prefix lengths (tile multiples and not) and head layouts."""
+    seen_balanced = 0
+    for hq, hkv in [(32, 8), (16, 8), (8, 8), (4, 1), (8, 2)]:
+        for n in [1, 2, 17, 33, 64, 65, 100, 129, 257, 300, 513, 1025]:
+            for past in [0, 1, 37, 127, 128, 1000, 4096, 8192, 16384, 32768, 65536, 131072]:
+                rc, plan = _plan(n, past, hq, hkv)
+                assert rc == 0, (hq, hkv, n, past, rc)
+                assert 1 <= plan[1] <= (148 if plan[0] else 1 << 20)
+                if plan[0]:
+                    seen_balanced += 1
+                    assert plan[2] >= 1 and plan[3] >= 1
+    assert seen_balanced > 100
+
+
 @pytest.mark.parametrize("depths,vocab,budget,expect", [
     (15, 151936, 256, 256), (3, 3, 40, 39), (0, 10, 5, 0), (15, 10, 0, 0), (1, 1000, 8, 8),
     (2, 4, 100, 20)])
