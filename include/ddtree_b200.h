@@ -150,7 +150,8 @@ int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride, c
                   int64_t kv_splits, void* workspace, size_t workspace_bytes, int32_t* status,
                   void* stream);
 
-/* Host-only query of the launch plan ddt_tree_attn uses for these sizes (no device work):
+/* Host-only query of the launch plan ddt_tree_attn uses for these sizes (key_end 0), or
+ * ddt_tree_attn_partial_merged for the key shard [key_begin, key_end) (no device work):
  * plan[0] = 1 for the balanced schedule (key tiles cut over the SMs by a cost model, parts
  * merged by a second kernel), 0 for uniform key splits; plan[1] = CTAs; plan[2] = partial
  * parts (0: none, one launch); plan[3] = the most work items one CTA runs.  Returns 0, a
@@ -158,7 +159,7 @@ int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride, c
  * consistency check (each key tile of each unit in exactly one item).  An inspection aid
  * for sizing and tests; it has no counterpart in the reference. */
 int ddt_tree_attn_plan(int64_t n_nodes, int64_t past_length, int64_t q_heads, int64_t kv_heads,
-                       int64_t kv_splits, int64_t* plan);
+                       int64_t kv_splits, int64_t key_begin, int64_t key_end, int64_t* plan);
 
 /* Partial-result attention: like ddt_tree_attn but writes un-normalised fp32 partials over
  * the key range [key_begin, key_end) of this shard, for a cross-GPU split-KV merge, split

@@ -42,7 +42,7 @@ SIGNATURES = {
     "ddt_tree_attn": (_i, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _i,
                            _F, _I, _P, _S, _P, _P]),
     "ddt_tree_attn_partial_splits": (_I, [_I, _I, _I, _I]),
-    "ddt_tree_attn_plan": (_i, [_I, _I, _I, _I, _I, _P]),
+    "ddt_tree_attn_plan": (_i, [_I, _I, _I, _I, _I, _I, _I, _P]),
     "ddt_tree_attn_partial": (_i, [_P, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I,
                                    _I, _P, _I, _i, _F, _I, _P, _P]),
     "ddt_tree_attn_partial_merged_workspace_bytes": (_S, [_I, _I, _I]),

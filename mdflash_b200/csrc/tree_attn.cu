@@ -1280,13 +1280,18 @@ extern "C" int64_t ddt_tree_attn_partial_splits(int64_t n_nodes, int64_t key_cou
   return attn::pick_splits(kv_heads * pairs, (key_count + attn::kBlockN - 1) / attn::kBlockN);
 }
 
-// The launch plan ddt_tree_attn would use for these sizes, computed on the host only, and a
-// check of the balanced table: every key tile of every work unit in exactly one item, the
-// items of a unit in key order with consecutive slots, every item in one CTA's list.
+// The launch plan ddt_tree_attn (key_end == 0) or ddt_tree_attn_partial_merged (the shard
+// [key_begin, key_end)) would use for these sizes, computed on the host only, and a check
+// of the balanced table: every key tile of every work unit in exactly one item, the items of
+// a unit in key order with consecutive slots, every item in one CTA's list.
 extern "C" int ddt_tree_attn_plan(int64_t n_nodes, int64_t past_length, int64_t q_heads,
-                                  int64_t kv_heads, int64_t kv_splits, int64_t* plan) {
+                                  int64_t kv_heads, int64_t kv_splits, int64_t key_begin,
+                                  int64_t key_end, int64_t* plan) {
   if (!plan || n_nodes <= 0 || past_length < 0 || q_heads <= 0 || kv_heads <= 0 ||
       q_heads % kv_heads || kv_splits < 0)
+    return DDT_ERR_INVALID;
+  const bool shard = key_end > 0;
+  if (shard && (key_begin < 0 || key_end < key_begin || key_end > past_length + n_nodes))
     return DDT_ERR_INVALID;
   const int64_t group = q_heads / kv_heads;
   if (group > attn::kBlockM || attn::kBlockM % group) return DDT_ERR_CAPACITY;
@@ -1299,15 +1304,22 @@ extern "C" int ddt_tree_attn_plan(int64_t n_nodes, int64_t past_length, int64_t 
   p.group = static_cast<int>(group);
   p.q_heads = static_cast<int>(q_heads);
   p.n_pairs = static_cast<int>((n_nodes * group + attn::kRowsPerCta - 1) / attn::kRowsPerCta);
-  p.key_base = p.key_lo = 0;
-  p.key_hi = static_cast<int>(S);
+  p.key_base = p.key_lo = shard ? static_cast<int>(key_begin) : 0;
+  p.key_hi = static_cast<int>(shard ? key_end : S);
   p.balanced = 0;
   const int64_t units = kv_heads * p.n_pairs;
-  const int64_t kv_tiles = (S + attn::kBlockN - 1) / attn::kBlockN;
-  const int splits = kv_splits > 0 ? static_cast<int>(kv_splits) : attn::pick_splits(units, kv_tiles);
+  const int64_t local = shard ? key_end - key_begin : S;
+  const int64_t kv_tiles = (local + attn::kBlockN - 1) / attn::kBlockN;
+  const int splits = kv_splits > 0 && !shard
+                         ? static_cast<int>(kv_splits)
+                         : attn::pick_splits(units, kv_tiles > 0 ? kv_tiles : 1);
   if (splits > 64) return DDT_ERR_CAPACITY;
-  if (kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::kv_fits_l2(S, kv_heads) &&
-      attn::build_balanced(L, units)) {
+  // ddt_tree_attn: balanced when automatic, fewer units than SMs, split and within L2;
+  // a shard: balanced whenever its K / V fit in L2
+  const bool try_balanced =
+      shard ? attn::kv_fits_l2(local, kv_heads)
+            : kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::kv_fits_l2(S, kv_heads);
+  if (try_balanced && attn::build_balanced(L, units)) {
     int64_t max_items = 0;
     for (int c = 0; c < L.grid; ++c) {
       const int64_t k = L.sched.cta_first[c + 1] - L.sched.cta_first[c];

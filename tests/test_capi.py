@@ -84,11 +84,12 @@ def test_attention_split_count(n, past, expect):
     assert attn_splits(n, 32, 8, past, kv_splits=5) == 5
 
 
-def _plan(n, past, hq, hkv, splits=0):
+def _plan(n, past, hq, hkv, splits=0, key_begin=0, key_end=0):
     import ctypes
     from mdflash_b200 import _lib
     out = (ctypes.c_int64 * 4)()
-    rc = _lib.load().ddt_tree_attn_plan(n, past, hq, hkv, splits, ctypes.cast(out, ctypes.c_void_p))
+    rc = _lib.load().ddt_tree_attn_plan(n, past, hq, hkv, splits, key_begin, key_end,
+                                        ctypes.cast(out, ctypes.c_void_p))
     return rc, list(out)
 
 
@@ -122,6 +123,27 @@ def test_attention_balanced_tables_cover_every_tile():
                     seen_balanced += 1
                     assert plan[2] >= 1 and plan[3] >= 1
     assert seen_balanced > 100
+
+
+def test_attention_shard_tables_cover_every_tile():
+    """The same check for the key shards of a split-KV call (ddt_tree_attn_partial_merged):
+    2, 4 and 8 contiguous shards of the prefix, the last one holding the tree keys."""
+    seen_balanced = 0
+    for hq, hkv in [(32, 8), (16, 8)]:
+        for n in [17, 65, 257, 513]:
+            for past in [1000, 8192, 32768, 131072]:
+                total = past + n
+                for world in (2, 4, 8):
+                    step = past // world
+                    for r in range(world):
+                        b = r * step
+                        e = total if r == world - 1 else (r + 1) * step
+                        rc, plan = _plan(n, past, hq, hkv, 0, b, e)
+                        assert rc == 0, (hq, hkv, n, past, world, r, rc)
+                        seen_balanced += plan[0]
+    assert seen_balanced > 50
+    # a shard outside the key range is rejected
+    assert _plan(65, 1000, 32, 8, 0, 500, 2000)[0] == -1
 
 
 @pytest.mark.parametrize("depths,vocab,budget,expect", [
