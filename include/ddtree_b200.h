@@ -89,7 +89,8 @@ int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths, int64_t v
  * ddt_topk_tree.  Scratch lives in a DDT_NOALLOC_SCRATCH_BYTES array inside the library's
  * device image, held by every GPU that loads the library until the process exits; its
  * address is looked up on a device's first call (make that call before any stream
- * capture).  Problems whose workspace (ddt_topk_tree_workspace_bytes) exceeds the array
+ * capture), and again on the first call after the device's context was replaced
+ * (cudaDeviceReset).  Problems whose workspace (ddt_topk_tree_workspace_bytes) exceeds the array
  * return DDT_ERR_SCRATCH_LIMIT: 15 depths x 151936 vocabulary fit up to budget 1024.
  * All calls share the array, so calls that overlap on the GPU race. */
 #define DDT_NOALLOC_SCRATCH_BYTES (2u << 20)
@@ -137,7 +138,9 @@ int ddt_compact_kv(const int64_t* keep, int64_t keep_count, void* const* kv_ptrs
  * < past_length + i + 1 (anc_bits unused).
  * kv_splits: number of KV partitions per (head, query tile); 0 picks one.  Partial
  * results go to the workspace and are merged in the same call.
- * status: device i32 (zeroed by the caller), set non-zero if a bounded wait expired. */
+ * status: device i32 (zeroed by the caller), set non-zero if a bounded wait expired; the
+ * output is then incomplete, and a caller that reads the status (after its own sync) reports
+ * DDT_ERR_TIMEOUT. */
 #define DDT_MASK_TREE 0
 #define DDT_MASK_CAUSAL 1
 size_t ddt_tree_attn_workspace_bytes(int64_t n_nodes, int64_t q_heads, int64_t head_dim,
@@ -150,14 +153,16 @@ int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride, c
                   int64_t kv_splits, void* workspace, size_t workspace_bytes, int32_t* status,
                   void* stream);
 
-/* Host-only query of the launch plan ddt_tree_attn uses for these sizes (key_end 0), or
- * ddt_tree_attn_partial_merged for the key shard [key_begin, key_end) (no device work):
+/* Host-only query of the launch plan ddt_tree_attn uses for these sizes (key_end < 0, e.g.
+ * -1), or ddt_tree_attn_partial_merged for the key shard [key_begin, key_end) (key_end >= 0;
+ * an empty shard [b, b) included), computed by the same host function those entry points
+ * launch through (no device work):
  * plan[0] = 1 for the balanced schedule (key tiles cut over the SMs by a cost model, parts
  * merged by a second kernel), 0 for uniform key splits; plan[1] = CTAs; plan[2] = partial
- * parts (0: none, one launch); plan[3] = the most work items one CTA runs.  Returns 0, a
- * DDT_ERR_* code for sizes ddt_tree_attn rejects, or 1 if the balanced table fails its own
- * consistency check (each key tile of each unit in exactly one item).  An inspection aid
- * for sizing and tests; it has no counterpart in the reference. */
+ * parts merged by a second kernel (0: none, one launch); plan[3] = the most work items one
+ * CTA runs.  Returns 0, a DDT_ERR_* code for sizes the entry points reject, or 1 if the
+ * balanced table fails its own consistency check (each key tile of each unit in exactly one
+ * item).  An inspection aid for sizing and tests; it has no counterpart in the reference. */
 int ddt_tree_attn_plan(int64_t n_nodes, int64_t past_length, int64_t q_heads, int64_t kv_heads,
                        int64_t kv_splits, int64_t key_begin, int64_t key_end, int64_t* plan);
 
@@ -195,6 +200,20 @@ int ddt_tree_attn_partial_merged(const void* q, int64_t q_node_stride, int64_t q
                                  int64_t head_dim, const uint32_t* anc_bits, int64_t anc_words,
                                  int mask_mode, float scale, void* workspace,
                                  size_t workspace_bytes, int32_t* status, void* stream);
+
+/* Check of the bounded waits of the tree-attention kernel; no counterpart in the reference.
+ * Every wait of that kernel gives up after a time limit (2 s in the entry points above),
+ * sets the caller's status word, frees the kernel's tensor memory and lets the CTA return,
+ * so a lost arrival cannot hang the GPU.  This launches the kernel once (tree mask, q
+ * [n_nodes, q_heads, 128], k / v [kv_heads, past_length + n_nodes, 128], out like q, all
+ * contiguous bf16) with its load-issuing warp withholding every load, so each consumer's
+ * first wait runs out after timeout_ns (100 us .. 2 s).  The kernel must return and leave
+ * *status (device i32, zeroed by the caller) non-zero; `out` holds zeros for the rows the
+ * kernel reached.  Returns 0 when the launch was issued. */
+int ddt_tree_attn_wait_check(const void* q, const void* k, const void* v, void* out,
+                             int64_t n_nodes, int64_t past_length, int64_t q_heads,
+                             int64_t kv_heads, const uint32_t* anc_bits, int64_t anc_words,
+                             uint64_t timeout_ns, int32_t* status, void* stream);
 
 /* Merge n_parts partials laid out [n_parts, rows, head_dim] / [n_parts, rows]
  * (rows = n_nodes * q_heads) into out (bf16, [n_nodes, q_heads, head_dim] at the given

@@ -12,6 +12,7 @@ from . import build as _build
 _lib = None
 
 DDT_OK = 0
+DDT_ERR_TIMEOUT = -6
 DDT_F32 = 0
 DDT_BF16 = 1
 DDT_MASK_TREE = 0
@@ -48,6 +49,8 @@ SIGNATURES = {
     "ddt_tree_attn_partial_merged_workspace_bytes": (_S, [_I, _I, _I]),
     "ddt_tree_attn_partial_merged": (_i, [_P, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I,
                                           _I, _I, _I, _P, _I, _i, _F, _P, _S, _P, _P]),
+    "ddt_tree_attn_wait_check": (_i, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _I, ctypes.c_uint64, _P,
+                                      _P]),
     "ddt_attn_merge": (_i, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P]),
     "ddt_mask_to_bits": (_i, [_P, _i, _I, _I, _P, _I, _P]),
     "ddt_add_rmsnorm": (_i, [_P, _P, _P, _I, _I, _F, _P, _P, _P]),

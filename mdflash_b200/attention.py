@@ -10,6 +10,11 @@ so an unmodified Qwen3 model runs its verify forward through it:
   has the reference's additive 4-D mask, the tree block of that mask is converted to
   bitmasks on the device;
 * no mask (prefill, plain decode): causal attention, node i sees keys < past + i + 1.
+
+The kernel computes in bf16 with fp32 accumulation; an fp32 model's q / k / v are rounded
+to bf16 for it (within the bf16 tolerance of fp32 attention).  Bounded-wait timeouts of the
+kernel are reported to a status word (the context's, or the device's default one), which
+``follow_verified_tree`` and ``TreeVerifier.check`` read when they sync.
 """
 from __future__ import annotations
 
@@ -28,6 +33,9 @@ class _TreeContext(threading.local):
         self.tree: K.DeviceTree | None = None
         self.past_length: int | None = None
         self.n_nodes: int = 0
+        # status word the plug-in's launches report bounded-wait timeouts to (None: the
+        # device's default word, kernels.attention_status)
+        self.status: torch.Tensor | None = None
 
 
 _CTX = _TreeContext()
@@ -51,13 +59,15 @@ def get_tree_context():
 
 
 @contextmanager
-def tree_verify(tree: "K.DeviceTree", past_length: int, n_nodes: int | None = None):
-    prev = (_CTX.tree, _CTX.past_length, _CTX.n_nodes)
+def tree_verify(tree: "K.DeviceTree", past_length: int, n_nodes: int | None = None,
+                status: torch.Tensor | None = None):
+    prev = (_CTX.tree, _CTX.past_length, _CTX.n_nodes, _CTX.status)
     set_tree_context(tree, past_length, n_nodes)
+    _CTX.status = status
     try:
         yield
     finally:
-        _CTX.tree, _CTX.past_length, _CTX.n_nodes = prev
+        _CTX.tree, _CTX.past_length, _CTX.n_nodes, _CTX.status = prev
 
 
 def ddtree_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: torch.Tensor,
@@ -73,15 +83,17 @@ def ddtree_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: 
     s = key.shape[2]
     past = s - n
     tree, ctx_past, ctx_n = get_tree_context()
+    st = _CTX.status
     if tree is not None and ctx_n == n and ctx_past == past:
-        out = K.tree_attention(query, key, value, tree.anc_bits, past, scale=scaling)
+        out = K.tree_attention(query, key, value, tree.anc_bits, past, scale=scaling, status=st)
     elif attention_mask is not None:
         if attention_mask.dim() != 4 or attention_mask.shape[-2] != n or attention_mask.shape[-1] < s:
             raise ValueError("expected the 4-D tree mask [1, 1, N, past + N]")
         bits = K.mask_to_bits(attention_mask[0, 0, :, past:past + n])
-        out = K.tree_attention(query, key, value, bits, past, scale=scaling)
+        out = K.tree_attention(query, key, value, bits, past, scale=scaling, status=st)
     else:
-        out = K.tree_attention(query, key, value, None, past, scale=scaling, causal=True)
+        out = K.tree_attention(query, key, value, None, past, scale=scaling, causal=True,
+                               status=st)
     return out.unsqueeze(0), None
 
 

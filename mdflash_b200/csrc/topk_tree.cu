@@ -883,9 +883,12 @@ extern "C" int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths
 // DDT_NOALLOC_SCRATCH_BYTES long and every GPU that loads the library keeps it until the
 // process exits.  Its device address is looked up once per device, on that device's first
 // call, with cudaGetSymbolAddress (so the first call on a device should happen before any
-// stream capture).  All calls share the one array: calls whose work overlaps on the GPU
+// stream capture), and again on the first call in a new context of that device (after a
+// cudaDeviceReset the module is loaded anew).  All calls share the one array: calls whose work overlaps on the GPU
 // (different streams, or several host threads) race and must be serialised by the caller.
 // ---------------------------------------------------------------------------------------
+#include <cuda.h>
+
 #include <mutex>
 
 namespace ddt {
@@ -895,18 +898,53 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[DDT_NOALLOC_SCR
 
 constexpr int kMaxDevices = 64;
 static void* g_noalloc_addr[kMaxDevices] = {};
+// unique id of the CUDA context the cached address belongs to: after cudaDeviceReset (or any
+// teardown of the primary context) the module is loaded anew, possibly elsewhere, so a call in
+// a new context looks the address up again instead of writing through a stale one
+static unsigned long long g_noalloc_ctx[kMaxDevices] = {};
 static std::mutex g_noalloc_mu;
 
-// Device address of this device's copy of the scratch array (looked up once per device).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context (0 if it cannot be read).
+static unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(fn);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx &&
+      get_id(ctx, &id) == CUDA_SUCCESS)
+    return id;
+  return 0;
+}
+
+// Device address of this device's copy of the scratch array, looked up with
+// cudaGetSymbolAddress once per device and context (set-up work of the first call).
 static int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DDT_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return DDT_ERR_CAPACITY;
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  if (!g_noalloc_addr[dev] || ctx == 0 || g_noalloc_ctx[dev] != ctx) {
+    // also makes the device's primary context current when no context is yet
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return DDT_ERR_CUDA;
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = current_context_id();
   }
   *out = g_noalloc_addr[dev];
   return DDT_OK;

@@ -94,6 +94,11 @@ struct Params {
   float* l_part;
   int partial;
   int* status;
+  // limit of every bounded wait of the kernel (2 s in the product entry points)
+  unsigned long long timeout_ns;
+  // diagnostic launches only (ddt_tree_attn_wait_check): the producer issues no load, so the
+  // first wait of every consumer runs out after timeout_ns and the kernel unwinds
+  int withhold_loads;
 };
 
 // Balanced schedule ("stream-K" over the key tiles): the flattened (work unit, key tile)
@@ -271,7 +276,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     tc::reg_dealloc<kRegsControl>();
     if (warp == 0) {
       // ---------------------------- TMA producer -------------------------------------
-      if (lane == 0 && total > 0) {
+      if (lane == 0 && total > 0 && !p.withhold_loads) {
         tc::tma_prefetch_desc(&tm_q);
         tc::tma_prefetch_desc(&tm_k);
         tc::tma_prefetch_desc(&tm_v);
@@ -301,14 +306,14 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             const int st = jg % kStages;
             const uint32_t ph = ((jg / kStages) - 1) & 1;  // release phase of tile jg - kStages
             const int key = lk0 + j * kBlockN;
-            if (jg >= kStages && !(ok = tc::mbar_wait(&bars.k_empty[st], ph, abort_flag, kTimeoutNs)))
+            if (jg >= kStages && !(ok = tc::mbar_wait(&bars.k_empty[st], ph, abort_flag, p.timeout_ns)))
               break;
             unsigned char* kd = sK + st * kTileBytes;
             tc::mbar_expect_tx(&bars.k_full[st], kTileBytes);
             tc::tma_load_3d(kd, &tm_k, &bars.k_full[st], 0, key, g.h);
             tc::tma_load_3d(kd + kHalfBytes, &tm_k, &bars.k_full[st], 64, key, g.h);
             issued_k = jg + 1;
-            if (jg >= kStages && !(ok = tc::mbar_wait(&bars.v_empty[st], ph, abort_flag, kTimeoutNs)))
+            if (jg >= kStages && !(ok = tc::mbar_wait(&bars.v_empty[st], ph, abort_flag, p.timeout_ns)))
               break;
             unsigned char* vd = sV + st * kTileBytes;
             tc::mbar_expect_tx(&bars.v_full[st], kTileBytes);
@@ -318,7 +323,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             if (j == 0 && i > 0) {
               // the item's Q replaces the previous item's once both its S MMAs are done;
               // the first K / V tile of the item is already on its way
-              if (!(ok = tc::mbar_wait(&bars.q_empty, (i - 1) & 1, abort_flag, kTimeoutNs))) break;
+              if (!(ok = tc::mbar_wait(&bars.q_empty, (i - 1) & 1, abort_flag, p.timeout_ns))) break;
               load_q(g);
             }
           }
@@ -394,7 +399,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             if ((it & 255u) == 255u) {
               const uint64_t now = global_timer_ns();
               if (t0 == 0) t0 = now;
-              if (__any_sync(DDT_FULL_MASK, *abort_flag != 0 || now - t0 > kTimeoutNs))
+              if (__any_sync(DDT_FULL_MASK, *abort_flag != 0 || now - t0 > p.timeout_ns))
                 return false;
             }
           }
@@ -407,9 +412,9 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int i = 0; ok && i < n_items; ++i) {
           int u, t0, nt, sl;
           item(i, u, t0, nt, sl);
-          if (!(ok = tc::mbar_wait_warp(&bars.q_full, i & 1, abort_flag, kTimeoutNs))) break;
+          if (!(ok = tc::mbar_wait_warp(&bars.q_full, i & 1, abort_flag, p.timeout_ns))) break;
           if (!(ok = tc::mbar_wait_warp(&bars.k_full[J % kStages], (J / kStages) & 1, abort_flag,
-                                        kTimeoutNs)))
+                                        p.timeout_ns)))
             break;
           if (!(ok = wait_turn(q == 0 ? base : base + 1))) break;
           tc::tc_fence_after();
@@ -425,17 +430,17 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             const bool more = j + 1 < nt;
             // K / V of the tile landed long before P_q(j): waited first, while the softmax runs
             if (!(ok = tc::mbar_wait_warp(&bars.v_full[st], (jg / kStages) & 1, abort_flag,
-                                          kTimeoutNs)))
+                                          p.timeout_ns)))
               break;
             if (more && !(ok = tc::mbar_wait_warp(&bars.k_full[sn], ((jg + 1) / kStages) & 1,
-                                                  abort_flag, kTimeoutNs)))
+                                                  abort_flag, p.timeout_ns)))
               break;
-            if (!(ok = tc::mbar_wait_warp(&bars.p_half[q], jg & 1, abort_flag, kTimeoutNs))) break;
+            if (!(ok = tc::mbar_wait_warp(&bars.p_half[q], jg & 1, abort_flag, p.timeout_ns))) break;
             if (!(ok = wait_turn(q == 0 ? base + j + 1 : base + j + 2))) break;
             tc::tc_fence_after();
             if (tc::elect_one()) issue_pv(jg, j, 0);
             __syncwarp();
-            if (!(ok = tc::mbar_wait_warp(&bars.p_full[q], jg & 1, abort_flag, kTimeoutNs))) break;
+            if (!(ok = tc::mbar_wait_warp(&bars.p_full[q], jg & 1, abort_flag, p.timeout_ns))) break;
             tc::tc_fence_after();
             if (tc::elect_one()) {
               issue_pv(jg, j, 1);
@@ -495,7 +500,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; ok && j < nt; ++j) {
         const int jg = J + j;
-        if (!tc::mbar_wait_warp(&bars.s_full[q], jg & 1, abort_flag, kTimeoutNs)) {
+        if (!tc::mbar_wait_warp(&bars.s_full[q], jg & 1, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
@@ -545,7 +550,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (__any_sync(DDT_FULL_MASK, rescale)) {
           // O_q is stable once the previous P V MMA of this item completed
-          if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready[q], (jg - 1) & 1, abort_flag, kTimeoutNs)) {
+          if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready[q], (jg - 1) & 1, abort_flag, p.timeout_ns)) {
             ok = false;
             break;
           }
@@ -610,7 +615,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         if (lane == 0) tc::mbar_arrive(&bars.p_full[q]);
       }
       if (ok && nt > 0 &&
-          !tc::mbar_wait_warp(&bars.o_ready[q], (J + nt - 1) & 1, abort_flag, kTimeoutNs))
+          !tc::mbar_wait_warp(&bars.o_ready[q], (J + nt - 1) & 1, abort_flag, p.timeout_ns))
         ok = false;
       const bool have = ok && nt > 0;  // warp-uniform
       if (have) tc::tc_fence_after();
@@ -1010,26 +1015,61 @@ struct Launch {
   int n_parts;
 };
 
-inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_head_stride,
-                   const void* k, const void* v, int64_t kv_head_stride, int64_t kv_seq_stride,
-                   int64_t kv_len_local, int64_t n_nodes, int64_t past_length, int64_t q_heads,
-                   int64_t kv_heads, int64_t head_dim, const uint32_t* anc_bits,
-                   int64_t anc_words, int mask_mode, float scale) {
-  if (!q || !k || !v) return DDT_ERR_INVALID;
-  if (head_dim != kHeadDim) return DDT_ERR_CAPACITY;
+// Size checks and the size-dependent Params fields of a launch over the global key range
+// [key_lo, key_hi) (no pointers, no device work): shared by the launching entry points and the
+// host-only plan query.
+inline int prepare_sizes(Params& p, int64_t n_nodes, int64_t past_length, int64_t q_heads,
+                         int64_t kv_heads, int64_t key_lo, int64_t key_hi) {
   if (n_nodes <= 0 || past_length < 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads)
     return DDT_ERR_INVALID;
   const int64_t group = q_heads / kv_heads;
   if (group > kBlockM || kBlockM % group) return DDT_ERR_CAPACITY;
+  if (past_length + n_nodes >= (int64_t(1) << 31)) return DDT_ERR_CAPACITY;
+  if (key_lo < 0 || key_hi < key_lo || key_hi > past_length + n_nodes) return DDT_ERR_INVALID;
+  p.n_nodes = static_cast<int>(n_nodes);
+  p.past_len = static_cast<int>(past_length);
+  p.group = static_cast<int>(group);
+  p.q_heads = static_cast<int>(q_heads);
+  p.n_pairs = static_cast<int>((n_nodes * group + kRowsPerCta - 1) / kRowsPerCta);
+  p.key_base = p.key_lo = static_cast<int>(key_lo);
+  p.key_hi = static_cast<int>(key_hi);
+  p.anc = nullptr;
+  p.anc_words = 0;
+  p.mask_mode = DDT_MASK_TREE;
+  p.scale_log2 = 0.f;
+  p.out = nullptr;
+  p.o_part = p.m_part = p.l_part = nullptr;
+  p.o_slot = nullptr;
+  p.partial = 0;
+  p.balanced = 0;
+  p.n_splits = 1;
+  p.status = nullptr;
+  p.timeout_ns = kTimeoutNs;
+  p.withhold_loads = 0;
+  return DDT_OK;
+}
+
+// prepare_sizes plus the pointer, mask and stride checks and the TMA tensor maps; the K / V
+// pointers address global key key_lo (the first key of the launch's range).
+inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                   const void* k, const void* v, int64_t kv_head_stride, int64_t kv_seq_stride,
+                   int64_t key_lo, int64_t key_hi, int64_t n_nodes, int64_t past_length,
+                   int64_t q_heads, int64_t kv_heads, int64_t head_dim, const uint32_t* anc_bits,
+                   int64_t anc_words, int mask_mode, float scale) {
+  if (!q || !k || !v) return DDT_ERR_INVALID;
+  if (head_dim != kHeadDim) return DDT_ERR_CAPACITY;
+  int rc = prepare_sizes(L.p, n_nodes, past_length, q_heads, kv_heads, key_lo, key_hi);
+  if (rc) return rc;
   if (mask_mode != DDT_MASK_TREE && mask_mode != DDT_MASK_CAUSAL) return DDT_ERR_INVALID;
   if (mask_mode == DDT_MASK_TREE && (!anc_bits || anc_words * 32 < n_nodes)) return DDT_ERR_INVALID;
-  if (past_length + n_nodes >= (int64_t(1) << 31)) return DDT_ERR_CAPACITY;
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16)) return DDT_ERR_ALIGN;
   if ((q_node_stride * 2) % 16 || (q_head_stride * 2) % 16 || (kv_head_stride * 2) % 16 ||
       (kv_seq_stride * 2) % 16)
     return DDT_ERR_ALIGN;
-  int rc = make_map(&L.q, q, kHeadDim, q_heads, n_nodes, q_head_stride * 2, q_node_stride * 2, 64,
-                    static_cast<uint32_t>(group), static_cast<uint32_t>(kBlockM / group));
+  const int64_t group = q_heads / kv_heads;
+  const int64_t kv_len_local = key_hi > key_lo ? key_hi - key_lo : 1;
+  rc = make_map(&L.q, q, kHeadDim, q_heads, n_nodes, q_head_stride * 2, q_node_stride * 2, 64,
+                static_cast<uint32_t>(group), static_cast<uint32_t>(kBlockM / group));
   if (rc) return rc;
   rc = make_map(&L.k, k, kHeadDim, kv_len_local, kv_heads, kv_seq_stride * 2, kv_head_stride * 2,
                 64, kBlockN, 1);
@@ -1038,22 +1078,10 @@ inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_he
                 64, kBlockN, 1);
   if (rc) return rc;
   Params& p = L.p;
-  p.n_nodes = static_cast<int>(n_nodes);
-  p.past_len = static_cast<int>(past_length);
-  p.group = static_cast<int>(group);
-  p.q_heads = static_cast<int>(q_heads);
-  p.n_pairs = static_cast<int>((n_nodes * group + kRowsPerCta - 1) / kRowsPerCta);
   p.anc = anc_bits;
   p.anc_words = static_cast<int>(anc_words);
   p.mask_mode = mask_mode;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.out = nullptr;
-  p.o_part = p.m_part = p.l_part = nullptr;
-  p.o_slot = nullptr;
-  p.partial = 0;
-  p.balanced = 0;
-  p.n_splits = 1;
-  p.status = nullptr;
   return DDT_OK;
 }
 
@@ -1168,16 +1196,112 @@ inline SlotPtrs slot_ptrs(void* ws, int64_t parts) {
 }
 
 inline int launch(const Launch& L, int64_t kv_heads, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(tree_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemAlloc) != cudaSuccess)
-      return DDT_ERR_CUDA;
-    attr = true;
-  }
+  // the attribute belongs to the current device: set on every launch (it costs a host call),
+  // so a process that uses several GPUs, from several threads, needs no per-device state
+  if (cudaFuncSetAttribute(tree_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kSmemAlloc) != cudaSuccess)
+    return DDT_ERR_CUDA;
   const int64_t grid = L.p.balanced ? L.grid : kv_heads * L.p.n_pairs * L.p.n_splits;
   tree_attn_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, st>>>(L.q, L.k, L.v, L.p,
                                                                              L.sched);
+  return launch_status();
+}
+
+// How a launch covers its work.
+//   kPlanSingle    one launch, every CTA one work unit over all its keys, bf16 out directly
+//   kPlanUniform   every unit's key tiles cut into p.n_splits equal splits, fp32 partials,
+//                  merge_kernel
+//   kPlanBalanced  the (unit, key tile) space cut over the SMs by the cost model
+//                  (build_balanced), bf16 parts in slots, merge_slots_kernel
+enum PlanKind { kPlanSingle = 0, kPlanUniform = 1, kPlanBalanced = 2 };
+
+// The one place that picks the plan, used by ddt_tree_attn (shard = false), by
+// ddt_tree_attn_partial_merged (shard = true) and by the host-only ddt_tree_attn_plan, so the
+// plan the query reports (and the CPU tests sweep) is the plan that is launched.  L.p must
+// come from prepare_sizes.  Full range: balanced when the split count is automatic, there
+// are fewer units than SMs, more than one split pays and the K / V fit in L2; otherwise
+// uniform splits (merged) or one launch.  A shard: balanced whenever its K / V fit in L2,
+// otherwise uniform splits, always merged to one partial per row (even with one split).
+inline int choose_plan(Launch& L, int64_t kv_heads, int64_t kv_splits, bool shard, int& kind) {
+  Params& p = L.p;
+  const int64_t units = kv_heads * p.n_pairs;
+  const int64_t local = static_cast<int64_t>(p.key_hi) - p.key_lo;
+  const int64_t kv_tiles = local > 0 ? (local + kBlockN - 1) / kBlockN : 1;
+  const int64_t splits = (!shard && kv_splits > 0) ? kv_splits : pick_splits(units, kv_tiles);
+  if (splits > 64) return DDT_ERR_CAPACITY;
+  p.n_splits = static_cast<int>(splits);
+  p.balanced = 0;
+  const bool try_balanced =
+      kv_fits_l2(local, kv_heads) &&
+      (shard || (kv_splits <= 0 && units < kMaxCtas && splits > 1));
+  if (try_balanced && build_balanced(L, units)) {
+    kind = kPlanBalanced;
+    return DDT_OK;
+  }
+  p.balanced = 0;
+  L.grid = static_cast<int>(units * splits);
+  L.n_parts = static_cast<int>(splits);
+  kind = (shard || splits > 1) ? kPlanUniform : kPlanSingle;
+  return DDT_OK;
+}
+
+// Workspace bytes a plan needs (0 for kPlanSingle).
+inline size_t plan_workspace(const Launch& L, int kind) {
+  if (kind == kPlanBalanced) return slot_bytes(L.n_parts);
+  if (kind == kPlanUniform)
+    return part_bytes(static_cast<int64_t>(L.p.n_nodes) * L.p.q_heads, L.p.n_splits);
+  return 0;
+}
+
+// Runs a chosen plan: the attention launch and, for split plans, its merge.  The result is
+// bf16 `out` (strides o_node_stride, o_head_stride) or, when out is null, one fp32 partial per
+// row in (node, q head) order: o_merged [rows, 128], m_merged / l_merged [rows].
+inline int run(Launch& L, int kind, int64_t kv_heads, void* workspace, size_t workspace_bytes,
+               __nv_bfloat16* out, int64_t o_node_stride, int64_t o_head_stride, float* o_merged,
+               float* m_merged, float* l_merged, cudaStream_t st) {
+  Params& p = L.p;
+  const int64_t rows = static_cast<int64_t>(p.n_nodes) * p.q_heads;
+  if (kind == kPlanSingle) {
+    if (!out) return DDT_ERR_INVALID;
+    p.out = out;
+    p.o_node_stride = o_node_stride;
+    p.o_head_stride = o_head_stride;
+    return launch(L, kv_heads, st);
+  }
+  if (!workspace || workspace_bytes < plan_workspace(L, kind)) return DDT_ERR_WORKSPACE;
+  if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
+  p.partial = 1;
+  if (kind == kPlanBalanced) {
+    const SlotPtrs sp = slot_ptrs(workspace, L.n_parts);
+    p.o_slot = sp.o;
+    p.m_part = sp.m;
+    p.l_part = sp.l;
+    int rc = launch(L, kv_heads, st);
+    if (rc) return rc;
+    const int64_t units = kv_heads * p.n_pairs;
+    const int64_t warps = units * (kRowsPerCta / 32) * (kHeadDim / kMergeDims);
+    const unsigned blocks = static_cast<unsigned>((warps + kMergeWarps - 1) / kMergeWarps);
+    if (out)
+      merge_slots_kernel<false><<<blocks, kMergeWarps * 32, 0, st>>>(
+          sp.o, sp.m, sp.l, L.slots, p, out, o_node_stride, o_head_stride, nullptr, nullptr,
+          nullptr);
+    else
+      merge_slots_kernel<true><<<blocks, kMergeWarps * 32, 0, st>>>(
+          sp.o, sp.m, sp.l, L.slots, p, nullptr, 0, 0, o_merged, m_merged, l_merged);
+    return launch_status();
+  }
+  float* op = static_cast<float*>(workspace);
+  float* mp = op + static_cast<size_t>(p.n_splits) * rows * kHeadDim;
+  float* lp = mp + static_cast<size_t>(p.n_splits) * rows;
+  p.o_part = op;
+  p.m_part = mp;
+  p.l_part = lp;
+  int rc = launch(L, kv_heads, st);
+  if (rc) return rc;
+  const int wpb = 8;
+  merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+      op, mp, lp, p.n_splits, rows, p.q_heads, out, o_node_stride, o_head_stride, o_merged,
+      m_merged, l_merged);
   return launch_status();
 }
 
@@ -1211,65 +1335,17 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
   if (!out) return DDT_ERR_INVALID;
   if (!aligned(out, 16) || (o_node_stride * 2) % 16 || (o_head_stride * 2) % 16) return DDT_ERR_ALIGN;
   attn::Launch L;
-  const int64_t S = past_length + n_nodes;
-  int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride, S,
-                         n_nodes, past_length, q_heads, kv_heads, head_dim, anc_bits, anc_words,
-                         mask_mode, scale);
+  int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride, 0,
+                         past_length + n_nodes, n_nodes, past_length, q_heads, kv_heads, head_dim,
+                         anc_bits, anc_words, mask_mode, scale);
   if (rc) return rc;
-  const int64_t units = kv_heads * L.p.n_pairs;
-  const int64_t kv_tiles = (S + attn::kBlockN - 1) / attn::kBlockN;
-  const int splits = kv_splits > 0 ? static_cast<int>(kv_splits) : attn::pick_splits(units, kv_tiles);
-  if (splits > 64) return DDT_ERR_CAPACITY;
-  L.p.n_splits = splits;
-  L.p.key_base = 0;
-  L.p.key_lo = 0;
-  L.p.key_hi = static_cast<int>(S);
+  int kind = 0;
+  rc = attn::choose_plan(L, kv_heads, kv_splits, false, kind);
+  if (rc) return rc;
   L.p.status = status;
-  L.p.out = static_cast<__nv_bfloat16*>(out);
-  L.p.o_node_stride = o_node_stride;
-  L.p.o_head_stride = o_head_stride;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t rows = n_nodes * q_heads;
-  // automatic split with fewer work units than SMs: balanced parts (every SM the same
-  // number of key tiles), merged per unit
-  if (kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::kv_fits_l2(S, kv_heads) &&
-      attn::build_balanced(L, units)) {
-    const size_t need = attn::slot_bytes(L.n_parts);
-    if (!workspace || workspace_bytes < need) return DDT_ERR_WORKSPACE;
-    if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
-    const attn::SlotPtrs sp = attn::slot_ptrs(workspace, L.n_parts);
-    L.p.o_slot = sp.o;
-    L.p.m_part = sp.m;
-    L.p.l_part = sp.l;
-    L.p.partial = 1;
-    rc = attn::launch(L, kv_heads, st);
-    if (rc) return rc;
-    const int wpb = attn::kMergeWarps;
-    const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
-    attn::merge_slots_kernel<false><<<static_cast<unsigned>((warps + wpb - 1) / wpb), wpb * 32, 0, st>>>(
-        sp.o, sp.m, sp.l, L.slots, L.p, static_cast<__nv_bfloat16*>(out), o_node_stride,
-        o_head_stride, nullptr, nullptr, nullptr);
-    return launch_status();
-  }
-  if (splits > 1) {
-    if (!workspace || workspace_bytes < attn::part_bytes(rows, splits)) return DDT_ERR_WORKSPACE;
-    if (!aligned(workspace, 16)) return DDT_ERR_ALIGN;
-    float* o_part = static_cast<float*>(workspace);
-    float* m_part = o_part + static_cast<size_t>(splits) * rows * attn::kHeadDim;
-    float* l_part = m_part + static_cast<size_t>(splits) * rows;
-    L.p.o_part = o_part;
-    L.p.m_part = m_part;
-    L.p.l_part = l_part;
-    L.p.partial = 1;
-    rc = attn::launch(L, kv_heads, st);
-    if (rc) return rc;
-    const int wpb = 8;
-    attn::merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0, st>>>(
-        o_part, m_part, l_part, splits, rows, static_cast<int>(q_heads),
-        static_cast<__nv_bfloat16*>(out), o_node_stride, o_head_stride, nullptr, nullptr, nullptr);
-    return launch_status();
-  }
-  return attn::launch(L, kv_heads, st);
+  return attn::run(L, kind, kv_heads, workspace, workspace_bytes, static_cast<__nv_bfloat16*>(out),
+                   o_node_stride, o_head_stride, nullptr, nullptr, nullptr,
+                   static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int64_t ddt_tree_attn_partial_splits(int64_t n_nodes, int64_t key_count,
@@ -1280,46 +1356,26 @@ extern "C" int64_t ddt_tree_attn_partial_splits(int64_t n_nodes, int64_t key_cou
   return attn::pick_splits(kv_heads * pairs, (key_count + attn::kBlockN - 1) / attn::kBlockN);
 }
 
-// The launch plan ddt_tree_attn (key_end == 0) or ddt_tree_attn_partial_merged (the shard
-// [key_begin, key_end)) would use for these sizes, computed on the host only, and a check
-// of the balanced table: every key tile of every work unit in exactly one item, the items of
-// a unit in key order with consecutive slots, every item in one CTA's list.
+// The launch plan of ddt_tree_attn (key_end < 0) or of ddt_tree_attn_partial_merged over the
+// shard [key_begin, key_end), from attn::choose_plan (the function both of them launch
+// through), plus a check of a balanced table: every key tile of every work unit in exactly
+// one item, the items of a unit in key order with consecutive slots, every item in one CTA's
+// list.
 extern "C" int ddt_tree_attn_plan(int64_t n_nodes, int64_t past_length, int64_t q_heads,
                                   int64_t kv_heads, int64_t kv_splits, int64_t key_begin,
                                   int64_t key_end, int64_t* plan) {
-  if (!plan || n_nodes <= 0 || past_length < 0 || q_heads <= 0 || kv_heads <= 0 ||
-      q_heads % kv_heads || kv_splits < 0)
-    return DDT_ERR_INVALID;
-  const bool shard = key_end > 0;
-  if (shard && (key_begin < 0 || key_end < key_begin || key_end > past_length + n_nodes))
-    return DDT_ERR_INVALID;
-  const int64_t group = q_heads / kv_heads;
-  if (group > attn::kBlockM || attn::kBlockM % group) return DDT_ERR_CAPACITY;
-  const int64_t S = past_length + n_nodes;
-  if (S >= (int64_t(1) << 31)) return DDT_ERR_CAPACITY;
+  if (!plan || kv_splits < 0) return DDT_ERR_INVALID;
+  const bool shard = key_end >= 0;
   attn::Launch L;
-  attn::Params& p = L.p;
-  p.n_nodes = static_cast<int>(n_nodes);
-  p.past_len = static_cast<int>(past_length);
-  p.group = static_cast<int>(group);
-  p.q_heads = static_cast<int>(q_heads);
-  p.n_pairs = static_cast<int>((n_nodes * group + attn::kRowsPerCta - 1) / attn::kRowsPerCta);
-  p.key_base = p.key_lo = shard ? static_cast<int>(key_begin) : 0;
-  p.key_hi = static_cast<int>(shard ? key_end : S);
-  p.balanced = 0;
+  int rc = attn::prepare_sizes(L.p, n_nodes, past_length, q_heads, kv_heads,
+                               shard ? key_begin : 0, shard ? key_end : past_length + n_nodes);
+  if (rc) return rc;
+  int kind = 0;
+  rc = attn::choose_plan(L, kv_heads, kv_splits, shard, kind);
+  if (rc) return rc;
+  const attn::Params& p = L.p;
   const int64_t units = kv_heads * p.n_pairs;
-  const int64_t local = shard ? key_end - key_begin : S;
-  const int64_t kv_tiles = (local + attn::kBlockN - 1) / attn::kBlockN;
-  const int splits = kv_splits > 0 && !shard
-                         ? static_cast<int>(kv_splits)
-                         : attn::pick_splits(units, kv_tiles > 0 ? kv_tiles : 1);
-  if (splits > 64) return DDT_ERR_CAPACITY;
-  // ddt_tree_attn: balanced when automatic, fewer units than SMs, split and within L2;
-  // a shard: balanced whenever its K / V fit in L2
-  const bool try_balanced =
-      shard ? attn::kv_fits_l2(local, kv_heads)
-            : kv_splits <= 0 && units < attn::kMaxCtas && splits > 1 && attn::kv_fits_l2(S, kv_heads);
-  if (try_balanced && attn::build_balanced(L, units)) {
+  if (kind == attn::kPlanBalanced) {
     int64_t max_items = 0;
     for (int c = 0; c < L.grid; ++c) {
       const int64_t k = L.sched.cta_first[c + 1] - L.sched.cta_first[c];
@@ -1345,8 +1401,8 @@ extern "C" int ddt_tree_attn_plan(int64_t n_nodes, int64_t past_length, int64_t 
     return DDT_OK;
   }
   plan[0] = 0;
-  plan[1] = units * splits;
-  plan[2] = splits > 1 ? splits : 0;
+  plan[1] = L.grid;
+  plan[2] = kind == attn::kPlanUniform ? p.n_splits : 0;
   plan[3] = 1;
   return DDT_OK;
 }
@@ -1360,23 +1416,19 @@ extern "C" int ddt_tree_attn_partial(const void* q, int64_t q_node_stride, int64
                                      int64_t anc_words, int mask_mode, float scale,
                                      int64_t kv_splits, int32_t* status, void* stream) {
   if (!o_part || !m_part || !l_part) return DDT_ERR_INVALID;
-  if (key_begin < 0 || key_end < key_begin || key_end > past_length + n_nodes) return DDT_ERR_INVALID;
   if (!aligned(o_part, 16)) return DDT_ERR_ALIGN;
   attn::Launch L;
-  const int64_t local = key_end - key_begin;
   int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride,
-                         local > 0 ? local : 1, n_nodes, past_length, q_heads, kv_heads, head_dim,
+                         key_begin, key_end, n_nodes, past_length, q_heads, kv_heads, head_dim,
                          anc_bits, anc_words, mask_mode, scale);
   if (rc) return rc;
+  const int64_t local = key_end - key_begin;
   if (kv_splits <= 0) {
-    const int64_t kv_tiles = (local + attn::kBlockN - 1) / attn::kBlockN;
+    const int64_t kv_tiles = local > 0 ? (local + attn::kBlockN - 1) / attn::kBlockN : 1;
     kv_splits = attn::pick_splits(kv_heads * L.p.n_pairs, kv_tiles);
   }
   if (kv_splits > 64) return DDT_ERR_CAPACITY;
   L.p.n_splits = static_cast<int>(kv_splits);
-  L.p.key_base = static_cast<int>(key_begin);
-  L.p.key_lo = static_cast<int>(key_begin);
-  L.p.key_hi = static_cast<int>(key_end);
   L.p.status = status;
   L.p.o_part = o_part;
   L.p.m_part = m_part;
@@ -1398,57 +1450,18 @@ extern "C" int ddt_tree_attn_partial_merged(
     int64_t anc_words, int mask_mode, float scale, void* workspace, size_t workspace_bytes,
     int32_t* status, void* stream) {
   if (!o_part || !m_part || !l_part) return DDT_ERR_INVALID;
-  if (key_begin < 0 || key_end < key_begin || key_end > past_length + n_nodes) return DDT_ERR_INVALID;
   if (!aligned(o_part, 16)) return DDT_ERR_ALIGN;
   attn::Launch L;
-  const int64_t local = key_end - key_begin;
   int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride,
-                         local > 0 ? local : 1, n_nodes, past_length, q_heads, kv_heads, head_dim,
+                         key_begin, key_end, n_nodes, past_length, q_heads, kv_heads, head_dim,
                          anc_bits, anc_words, mask_mode, scale);
   if (rc) return rc;
-  L.p.key_base = static_cast<int>(key_begin);
-  L.p.key_lo = static_cast<int>(key_begin);
-  L.p.key_hi = static_cast<int>(key_end);
-  L.p.status = status;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t units = kv_heads * L.p.n_pairs;
-  const int64_t rows = n_nodes * q_heads;
-  if (!workspace || !aligned(workspace, 16)) return DDT_ERR_WORKSPACE;
-  const int wpb = 8;
-  if (attn::kv_fits_l2(local, kv_heads) && attn::build_balanced(L, units)) {
-    if (workspace_bytes < attn::slot_bytes(L.n_parts)) return DDT_ERR_WORKSPACE;
-    const attn::SlotPtrs sp = attn::slot_ptrs(workspace, L.n_parts);
-    L.p.o_slot = sp.o;
-    L.p.m_part = sp.m;
-    L.p.l_part = sp.l;
-    L.p.partial = 1;
-    rc = attn::launch(L, kv_heads, st);
-    if (rc) return rc;
-    const int64_t warps = units * (attn::kRowsPerCta / 32) * (attn::kHeadDim / attn::kMergeDims);
-    attn::merge_slots_kernel<true><<<static_cast<unsigned>((warps + attn::kMergeWarps - 1) /
-                                                          attn::kMergeWarps),
-                                    attn::kMergeWarps * 32, 0, st>>>(
-        sp.o, sp.m, sp.l, L.slots, L.p, nullptr, 0, 0, o_part, m_part, l_part);
-    return launch_status();
-  }
-  // large shards (K / V beyond L2), units with no key in this shard, or tables too small:
-  // uniform splits, merged
-  const int64_t kv_tiles = (local + attn::kBlockN - 1) / attn::kBlockN;
-  const int splits = attn::pick_splits(units, kv_tiles > 0 ? kv_tiles : 1);
-  if (workspace_bytes < attn::part_bytes(rows, splits)) return DDT_ERR_WORKSPACE;
-  float* op = static_cast<float*>(workspace);
-  float* mp = op + static_cast<size_t>(splits) * rows * attn::kHeadDim;
-  float* lp = mp + static_cast<size_t>(splits) * rows;
-  L.p.n_splits = splits;
-  L.p.o_part = op;
-  L.p.m_part = mp;
-  L.p.l_part = lp;
-  L.p.partial = 1;
-  rc = attn::launch(L, kv_heads, st);
+  int kind = 0;
+  rc = attn::choose_plan(L, kv_heads, 0, true, kind);
   if (rc) return rc;
-  attn::merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0, st>>>(
-      op, mp, lp, splits, rows, static_cast<int>(q_heads), nullptr, 0, 0, o_part, m_part, l_part);
-  return launch_status();
+  L.p.status = status;
+  return attn::run(L, kind, kv_heads, workspace, workspace_bytes, nullptr, 0, 0, o_part, m_part,
+                   l_part, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_parts,
@@ -1485,4 +1498,31 @@ extern "C" int ddt_mask_to_bits(const void* mask, int dtype, int64_t n_nodes, in
   else
     return DDT_ERR_DTYPE;
   return launch_status();
+}
+
+extern "C" int ddt_tree_attn_wait_check(const void* q, const void* k, const void* v, void* out,
+                                        int64_t n_nodes, int64_t past_length, int64_t q_heads,
+                                        int64_t kv_heads, const uint32_t* anc_bits,
+                                        int64_t anc_words, uint64_t timeout_ns, int32_t* status,
+                                        void* stream) {
+  if (!out || !status) return DDT_ERR_INVALID;
+  if (timeout_ns < 100000ull || timeout_ns > attn::kTimeoutNs) return DDT_ERR_INVALID;
+  if (!aligned(out, 16)) return DDT_ERR_ALIGN;
+  attn::Launch L;
+  const int64_t S = past_length + n_nodes;
+  int rc = attn::prepare(L, q, q_heads * attn::kHeadDim, attn::kHeadDim, k, v, S * attn::kHeadDim,
+                         attn::kHeadDim, 0, S, n_nodes, past_length, q_heads, kv_heads,
+                         attn::kHeadDim, anc_bits, anc_words, DDT_MASK_TREE,
+                         1.0f / sqrtf(static_cast<float>(attn::kHeadDim)));
+  if (rc) return rc;
+  // one CTA per work unit over all of its keys, output written directly (no workspace)
+  L.p.n_splits = 1;
+  L.p.balanced = 0;
+  L.p.status = status;
+  L.p.timeout_ns = timeout_ns;
+  L.p.withhold_loads = 1;
+  L.p.out = static_cast<__nv_bfloat16*>(out);
+  L.p.o_node_stride = q_heads * attn::kHeadDim;
+  L.p.o_head_stride = attn::kHeadDim;
+  return attn::launch(L, kv_heads, static_cast<cudaStream_t>(stream));
 }

@@ -142,27 +142,63 @@ def compile_ddtree_tree(root_token_id, start: int, node_token_ids: torch.Tensor,
 
 def follow_verified_tree(child_maps: list[dict[int, int]], posterior: torch.Tensor):
     """ddtree.py:270-281: greedy walk from the root; returns (accepted_indices, next_token).
-    Runs the device walk over the tree registered by ``build_ddtree_tree`` when
-    ``child_maps`` describes that tree; otherwise walks ``child_maps`` itself."""
+    The walk runs on the device (ddt_accept_compact without cache tensors): over the tree
+    registered by ``build_ddtree_tree`` when ``child_maps`` describes that tree, otherwise over
+    the tree ``child_maps`` describes, copied to the device first.  Raises DDTreeError
+    (DDT_ERR_TIMEOUT) if the verify attention reported a bounded-wait timeout."""
     _require_cuda_tensor(posterior, "posterior")
     n = len(child_maps)
     post = posterior.reshape(-1)
     tree = _LAST.tree
+    status = K.attention_status(post.device)
     if tree is not None and _LAST.n_nodes == n and post.numel() >= n:
         empty = _EmptyKv.get(post.device)
         acc, cnt, nxt = K.accept_compact(post[:n], tree, empty, 0, n_nodes=n)
-        host = torch.cat([cnt.to(torch.int64), nxt, acc]).cpu().tolist()
-        c = host[0]
-        return host[2:2 + c], int(host[1])
-    tokens = post.tolist()
-    accepted = [0]
-    cur = 0
-    nxt = int(tokens[cur])
-    while nxt in child_maps[cur]:
-        cur = child_maps[cur][nxt]
-        accepted.append(cur)
-        nxt = int(tokens[cur])
-    return accepted, nxt
+        host = torch.cat([status.to(torch.int64), cnt.to(torch.int64), nxt, acc]).cpu().tolist()
+        if host[0] != 0:  # the verify attention gave up a bounded wait: the posterior is void
+            K.check_status(status, "tree attention of the verify forward")
+        c = host[1]
+        return host[3:3 + c], int(host[2])
+    # a tree this thread did not just build: its topology goes to the device and the same
+    # walk kernel runs over it
+    foreign = _tree_from_child_maps(child_maps, post.device)
+    if post.numel() < n:
+        raise ValueError("posterior shorter than the tree")
+    acc, cnt, nxt = K.accept_compact(post[:n], foreign, _EmptyKv.get(post.device), 0, n_nodes=n)
+    host = torch.cat([status.to(torch.int64), cnt.to(torch.int64), nxt, acc]).cpu().tolist()
+    if host[0] != 0:
+        K.check_status(status, "tree attention of the verify forward")
+    c = host[1]
+    return host[3:3 + c], int(host[2])
+
+
+def _tree_from_child_maps(child_maps: list[dict[int, int]], device) -> SimpleNamespace:
+    """Parents (i32 [n]) and node tokens (i64 [n - 1]) of the tree child_maps describes
+    (child_maps[p][token] = child, node i >= 1 carries token node_token_ids[i - 1])."""
+    n = len(child_maps)
+    parents = np.full(n, -1, np.int32)
+    tokens = np.zeros(max(n - 1, 1), np.int64)
+    for p, m in enumerate(child_maps):
+        for tok, c in m.items():
+            if not 0 < c < n or parents[c] != -1:
+                raise ValueError("child_maps does not describe a tree over nodes 0..n-1")
+            parents[c] = p
+            tokens[c - 1] = int(tok)
+    if n > 1 and (parents[1:] < 0).any():
+        raise ValueError("child_maps leaves a node without a parent")
+    depth = np.zeros(n, np.int64)
+    for c in range(1, n):  # a walk accepts at most DDT_MAX_DEPTH nodes below the root
+        d, j = 0, c
+        while j > 0 and d <= n:
+            j = int(parents[j])
+            d += 1
+        if d > n:
+            raise ValueError("child_maps contains a cycle")
+        depth[c] = d
+    if n > 1 and depth.max() > K._lib.DDT_MAX_DEPTH:
+        raise ValueError(f"tree deeper than {K._lib.DDT_MAX_DEPTH} levels")
+    return SimpleNamespace(parents=torch.from_numpy(parents).to(device),
+                           node_token_ids=torch.from_numpy(tokens).to(device), n_nodes=n)
 
 
 class _EmptyKv:

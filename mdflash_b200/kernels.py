@@ -13,7 +13,7 @@ from ._lib import DDT_BF16, DDT_F32, DDT_MASK_CAUSAL, DDT_MASK_TREE, check
 __all__ = [
     "DeviceTree", "expected_node_count", "topk_tree", "argmax", "accept_compact", "compact_kv",
     "tree_attention", "tree_attention_partial", "attn_merge", "mask_to_bits", "KvTable",
-    "anc_words_for",
+    "anc_words_for", "attention_status", "check_status", "tree_attention_wait_check",
 ]
 
 
@@ -80,6 +80,22 @@ class _Workspaces:
 
 
 WORKSPACES = _Workspaces()
+
+
+def attention_status(device: torch.device) -> torch.Tensor:
+    """The device's default status word (i32 [1]) of tree-attention launches that are given
+    none: a bounded wait of the kernel that ran out sets it non-zero."""
+    return WORKSPACES.get(device, "attn_status", 256)[:4].view(torch.int32)
+
+
+def check_status(status: torch.Tensor, what: str = "ddt_tree_attn") -> None:
+    """Reads a status word (this syncs with its stream) and raises DDTreeError with
+    DDT_ERR_TIMEOUT when a launch that wrote to it gave up a bounded wait; the word is
+    cleared first, so the next launches start clean."""
+    v = int(status.reshape(-1)[0].item())
+    if v != 0:
+        status.zero_()
+        check(_lib.DDT_ERR_TIMEOUT, what)
 
 
 def anc_words_for(n_nodes: int) -> int:
@@ -289,8 +305,20 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    causal: bool = False, out: torch.Tensor | None = None, kv_splits: int = 0,
                    status: torch.Tensor | None = None) -> torch.Tensor:
     """softmax(Q K^T * scale, tree / causal mask) V on tcgen05.  q: [N, Hq, D] (or HF
-    [1, Hq, N, D]); k, v: [Hkv, past_length + N, D] (or [1, ...]); returns [N, Hq, D]."""
+    [1, Hq, N, D]); k, v: [Hkv, past_length + N, D] (or [1, ...]); returns [N, Hq, D].
+
+    The kernel computes in bf16 (fp32 accumulation).  fp32 inputs (an fp32 model) are rounded
+    to bf16 for the kernel and the output is returned in fp32: the result is within the bf16
+    tolerance of fp32 attention, not fp32-exact."""
     dev = _require_cuda(q, k, v)
+    if q.dtype == torch.float32 and k.dtype == torch.float32 and v.dtype == torch.float32:
+        res = tree_attention(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16),
+                             anc_bits, past_length, scale=scale, causal=causal,
+                             kv_splits=kv_splits, status=status)
+        if out is None:
+            return res.float()
+        out.copy_(res)
+        return out
     n, hq, qns, qhs = _q_view(q)
     hkv, s, khs, kss = _kv_view(k)
     _, _, vhs, vss = _kv_view(v)
@@ -300,7 +328,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if s != past_length + n:
         raise ValueError(f"key length {s} != past_length + nodes ({past_length} + {n})")
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
-        raise TypeError("tree attention runs in bf16")
+        raise TypeError("tree attention takes bf16 (or all-fp32) q / k / v")
     if out is None:
         out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=dev)
     if scale is None:
@@ -309,7 +337,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     ws_bytes = lib.ddt_tree_attn_workspace_bytes(n, hq, d, kv_splits)
     ws = WORKSPACES.get(dev, "tree_attn", ws_bytes)
     if status is None:
-        status = WORKSPACES.get(dev, "attn_status", 256)[:4].view(torch.int32)
+        status = attention_status(dev)
     mode = DDT_MASK_CAUSAL if causal else DDT_MASK_TREE
     if not causal and anc_bits is None:
         raise ValueError("tree mode needs ancestor bitmasks")
@@ -366,7 +394,7 @@ def tree_attention_partial(q, k_shard, v_shard, key_begin: int, key_end: int, an
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     if status is None:
-        status = WORKSPACES.get(dev, "attn_status", 256)[:4].view(torch.int32)
+        status = attention_status(dev)
     words = anc_bits.shape[1] if anc_bits is not None else 0
     rc = lib.ddt_tree_attn_partial(
         q.data_ptr(), qns, qhs, k_shard.data_ptr(), v_shard.data_ptr(), khs, kss, key_begin,
@@ -401,7 +429,7 @@ def tree_attention_partial_merged(q, k_shard, v_shard, key_begin: int, key_end: 
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     if status is None:
-        status = WORKSPACES.get(dev, "attn_status", 256)[:4].view(torch.int32)
+        status = attention_status(dev)
     ws_bytes = lib.ddt_tree_attn_partial_merged_workspace_bytes(n, hq, d)
     ws = WORKSPACES.get(dev, "attn_partial_merged", ws_bytes)
     words = anc_bits.shape[1] if anc_bits is not None else 0
@@ -414,6 +442,27 @@ def tree_attention_partial_merged(q, k_shard, v_shard, key_begin: int, key_end: 
     check(rc, "ddt_tree_attn_partial_merged")
     STATS.launches += 2
     return o, m, l
+
+
+def tree_attention_wait_check(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                              anc_bits: torch.Tensor, past_length: int, timeout_ns: int,
+                              status: torch.Tensor) -> torch.Tensor:
+    """ddt_tree_attn_wait_check: one attention launch whose producer withholds every load,
+    so each wait of the kernel runs out after timeout_ns; returns the output buffer (zeros
+    where the kernel reached its epilogue).  The caller reads `status` afterwards."""
+    dev = _require_cuda(q, k, v, anc_bits, status)
+    n, hq, d = q.shape
+    hkv = k.shape[0]
+    for t in (q, k, v):
+        if not t.is_contiguous() or t.dtype != torch.bfloat16:
+            raise ValueError("contiguous bf16 q / k / v expected")
+    out = torch.zeros_like(q)
+    check(_lib.load().ddt_tree_attn_wait_check(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), n, past_length, hq, hkv,
+        anc_bits.data_ptr(), anc_bits.shape[1], int(timeout_ns), status.data_ptr(),
+        _stream(dev)), "ddt_tree_attn_wait_check")
+    STATS.launches += 1
+    return out
 
 
 def attn_merge(o_parts: torch.Tensor, m_parts: torch.Tensor, l_parts: torch.Tensor, n_nodes: int,

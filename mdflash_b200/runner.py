@@ -64,10 +64,12 @@ class Qwen3VerifyRunner:
         return torch.cuda.current_stream(self.device).cuda_stream
 
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, cache, past_length: int,
-                anc_bits: torch.Tensor | None, causal: bool = False) -> torch.Tensor:
+                anc_bits: torch.Tensor | None, causal: bool = False,
+                status: torch.Tensor | None = None) -> torch.Tensor:
         """ids, positions: i64 [N] (device).  Writes the N new K/V rows into `cache`
         (a TreeKVCache) at [past_length, past_length + N) and returns logits [N, V] (bf16).
-        Tree mode attends with anc_bits; causal=True attends causally (prefill)."""
+        Tree mode attends with anc_bits; causal=True attends causally (prefill).  Attention
+        timeouts go to `status` (default: the device's status word)."""
         lib = _lib.load()
         st = self._stream()
         n = ids.numel()
@@ -93,7 +95,7 @@ class Qwen3VerifyRunner:
             K.STATS.launches += 3
             s = past_length + n
             attn = K.tree_attention(q, kbuf[:, :s], vbuf[:, :s], anc_bits, past_length,
-                                    scale=self.scaling, causal=causal)
+                                    scale=self.scaling, causal=causal, status=status)
             o = torch.matmul(attn.view(n, hq * d), w["w_o"].t())
             check(lib.ddt_add_rmsnorm(x.data_ptr(), o.data_ptr(), w["ln2"].data_ptr(), n, H,
                                       self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")

@@ -128,6 +128,24 @@ def owner_rank(world: int) -> int:
     return world - 1
 
 
+def compact_owner_shard(keep, kv_table, shard: tuple[int, int], past_length: int) -> None:
+    """KV compaction of a split-KV request (ddtree.py:284-335) on the rank that owns the tree
+    keys: global rows past_length + keep[j] move to past_length + j inside this rank's shard
+    [key_begin, key_end), whose K / V tensors are kv_table (local row r holds global key
+    key_begin + r).  The other ranks hold prefix keys only, which compaction never moves.
+    Raises ValueError on a rank whose shard does not hold the tree window."""
+    from . import kernels as K
+    key_begin, key_end = int(shard[0]), int(shard[1])
+    keep_list = keep.tolist() if isinstance(keep, torch.Tensor) else [int(x) for x in keep]
+    if not keep_list:
+        return
+    if not (key_begin <= past_length and past_length + max(keep_list) < key_end):
+        raise ValueError(f"shard [{key_begin}, {key_end}) does not own the tree keys at "
+                         f"{past_length}: compaction runs on the owner rank")
+    K.compact_kv(keep if isinstance(keep, torch.Tensor) else keep_list, kv_table,
+                 past_length - key_begin)
+
+
 def exchange_partials(o: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=None):
     """All-gathers this rank's partials (O [S, rows, D], m [S, rows], l [S, rows]; a single
     partial may drop the leading S) into ([world * S, rows, D], [world * S, rows] x 2).

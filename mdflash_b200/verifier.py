@@ -33,6 +33,7 @@ class StepResult:
     n_accepted: torch.Tensor    # i32 [1], device
     next_token: torch.Tensor    # i64 [1], device
     posterior: torch.Tensor     # i64 [n_nodes], device
+    status: torch.Tensor        # i32 [1], device: non-zero if an attention wait timed out
     logits: torch.Tensor | None = None
 
 
@@ -60,6 +61,7 @@ class TreeVerifier:
         self.accepted = torch.zeros(n_cap, dtype=torch.int64, device=self.device)
         self.n_accepted = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.next_token = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     @torch.inference_mode()
     def step(self, draft_logits: torch.Tensor, root_token: torch.Tensor, start: int) -> StepResult:
@@ -74,20 +76,28 @@ class TreeVerifier:
         pos = tree.verify_pos[:n].view(1, n)
         if self.runner is not None:
             logits = self.runner.forward(tree.verify_ids[:n], tree.verify_pos[:n], self.cache,
-                                         start, tree.anc_bits)
+                                         start, tree.anc_bits, status=self.status)
         else:
-            with A.tree_verify(tree, start, n):
+            with A.tree_verify(tree, start, n, status=self.status):
                 out = self.target(ids, position_ids=pos, past_key_values=self.cache,
                                   use_cache=True)
             logits = out.logits[0]
         post = K.argmax(logits, out=self.posterior[:n])
         K.accept_compact(post, tree, self.cache.kv_table(), start, accepted=self.accepted,
                          n_accepted=self.n_accepted, next_token=self.next_token, n_nodes=n)
-        return StepResult(n, self.accepted, self.n_accepted, self.next_token, post,
+        return StepResult(n, self.accepted, self.n_accepted, self.next_token, post, self.status,
                           logits if self.keep_logits else None)
 
+    def check(self) -> None:
+        """Raises DDTreeError (DDT_ERR_TIMEOUT) if an attention launch of the steps since the
+        last check gave up a bounded wait (its output, and so the step's result, is then
+        incomplete).  Reads the status word, so it syncs with the device."""
+        K.check_status(self.status, "tree attention of the verify step")
+
     def commit(self, start: int, n_accepted: int) -> None:
-        """Sets the cache length to start + n_accepted after the caller read the count."""
+        """Sets the cache length to start + n_accepted after the caller read the count, and
+        raises if the step's attention reported a timeout (the caller has synced already)."""
+        self.check()
         self.cache.crop(start + n_accepted)
 
 

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/ by running the reference's own code.
 
-Run in a container where the DDTree research code is mounted (default path below, or
---reference PATH).  It imports ddtree.py / dflash.py / model/ unchanged except:
+Run where the DDTree research code is checked out: --reference PATH, or the environment
+variable DDTREE_REFERENCE.  It imports ddtree.py / dflash.py / model/ unchanged except:
   * ``cuda_time`` is replaced by ``time.perf_counter`` (the original calls
     torch.cuda.synchronize, dflash.py:140-142, and this generator runs on a CPU);
   * for inputs with value ties (bf16 logits, crafted small vocabularies) ``torch.topk``
@@ -221,6 +221,7 @@ def gen_e2e(ddtree, out: dict, manifest: dict):
         o = model(ids, position_ids=torch.arange(P)[None], past_key_values=cache, use_cache=True,
                   logits_to_keep=1)
         root = o.logits.argmax(-1)[0, -1]
+        root_top2 = torch.topk(o.logits[0, -1], 2)
         res = ddtree.build_ddtree_tree(draft_logits, B)
         node_ids, depths, parents, child_maps, vis, _ = res
         ids_buf = torch.empty((1, N), dtype=torch.long)
@@ -234,7 +235,8 @@ def gen_e2e(ddtree, out: dict, manifest: dict):
         logits = o2.logits[0]
         post = logits.argmax(-1)
         acc, nxt = ddtree.follow_verified_tree(child_maps, post[None])
-        top2 = torch.topk(logits, 2, dim=-1).values
+        top2v, top2i = torch.topk(logits, 2, dim=-1)
+        top2 = top2v
         kv_before = [(l.keys.clone(), l.values.clone()) for l in cache.layers]
         ddtree.compact_dynamic_cache(cache, P, acc)
     out["e2e/root"] = np.array([int(root)], np.int64)
@@ -244,6 +246,13 @@ def gen_e2e(ddtree, out: dict, manifest: dict):
     out["e2e/posterior"] = post.numpy().astype(np.int64)
     out["e2e/logit_top2"] = top2.numpy()
     out["e2e/logits_row_sum"] = logits.double().sum(-1).numpy()
+    out["e2e/logit_top2_ids"] = top2i.numpy().astype(np.int64)
+    out["e2e/root_top2"] = root_top2.values.numpy()
+    out["e2e/root_top2_ids"] = root_top2.indices.numpy().astype(np.int64)
+    # a seeded sample of 4096 vocabulary columns of every verify row, for per-element checks
+    cols = np.sort(np.random.default_rng(20260).choice(logits.shape[-1], 4096, replace=False))
+    out["e2e/logit_cols"] = cols.astype(np.int64)
+    out["e2e/logit_sample"] = logits[:, torch.from_numpy(cols)].numpy().astype(np.float32)
     out["e2e/accepted"] = np.asarray(acc, np.int64)
     out["e2e/next_token"] = np.array([nxt], np.int64)
     out["e2e/seq_len_after"] = np.array([cache.get_seq_length()], np.int64)
@@ -254,10 +263,15 @@ def gen_e2e(ddtree, out: dict, manifest: dict):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DDTREE_REFERENCE"),
+                    help="checkout of the DDTree research code (default: $DDTREE_REFERENCE)")
+    ap.add_argument("--only-e2e", action="store_true",
+                    help="regenerate only the e2e/* arrays, keeping the others of golden.npz")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--no-cpp", action="store_true")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference PATH (or DDTREE_REFERENCE) is required")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     # the reference builds its inline C++ extension; keep that build out of the home dir
     os.environ.setdefault("TORCH_EXTENSIONS_DIR", tempfile.mkdtemp(prefix="ddtree_ref_ext_"))
@@ -265,6 +279,17 @@ def main():
     out: dict = {}
     manifest: dict = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__}
     t0 = time.time()
+    if args.only_e2e:
+        old = np.load(os.path.join(HERE, "golden.npz"))
+        out = {k: old[k] for k in old.files if not k.startswith("e2e/")}
+        with open(os.path.join(HERE, "manifest.json")) as f:
+            manifest = json.load(f)
+        gen_e2e(ddtree, out, manifest)
+        np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)
+        with open(os.path.join(HERE, "manifest.json"), "w") as f:
+            json.dump(manifest, f, indent=1, sort_keys=True)
+        print(f"wrote {len(out)} arrays in {time.time() - t0:.1f}s")
+        return
     gen_trees(ddtree, out, manifest)
     gen_compile(ddtree, out, manifest)
     gen_follow(ddtree, out, manifest)

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
 def test_error_strings_and_version():
     lib = _lib.load()
     assert lib.ddt_version() >= 1
-    for code in (0, -1, -2, -3, -4, -5, -6, -7):
+    for code in (0, -1, -2, -3, -4, -5, -6, -7, -8):
         assert lib.ddt_error_string(code)
     assert lib.ddt_error_string(-99) == b"unknown error"
 
@@ -60,6 +60,10 @@ def test_host_side_validation_rejects_bad_arguments():
     assert lib.ddt_compact_kv(ctypes.c_void_p(256), 64, ctypes.c_void_p(256), 2, 2, 128, 1024,
                               128, 2, 10, None) == -2
     assert lib.ddt_argmax(None, 2, 4, 4, 4, None, None) == -3
+    # the bounded-wait check takes limits from 100 us to 2 s and needs a status word
+    p = ctypes.c_void_p(256)
+    assert lib.ddt_tree_attn_wait_check(p, p, p, p, 65, 256, 32, 8, p, 3, 10, p, None) == -1
+    assert lib.ddt_tree_attn_wait_check(p, p, p, p, 65, 256, 32, 8, p, 3, 10**6, None, None) == -1
 
 
 def test_workspace_queries():
@@ -84,7 +88,7 @@ def test_attention_split_count(n, past, expect):
     assert attn_splits(n, 32, 8, past, kv_splits=5) == 5
 
 
-def _plan(n, past, hq, hkv, splits=0, key_begin=0, key_end=0):
+def _plan(n, past, hq, hkv, splits=0, key_begin=0, key_end=-1):
     import ctypes
     from mdflash_b200 import _lib
     out = (ctypes.c_int64 * 4)()
@@ -144,6 +148,23 @@ def test_attention_shard_tables_cover_every_tile():
     assert seen_balanced > 50
     # a shard outside the key range is rejected
     assert _plan(65, 1000, 32, 8, 0, 500, 2000)[0] == -1
+
+
+def test_attention_shard_plans_report_their_merge():
+    """A shard's result is always one merged partial per row, so a shard plan reports at
+    least one part to merge, and an empty shard is planned as a shard, not as the full range."""
+    # the first shard of a prefix beyond L2 with few key tiles per unit: uniform splits
+    for b, e in [(0, 512), (0, 131072 // 8), (0, 128)]:
+        rc, plan = _plan(513, 131072, 32, 8, 0, b, e)
+        assert rc == 0 and plan[2] >= 1, (b, e, plan)
+    rc, plan = _plan(257, 300000, 32, 8, 0, 0, 300000)
+    assert rc == 0 and plan[0] == 0 and plan[2] >= 1
+    # the empty shard [0, 0) (rank 0's shard of an empty prefix): uniform, one part, merged
+    rc, plan = _plan(65, 0, 32, 8, 0, 0, 0)
+    assert rc == 0 and plan == [0, 8 * 2, 1, 1]
+    # the full-range call of the same sizes: one launch, nothing to merge
+    rc, plan = _plan(65, 0, 32, 8)
+    assert rc == 0 and plan[2] == 0
 
 
 @pytest.mark.parametrize("depths,vocab,budget,expect", [

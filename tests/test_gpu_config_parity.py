@@ -1,0 +1,375 @@
+"""Config-level parity of the verify path at the stated tolerance, on the benchmark configs.
+
+Tolerance (bf16): logits and attention outputs are compared element by element,
+|ours - ref| <= 2e-2 * max(|ref|, rms(ref row)): a relative error of 2e-2, with the row's
+root-mean-square as the floor for elements near zero (their error is set by the row's scale,
+not their own).  The normalised check max|err| / max|ref| <= 2e-2 is kept beside it.
+
+Greedy posteriors must agree on >= 99.9% of the rows whose reference top-1 / top-2 gap is
+larger than TIE_GAP (a few bf16 steps of the largest logit: below it the order of the two
+best tokens is within the bf16 rounding of the logits).  Rows at or below it are near-ties:
+every disagreeing row is logged with its gap, tie or not.  Tree topology, verify ids and
+positions, accepted paths (whenever the posteriors agree along the path) and compacted
+caches are bit-exact.
+
+  cfg 1  random-init Qwen3-0.6B shape (28 layers, fp32), prompt 512, budget 32, against the
+         golden step produced by running the reference on the CPU (tests/golden)
+  cfg 3  random-init Qwen3-8B shape (36 layers, bf16), prefix 8192, budget 256, against
+         transformers' sdpa path (the reference's verify forward, ddtree.py:440-486) on the
+         same GPU and the same weights
+  cfg 5  split-KV attention at 131072 prefix keys and 513 tree rows (Qwen3-8B attention
+         shape), sharded over 2 / 4 / 8 key ranges in one process, against the single-launch
+         kernel and an fp32 reference on sampled rows; compaction on the owning shard
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import inputs as gin
+import oracle
+from mdflash_b200 import attention as A
+from mdflash_b200 import ddtree as D
+from mdflash_b200 import kernels as K
+from mdflash_b200 import sharding as S
+from mdflash_b200.cache import TreeKVCache
+from mdflash_b200.verifier import TreeVerifier
+from parity_util import elem_rel_err, norm_rel_err, posterior_agreement, walk_agrees
+
+pytestmark = pytest.mark.gpu
+RTOL = 2e-2
+AGREE = 0.999
+
+
+# ------------------------------------------------------------------------------ cfg 1
+@pytest.fixture(scope="module")
+def cfg1(cuda_device):
+    spec = gin.E2E_CASE
+    A.register()
+    model = gin.e2e_model(spec, attn_implementation=A.ATTN_IMPLEMENTATION)  # fp32, CPU init
+    model = model.to(cuda_device)
+    ids, draft_logits = gin.e2e_inputs(spec)
+    return spec, model, ids.to(cuda_device), draft_logits.to(cuda_device)
+
+
+def _cfg1_tie_gap(golden):
+    # fp32 model, attention in bf16: 4 bf16 steps (2^-8 relative) of the largest logit
+    return 4 * 2.0 ** -8 * float(np.abs(golden["e2e/logit_sample"]).max())
+
+
+def _check_cfg1_logits(golden, logits, label):
+    cols = torch.from_numpy(golden["e2e/logit_cols"]).to(logits.device)
+    sample = logits[:, cols]
+    ref = torch.from_numpy(golden["e2e/logit_sample"])
+    e1, e2 = elem_rel_err(sample, ref), norm_rel_err(sample, ref)
+    top_ids = torch.from_numpy(golden["e2e/logit_top2_ids"]).to(logits.device)
+    top_ours = torch.gather(logits, 1, top_ids)
+    top_ref = torch.from_numpy(golden["e2e/logit_top2"])
+    e3 = (top_ours.float().cpu() - top_ref).abs().max().item()
+    print(f"[{label}] logits: elem rel err {e1:.3e}, norm rel err {e2:.3e}, top-2 abs err {e3:.3e}")
+    assert e1 <= RTOL and e2 <= RTOL
+    return e3
+
+
+def test_cfg1_dropin_step_matches_reference_golden(golden, cfg1, cuda_device):
+    """The drop-in functions + the ddtree_tree plug-in, called as ddtree_generate calls them
+    (ddtree.py:440-486), on the fp32 Qwen3-0.6B-shaped model."""
+    from transformers import DynamicCache
+    spec, model, ids, draft_logits = cfg1
+    P, B = spec["prompt"], spec["budget"]
+    N = B + 1
+    with torch.inference_mode():
+        cache = DynamicCache()
+        out = model(ids, position_ids=torch.arange(P, device=cuda_device)[None],
+                    past_key_values=cache, use_cache=True, logits_to_keep=1)
+        root_top2 = golden["e2e/root_top2"]
+        root = out.logits[0, -1].argmax()
+        print(f"[cfg1] root {int(root)} golden {int(golden['e2e/root'][0])} "
+              f"(golden gap {root_top2[0] - root_top2[1]:.4g})")
+        assert int(root) == int(golden["e2e/root"][0])
+        node_ids, depths, parents, child_maps, vis, _ = D.build_ddtree_tree(draft_logits, B)
+        np.testing.assert_array_equal(node_ids.numpy(), golden["e2e/node_ids"])
+        np.testing.assert_array_equal(depths.numpy(), golden["e2e/depths"])
+        np.testing.assert_array_equal(np.asarray(parents, np.int32), golden["e2e/parents"])
+        vib = torch.empty((1, N), dtype=torch.long, device=cuda_device)
+        vpb = torch.empty((1, N), dtype=torch.long, device=cuda_device)
+        amb = torch.zeros((1, 1, N, P + N), dtype=torch.float32, device=cuda_device)
+        tvb = torch.empty((N, N), dtype=torch.bool, device=cuda_device)
+        vi, vp, am, _, cl = D.compile_ddtree_tree(root, P, node_ids, depths, vis, P, torch.float32,
+                                                  cuda_device, vib, vpb, amb, tvb, 0, 0)
+        assert cl == N
+        logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=cache,
+                       use_cache=True).logits[0]
+        post = K.argmax(logits)
+        torch.cuda.synchronize()
+        _check_cfg1_logits(golden, logits, "cfg1 drop-in")
+        top2 = golden["e2e/logit_top2"]
+        frac = posterior_agreement("cfg1 drop-in", post.cpu().numpy(), golden["e2e/posterior"],
+                                   top2[:, 0] - top2[:, 1], _cfg1_tie_gap(golden))
+        assert frac >= AGREE
+        acc, nxt = D.follow_verified_tree(child_maps, post[None])
+        g_acc = golden["e2e/accepted"].tolist()
+        if walk_agrees(g_acc, post.cpu().numpy(), golden["e2e/posterior"]):
+            assert acc == g_acc and nxt == int(golden["e2e/next_token"][0])
+        k0_before = cache.layers[0].keys[0, :, P:, :].float().cpu()
+        assert elem_rel_err(k0_before, torch.from_numpy(golden["e2e/k0_tree"])) <= RTOL
+        D.compact_dynamic_cache(cache, P, acc)
+        assert cache.get_seq_length() == P + len(acc)
+        if acc == g_acc:
+            assert cache.get_seq_length() == int(golden["e2e/seq_len_after"][0])
+
+
+def test_cfg1_tree_verifier_matches_reference_golden(golden, cfg1, cuda_device):
+    """The device-resident step (TreeVerifier over the transformers model with the plug-in,
+    fp32 static-capacity cache) on the same inputs."""
+    spec, model, ids, draft_logits = cfg1
+    P, B = spec["prompt"], spec["budget"]
+    cfg = model.config
+    cache = TreeKVCache(cfg.num_hidden_layers, P + B + 8).allocate(
+        cfg.num_key_value_heads, cfg.head_dim, torch.float32, cuda_device)
+    ver = TreeVerifier(model, cache, B, spec["depths"], spec["vocab"], cuda_device,
+                       keep_logits=True)
+    with torch.inference_mode():
+        out = model(ids, position_ids=torch.arange(P, device=cuda_device)[None],
+                    past_key_values=cache, use_cache=True, logits_to_keep=1)
+        root = K.argmax(out.logits[0, -1:]).view(1)
+        res = ver.step(draft_logits, root, P)
+        torch.cuda.synchronize()
+    n = res.n_nodes
+    assert n == B + 1
+    np.testing.assert_array_equal(ver.tree.parents[:n].cpu().numpy(), golden["e2e/parents"])
+    np.testing.assert_array_equal(ver.tree.node_token_ids[:n - 1].cpu().numpy(),
+                                  golden["e2e/node_ids"])
+    np.testing.assert_array_equal(ver.tree.verify_pos[1:n].cpu().numpy(),
+                                  golden["e2e/depths"] + P)
+    _check_cfg1_logits(golden, res.logits, "cfg1 verifier")
+    top2 = golden["e2e/logit_top2"]
+    post = res.posterior.cpu().numpy()
+    frac = posterior_agreement("cfg1 verifier", post, golden["e2e/posterior"],
+                               top2[:, 0] - top2[:, 1], _cfg1_tie_gap(golden))
+    assert frac >= AGREE
+    k = int(res.n_accepted.item())
+    acc = res.accepted[:k].tolist()
+    o_acc, o_next = oracle.follow_verified_tree(
+        (golden["e2e/parents"], golden["e2e/node_ids"]), post)
+    assert acc == o_acc and int(res.next_token.item()) == o_next
+    g_acc = golden["e2e/accepted"].tolist()
+    if walk_agrees(g_acc, post, golden["e2e/posterior"]):
+        assert acc == g_acc
+    ver.commit(P, k)  # also checks the attention status word
+    assert cache.get_seq_length() == P + k
+
+
+# ------------------------------------------------------------------------------ cfg 3
+QWEN3_8B = dict(layers=36, hidden=4096, heads=32, kv_heads=8, head_dim=128, mlp=12288,
+                vocab=gin.V_QWEN3, rope_theta=1e6)
+
+
+@pytest.fixture(scope="module")
+def cfg3(cuda_device):
+    """Qwen3-8B-shaped random-init model in bf16, prefix 8192 prefilled by the reference path
+    (sdpa), and the reference tree-verify step of a 256-node tree (sdpa + additive mask)."""
+    from transformers import DynamicCache, Qwen3Config, Qwen3ForCausalLM
+    s = QWEN3_8B
+    cfg = Qwen3Config(vocab_size=s["vocab"], hidden_size=s["hidden"], intermediate_size=s["mlp"],
+                      num_hidden_layers=s["layers"], num_attention_heads=s["heads"],
+                      num_key_value_heads=s["kv_heads"], head_dim=s["head_dim"],
+                      rope_theta=s["rope_theta"], max_position_embeddings=40960,
+                      rms_norm_eps=1e-6, tie_word_embeddings=False, attn_implementation="sdpa")
+    A.register()
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(cuda_device):
+        model = Qwen3ForCausalLM(cfg).eval()
+    torch.set_default_dtype(prev)
+    P, B, L = 8192, 256, 15
+    rng = np.random.default_rng(2024)
+    ids = torch.from_numpy(rng.integers(0, s["vocab"], (1, P))).to(cuda_device)
+    draft = torch.from_numpy(rng.standard_normal((L, s["vocab"])).astype(np.float32) *
+                             np.float32(3.0)).to(torch.bfloat16).to(cuda_device)
+    model.config._attn_implementation = "sdpa"
+    ref_cache = DynamicCache()
+    with torch.inference_mode():
+        out = model(ids, position_ids=torch.arange(P, device=cuda_device)[None],
+                    past_key_values=ref_cache, use_cache=True, logits_to_keep=1)
+        root = out.logits[0, -1].argmax()
+        del out
+        tree = oracle.build_ddtree_tree(draft.cpu(), B)
+        node_ids, depths, parents, child_maps, vis, _ = tree
+        n = 1 + node_ids.numel()
+        vib = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        vpb = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        amb = torch.zeros((1, 1, n, P + n), dtype=torch.bfloat16, device=cuda_device)
+        tvb = torch.empty((n, n), dtype=torch.bool, device=cuda_device)
+        vi, vp, am, _, _ = oracle.compile_ddtree_tree(root, P, node_ids, depths, vis, P,
+                                                      torch.bfloat16, cuda_device, vib, vpb, amb,
+                                                      tvb, 0, 0)
+        # the prefix K / V before the verify step appends the tree rows
+        prefix_kv = [(l.keys[..., :P, :].clone(), l.values[..., :P, :].clone())
+                     for l in ref_cache.layers]
+        ref_logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=ref_cache,
+                           use_cache=True).logits[0]
+    top2 = torch.topk(ref_logits.float(), 2, dim=-1).values
+    return dict(model=model, P=P, B=B, L=L, root=root, draft=draft, tree=tree, n=n,
+                prefix_kv=prefix_kv, ref_logits=ref_logits, ref_post=ref_logits.argmax(-1),
+                ref_gap=(top2[:, 0] - top2[:, 1]).cpu().numpy(), ref_cache=ref_cache, vi=vi,
+                vp=vp)
+
+
+def _cfg3_tie_gap(ref_logits):
+    # both paths round the logits to bf16: 2 bf16 steps (2^-7 relative each) of the largest
+    # logit, plus the accumulated difference of the two forwards, as much again
+    return 4 * 2.0 ** -7 * ref_logits.float().abs().max().item()
+
+
+@pytest.mark.parametrize("fused", [True, False], ids=["fused_runner", "transformers_plugin"])
+def test_cfg3_verify_step_matches_sdpa(cfg3, cuda_device, fused):
+    c = cfg3
+    model, P, B = c["model"], c["P"], c["B"]
+    model.config._attn_implementation = A.ATTN_IMPLEMENTATION
+    cache = TreeKVCache(36, P + B + 8).allocate(8, 128, torch.bfloat16, cuda_device)
+    for layer, (k, v) in zip(cache.layers, c["prefix_kv"]):
+        layer.k_buf[..., :P, :].copy_(k)
+        layer.v_buf[..., :P, :].copy_(v)
+        layer.length = P
+        layer.keys = layer.k_buf[..., :P, :]
+        layer.values = layer.v_buf[..., :P, :]
+    ver = TreeVerifier(model, cache, B, c["L"], QWEN3_8B["vocab"], cuda_device, keep_logits=True,
+                       fused=fused)
+    with torch.inference_mode():
+        res = ver.step(c["draft"], c["root"].view(1), P)
+        torch.cuda.synchronize()
+    n = c["n"]
+    o_ids, o_depths, o_par, o_cm, _, _ = c["tree"]
+    assert res.n_nodes == n
+    assert ver.tree.parents[:n].tolist() == o_par
+    assert torch.equal(ver.tree.node_token_ids[:n - 1].cpu(), o_ids)
+    assert torch.equal(ver.tree.verify_ids[:n].view(1, n), c["vi"])
+    assert torch.equal(ver.tree.verify_pos[:n].view(1, n), c["vp"])
+    label = "cfg3 " + ("fused" if fused else "plugin")
+    e1, e2 = elem_rel_err(res.logits, c["ref_logits"]), norm_rel_err(res.logits, c["ref_logits"])
+    print(f"[{label}] logits: elem rel err {e1:.3e}, norm rel err {e2:.3e}")
+    assert e1 <= RTOL and e2 <= RTOL
+    # the tree rows' K / V written by the step, every layer
+    for li in (0, 17, 35):
+        ours = cache.layers[li].k_buf[0, :, P:P + n, :]
+        ref = c["ref_cache"].layers[li].keys[0, :, P:P + n, :]
+        assert elem_rel_err(ours, ref) <= RTOL, li
+    frac = posterior_agreement(label, res.posterior.cpu().numpy(), c["ref_post"].cpu().numpy(),
+                               c["ref_gap"], _cfg3_tie_gap(c["ref_logits"]))
+    assert frac >= AGREE
+    k = int(res.n_accepted.item())
+    acc = res.accepted[:k].tolist()
+    o_acc, o_next = oracle.follow_verified_tree((np.asarray(o_par, np.int32), o_ids.numpy()),
+                                                res.posterior.cpu())
+    assert acc == o_acc and int(res.next_token.item()) == o_next
+    ref_acc, ref_next = oracle.follow_verified_tree(o_cm, c["ref_post"].cpu())
+    if walk_agrees(ref_acc, res.posterior.cpu(), c["ref_post"].cpu()):
+        assert acc == ref_acc
+    ver.commit(P, k)
+
+
+# ------------------------------------------------------------------------------ cfg 5
+@pytest.fixture(scope="module")
+def cfg5(cuda_device):
+    P, N = 131072, 513
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    sc = 128 ** -0.5
+    q = (torch.randn((N, 32, 128), generator=g, device=cuda_device) * sc).to(torch.bfloat16)
+    k = (torch.randn((8, P + N, 128), generator=g, device=cuda_device) * sc).to(torch.bfloat16)
+    v = torch.randn((8, P + N, 128), generator=g, device=cuda_device).to(torch.bfloat16)
+    parents = gin.random_tree(N, 55)
+    bits = torch.from_numpy(oracle.ancestor_bits(parents).view(np.int32)).to(cuda_device)
+    full = K.tree_attention(q, k, v, bits, P)
+    torch.cuda.synchronize()
+    return dict(P=P, N=N, q=q, k=k, v=v, parents=parents, bits=bits, full=full)
+
+
+def _fp32_rows(c, nodes):
+    """Exact fp32 attention of the given nodes (all 32 q heads) over the prefix and their
+    tree ancestors."""
+    P = c["P"]
+    parents = c["parents"]
+    out = []
+    for i in nodes:
+        anc = []
+        j = int(i)
+        while j >= 0:
+            anc.append(j)
+            j = int(parents[j]) if j > 0 else -1
+        keys = torch.cat([torch.arange(P, device=c["k"].device),
+                          torch.tensor(sorted(anc), device=c["k"].device) + P])
+        kk = c["k"][:, keys].float()  # [8, S, 128]
+        vv = c["v"][:, keys].float()
+        qq = c["q"][i].float().view(8, 4, 128)  # q head h -> kv head h // 4
+        s = torch.einsum("hgd,hsd->hgs", qq, kk) / math.sqrt(128)
+        o = torch.einsum("hgs,hsd->hgd", torch.softmax(s, -1), vv)
+        out.append(o.reshape(32, 128))
+    return torch.stack(out)
+
+
+def test_cfg5_single_launch_matches_fp32_rows(cfg5):
+    c = cfg5
+    depth = np.zeros(c["N"], np.int64)
+    for i in range(1, c["N"]):
+        depth[i] = depth[c["parents"][i]] + 1
+    nodes = [0, 1, 2, 255, 256, 511, 512, int(np.argmax(depth))]
+    ref = _fp32_rows(c, nodes)
+    ours = c["full"][nodes]
+    e1, e2 = elem_rel_err(ours, ref), norm_rel_err(ours, ref)
+    print(f"[cfg5 single] elem rel err {e1:.3e}, norm rel err {e2:.3e}")
+    assert e1 <= RTOL and e2 <= RTOL
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_cfg5_splitkv_shards_match_single_launch(cfg5, world):
+    """Every shard's in-GPU-merged partial (the owner shard holding the tree keys), then the
+    cross-shard merge, against the single launch and the fp32 rows."""
+    c = cfg5
+    P, N = c["P"], c["N"]
+    parts = []
+    for r in range(world):
+        kb, ke = S.shard_range(P, N, world, r)
+        parts.append(K.tree_attention_partial_merged(
+            c["q"], c["k"][:, kb:ke], c["v"][:, kb:ke], kb, ke, c["bits"], P))
+    o = torch.stack([p[0] for p in parts])
+    m = torch.stack([p[1] for p in parts])
+    l = torch.stack([p[2] for p in parts])
+    merged = K.attn_merge(o, m, l, N, 32)
+    torch.cuda.synchronize()
+    e1, e2 = elem_rel_err(merged, c["full"]), norm_rel_err(merged, c["full"])
+    print(f"[cfg5 world {world}] vs single launch: elem rel err {e1:.3e}, norm {e2:.3e}")
+    assert e1 <= RTOL and e2 <= RTOL
+    nodes = [0, 300, 512]
+    assert elem_rel_err(merged[nodes], _fp32_rows(c, nodes)) <= RTOL
+
+
+def test_cfg5_owner_shard_compaction(cfg5, cuda_device):
+    """Compaction of the accepted path runs on the rank that owns the tree keys, inside its
+    shard (sharding.compact_owner_shard), and moves the same rows as on one GPU."""
+    c = cfg5
+    P, N, world = c["P"], c["N"], 4
+    owner = S.owner_rank(world)
+    kb, ke = S.shard_range(P, N, world, owner)
+    parents = c["parents"]
+    depth = np.zeros(N, np.int64)
+    for i in range(1, N):
+        depth[i] = depth[parents[i]] + 1
+    target = int(np.argmax(depth))
+    path = [target]
+    while path[-1] != 0:
+        path.append(int(parents[path[-1]]))
+    keep = path[::-1]
+    shard = [c["k"][:, kb:ke].clone(), c["v"][:, kb:ke].clone()]  # one layer's K and V
+    before = [t.float().cpu().numpy() for t in shard]
+    table = K.KvTable(shard)
+    S.compact_owner_shard(keep, table, (kb, ke), P)
+    torch.cuda.synchronize()
+    for t, b in zip(shard, before):
+        got = t.float().cpu().numpy()[:, :P - kb + len(keep)]
+        np.testing.assert_array_equal(got, oracle.compact_rows(b, P - kb, keep))
+    # a rank that does not own the tree keys refuses to compact
+    with pytest.raises(ValueError):
+        S.compact_owner_shard(keep, table, S.shard_range(P, N, world, 0), P)

@@ -6,7 +6,9 @@ as ddtree_generate calls them (ddtree.py:440-486).  Our paths: (1) the drop-in f
 mdflash_b200.ddtree with the "ddtree_tree" attention plug-in, (2) TreeVerifier (device
 resident) over transformers, (3) TreeVerifier over the fused runner.  Tree topology,
 accepted paths and compaction are bit-exact; logits / KV rows are within bf16 tolerance
-(max |err| / max |ref| <= 2e-2) and the greedy posteriors agree.
+(max |err| / max |ref| <= 2e-2, and element-wise 2e-2 relative with the row RMS as floor),
+and the greedy posteriors agree on >= 99.9% of the rows whose reference top-1 / top-2 gap
+exceeds 4 bf16 steps of the largest logit (near-ties are logged).
 """
 import numpy as np
 import pytest
@@ -19,6 +21,7 @@ from mdflash_b200 import ddtree as D
 from mdflash_b200 import kernels as K
 from mdflash_b200.cache import TreeKVCache
 from mdflash_b200.verifier import TreeVerifier
+from parity_util import elem_rel_err, posterior_agreement
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-2
@@ -27,6 +30,14 @@ V, P, BUDGET, DEPTHS = 2048, 96, 24, 4
 
 def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-30)).item()
+
+
+def _agreement(label, post, s):
+    ref = s["ref_logits"].float()
+    top2 = torch.topk(ref, 2, dim=-1).values
+    tie_gap = 4 * 2.0 ** -7 * ref.abs().max().item()
+    return posterior_agreement(label, post.cpu().numpy(), s["ref_post"].cpu().numpy(),
+                               (top2[:, 0] - top2[:, 1]).cpu().numpy(), tie_gap)
 
 
 @pytest.fixture(scope="module")
@@ -101,9 +112,9 @@ def test_dropin_functions_and_plugin(setup, cuda_device):
         logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=cache,
                        use_cache=True).logits[0]
         assert _rel(logits, s["ref_logits"]) <= TOL
+        assert elem_rel_err(logits, s["ref_logits"]) <= TOL
         post = logits.argmax(-1)
-        agree = (post == s["ref_post"]).float().mean().item()
-        assert agree >= 0.95, agree
+        assert _agreement("e2e drop-in", post, s) >= 0.999
         acc, nxt = D.follow_verified_tree(child_maps, post[None])
         acc_host, nxt_host = oracle.follow_verified_tree(child_maps, post.cpu())
         assert (acc, nxt) == (acc_host, nxt_host)
@@ -163,8 +174,8 @@ def test_tree_verifier_matches_reference(setup, cuda_device, fused):
     assert verifier.tree.parents[:n].tolist() == o_par
     assert torch.equal(verifier.tree.node_token_ids[:n - 1].cpu(), o_ids)
     assert _rel(res.logits, s["ref_logits"]) <= TOL
-    agree = (res.posterior == s["ref_post"]).float().mean().item()
-    assert agree >= 0.95, agree
+    assert elem_rel_err(res.logits, s["ref_logits"]) <= TOL
+    assert _agreement("e2e verifier fused" if fused else "e2e verifier", res.posterior, s) >= 0.999
     k = int(res.n_accepted.item())
     acc = res.accepted[:k].tolist()
     o_acc, o_next = oracle.follow_verified_tree((np.asarray(o_par, np.int32), o_ids.numpy()),
@@ -174,3 +185,18 @@ def test_tree_verifier_matches_reference(setup, cuda_device, fused):
         assert acc == s["ref_acc"]
     verifier.commit(P, k)
     assert cache.get_seq_length() == P + k
+
+
+def test_follow_verified_tree_on_a_foreign_tree(setup, cuda_device):
+    """child_maps that are not the tree build_ddtree_tree just built (here: the oracle's tree
+    of other logits) are walked on the device too, with the reference's result."""
+    s = setup
+    D.build_ddtree_tree(s["logits"].to(cuda_device), BUDGET)  # registers a different tree
+    other = gin.tree_logits(gin.TREE_CASES[7])  # ties_v50_b10: V = 50, 4 depths
+    node_ids, depths, parents, child_maps, vis, _ = oracle.build_ddtree_tree(other, 10)
+    par = np.asarray(parents, np.int32)
+    for kind, seed in (("path", 1), ("random", 2), ("none", 3)):
+        spec = dict(kind=kind, target=-1, seed=seed, V=50)
+        post = gin.follow_posterior(spec, node_ids.numpy(), par)
+        got = D.follow_verified_tree(child_maps, torch.from_numpy(post).to(cuda_device)[None])
+        assert got == oracle.follow_verified_tree(child_maps, post), kind

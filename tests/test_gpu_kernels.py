@@ -12,6 +12,8 @@ import torch
 import inputs as gin
 import oracle
 from mdflash_b200 import kernels as K
+from mdflash_b200._lib import DDTreeError
+from parity_util import elem_rel_err
 
 pytestmark = pytest.mark.gpu
 ATTN_TOL = 2e-2
@@ -236,6 +238,52 @@ def test_tree_attention_shapes(cuda_device, hq, hkv, past, n, seed):
                            v.to(cuda_device), bits, past)
     torch.cuda.synchronize()
     ref = _sdpa_ref(q, k, v, vis, past)
+    assert _rel_err(out.cpu(), ref) <= ATTN_TOL
+    assert elem_rel_err(out.cpu(), ref) <= ATTN_TOL
+
+
+def test_tree_attention_fp32_inputs(cuda_device):
+    """An fp32 model's q / k / v: rounded to bf16 for the kernel, the output returned in
+    fp32, within the bf16 tolerance of fp32 attention."""
+    g = torch.Generator().manual_seed(21)
+    hq, hkv, past, n, d = 16, 8, 512, 33, 128
+    q = torch.randn((n, hq, d), generator=g) * 0.09
+    k = torch.randn((hkv, past + n, d), generator=g) * 0.09
+    v = torch.randn((hkv, past + n, d), generator=g)
+    parents = gin.random_tree(n, 8)
+    bits = torch.from_numpy(oracle.ancestor_bits(parents).view(np.int32)).to(cuda_device)
+    out = K.tree_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), bits, past)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32
+    ref = _sdpa_ref(q.transpose(0, 1), k, v, oracle.visibility(parents), past)
+    assert _rel_err(out.cpu(), ref) <= ATTN_TOL
+    assert elem_rel_err(out.cpu(), ref) <= ATTN_TOL
+
+
+def test_tree_attention_wait_timeout_sets_status(cuda_device):
+    """Every wait of the attention kernel is bounded.  ddt_tree_attn_wait_check launches the
+    kernel with its load-issuing warp withholding every load, so the consumers' waits run out
+    (after 2 ms here): the kernel must return, set the status word (read by check_status as
+    DDT_ERR_TIMEOUT) and leave the context usable for the next launch."""
+    g = torch.Generator().manual_seed(3)
+    hq, hkv, past, n, d = 32, 8, 256, 65, 128
+    q = (torch.randn((n, hq, d), generator=g) * 0.09).to(torch.bfloat16).to(cuda_device)
+    k = (torch.randn((hkv, past + n, d), generator=g) * 0.09).to(torch.bfloat16).to(cuda_device)
+    v = torch.randn((hkv, past + n, d), generator=g).to(torch.bfloat16).to(cuda_device)
+    parents = gin.random_tree(n, 9)
+    bits = torch.from_numpy(oracle.ancestor_bits(parents).view(np.int32)).to(cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    K.tree_attention_wait_check(q, k, v, bits, past, 2_000_000, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) != 0
+    with pytest.raises(DDTreeError, match="bounded device wait expired"):
+        K.check_status(status)
+    assert int(status.item()) == 0
+    # the same sizes right after, on the same status word: correct and no timeout
+    out = K.tree_attention(q, k, v, bits, past, status=status)
+    torch.cuda.synchronize()
+    K.check_status(status)
+    ref = _sdpa_ref(q.transpose(0, 1), k, v, oracle.visibility(parents), past)
     assert _rel_err(out.cpu(), ref) <= ATTN_TOL
 
 
