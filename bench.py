@@ -1,26 +1,37 @@
 #!/usr/bin/env python
-"""Benchmark of the DDTree verify step on B200.
+"""Benchmark of the DDTree verification hot path on B200.
 
-Workload (one "step"): the single-GPU verify step of a random-init Qwen3-8B-shaped target
-(36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, MLP 12288, vocab 151936, bf16)
-over a prefix of 8192 uniform-random tokens, with per-depth drafter logits for block
-length 16 (15 depths, seeded N(0,1)*3) driving a 256-node best-first tree (257 rows with
-the root): tree build -> tree-attention verify forward -> greedy posterior -> accept walk
--> KV compaction.  Metric: verified + accepted tokens per second (257 verified rows plus
-the committed path per step), summed over GPUs.
+Default workload, at every GPU count (one process per GPU under torchrun): a batch of 64
+independent requests on a random-init Qwen3-8B-shaped target (36 layers, hidden 4096,
+32 q / 8 kv heads, head_dim 128, MLP 12288, vocab 151936, bf16).  Prefix lengths are
+log-uniform in 1k..32k, tree budgets uniform over {64, 128, 256, 512}, drafter logits
+seeded per request (15 depths of N(0,1)*3).  A "step" verifies every request once: tree
+build -> tree-attention verify forward -> greedy posterior -> accept walk -> KV compaction,
+one CUDA-graph replay per request, then the result records are all-gathered.  Requests are
+assigned to ranks by longest-processing-time first; there is no other cross-GPU traffic.
+Metric: verified + accepted tokens per second over all GPUs.
 
-  value      inputs resident in HBM; K steps back to back, CUDA events on the step stream
-  e2e        the same through the public API with host buffers: each step copies the
-             draft logits + root token from pinned host memory and reads the result back
-  roofline   the tree-attention launches are bracketed by CUDA events inside the timed
-             region; achieved TFLOP/s = algorithmic FLOPs per launch / mean launch time
-  cpu_baseline  the CPU oracle path (C tree build, torch CPU Qwen3 layers with the
-             reference's SDPA + additive mask, argmax, walk, compaction) on a bounded
-             sample: 2 of the 36 layers timed per layer and scaled to 36
+  value      inputs resident in HBM; K steps bracketed by a barrier + synchronize, CUDA
+             events on the step stream, max over ranks
+  e2e        the same through the public API with host buffers: every request's drafter
+             logits and root token are copied from pinned host memory each step, and the
+             gathered result records are read back
+  roofline   tree attention (the dominant kernel) at the single-request Qwen3-8B verify
+             shape (prefix 8192, 257 tree rows): algorithmic FLOPs per launch over the
+             launch time measured with CUDA events inside the step's graph, against the
+             measured bf16 burst peak
+  verify_step   sub-record: that single-request step alone (rank 0)
+  kernels    sub-record (N = 1): op-level tree build, argmax, compaction and attention at
+             the same shape, L2 flushed between launches
+  cpu_baseline  (N = 1) the CPU path of the reference restated (oracle): C tree build,
+             torch CPU Qwen3 forward with SDPA + additive mask (fp32, all 36 layers; the
+             layers share one set of weights to bound host memory, which leaves the
+             compute unchanged), argmax, walk, compaction, over a bounded sample of the
+             request mix
 
---gpus N (under torchrun): every rank verifies its own request (request data
-parallelism, no data-path collective); the step time is the max over ranks.
---impl reference: the CPU oracle path alone on this host's cores (rank 0 only).
+--impl reference: that CPU path alone on this host's cores (rank 0 only), one request of
+the mix per step, as many steps as fit a time budget (reported).
+--workload verify / attn / tree / argmax / compact / splitkv: one sub-workload alone.
 """
 from __future__ import annotations
 
@@ -44,37 +55,46 @@ V = 151936
 DEPTHS = 15
 QWEN3_8B = dict(layers=36, hidden=4096, heads=32, kv_heads=8, head_dim=128, mlp=12288,
                 vocab=V, rope_theta=1e6)
+PARAMS_8B = 8.19e9
 METRIC = "verified+accepted tokens/s"
+VERIFY_PREFIX, VERIFY_BUDGET = 8192, 256
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["verify", "attn", "tree", "argmax", "compact",
-                                           "requests", "splitkv"],
-                    default="verify",
-                    help="verify: the single-request verify step (default); attn / tree / argmax "
-                         "/ compact: one op alone; requests: 64 requests sharded over the GPUs; "
-                         "splitkv: attention over a prefix sharded along the sequence")
+    ap.add_argument("--workload", choices=["requests", "verify", "attn", "tree", "argmax",
+                                           "compact", "splitkv"], default="requests",
+                    help="requests: the 64-request mix sharded over the GPUs (default); verify: "
+                         "one Qwen3-8B verify step (prefix 8192, budget 256); attn / tree / "
+                         "argmax / compact: one op alone; splitkv: attention over a prefix "
+                         "sharded along the sequence")
     ap.add_argument("--prefix", type=int, default=None,
-                    help="prefix length (default 8192; 131072 for --workload splitkv)")
+                    help="prefix length of the single-request workloads (default 8192; 131072 "
+                         "for splitkv)")
     ap.add_argument("--budget", type=int, default=None,
-                    help="tree budget (default 256; 512 for --workload splitkv)")
+                    help="tree budget of the single-request workloads (default 256; 512 for "
+                         "splitkv)")
     ap.add_argument("--requests", type=int, default=64)
-    ap.add_argument("--cpu-sample-layers", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=120.0,
+                    help="time budget of the reference arm's measured steps")
+    ap.add_argument("--cpu-baseline-seconds", type=float, default=20.0,
+                    help="time budget of the cpu_baseline sample inside our arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="skip the verify_step / kernels sub-records")
     ap.add_argument("--fused", type=int, default=1,
                     help="1: verify forward through the fused Qwen3 runner (default); 0: through "
                          "transformers' Qwen3 with the ddtree_tree attention plug-in")
     args = ap.parse_args()
     long_ctx = args.workload == "splitkv"
     if args.prefix is None:
-        args.prefix = 131072 if long_ctx else 8192
+        args.prefix = 131072 if long_ctx else VERIFY_PREFIX
     if args.budget is None:
-        args.budget = 512 if long_ctx else 256
+        args.budget = 512 if long_ctx else VERIFY_BUDGET
     return args
 
 
@@ -88,8 +108,14 @@ def qwen3_config(attn: str, layers: int | None = None):
                        tie_word_embeddings=False, attn_implementation=attn)
 
 
-def request_inputs(rank: int, prefix: int):
-    rng = np.random.default_rng(1000 + rank)
+def request_logits(seed: int) -> torch.Tensor:
+    rng = np.random.default_rng(seed)
+    return torch.from_numpy(rng.standard_normal((DEPTHS, V)).astype(np.float32) *
+                            np.float32(3.0))
+
+
+def single_request_inputs(prefix: int):
+    rng = np.random.default_rng(1000)
     ids = torch.from_numpy(rng.integers(0, V, (1, prefix)).astype(np.int64))
     logits = torch.from_numpy(rng.standard_normal((DEPTHS, V)).astype(np.float32) *
                               np.float32(3.0))
@@ -104,6 +130,16 @@ def tree_flops(depths: torch.Tensor, past: int, heads: int, head_dim: int) -> fl
     return 4.0 * heads * head_dim * (n * past + anc)
 
 
+def step_roofline_ms(prefix: int, n_rows: int, peaks) -> float:
+    """Lower bound of one verify step on one GPU: the slower of streaming the weights and the
+    prefix K / V once (HBM) and the step's FLOPs (projections, MLP, lm_head: 2 * params * N;
+    attention: 4 * Hq * D * N * P per layer) at the bf16 peak."""
+    s = QWEN3_8B
+    bytes_ = 2 * PARAMS_8B + 2 * s["layers"] * s["kv_heads"] * prefix * s["head_dim"] * 2
+    flops = 2 * PARAMS_8B * n_rows + 4.0 * s["heads"] * s["head_dim"] * n_rows * prefix * s["layers"]
+    return max(bytes_ / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) * 1e3
+
+
 def measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -112,9 +148,9 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def profile_traffic():
-    """DRAM bytes per tree-attention launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "tree_attn_traffic.json")
+def profile_traffic(name: str):
+    """DRAM bytes per launch of a kernel from the committed ncu summaries, if any."""
+    path = os.path.join(ROOT, "profiles", f"{name}_traffic.json")
     if os.path.exists(path):
         with open(path) as f:
             return json.load(f)
@@ -137,7 +173,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "20", "-i", str(self.gpu_index)], stdout=self.tmp,
+                 "-lms", "50", "-i", str(self.gpu_index)], stdout=self.tmp,
                 stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
@@ -171,119 +207,166 @@ class ClockSampler:
                 "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+def _gpu_index(local: int) -> int:
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return int(visible.split(",")[local]) if visible else local
+
+
 # ------------------------------------------------------------------ CPU oracle path
-def cpu_verify_sample(sample_layers: int, prefix: int, budget: int, steps: int, warmup: int):
-    """The reference's verify step on the host cores through the CPU oracle: C tree build,
-    compile (additive mask), a Qwen3-8B-shaped forward of `sample_layers` decoder layers
-    with SDPA + mask (fp32), argmax, walk and compaction of `sample_layers` layers.  The
-    per-layer costs are timed with hooks and scaled to the 36 layers of the model."""
+def cpu_target_model():
+    """Qwen3-8B-shaped target for the CPU path, fp32: 36 decoder layers that share ONE set of
+    random weights, and an lm_head that shares the embedding's array (the compute of every
+    layer and of the lm_head is unchanged; host memory stays ~4 GB instead of 33 GB).  Each
+    layer keeps its own layer index, so the KV cache has 36 layers."""
+    from transformers import Qwen3ForCausalLM
+    from transformers.models.qwen3.modeling_qwen3 import (Qwen3DecoderLayer, Qwen3RMSNorm,
+                                                          Qwen3RotaryEmbedding)
+    cfg = qwen3_config("sdpa")
+    with torch.device("meta"):
+        model = Qwen3ForCausalLM(cfg)
+        layer0 = Qwen3DecoderLayer(cfg, 0)
+    layer0.to_empty(device="cpu")
+    g = torch.Generator().manual_seed(0)
+
+    def fill(t: torch.Tensor, std: float):
+        # a seeded 64 Ki block tiled over the tensor (random values, cheap to make)
+        blk = torch.randn(1 << 16, generator=g) * std
+        flat = t.view(-1)
+        full = flat.numel() // blk.numel()
+        if full:
+            flat[:full * blk.numel()].view(full, -1).copy_(blk.expand(full, -1))
+        rest = flat.numel() - full * blk.numel()
+        if rest:
+            flat[full * blk.numel():].copy_(blk[:rest])
+
+    with torch.no_grad():
+        for name, p in layer0.named_parameters():
+            if "norm" in name:
+                p.fill_(1.0)
+            else:
+                fill(p, 0.02)
+        sd = layer0.state_dict()
+        for layer in model.model.layers:
+            layer.load_state_dict(sd, assign=True)
+        emb = torch.nn.Embedding(V, QWEN3_8B["hidden"])
+        fill(emb.weight, 0.02)
+        head = torch.nn.Linear(QWEN3_8B["hidden"], V, bias=False, device="meta")
+        head.weight = emb.weight  # one [V, hidden] array for both (the lm_head GEMM is unchanged)
+    model.model.embed_tokens = emb
+    model.lm_head = head
+    model.model.norm = Qwen3RMSNorm(QWEN3_8B["hidden"], eps=1e-6)
+    model.model.rotary_emb = Qwen3RotaryEmbedding(cfg)
+    return model.eval()
+
+
+def cpu_request_step(model, spec, kv_cache_rows: dict):
+    """One request's verify step on the CPU path: C tree build (ddtree.py:84-166 restated),
+    compile with the additive mask (ddtree.py:227-267), the 36-layer fp32 forward with SDPA +
+    mask, argmax (model/utils.py:28-30), walk (ddtree.py:270-281) and compaction of every
+    layer (ddtree.py:284-335).  Returns (seconds, tokens = verified rows + accepted)."""
     import oracle
-    from transformers import DynamicCache, Qwen3ForCausalLM
+    from transformers import DynamicCache
+    P, B = spec.prefix, spec.budget
+    logits = request_logits(spec.seed).to(torch.bfloat16)  # the drafter logits the GPU sees
+    root = int(np.random.default_rng(spec.seed).integers(0, V))
+    k = kv_cache_rows.get(P)
+    if k is None:
+        g = torch.Generator().manual_seed(P)
+        k = torch.randn((1, QWEN3_8B["kv_heads"], P, QWEN3_8B["head_dim"]), generator=g) * 0.5
+        kv_cache_rows.clear()
+        kv_cache_rows[P] = k
+    cache = DynamicCache()
+    for li in range(QWEN3_8B["layers"]):
+        cache.update(k[..., :1, :], k[..., :1, :], li)  # creates layer li
+        cache.layers[li].keys = k  # every layer's prefix is the same tensor: the verify's
+        cache.layers[li].values = k  # torch.cat gives each layer its own copy
+    n_cap = B + 1
+    t0 = time.perf_counter()
+    node_ids, depths, parents, child_maps, vis, _ = oracle.build_ddtree_tree(logits, B)
+    vib = torch.empty((1, n_cap), dtype=torch.long)
+    vpb = torch.empty((1, n_cap), dtype=torch.long)
+    amb = torch.zeros((1, 1, n_cap, P + n_cap), dtype=torch.float32)
+    tvb = torch.empty((n_cap, n_cap), dtype=torch.bool)
+    vi, vp, am, _, n = oracle.compile_ddtree_tree(root, P, node_ids, depths, vis, P,
+                                                  torch.float32, None, vib, vpb, amb, tvb, 0, 0)
+    with torch.inference_mode():
+        out = model(vi, position_ids=vp, attention_mask=am, past_key_values=cache, use_cache=True)
+        post = oracle.argmax(out.logits[0])
+        acc, nxt = oracle.follow_verified_tree(child_maps, post)
+        layers_np = [(l.keys.numpy(), l.values.numpy()) for l in cache.layers]
+        oracle.compact_dynamic_cache(layers_np, P, acc)
+    return time.perf_counter() - t0, n + len(acc)
+
+
+def cpu_sample(n_requests: int, budget_s: float, warmup: int, max_steps: int):
+    """Runs requests of the mix (seeded order) one per step on the host cores: `warmup`
+    untimed steps, then measured steps until `budget_s` seconds are spent (at least one, at
+    most max_steps).  Returns tokens/s over the measured steps and what was run."""
+    from mdflash_b200 import sharding as S
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    torch.manual_seed(0)
-    with torch.inference_mode():
-        model = Qwen3ForCausalLM(qwen3_config("sdpa", sample_layers)).eval().float()
-    ids, logits = request_inputs(0, prefix)
-    logits = logits.to(torch.bfloat16)  # the drafter logits the GPU arm sees
-    n_cap = budget + 1
-    g = torch.Generator().manual_seed(0)
-    kv = [(torch.randn((1, 8, prefix, 128), generator=g) * 0.5,
-           torch.randn((1, 8, prefix, 128), generator=g) * 0.5) for _ in range(sample_layers)]
-    layer_times: list[float] = []
-    starts: dict[int, float] = {}
-
-    def pre(mod, args, kwargs):
-        starts[id(mod)] = time.perf_counter()
-
-    def post(mod, args, kwargs, out):
-        layer_times.append(time.perf_counter() - starts[id(mod)])
-
-    for layer in model.model.layers:
-        layer.register_forward_pre_hook(pre, with_kwargs=True)
-        layer.register_forward_hook(post, with_kwargs=True)
-    per_step = []
-    n_acc = 1
-    root = int(ids[0, -1])
-    for it in range(warmup + steps):
-        cache = DynamicCache()
-        for li, (k, v) in enumerate(kv):
-            cache.update(k.clone(), v.clone(), li)
-        layer_times.clear()
-        t0 = time.perf_counter()
-        node_ids, depths, parents, child_maps, vis, _ = oracle.build_ddtree_tree(logits, budget)
-        t1 = time.perf_counter()
-        vib = torch.empty((1, n_cap), dtype=torch.long)
-        vpb = torch.empty((1, n_cap), dtype=torch.long)
-        amb = torch.zeros((1, 1, n_cap, prefix + n_cap), dtype=torch.float32)
-        tvb = torch.empty((n_cap, n_cap), dtype=torch.bool)
-        vi, vp, am, _, n = oracle.compile_ddtree_tree(root, prefix, node_ids, depths, vis, prefix,
-                                                      torch.float32, None, vib, vpb, amb, tvb, 0, 0)
-        with torch.inference_mode():
-            t2 = time.perf_counter()
-            out = model(vi, position_ids=vp, attention_mask=am, past_key_values=cache,
-                        use_cache=True)
-            t3 = time.perf_counter()
-            post_tokens = oracle.argmax(out.logits[0])
-            acc, nxt = oracle.follow_verified_tree(child_maps, post_tokens)
-            layers_np = [(l.keys.numpy(), l.values.numpy()) for l in cache.layers]
-            oracle.compact_dynamic_cache(layers_np, prefix, acc)
-            t4 = time.perf_counter()
-        fwd_layers = sum(layer_times)
-        fwd_other = (t3 - t2) - fwd_layers
-        commit = t4 - t3
-        step = ((t1 - t0) + (t2 - t1) + fwd_other + fwd_layers * 36 / sample_layers +
-                commit * 36 / sample_layers)  # compaction also covers every layer
-        n_acc = len(acc)
-        if it >= warmup:
-            per_step.append(step)
-    t = float(np.mean(per_step))
-    return {"seconds_per_step": t, "tokens_per_step": n + n_acc, "threads": threads,
-            "sample": f"{sample_layers} of 36 decoder layers timed (forward hooks) and scaled to "
-                      f"36; tree build, compile, embed, lm_head and argmax at full size; "
-                      f"prefix {prefix} K/V random fp32; {steps} steps after {warmup} warm-up"}
+    t_build = time.perf_counter()
+    model = cpu_target_model()
+    t_build = time.perf_counter() - t_build
+    specs = S.request_specs(n_requests, seed=0)
+    order = np.random.default_rng(7).permutation(len(specs))
+    kv_rows: dict = {}
+    i = 0
+    for _ in range(warmup):
+        cpu_request_step(model, specs[order[i % len(order)]], kv_rows)
+        i += 1
+    times, tokens, ran = [], 0, []
+    spent = 0.0
+    while len(times) < max(1, max_steps) and (not times or spent < budget_s):
+        sp = specs[order[i % len(order)]]
+        dt, tok = cpu_request_step(model, sp, kv_rows)
+        times.append(dt)
+        tokens += tok
+        ran.append((sp.index, sp.prefix, sp.budget))
+        spent += dt
+        i += 1
+    return {"value": tokens / sum(times), "seconds": sum(times), "steps": len(times),
+            "ms_per_step": 1e3 * sum(times) / len(times), "threads": threads,
+            "model_build_s": t_build,
+            "sample": f"{len(times)} requests of the {n_requests}-request mix after {warmup} "
+                      f"warm-up, one full verify step each (36 fp32 decoder layers sharing one "
+                      f"weight set, SDPA + additive mask; C tree build, argmax, walk, "
+                      f"compaction of all layers); requests (index, prefix, budget): {ran}"}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    r = cpu_verify_sample(args.cpu_sample_layers, args.prefix, args.budget, args.steps,
-                          args.warmup)
-    value = r["tokens_per_step"] / r["seconds_per_step"]
+    r = cpu_sample(args.requests, args.cpu_seconds, min(args.warmup, 1), args.steps)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": r["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(args, args.gpus),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["threads"],
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": r["steps"], "requested_steps": args.steps,
+        "warmup": min(args.warmup, 1), "ms_per_step": r["ms_per_step"],
+        "step": "one request of the mix (the CPU path verifies requests one at a time)",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": requests_config(args, args.gpus),
+        "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["threads"],
                          "kind": "port", "sample": r["sample"]},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+        "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "timed_seconds": r["seconds"], "model_build_s": r["model_build_s"],
     }
     print(json.dumps(line), flush=True)
 
 
-def workload_config(args, n):
-    return {"workload": f"Qwen3-8B-shaped verify step: 36 layers, prefix {args.prefix}, "
-                        f"{args.budget}-node best-first tree (block 16 -> 15 depths), bf16",
-            "model": "Qwen3-8B shape, random init", "global_batch": n,
-            "seq_len": args.prefix, "tree_nodes": args.budget + 1,
-            "parallelism": f"request-dp{n}",
-            "l2": "inputs larger than L2: 16 GB of weights and 1.2 GB of KV streamed per step"}
+def requests_config(args, n):
+    return {"workload": f"{args.requests} independent DDTree verify requests on a Qwen3-8B-shaped "
+                        "target (36 layers, bf16): prefix log-uniform 1k-32k, budget in "
+                        "{64,128,256,512}, 15 drafted depths; one verify step of every request",
+            "model": "Qwen3-8B shape, random init", "global_batch": args.requests,
+            "seq_len": "1024-32768 (log-uniform)", "parallelism": f"request-dp{n} (LPT)",
+            "l2": "inputs larger than L2: 16 GB of weights streamed per request step"}
 
 
 # ------------------------------------------------------------------------ our arm
-def run_ours(args):
+def _dist_setup():
     import torch.distributed as dist
-    from transformers import Qwen3ForCausalLM
-
-    from mdflash_b200 import attention as A
-    from mdflash_b200 import kernels as K
-    from mdflash_b200.cache import TreeKVCache
-    from mdflash_b200.verifier import CapturedStep, TreeVerifier
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -291,148 +374,167 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    K._lib.load(build_if_missing=False)
-    attn = A.register()
-    torch.manual_seed(rank)
-    prev_dtype = torch.get_default_dtype()
+    return world, rank, local, dev
+
+
+def gpu_model(dev, attn):
+    from transformers import Qwen3ForCausalLM
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
     torch.set_default_dtype(torch.bfloat16)
     with torch.device(dev), torch.inference_mode():
         model = Qwen3ForCausalLM(qwen3_config(attn)).eval()
-    torch.set_default_dtype(prev_dtype)
-    ids, logits = request_inputs(rank, args.prefix)
-    P, B = args.prefix, args.budget
-    cache = TreeKVCache(QWEN3_8B["layers"], P + B + 1 + 64).allocate(
-        QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
-    verifier = TreeVerifier(model, cache, B, DEPTHS, V, dev, fused=args.fused)
-    with torch.inference_mode():
-        if verifier.runner is not None:  # causal prefill on the same kernels
-            out_logits = verifier.runner.forward(ids[0].to(dev), torch.arange(P, device=dev),
-                                                 cache, 0, None, causal=True)
-            root_dev = K.argmax(out_logits[-1:]).view(1).clone()
-            del out_logits
-        else:
-            out = model(ids.to(dev), position_ids=torch.arange(P, device=dev)[None],
-                        past_key_values=cache, use_cache=True, logits_to_keep=1)
-            root_dev = K.argmax(out.logits[0, -1:]).view(1).clone()
-            del out
-    draft_dev = logits.to(torch.bfloat16).to(dev)
-    n_nodes = 1 + K.expected_node_count(DEPTHS, V, B)
-    for _ in range(args.warmup):  # eager steps: allocations, kernel attributes, TMA encode
-        verifier.step(draft_dev, root_dev, P)
-        cache.crop(P)  # every step verifies the same prefix (the commit is undone)
-    # the whole step (tree build, 36-layer forward, argmax, walk + compaction) as one graph
-    cap = CapturedStep(verifier, P, warmup=1, time_attention=True)
-    cap.draft_logits.copy_(draft_dev)
-    cap.root_token.copy_(root_dev)
-    for _ in range(args.warmup):
-        cap.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    torch.set_default_dtype(prev)
+    return model
 
-    # ---- device-resident timing (value + attention roofline) ----
-    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-    gpu_index = int(visible.split(",")[local]) if visible else local
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(gpu_index) as clocks:
+
+def _fill_prefix(cache, prefix: int, g: torch.Generator):
+    for layer in cache.layers:
+        layer.k_buf[..., :prefix, :].normal_(0.0, 1.0, generator=g)
+        layer.v_buf[..., :prefix, :].normal_(0.0, 1.0, generator=g)
+        layer.length = prefix
+        layer.keys = layer.k_buf[..., :prefix, :]
+        layer.values = layer.v_buf[..., :prefix, :]
+
+
+def run_requests(args):
+    """The default workload (see the module docstring); prints the JSON line on rank 0."""
+    import torch.distributed as dist
+
+    from mdflash_b200 import attention as A
+    from mdflash_b200 import kernels as K
+    from mdflash_b200 import sharding as S
+    from mdflash_b200.cache import TreeKVCache
+    from mdflash_b200.runner import Qwen3VerifyRunner
+    from mdflash_b200.verifier import CapturedStep, TreeVerifier
+
+    world, rank, local, dev = _dist_setup()
+    K._lib.load(build_if_missing=False)
+    attn = A.register()
+    model = gpu_model(dev, attn)
+    runner = Qwen3VerifyRunner(model)
+    specs = S.request_specs(args.requests, seed=0)
+    assignment = S.assign_requests([S.request_cost(s) for s in specs], world)
+    mine = assignment[rank]
+    pool = torch.cuda.graph_pool_handle()
+    caps = []
+    g = torch.Generator(device=dev).manual_seed(rank)
+    for i in mine:
+        sp = specs[i]
+        cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
+            QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
+        _fill_prefix(cache, sp.prefix, g)  # the verify work does not depend on the K / V values
+        ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
+        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pool)
+        host = request_logits(sp.seed).to(torch.bfloat16).pin_memory()
+        root = torch.tensor([int(np.random.default_rng(sp.seed).integers(0, V))],
+                            dtype=torch.int64).pin_memory()
+        cap.draft_logits.copy_(host)
+        cap.root_token.copy_(root)
+        caps.append((sp, cap, host, root))
+    records = torch.full((len(caps), S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
+    for j, (sp, cap, _, _) in enumerate(caps):
+        records[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
+        records[j, 5] = 0
+
+    def one_step(e2e: bool):
+        for j, (sp, cap, host, root) in enumerate(caps):
+            if e2e:
+                cap.draft_logits.copy_(host, non_blocking=True)
+                cap.root_token.copy_(root, non_blocking=True)
+            r = cap.replay()
+            # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
+            records[j, 3] = r.n_accepted[0]
+            records[j, 4] = r.next_token[0]
+            m = min(S.MAX_PATH, r.n_nodes)
+            records[j, 6:6 + m] = r.accepted[:m]
+        return S.gather_results(records)
+
+    def check_statuses():
+        st = torch.stack([cap.verifier.status for _, cap, _, _ in caps])
+        if int(st.abs().sum().item()) != 0:
+            raise RuntimeError("a tree-attention launch reported a bounded-wait timeout")
+
+    for _ in range(args.warmup):
+        one_step(False)
+    torch.cuda.synchronize()
+    check_statuses()
+
+    def timed(e2e: bool):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        allrec = None
+        host_rec = None
+        for _ in range(args.steps):
+            allrec = one_step(e2e)
+            if e2e:
+                host_rec = allrec.cpu()  # the step's results on the host (syncs)
+        ev1.record()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        torch.cuda.nvtx.range_push("timed")
-        ev0.record()
-        for _ in range(args.steps):
-            res = cap.replay()
-        ev1.record()
-        torch.cuda.nvtx.range_pop()
-        torch.cuda.synchronize()
-    launches = cap.launches_per_replay * args.steps
-    attn_ms = cap.attention_ms()  # the last replay of the timed region
-    ms = ev0.elapsed_time(ev1) / args.steps
-    n_acc = int(res.n_accepted.item())
-    depths = verifier.tree.node_depths[:n_nodes - 1].cpu()
-    ms_t = torch.tensor([ms], device=dev)
-    acc_t = torch.tensor([float(n_nodes + n_acc)], device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(acc_t, op=dist.ReduceOp.SUM)
-        dist.barrier()
-    ms_max = ms_t.item()
-    tokens_all = acc_t.item()
-    value = tokens_all / (ms_max / 1e3)
+        ms = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return ms.item(), (host_rec if host_rec is not None else allrec.cpu())
 
-    # ---- end to end through the public API with host buffers ----
-    draft_host = logits.to(torch.bfloat16).pin_memory()
-    root_host = torch.zeros(1, dtype=torch.int64).pin_memory()
-    root_host.copy_(root_dev.cpu())
-    result_host = torch.zeros(2 + n_nodes, dtype=torch.int64).pin_memory()
-
-    def e2e_step():
-        cap.draft_logits.copy_(draft_host, non_blocking=True)
-        cap.root_token.copy_(root_host, non_blocking=True)
-        r = cap.replay()
-        packed = torch.cat([r.n_accepted.to(torch.int64), r.next_token, r.accepted[:n_nodes]])
-        result_host.copy_(packed, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        return int(result_host[0])
-
+    with ClockSampler(_gpu_index(local)) as clocks:
+        ms, allrec = timed(False)
+    clock_summary = clocks.summary()
+    tokens = int((allrec[:, 2] + allrec[:, 3]).sum())
+    value = tokens / (ms / 1e3)
     for _ in range(args.warmup):
-        e2e_step()
+        one_step(True)
+    e2e_ms, e2e_rec = timed(True)
+    e2e_tokens = int((e2e_rec[:, 2] + e2e_rec[:, 3]).sum())
+    check_statuses()
+    h2d = sum(h.numel() * h.element_size() + 8 for _, _, h, _ in caps)
+    d2h = int(allrec.numel()) * 8
+    launches = sum(cap.launches_per_replay for _, cap, _, _ in caps) * args.steps
+    sums = torch.tensor([float(h2d), float(launches)], device=dev)
     if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    ks = [e2e_step() for _ in range(args.steps)]
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
-    e2e_tok = torch.tensor([float(sum(n_nodes + k for k in ks) / args.steps)], device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-        dist.all_reduce(e2e_tok, op=dist.ReduceOp.SUM)
-    e2e_value = e2e_tok.item() / (e2e_ms.item() / 1e3)
-    h2d = draft_host.numel() * draft_host.element_size() + root_host.numel() * 8
-    d2h = result_host.numel() * 8
-
-    # ---- roofline of the dominant kernel (tree attention, one launch per layer) ----
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
     peaks, peak_kind = measured_peaks()
-    flops = tree_flops(depths, P, QWEN3_8B["heads"], QWEN3_8B["head_dim"])
-    attn_mean_ms = float(np.mean(attn_ms)) if attn_ms else float("nan")
-    achieved = flops / (attn_mean_ms / 1e3) / 1e12
-    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    traffic = profile_traffic()
+    # lower bound of the whole job: each GPU's requests back to back at their step roofline
+    bound = max(sum(step_roofline_ms(specs[i].prefix, specs[i].budget + 1, peaks)
+                    for i in a) for a in assignment)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: seeded uniform prefix tokens, N(0,1)*3 drafter logits, random-init "
-                "Qwen3-8B-shaped weights",
-        "config": workload_config(args, world),
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms.item()},
-        "roofline": {"kernel": "ddt_tree_attn (+ split merge), one launch per layer",
-                     "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} bf16 sustained (MEASURED_PEAKS.json)",
-                     "flops_per_launch": flops, "launch_ms": attn_mean_ms,
-                     "launches_timed": len(attn_ms),
-                     "traffic": traffic.get("bytes_per_launch") if traffic else None},
-        "gpu_launches": launches,
-        "launches_per_step": launches / args.steps,
-        "execution": "each step is one CUDA-graph replay of the full verify step (tree build, "
-                     "36-layer forward, argmax, accept walk + compaction) at prefix length "
-                     f"{P}; eager warm-up steps precede the capture; forward: "
-                     + ("fused Qwen3 runner (cuBLAS GEMMs + fused norm/rope/silu kernels)"
-                        if args.fused else "transformers Qwen3 + ddtree_tree attention"),
-        "accepted_per_step": n_acc, "verified_per_step": n_nodes,
-        "attention_share": (attn_mean_ms * QWEN3_8B["layers"]) / ms,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded request mix, random prefix K/V, N(0,1)*3 drafter logits, "
+                "random-init Qwen3-8B-shaped weights",
+        "config": requests_config(args, world),
+        "e2e": {"value": e2e_tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(sums[0].item()), "d2h_bytes_per_step": d2h * world,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": int(sums[1].item()),
+        "tokens_per_step": tokens,
+        "requests_per_rank": [len(a) for a in assignment],
+        "step_roofline": {"bound": "max(HBM: weights + prefix K/V once, bf16 FLOPs) per request, "
+                                   "the slowest rank's requests back to back",
+                          "ms": bound, "frac": bound / ms, "peak_source": peak_kind},
+        "execution": "one CUDA-graph replay per request (tree build, 36-layer fused verify "
+                     "forward, argmax, accept walk + compaction), records all-gathered per step",
     }
+    del caps
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if rank == 0 and not args.no_subrecords:
+        sub = verify_step(args, model, runner, dev, steps=max(3, min(args.steps, 20)),
+                          warmup=args.warmup)
+        line["verify_step"] = sub
+        line["roofline"] = sub["roofline"]
+        if world == 1:
+            line["kernels"] = kernel_table(dev, args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_verify_sample(args.cpu_sample_layers, args.prefix, args.budget, 1, 1)
-        line["cpu_baseline"] = {"value": r["tokens_per_step"] / r["seconds_per_step"],
-                                "unit": "tokens/s", "cores": r["threads"], "kind": "port",
-                                "sample": r["sample"]}
-    line["clocks"] = clocks.summary()
+        r = cpu_sample(args.requests, args.cpu_baseline_seconds, 0, 1 << 30)
+        line["cpu_baseline"] = {"value": r["value"], "unit": "tokens/s", "cores": r["threads"],
+                                "kind": "port", "sample": r["sample"]}
+    line["clocks"] = clock_summary
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -440,7 +542,97 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
 
 
-# ------------------------------------------------------------- op-level attention
+def verify_step(args, model, runner, dev, steps: int, warmup: int, prefix: int = VERIFY_PREFIX,
+                budget: int = VERIFY_BUDGET):
+    """One Qwen3-8B verify step (causal prefill of `prefix` tokens on the same kernels, then a
+    `budget`-node tree), replayed as one CUDA graph; the tree-attention launches are bracketed
+    by CUDA events inside the graph."""
+    from mdflash_b200 import kernels as K
+    from mdflash_b200.cache import TreeKVCache
+    from mdflash_b200.verifier import CapturedStep, TreeVerifier
+    ids, logits = single_request_inputs(prefix)
+    P, B = prefix, budget
+    cache = TreeKVCache(QWEN3_8B["layers"], P + B + 1 + 64).allocate(
+        QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
+    verifier = TreeVerifier(model, cache, B, DEPTHS, V, dev, runner=runner)
+    with torch.inference_mode():
+        out_logits = runner.forward(ids[0].to(dev), torch.arange(P, device=dev), cache, 0, None,
+                                    causal=True)
+        root_dev = K.argmax(out_logits[-1:]).view(1).clone()
+        del out_logits
+    draft_dev = logits.to(torch.bfloat16).to(dev)
+    n_nodes = 1 + K.expected_node_count(DEPTHS, V, B)
+    for _ in range(warmup):
+        verifier.step(draft_dev, root_dev, P)
+        cache.crop(P)  # every step verifies the same prefix (the commit is undone)
+    cap = CapturedStep(verifier, P, warmup=1, time_attention=True)
+    cap.draft_logits.copy_(draft_dev)
+    cap.root_token.copy_(root_dev)
+    for _ in range(warmup):
+        cap.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        res = cap.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    verifier.check()
+    ms = ev0.elapsed_time(ev1) / steps
+    attn_ms = cap.attention_ms()
+    n_acc = int(res.n_accepted.item())
+    depths = verifier.tree.node_depths[:n_nodes - 1].cpu()
+    peaks, peak_kind = measured_peaks()
+    flops = tree_flops(depths, P, QWEN3_8B["heads"], QWEN3_8B["head_dim"])
+    attn_mean = float(np.mean(attn_ms))
+    achieved = flops / (attn_mean / 1e3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    traffic = profile_traffic("tree_attn")
+    step_bound = step_roofline_ms(P, n_nodes, peaks)
+    launches = cap.launches_per_replay
+    del cap
+    return {
+        "workload": f"Qwen3-8B-shaped verify step: 36 layers, prefix {P}, {B}-node best-first tree "
+                    "(15 depths), bf16, one CUDA-graph replay per step",
+        "value": (n_nodes + n_acc) / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+        "steps": steps, "verified_per_step": n_nodes, "accepted_per_step": n_acc,
+        "launches_per_step": launches,
+        "attention_share": attn_mean * QWEN3_8B["layers"] / ms,
+        "step_roofline": {"ms": step_bound, "frac": step_bound / ms},
+        "roofline": {"kernel": "ddt_tree_attn (+ its split merge), one launch per layer, inside "
+                               "the verify step's graph",
+                     "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} bf16 burst (MEASURED_PEAKS.json bf16_tflops): "
+                                    "the kernel runs ~50 us at a time",
+                     "flops_per_launch": flops, "launch_ms": attn_mean,
+                     "launches_timed": len(attn_ms),
+                     "traffic": traffic.get("bytes_per_launch") if traffic else None},
+    }
+
+
+# ------------------------------------------------------------ op-level measurements
+def _timed_launches(fn, steps: int, warmup: int, dev) -> float:
+    """Mean device time (ms) of `fn` over `steps` launches, each bracketed by CUDA events,
+    with a 256 MB buffer written before each launch (L2 flushed)."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    torch.cuda.nvtx.range_push("timed")
+    for _ in range(steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        times.append((a, b))
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in times]))
+
+
 def attn_inputs(prefix: int, budget: int, seed: int = 0):
     """Tree attention op inputs: Hq=32, Hkv=8, D=128, Q/K/V ~ N(0,1)/sqrt(128), parents of
     a seeded random tree (BFS growth, Geometric(0.5) child counts, depth <= 16)."""
@@ -476,150 +668,69 @@ def attn_flops(parents: np.ndarray, past: int) -> float:
     return 4.0 * 32 * 128 * float(n * past + int((depth + 1).sum()))
 
 
-def run_attn(args):
+def measure_attn(dev, prefix, budget, steps, warmup):
     from mdflash_b200 import kernels as K
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    q, k, v, parents = attn_inputs(args.prefix, args.budget)
+    q, k, v, parents = attn_inputs(prefix, budget)
     qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
     bits = torch.from_numpy(anc_bits_host(parents).view(np.int32)).to(dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > 126 MB L2
-    out = K.tree_attention(qd, kd, vd, bits, args.prefix)
-    for _ in range(args.warmup):
-        K.tree_attention(qd, kd, vd, bits, args.prefix, out=out)
-    torch.cuda.synchronize()
-    times = []
-    torch.cuda.nvtx.range_push("timed")
-    for _ in range(args.steps):
-        flush.fill_(1)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        K.tree_attention(qd, kd, vd, bits, args.prefix, out=out)
-        b.record()
-        times.append((a, b))
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    ms = float(np.mean([a.elapsed_time(b) for a, b in times]))
-    flops = attn_flops(parents, args.prefix)
+    out = K.tree_attention(qd, kd, vd, bits, prefix)
+    ms = _timed_launches(lambda: K.tree_attention(qd, kd, vd, bits, prefix, out=out), steps,
+                         warmup, dev)
+    K.check_status(K.attention_status(dev))
+    flops = attn_flops(parents, prefix)
     peaks, kind = measured_peaks()
-    peak = float(peaks["bf16_tflops"])
     tflops = flops / (ms / 1e3) / 1e12
-    kv_bytes = 2 * 8 * (args.prefix + args.budget + 1) * 128 * 2
-    print(json.dumps({
-        "metric": "tree-attn TFLOP/s", "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"tree attention op: Hq 32 / Hkv 8, D 128, prefix {args.prefix}, "
-                               f"{args.budget + 1} tree rows (random tree, Geometric(0.5))",
-                   "l2": "256 MB buffer written between launches (L2 flushed)",
-                   "kv_splits": K.attn_splits(args.budget + 1, 32, 8, args.prefix)},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
-                     "frac": tflops / peak, "peak_source": f"{kind} bf16 burst",
-                     "flops_per_launch": flops, "kv_bytes": kv_bytes},
-    }), flush=True)
+    return {"ms": ms, "tflops": tflops, "frac": tflops / peaks["bf16_tflops"],
+            "peak": peaks["bf16_tflops"], "peak_source": f"{kind} bf16 burst",
+            "flops_per_launch": flops,
+            "kv_splits": K.attn_splits(budget + 1, 32, 8, prefix),
+            "shape": f"Hq 32 / Hkv 8, D 128, prefix {prefix}, {budget + 1} tree rows"}
 
 
-def run_tree(args):
-    """Tree construction op alone: [15, 151936] bf16 drafter logits -> tree (top-k, heap,
-    bitmasks, verify ids / positions).  Reports GB/s of the algorithmic bytes (one read of
-    the logits) over the launch time, L2 flushed between launches."""
+def measure_tree(dev, budget, steps, warmup):
     from mdflash_b200 import kernels as K
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    _, logits = request_inputs(0, 16)
+    _, logits = single_request_inputs(16)
     x = logits.to(torch.bfloat16).to(dev)
     root = torch.zeros(1, dtype=torch.int64, device=dev)
-    tree = K.topk_tree(x, args.budget, root, args.prefix)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    for _ in range(args.warmup):
-        K.topk_tree(x, args.budget, root, args.prefix, out=tree)
-    torch.cuda.synchronize()
-    times = []
-    torch.cuda.nvtx.range_push("timed")
-    for _ in range(args.steps):
-        flush.fill_(1)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        K.topk_tree(x, args.budget, root, args.prefix, out=tree)
-        b.record()
-        times.append((a, b))
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    ms = float(np.mean([a.elapsed_time(b) for a, b in times]))
+    tree = K.topk_tree(x, budget, root, VERIFY_PREFIX)
+    ms = _timed_launches(lambda: K.topk_tree(x, budget, root, VERIFY_PREFIX, out=tree), steps,
+                         warmup, dev)
     nbytes = x.numel() * x.element_size()
     peaks, kind = measured_peaks()
     gbs = nbytes / (ms / 1e3) / 1e9
-    print(json.dumps({
-        "metric": "tree build GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"tree build: 15 x {V} bf16 logits, budget {args.budget}",
-                   "l2": "256 MB buffer written between launches (L2 flushed)"},
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind},
-        "node_count": int(tree.node_count.item()),
-    }), flush=True)
+    return {"ms": ms, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
+            "peak_source": kind, "bytes_per_launch": nbytes,
+            "shape": f"15 x {V} bf16 drafter logits, budget {budget}",
+            "node_count": int(tree.node_count.item())}
 
 
-def _timed_launches(fn, steps: int, warmup: int, dev) -> float:
-    """Mean device time (ms) of `fn` over `steps` launches, each bracketed by CUDA events,
-    with a 256 MB buffer written before each launch (L2 flushed)."""
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    times = []
-    torch.cuda.nvtx.range_push("timed")
-    for _ in range(steps):
-        flush.fill_(1)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        times.append((a, b))
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    return float(np.mean([a.elapsed_time(b) for a, b in times]))
-
-
-def run_argmax(args):
-    """Greedy posterior (model/utils.py:28-30 at T=0) alone: argmax over [N, 151936] bf16
-    verify logits, N = budget + 1.  GB/s of the algorithmic bytes (one read of the logits)."""
+def measure_argmax(dev, rows, steps, warmup):
     from mdflash_b200 import kernels as K
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    n = args.budget + 1
     g = torch.Generator(device=dev).manual_seed(0)
-    logits = torch.randn((n, V), generator=g, device=dev).mul_(3).to(torch.bfloat16)
-    out = torch.empty(n, dtype=torch.int64, device=dev)
-    ms = _timed_launches(lambda: K.argmax(logits, out=out), args.steps, args.warmup, dev)
+    logits = torch.randn((rows, V), generator=g, device=dev).mul_(3).to(torch.bfloat16)
+    out = torch.empty(rows, dtype=torch.int64, device=dev)
+    ms = _timed_launches(lambda: K.argmax(logits, out=out), steps, warmup, dev)
+    ref = logits.float().argmax(-1)
+    if not torch.equal(out, ref):
+        raise RuntimeError("argmax disagrees with torch.argmax on the bench data")
     nbytes = logits.numel() * logits.element_size()
     peaks, kind = measured_peaks()
     gbs = nbytes / (ms / 1e3) / 1e9
-    print(json.dumps({
-        "metric": "argmax GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"argmax over [{n}, {V}] bf16 verify logits (N(0,1)*3)",
-                   "l2": "256 MB buffer written between launches (L2 flushed)"},
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
-                     "bytes_per_launch": nbytes},
-    }), flush=True)
+    return {"ms": ms, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
+            "peak_source": kind, "bytes_per_launch": nbytes,
+            "shape": f"[{rows}, {V}] bf16 verify logits, N(0,1)*3"}
 
 
-def run_compact(args):
+def measure_compact(dev, prefix, budget, steps, warmup):
     """Accept walk + KV compaction alone on the Qwen3-8B cache shape (36 layers x K, V
     [1, 8, P + N, 128] bf16) with a forced accepted path: the posterior follows the tree
     from the root to its deepest node (the drafter logits make the tree reach all 15
     depths), so a 16-row path is accepted and each layer's K and V move one row per
-    accepted node not already in place.  GB/s of the algorithmic
-    bytes (read + write of every moved row) over the launch time."""
+    accepted node not already in place.  GB/s of the algorithmic bytes (read + write of
+    every moved row) over the launch time."""
     from mdflash_b200 import kernels as K
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     layers, hkv, d = 36, 8, 128
-    _, logits = request_inputs(0, 16)
+    _, logits = single_request_inputs(16)
     # one token per depth lifted to about the log-sum-exp of the rest (log-prob ~ -0.7), so
     # the best-first tree reaches every drafted depth while its siblings interleave with the
     # path in node order (the moved rows are then the path's nodes past their slots)
@@ -629,7 +740,7 @@ def run_compact(args):
         lg[dep, int(rng.integers(V))] = 16.4
     x = lg.to(torch.bfloat16).to(dev)
     root = torch.zeros(1, dtype=torch.int64, device=dev)
-    tree = K.topk_tree(x, args.budget, root, args.prefix)
+    tree = K.topk_tree(x, budget, root, prefix)
     n = int(tree.node_count.item()) + 1
     parents = tree.parents[:n].cpu().numpy()
     tokens = tree.verify_ids[:n].cpu().numpy()
@@ -650,7 +761,7 @@ def run_compact(args):
         t += 1
     post[target] = t
     posterior = torch.from_numpy(post).to(dev)
-    seq = args.prefix + n
+    seq = prefix + n
     cache = [torch.randn((1, hkv, seq, d), device=dev).to(torch.bfloat16)
              for _ in range(2 * layers)]
     table = K.KvTable(cache)
@@ -659,159 +770,95 @@ def run_compact(args):
     nxt = torch.zeros(1, dtype=torch.int64, device=dev)
 
     def step():
-        K.accept_compact(posterior, tree, table, args.prefix, accepted, n_acc, nxt, n_nodes=n)
+        K.accept_compact(posterior, tree, table, prefix, accepted, n_acc, nxt, n_nodes=n)
 
-    ms = _timed_launches(step, args.steps, args.warmup, dev)
+    ms = _timed_launches(step, steps, warmup, dev)
     acc = accepted[:int(n_acc.item())].cpu().tolist()
-    assert acc == path, (acc, path)
+    if acc != path:
+        raise RuntimeError(f"forced path not accepted: {acc} vs {path}")
     moved = sum(1 for i, a in enumerate(acc) if a != i)
     nbytes = 2 * layers * hkv * moved * d * 2 * 2
     peaks, kind = measured_peaks()
     gbs = nbytes / (ms / 1e3) / 1e9
-    print(json.dumps({
-        "metric": "compaction GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"accept walk + KV compaction, Qwen3-8B cache (36 layers x K/V "
-                               f"[1, 8, {seq}, 128] bf16), forced path of {len(acc)} accepted "
-                               f"rows, {moved} moved per tensor",
-                   "l2": "256 MB buffer written between launches (L2 flushed)"},
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
-                     "bytes_per_launch": nbytes},
-        "accepted": len(acc),
-    }), flush=True)
+    return {"ms": ms, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
+            "peak_source": kind, "bytes_per_launch": nbytes, "accepted": len(acc),
+            "moved_rows_per_tensor": moved,
+            "shape": f"36 layers x K/V [1, 8, {seq}, 128] bf16, forced path of {len(acc)} rows"}
 
 
-# ------------------------------------------------------------- multi-GPU workloads
-def _dist_setup():
-    import torch.distributed as dist
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    return world, rank, dev
+def kernel_table(dev, args):
+    steps, warmup = 20, 3
+    return {
+        "l2": "256 MB buffer written before every launch (L2 flushed); CUDA events per launch",
+        "tree_build": measure_tree(dev, VERIFY_BUDGET, steps, warmup),
+        "argmax": measure_argmax(dev, VERIFY_BUDGET + 1, steps, warmup),
+        "accept_compact": measure_compact(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
+        "tree_attention": measure_attn(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
+    }
 
 
-def run_requests(args):
-    """64 independent requests (prefix log-uniform 1k..32k, budget in {64,128,256,512},
-    per-request drafter seeds) assigned to ranks by longest-processing-time; each rank
-    verifies its requests one after another (one CUDA-graph replay each), then the result
-    records are all-gathered.  Prefix K/V are random bf16 (the verify work does not depend
-    on their values); the step for each request is the full verify step."""
-    import torch.distributed as dist
-    from transformers import Qwen3ForCausalLM
+def _op_line(metric, unit, r, args, workload, bound, value_key):
+    return {"metric": metric, "value": r[value_key], "unit": unit, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": workload,
+                       "l2": "256 MB buffer written between launches (L2 flushed)"},
+            "roofline": {"bound": bound, "achieved": r[value_key], "peak": r["peak"],
+                         "unit": unit, "frac": r["frac"], "peak_source": r["peak_source"]},
+            "detail": r}
 
+
+def run_single(args):
+    """--workload verify / attn / tree / argmax / compact on one GPU."""
     from mdflash_b200 import attention as A
     from mdflash_b200 import kernels as K
-    from mdflash_b200 import sharding as S
-    from mdflash_b200.cache import TreeKVCache
-    from mdflash_b200.runner import Qwen3VerifyRunner
-    from mdflash_b200.verifier import CapturedStep, TreeVerifier
-
-    world, rank, dev = _dist_setup()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
     K._lib.load(build_if_missing=False)
-    attn = A.register()
-    torch.manual_seed(0)
-    prev = torch.get_default_dtype()
-    torch.set_default_dtype(torch.bfloat16)
-    with torch.device(dev), torch.inference_mode():
-        model = Qwen3ForCausalLM(qwen3_config(attn)).eval()
-    torch.set_default_dtype(prev)
-    runner = Qwen3VerifyRunner(model)
-    specs = S.request_specs(args.requests, seed=0)
-    mine = S.assign_requests([S.request_cost(s) for s in specs], world)[rank]
-    pool = torch.cuda.graph_pool_handle()
-    caps = []
-    g = torch.Generator(device=dev).manual_seed(rank)
-    for i in mine:
-        sp = specs[i]
-        cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
-            QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
-        for layer in cache.layers:
-            layer.k_buf.normal_(0.0, 1.0, generator=g)
-            layer.v_buf.normal_(0.0, 1.0, generator=g)
-            layer.length = sp.prefix
-            layer.keys = layer.k_buf[..., :sp.prefix, :]
-            layer.values = layer.v_buf[..., :sp.prefix, :]
-        ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
-        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pool)
-        rng = np.random.default_rng(sp.seed)
-        cap.draft_logits.copy_(torch.from_numpy(
-            rng.standard_normal((DEPTHS, V)).astype(np.float32) * np.float32(3.0)).to(torch.bfloat16))
-        cap.root_token.fill_(int(rng.integers(0, V)))
-        caps.append((sp, cap))
-    for _ in range(args.warmup):
-        for _, cap in caps:
-            cap.replay()
-    local = torch.full((len(caps), S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
-    for j, (sp, cap) in enumerate(caps):
-        local[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
-        local[j, 5] = 0
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    times = []
-    allrec = None
-    for _ in range(args.steps):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        ev0.record()
-        for j, (sp, cap) in enumerate(caps):
-            r = cap.replay()
-            # record on the device: [index, rank, n_nodes | n_accepted, next | 0 | path]
-            local[j, 3] = r.n_accepted[0]
-            local[j, 4] = r.next_token[0]
-            m = min(S.MAX_PATH, r.n_nodes)
-            local[j, 6:6 + m] = r.accepted[:m]
-        allrec = S.gather_results(local)
-        ev1.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        times.append(t.item())
-    ms = float(np.mean(times))
-    host = allrec.cpu()
-    tokens = int((host[:, 2] + host[:, 3]).sum())
-    value = tokens / (ms / 1e3)
-    line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: seeded request mix, random prefix K/V, N(0,1)*3 drafter logits, "
-                "random-init Qwen3-8B-shaped weights",
-        "config": {"workload": f"{args.requests} requests, prefix log-uniform 1k-32k, budget "
-                               "{64,128,256,512}, Qwen3-8B shape, one verify step each",
-                   "parallelism": f"request-dp{world} (longest-processing-time assignment)",
-                   "requests_per_rank": [len(x) for x in S.assign_requests(
-                       [S.request_cost(s) for s in specs], world)],
-                   "step": "every request's verify step once + all-gather of result records"},
-        "tokens_per_step": tokens,
-    }
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    if args.workload == "verify":
+        from mdflash_b200.runner import Qwen3VerifyRunner
+        model = gpu_model(dev, A.register())
+        with ClockSampler(_gpu_index(0)) as clocks:
+            r = verify_step(args, model, Qwen3VerifyRunner(model), dev, args.steps, args.warmup,
+                            args.prefix, args.budget)
+        line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": 1,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic", "config": {"workload": r["workload"]},
+                "roofline": r["roofline"], "detail": r, "clocks": clocks.summary()}
+    elif args.workload == "attn":
+        r = measure_attn(dev, args.prefix, args.budget, args.steps, args.warmup)
+        line = _op_line("tree-attn TFLOP/s", "TFLOP/s", r, args, "tree attention op: " + r["shape"],
+                        "tensor", "tflops")
+    elif args.workload == "tree":
+        r = measure_tree(dev, args.budget, args.steps, args.warmup)
+        line = _op_line("tree build GB/s", "GB/s", r, args, "tree build: " + r["shape"], "hbm",
+                        "gbs")
+    elif args.workload == "argmax":
+        r = measure_argmax(dev, args.budget + 1, args.steps, args.warmup)
+        line = _op_line("argmax GB/s", "GB/s", r, args, "argmax over " + r["shape"], "hbm", "gbs")
+    else:
+        r = measure_compact(dev, args.prefix, args.budget, args.steps, args.warmup)
+        line = _op_line("compaction GB/s", "GB/s", r, args,
+                        "accept walk + KV compaction: " + r["shape"], "hbm", "gbs")
+    print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------- split-KV (cfg 5)
 def run_splitkv(args):
     """Tree attention over one 131072-key prefix (Hq 32 / Hkv 8, D 128, 513 tree rows of a
     seeded random tree) whose K/V are sharded along the sequence across the GPUs: each rank
     computes the partial (O, m, l) of its shard, one NCCL all-gather exchanges them and
-    ddt_attn_merge combines them (the last rank also holds the tree rows)."""
+    ddt_attn_merge combines them; the last rank owns the tree keys and compacts the accepted
+    path inside its shard.  The exchange and merge are timed apart from the shard's
+    attention (CUDA events on the step stream)."""
     import torch.distributed as dist
 
     from mdflash_b200 import kernels as K
     from mdflash_b200 import sharding as S
 
-    world, rank, dev = _dist_setup()
+    world, rank, local, dev = _dist_setup()
     K._lib.load(build_if_missing=False)
     P, B = args.prefix, args.budget
     n = B + 1
@@ -827,24 +874,54 @@ def run_splitkv(args):
     k = (torch.randn((8, ke - kb, 128), generator=gk, device=dev) * sc).to(torch.bfloat16)
     v = torch.randn((8, ke - kb, 128), generator=gk, device=dev).to(torch.bfloat16)
     out = torch.empty((n, 32, 128), dtype=torch.bfloat16, device=dev)
+    owner = rank == S.owner_rank(world)
+    depth = np.zeros(n, np.int64)
+    for i in range(1, n):
+        depth[i] = depth[parents[i]] + 1
+    path = [int(np.argmax(depth))]
+    while path[-1] != 0:
+        path.append(int(parents[path[-1]]))
+    keep = torch.tensor(path[::-1], dtype=torch.int64, device=dev)
+    table = K.KvTable([k, v])
+
+    def step(events=None):
+        if events:
+            events[0].record()
+        o, m, l = K.tree_attention_partial_merged(q, k, v, kb, ke, bits, P)
+        if events:
+            events[1].record()
+        og, mg, lg = S.gather_partials(o, m, l)
+        K.attn_merge(og, mg, lg, n, 32, out=out)
+        if events:
+            events[2].record()
+        if owner:  # compaction of the accepted path on the rank holding the tree keys
+            S.compact_owner_shard(keep, table, (kb, ke), P)
+
     for _ in range(args.warmup):
-        S.splitkv_attention(q, k, v, kb, ke, bits, P, out=out)
+        step()
     torch.cuda.synchronize()
-    times = []
+    K.check_status(K.attention_status(dev))
+    parts = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
     for _ in range(args.steps):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        S.splitkv_attention(q, k, v, kb, ke, bits, P, out=out)
-        b.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([a.elapsed_time(b)], device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        times.append(t.item())
-    ms = float(np.mean(times))
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        step(evs)
+        parts.append(evs)
+    b.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    K.check_status(K.attention_status(dev))
+    shard_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in parts]))
+    xchg_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in parts]))
+    t = torch.tensor([a.elapsed_time(b) / args.steps, shard_ms, xchg_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, shard_ms, xchg_ms = t.tolist()
     flops = attn_flops(parents, P)
     peaks, kind = measured_peaks()
     tflops = flops / (ms / 1e3) / 1e12
@@ -854,9 +931,13 @@ def run_splitkv(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"split-KV tree attention: prefix {P} sharded over {world} GPUs, "
-                               f"{n} tree rows, Hq 32 / Hkv 8, D 128",
+                               f"{n} tree rows, Hq 32 / Hkv 8, D 128; compaction of a "
+                               f"{len(path)}-row path on the owner shard",
                    "exchange": "NCCL all-gather of fp32 (O, m, l) partials + ddt_attn_merge",
                    "partial_bytes_received_per_rank": link_bytes},
+        "split": {"shard_attention_ms": shard_ms, "exchange_and_merge_ms": xchg_ms,
+                  "note": "max over ranks of each part; the rest of ms_per_step is the owner's "
+                          "compaction and host launch gaps"},
         "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s per GPU", "frac": tflops / world / peaks["bf16_tflops"],
                      "peak_source": f"{kind} bf16 burst", "flops_per_step": flops},
@@ -870,22 +951,13 @@ def run_splitkv(args):
 
 def main():
     args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
     if args.workload == "requests":
         return run_requests(args)
     if args.workload == "splitkv":
         return run_splitkv(args)
-    if args.workload == "attn":
-        run_attn(args)
-    elif args.workload == "tree":
-        run_tree(args)
-    elif args.workload == "argmax":
-        run_argmax(args)
-    elif args.workload == "compact":
-        run_compact(args)
-    elif args.impl == "reference":
-        run_reference(args)
-    else:
-        run_ours(args)
+    return run_single(args)
 
 
 if __name__ == "__main__":
