@@ -135,7 +135,9 @@ int ddt_compact_kv(const int64_t* keep, int64_t keep_count, void* const* kv_ptrs
  * o_head_stride).  head_dim must be 128; q_heads a multiple of kv_heads.
  * mask_mode DDT_MASK_TREE: node i sees every prefix key and the tree keys of its
  * ancestors-or-self (anc_bits [n_nodes, anc_words]); DDT_MASK_CAUSAL: node i sees keys
- * < past_length + i + 1 (anc_bits unused).
+ * < past_length + i + 1 (anc_bits unused); DDT_MASK_NONE: every query row sees every key
+ * (anc_bits unused) -- the drafter's non-causal attention over context + block
+ * (model/dflash.py:58-102, is_causal = False, no mask).
  * kv_splits: number of KV partitions per (head, query tile); 0 picks one.  Partial
  * results go to the workspace and are merged in the same call.
  * status: device i32 (zeroed by the caller), set non-zero if a bounded wait expired; the
@@ -143,6 +145,7 @@ int ddt_compact_kv(const int64_t* keep, int64_t keep_count, void* const* kv_ptrs
  * DDT_ERR_TIMEOUT. */
 #define DDT_MASK_TREE 0
 #define DDT_MASK_CAUSAL 1
+#define DDT_MASK_NONE 2
 size_t ddt_tree_attn_workspace_bytes(int64_t n_nodes, int64_t q_heads, int64_t head_dim,
                                      int64_t kv_splits);
 int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride, const void* k,

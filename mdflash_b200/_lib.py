@@ -17,6 +17,7 @@ DDT_F32 = 0
 DDT_BF16 = 1
 DDT_MASK_TREE = 0
 DDT_MASK_CAUSAL = 1
+DDT_MASK_NONE = 2
 DDT_MAX_BUDGET = 1024
 DDT_MAX_DEPTH = 20
 DDT_MAX_NODES = DDT_MAX_BUDGET + 1

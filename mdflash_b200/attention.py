@@ -9,7 +9,9 @@ so an unmodified Qwen3 model runs its verify forward through it:
   (set by this package's ``compile_ddtree_tree`` or ``tree_verify``); when a caller only
   has the reference's additive 4-D mask, the tree block of that mask is converted to
   bitmasks on the device;
-* no mask (prefill, plain decode): causal attention, node i sees keys < past + i + 1.
+* no mask (prefill, plain decode): causal attention, node i sees keys < past + i + 1;
+* no mask on a non-causal module (``module.is_causal`` False: the DFlash drafter's attention
+  over context + noise block, model/dflash.py:58-102): every query sees every key.
 
 The kernel computes in bf16 with fp32 accumulation; an fp32 model's q / k / v are rounded
 to bf16 for it (within the bf16 tolerance of fp32 attention).  Bounded-wait timeouts of the
@@ -91,6 +93,11 @@ def ddtree_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: 
             raise ValueError("expected the 4-D tree mask [1, 1, N, past + N]")
         bits = K.mask_to_bits(attention_mask[0, 0, :, past:past + n])
         out = K.tree_attention(query, key, value, bits, past, scale=scaling, status=st)
+    elif is_causal is False or getattr(module, "is_causal", True) is False:
+        # a non-causal module without a mask (the DFlash drafter's context + block
+        # attention, model/dflash.py:58-102): every query sees every key
+        out = K.tree_attention(query, key, value, None, past, scale=scaling, unmasked=True,
+                               status=st)
     else:
         out = K.tree_attention(query, key, value, None, past, scale=scaling, causal=True,
                                status=st)

@@ -147,8 +147,9 @@ __host__ __device__ inline UnitGeo unit_geo(const Params& p, int u) {
   g.row0 = (u % p.n_pairs) * kRowsPerCta;
   int node_hi = (g.row0 + kRowsPerCta - 1) / p.group;
   if (node_hi > p.n_nodes - 1) node_hi = p.n_nodes - 1;
-  // keys beyond past + node_hi are invisible to every row of the unit (both mask modes)
-  g.g_end = p.past_len + node_hi + 1;
+  // keys beyond past + node_hi are invisible to every row of the unit (tree and causal
+  // masks); without a mask every row sees every key
+  g.g_end = p.mask_mode == DDT_MASK_NONE ? p.key_hi : p.past_len + node_hi + 1;
   if (g.g_end > p.key_hi) g.g_end = p.key_hi;
   g.ntot = g.g_end > p.key_lo ? (g.g_end - p.key_lo + kBlockN - 1) / kBlockN : 0;
   return g;
@@ -182,6 +183,7 @@ __device__ __forceinline__ uint32_t visible32(const Params& p, int node, int g0,
   const int n_ok = g_end - g0;
   if (n_ok <= 0) return 0u;
   if (n_ok < 32) m = (1u << n_ok) - 1u;
+  if (p.mask_mode == DDT_MASK_NONE) return m;
   if (p.mask_mode == DDT_MASK_CAUSAL) {
     const int lim = p.past_len + node + 1 - g0;  // keys < lim visible
     if (lim <= 0) return 0u;
@@ -482,7 +484,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const int g_end = g.g_end;
       // the whole key range of a sub-tile is visible to this row (no mask needed) when it
       // ends before the tree window / the launch's last key
-      const int full_end = p.mask_mode == DDT_MASK_CAUSAL
+      const int full_end = p.mask_mode == DDT_MASK_NONE ? g_end
+                           : p.mask_mode == DDT_MASK_CAUSAL
                                ? (g_end < p.past_len + vnode + 1 ? g_end : p.past_len + vnode + 1)
                                : (g_end < p.past_len ? g_end : p.past_len);
       float m_used = -INFINITY, l = 0.f;
@@ -1046,7 +1049,8 @@ inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_he
   if (head_dim != kHeadDim) return DDT_ERR_CAPACITY;
   int rc = prepare_sizes(L.p, n_nodes, past_length, q_heads, kv_heads, key_lo, key_hi);
   if (rc) return rc;
-  if (mask_mode != DDT_MASK_TREE && mask_mode != DDT_MASK_CAUSAL) return DDT_ERR_INVALID;
+  if (mask_mode != DDT_MASK_TREE && mask_mode != DDT_MASK_CAUSAL && mask_mode != DDT_MASK_NONE)
+    return DDT_ERR_INVALID;
   if (mask_mode == DDT_MASK_TREE && (!anc_bits || anc_words * 32 < n_nodes)) return DDT_ERR_INVALID;
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16)) return DDT_ERR_ALIGN;
   if ((q_node_stride * 2) % 16 || (q_head_stride * 2) % 16 || (kv_head_stride * 2) % 16 ||

@@ -8,7 +8,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import DDT_BF16, DDT_F32, DDT_MASK_CAUSAL, DDT_MASK_TREE, check
+from ._lib import DDT_BF16, DDT_F32, DDT_MASK_CAUSAL, DDT_MASK_NONE, DDT_MASK_TREE, check
 
 __all__ = [
     "DeviceTree", "expected_node_count", "topk_tree", "argmax", "accept_compact", "compact_kv",
@@ -300,12 +300,20 @@ def _kv_view(k: torch.Tensor):
     return k.shape[0], k.shape[1], k.stride(0), k.stride(1)
 
 
+def _mask_mode(causal: bool, unmasked: bool) -> int:
+    if causal and unmasked:
+        raise ValueError("causal and unmasked are exclusive")
+    return DDT_MASK_NONE if unmasked else (DDT_MASK_CAUSAL if causal else DDT_MASK_TREE)
+
+
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    anc_bits: torch.Tensor | None, past_length: int, scale: float | None = None,
                    causal: bool = False, out: torch.Tensor | None = None, kv_splits: int = 0,
-                   status: torch.Tensor | None = None) -> torch.Tensor:
+                   status: torch.Tensor | None = None, unmasked: bool = False) -> torch.Tensor:
     """softmax(Q K^T * scale, tree / causal mask) V on tcgen05.  q: [N, Hq, D] (or HF
     [1, Hq, N, D]); k, v: [Hkv, past_length + N, D] (or [1, ...]); returns [N, Hq, D].
+    Mask: the tree (anc_bits), causal=True (node i sees keys < past_length + i + 1), or
+    unmasked=True (every row sees every key: the drafter's non-causal attention).
 
     The kernel computes in bf16 (fp32 accumulation).  fp32 inputs (an fp32 model) are rounded
     to bf16 for the kernel and the output is returned in fp32: the result is within the bf16
@@ -314,7 +322,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if q.dtype == torch.float32 and k.dtype == torch.float32 and v.dtype == torch.float32:
         res = tree_attention(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16),
                              anc_bits, past_length, scale=scale, causal=causal,
-                             kv_splits=kv_splits, status=status)
+                             kv_splits=kv_splits, status=status, unmasked=unmasked)
         if out is None:
             return res.float()
         out.copy_(res)
@@ -338,8 +346,8 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     ws = WORKSPACES.get(dev, "tree_attn", ws_bytes)
     if status is None:
         status = attention_status(dev)
-    mode = DDT_MASK_CAUSAL if causal else DDT_MASK_TREE
-    if not causal and anc_bits is None:
+    mode = _mask_mode(causal, unmasked)
+    if mode == DDT_MASK_TREE and anc_bits is None:
         raise ValueError("tree mode needs ancestor bitmasks")
     words = anc_bits.shape[1] if anc_bits is not None else 0
     stream = _stream(dev)

@@ -287,6 +287,32 @@ def test_tree_attention_wait_timeout_sets_status(cuda_device):
     assert _rel_err(out.cpu(), ref) <= ATTN_TOL
 
 
+@pytest.mark.parametrize("hq,hkv,ctx,n", [(32, 8, 700, 16), (16, 8, 0, 16), (32, 8, 4000, 64)])
+def test_tree_attention_unmasked_drafter_attention(cuda_device, hq, hkv, ctx, n):
+    """The DFlash drafter's attention (model/dflash.py:58-102): a block of n noise queries
+    over context + block keys, non-causal, no mask; through the kernel's unmasked mode and
+    through the plug-in on a module with is_causal = False."""
+    from mdflash_b200 import attention as A
+    g = torch.Generator().manual_seed(ctx + n)
+    d = 128
+    q = (torch.randn((1, hq, n, d), generator=g) * 0.09).to(torch.bfloat16)
+    k = (torch.randn((1, hkv, ctx + n, d), generator=g) * 0.09).to(torch.bfloat16)
+    v = torch.randn((1, hkv, ctx + n, d), generator=g).to(torch.bfloat16)
+    ref = oracle.tree_attention(q[0], k[0], v[0], np.ones((n, n), bool), ctx)
+    out = K.tree_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, ctx,
+                           unmasked=True)
+
+    class _Drafter(torch.nn.Module):
+        is_causal = False
+
+    plug, _ = A.ddtree_attention_forward(_Drafter(), q.to(cuda_device), k.to(cuda_device),
+                                         v.to(cuda_device), None, scaling=d ** -0.5)
+    torch.cuda.synchronize()
+    for o in (out.cpu(), plug[0].cpu()):
+        assert _rel_err(o, ref) <= ATTN_TOL
+        assert elem_rel_err(o, ref) <= ATTN_TOL
+
+
 def test_tree_attention_hf_layout_and_causal(cuda_device):
     """HF passes query as a [1, Hq, N, D] view of [1, N, Hq, D]; prefill is causal."""
     g = torch.Generator().manual_seed(9)
