@@ -27,6 +27,8 @@
  *                        (within one GPU, and across GPUs after an NCCL exchange)
  *   ddt_mask_to_bits     ddtree.py:262-264 read backwards: additive mask block ->
  *                        ancestor bitmasks, for callers that only hold the mask
+ *   ddt_sample_chains    mdflash.py:19-40 sample_candidate_chains
+ *   ddt_chain_tree       ddtree.py:169-224 build_sampled_candidate_tree
  */
 #ifndef DDTREE_B200_H_
 #define DDTREE_B200_H_
@@ -101,6 +103,26 @@ int ddt_topk_tree_noalloc(const void* draft_logits, int dtype, int64_t depths, i
                           uint32_t* anc_bits, int64_t anc_words, const int64_t* root_token,
                           int64_t start, int64_t* verify_ids, int64_t* verify_pos,
                           void* stream);
+
+/* ---- sampled draft trees (MDFlash / P-Express variants) ---------------------
+ * ddt_sample_chains: chains i64 [num_samples, depths] (row-major); chain s holds sample s of
+ * every depth, drawn with replacement from softmax(draft_logits[d] / temperature) by inverse
+ * CDF with counter-based uniforms of (seed, offset, depth, sample), or, for temperature
+ * < 1e-5, the depth's argmax (ties to the lowest index) for every sample.  Logits must be
+ * finite.  Replaces sample_candidate_chains (mdflash.py:19-40); the draws follow the same
+ * distribution as torch.multinomial, not its random stream.
+ * ddt_chain_tree: the trie of the chains (chain stride in elements) with at most budget
+ * nodes, in the reference's node order, written like ddt_topk_tree's outputs (node tokens,
+ * depths, parents, node_count, ancestor bitmasks, verify ids / positions).  Replaces
+ * build_sampled_candidate_tree (ddtree.py:169-224).  num_chains <= DDT_MAX_BUDGET. */
+int ddt_sample_chains(const void* draft_logits, int dtype, int64_t depths, int64_t vocab,
+                      int64_t row_stride, int64_t num_samples, float temperature, uint64_t seed,
+                      uint64_t offset, int64_t* chains, void* stream);
+int ddt_chain_tree(const int64_t* chains, int64_t num_chains, int64_t depths,
+                   int64_t chain_stride, int64_t budget, int64_t* node_token_ids,
+                   int64_t* node_depths, int32_t* parents, int32_t* node_count,
+                   uint32_t* anc_bits, int64_t anc_words, const int64_t* root_token,
+                   int64_t start, int64_t* verify_ids, int64_t* verify_pos, void* stream);
 
 /* ---- greedy posterior ---------------------------------------------------
  * logits [rows, cols] (row stride in elements) -> out i64 [rows]; ties go to the lowest

@@ -37,6 +37,9 @@ SIGNATURES = {
                            _P, _S, _P]),
     "ddt_topk_tree_noalloc": (_i, [_P, _i, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I,
                                    _P, _P, _P]),
+    "ddt_sample_chains": (_i, [_P, _i, _I, _I, _I, _I, _F, ctypes.c_uint64, ctypes.c_uint64, _P,
+                               _P]),
+    "ddt_chain_tree": (_i, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P]),
     "ddt_argmax": (_i, [_P, _i, _I, _I, _I, _P, _P]),
     "ddt_accept_compact": (_i, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "ddt_compact_kv": (_i, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P]),

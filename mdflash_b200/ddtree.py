@@ -3,6 +3,7 @@ code), same names, arguments, return types and error behaviour, running on the B
 kernels of ``libddtree_b200.so``:
 
   build_ddtree_tree        ddtree.py:84-166
+  build_sampled_candidate_tree  ddtree.py:169-224
   compile_ddtree_tree      ddtree.py:227-267
   follow_verified_tree     ddtree.py:270-281
   compact_dynamic_cache    ddtree.py:303-335
@@ -92,6 +93,48 @@ def build_ddtree_tree(draft_logits: torch.Tensor, budget: int):
     subtimes.update(tree_build_copy=t1 - t0, tree_build_heap=t2 - t1, tree_build_visibility=t3 - t2)
     _LAST.tree, _LAST.n_nodes = tree, n
     return node_ids, depths, parents, child_maps, vis, subtimes
+
+
+def _host_tree(tree: K.DeviceTree, n: int):
+    """One device->host copy of a built tree: (node_ids, depths, parents list, child_maps,
+    visibility) in the reference's types."""
+    cnt = n - 1
+    host = torch.cat([tree.node_token_ids[:cnt], tree.node_depths[:cnt],
+                      tree.parents[:n].to(torch.int64),
+                      tree.anc_bits[:n].reshape(-1).to(torch.int64)]).cpu()
+    node_ids = host[:cnt].clone()
+    depths = host[cnt:2 * cnt].clone()
+    parents_np = host[2 * cnt:2 * cnt + n].numpy()
+    bits = host[2 * cnt + n:].numpy().astype(np.uint32).reshape(n, tree.anc_words)
+    vis = torch.from_numpy(unpack_visibility(bits, n))
+    parents = parents_np.astype(np.int64).tolist()
+    child_maps: list[dict[int, int]] = [dict() for _ in range(n)]
+    ids_list = node_ids.tolist()
+    for i in range(1, n):
+        child_maps[parents[i]][ids_list[i - 1]] = i
+    return node_ids, depths, parents, child_maps, vis
+
+
+def build_sampled_candidate_tree(candidate_token_ids: torch.Tensor, budget: int):
+    """ddtree.py:169-224: the trie of the sampled chains (i64 [num_chains, depths], chain
+    order, at most `budget` nodes), built on the device by ddt_chain_tree.  Returns
+    (node_token_ids i64 CPU, node_depths i64 CPU, parents list, child_maps list[dict],
+    visibility bool CPU [N, N]) like the reference, and registers the device tree for
+    compile_ddtree_tree / the attention plug-in / follow_verified_tree."""
+    if (budget <= 0 or candidate_token_ids.dim() != 2 or candidate_token_ids.shape[0] == 0
+            or candidate_token_ids.shape[1] == 0):
+        visibility = torch.zeros((1, 1), dtype=torch.bool)
+        visibility[0, 0] = True
+        _LAST.tree, _LAST.n_nodes = None, 1
+        return (torch.empty(0, dtype=torch.long), torch.empty(0, dtype=torch.long), [-1], [dict()],
+                visibility)
+    _require_cuda_tensor(candidate_token_ids, "candidate_token_ids")
+    tree = K.chain_tree(candidate_token_ids, budget)
+    n = 1 + int(tree.node_count.item())
+    tree.n_nodes = n
+    node_ids, depths, parents, child_maps, vis = _host_tree(tree, n)
+    _LAST.tree, _LAST.n_nodes = tree, n
+    return node_ids, depths, parents, child_maps, vis
 
 
 def compile_ddtree_tree(root_token_id, start: int, node_token_ids: torch.Tensor,

@@ -14,6 +14,7 @@ __all__ = [
     "DeviceTree", "expected_node_count", "topk_tree", "argmax", "accept_compact", "compact_kv",
     "tree_attention", "tree_attention_partial", "attn_merge", "mask_to_bits", "KvTable",
     "anc_words_for", "attention_status", "check_status", "tree_attention_wait_check",
+    "sample_chains", "chain_tree",
 ]
 
 
@@ -186,6 +187,58 @@ def topk_tree(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor 
         tree.verify_ids.data_ptr(), tree.verify_pos.data_ptr(), ws.data_ptr(), ws.numel(),
         _stream(dev))
     check(rc, "ddt_topk_tree")
+    STATS.launches += 1
+    return tree
+
+
+def sample_chains(draft_logits: torch.Tensor, num_samples: int, temperature: float, seed: int,
+                  offset: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """ddt_sample_chains: i64 [num_samples, depths] chains, sample s of every depth drawn
+    from softmax(draft_logits / temperature) (argmax for temperature < 1e-5)."""
+    if draft_logits.dim() != 2:
+        raise ValueError("draft_logits must be [depths, vocab]")
+    dev = _require_cuda(draft_logits)
+    L, V = draft_logits.shape
+    if draft_logits.stride(1) != 1:
+        draft_logits = draft_logits.contiguous()
+    if out is None:
+        out = torch.empty((max(num_samples, 0), L), dtype=torch.int64, device=dev)
+    check(_lib.load().ddt_sample_chains(
+        draft_logits.data_ptr(), _dtype_code(draft_logits), L, V, draft_logits.stride(0),
+        num_samples, float(temperature), int(seed) & ((1 << 64) - 1),
+        int(offset) & ((1 << 64) - 1), out.data_ptr(), _stream(dev)), "ddt_sample_chains")
+    STATS.launches += 1
+    return out
+
+
+def chain_tree(chains: torch.Tensor, budget: int, root_token: torch.Tensor | None = None,
+               start: int = 0, out: DeviceTree | None = None) -> DeviceTree:
+    """ddt_chain_tree: the trie of i64 [num_chains, depths] chains with at most `budget`
+    nodes (ddtree.py:169-224), as a DeviceTree.  Its node count is data-dependent:
+    tree.n_nodes is set to 1 + budget (an upper bound); tree.node_count holds the count."""
+    if chains.dim() != 2:
+        raise ValueError("chains must be [num_chains, depths]")
+    dev = _require_cuda(chains)
+    S, L = chains.shape
+    if chains.dtype != torch.int64:
+        chains = chains.to(torch.int64)
+    if chains.stride(1) != 1:
+        chains = chains.contiguous()
+    b = max(int(budget), 0)
+    tree = out if out is not None else DeviceTree.allocate(dev, b, max(L, 1), b if b > 0 else 1)
+    if tree.budget != b:
+        raise ValueError("output DeviceTree was allocated for another budget")
+    tree.n_nodes = 1 + b
+    if root_token is not None:
+        root_token = root_token.reshape(-1)[:1]
+        if root_token.dtype != torch.int64:
+            root_token = root_token.to(torch.int64)
+    check(_lib.load().ddt_chain_tree(
+        chains.data_ptr() if chains.numel() else None, S, L, max(chains.stride(0), L), b,
+        tree.node_token_ids.data_ptr(), tree.node_depths.data_ptr(), tree.parents.data_ptr(),
+        tree.node_count.data_ptr(), tree.anc_bits.data_ptr(), tree.anc_words,
+        root_token.data_ptr() if root_token is not None else None, int(start),
+        tree.verify_ids.data_ptr(), tree.verify_pos.data_ptr(), _stream(dev)), "ddt_chain_tree")
     STATS.launches += 1
     return tree
 

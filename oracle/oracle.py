@@ -153,6 +153,42 @@ def build_ddtree_tree(draft_logits: torch.Tensor, budget: int):
             torch.from_numpy(vis), subtimes)
 
 
+def build_sampled_candidate_tree(candidate_token_ids, budget: int):
+    """Restatement of ddtree.py:169-224 (the trie of sampled chains, in chain order, stopping
+    at the first new node past the budget) with the same return types: (node_token_ids i64
+    CPU, node_depths i64 CPU, parents list, child_maps list[dict], visibility bool [N, N])."""
+    chains = np.asarray(candidate_token_ids, np.int64)
+    if budget <= 0 or chains.ndim != 2 or chains.shape[0] == 0 or chains.shape[1] == 0:
+        vis = torch.zeros((1, 1), dtype=torch.bool)
+        vis[0, 0] = True
+        return torch.empty(0, dtype=torch.long), torch.empty(0, dtype=torch.long), [-1], [dict()], vis
+    parents = [-1]
+    child_maps: list[dict[int, int]] = [dict()]
+    tokens: list[int] = []
+    depths: list[int] = []
+    full = False
+    for chain in chains.tolist():
+        cur = 0
+        for depth, tok in enumerate(chain, start=1):
+            nxt = child_maps[cur].get(tok)
+            if nxt is None:
+                if len(tokens) >= budget:
+                    full = True
+                    break
+                nxt = len(parents)
+                parents.append(cur)
+                child_maps.append(dict())
+                child_maps[cur][tok] = nxt
+                tokens.append(tok)
+                depths.append(depth)
+            cur = nxt
+        if full:
+            break
+    par = np.asarray(parents, np.int32)
+    return (torch.tensor(tokens, dtype=torch.long), torch.tensor(depths, dtype=torch.long), parents,
+            child_maps, torch.from_numpy(visibility(par)))
+
+
 def compile_ddtree_tree(root_token_id, start, node_token_ids, node_depths, visibility_cpu,
                         past_length, dtype, device, verify_input_ids_buffer,
                         verify_position_ids_buffer, attention_mask_buffer, tree_visibility_buffer,

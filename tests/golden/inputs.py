@@ -228,3 +228,29 @@ def e2e_inputs(spec: dict):
     logits = torch.from_numpy(
         rng.standard_normal((spec["depths"], spec["vocab"])).astype(np.float32) * np.float32(3.0))
     return ids, logits
+
+
+# Sampled-chain trees (build_sampled_candidate_tree, ddtree.py:169-224): chains over a small
+# vocabulary so that prefixes are shared, budgets that cut a chain in the middle, exact fits,
+# identical chains and the empty cases.
+SAMPLED_CASES = [
+    dict(name="chains_s32_l15_v4_b32", seed=400, S=32, L=15, V=4, budget=32),
+    dict(name="chains_s256_l15_v3_b256", seed=401, S=256, L=15, V=3, budget=256),
+    dict(name="chains_s1024_l15_v2_b1024", seed=402, S=1024, L=15, V=2, budget=1024),
+    dict(name="chains_s512_l16_v6_b300", seed=403, S=512, L=16, V=6, budget=300),
+    dict(name="chains_s20_l5_v50_b200", seed=404, S=20, L=5, V=50, budget=200),
+    dict(name="chains_s64_l10_same_b64", seed=405, S=64, L=10, V=1, budget=64),
+    dict(name="chains_s8_l20_v151936_b8", seed=406, S=8, L=20, V=151936, budget=8),
+    dict(name="chains_s0_l15_b8", seed=407, S=0, L=15, V=4, budget=8),
+    dict(name="chains_s8_l0_b8", seed=408, S=8, L=0, V=4, budget=8),
+    dict(name="chains_s8_l4_b0", seed=409, S=8, L=4, V=4, budget=0),
+]
+
+
+def sampled_chains(spec: dict) -> torch.Tensor:
+    rng = np.random.default_rng(spec["seed"])
+    return torch.from_numpy(rng.integers(0, spec["V"], (spec["S"], spec["L"])).astype(np.int64))
+
+
+# sample_candidate_chains at temperature 0 (mdflash.py:19-40): the argmax chain repeated
+GREEDY_CHAIN_CASE = dict(name="greedy_chains", seed=410, L=15, V=V_QWEN3, S=16)

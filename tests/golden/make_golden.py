@@ -207,6 +207,29 @@ def gen_attention(ddtree, out: dict, manifest: dict):
     manifest["attention"] = cases
 
 
+def gen_sampled(ddtree, out: dict, manifest: dict, reference: str):
+    """build_sampled_candidate_tree on seeded chains, and sample_candidate_chains at
+    temperature 0 on seeded logits."""
+    cases = []
+    for spec in gin.SAMPLED_CASES:
+        chains = gin.sampled_chains(spec)
+        node_ids, depths, parents, child_maps, vis = ddtree.build_sampled_candidate_tree(
+            chains, spec["budget"])
+        name = spec["name"]
+        out[f"{name}/node_ids"] = node_ids.numpy().astype(np.int64)
+        out[f"{name}/depths"] = depths.numpy().astype(np.int64)
+        out[f"{name}/parents"] = np.asarray(parents, np.int32)
+        out[f"{name}/visibility"] = np.packbits(vis.numpy(), axis=-1)
+        cases.append(name)
+    manifest["sampled"] = cases
+    import mdflash  # noqa: F401  (the reference's module; imports ddtree / dflash / model)
+    spec = gin.GREEDY_CHAIN_CASE
+    logits = gin._logits(spec["seed"], spec["L"], spec["V"], "normal3")
+    chains = mdflash.sample_candidate_chains(torch.from_numpy(logits), spec["S"], 0.0)
+    out["greedy_chains/chains"] = chains.numpy().astype(np.int64)
+    manifest["greedy_chains"] = dict(spec)
+
+
 def gen_e2e(ddtree, out: dict, manifest: dict):
     """One DDTree verify step on the CPU-runnable Qwen3-0.6B-shaped target (fp32)."""
     from transformers import DynamicCache
@@ -265,8 +288,9 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DDTREE_REFERENCE"),
                     help="checkout of the DDTree research code (default: $DDTREE_REFERENCE)")
-    ap.add_argument("--only-e2e", action="store_true",
-                    help="regenerate only the e2e/* arrays, keeping the others of golden.npz")
+    ap.add_argument("--only", default="",
+                    help="comma-separated groups to regenerate (e2e, sampled), keeping the other "
+                         "arrays of golden.npz")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--no-cpp", action="store_true")
     args = ap.parse_args()
@@ -279,12 +303,20 @@ def main():
     out: dict = {}
     manifest: dict = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__}
     t0 = time.time()
-    if args.only_e2e:
+    if args.only:
+        groups = set(args.only.split(","))
+        prefixes = {"e2e": ("e2e/",),
+                    "sampled": tuple(f"{c['name']}/" for c in gin.SAMPLED_CASES) +
+                    ("greedy_chains/",)}
+        drop = tuple(p for g in groups for p in prefixes[g])
         old = np.load(os.path.join(HERE, "golden.npz"))
-        out = {k: old[k] for k in old.files if not k.startswith("e2e/")}
+        out = {k: old[k] for k in old.files if not k.startswith(drop)}
         with open(os.path.join(HERE, "manifest.json")) as f:
             manifest = json.load(f)
-        gen_e2e(ddtree, out, manifest)
+        if "e2e" in groups:
+            gen_e2e(ddtree, out, manifest)
+        if "sampled" in groups:
+            gen_sampled(ddtree, out, manifest, args.reference)
         np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)
         with open(os.path.join(HERE, "manifest.json"), "w") as f:
             json.dump(manifest, f, indent=1, sort_keys=True)
@@ -295,6 +327,7 @@ def main():
     gen_follow(ddtree, out, manifest)
     gen_compact(ddtree, out, manifest, use_cpp=not args.no_cpp)
     gen_attention(ddtree, out, manifest)
+    gen_sampled(ddtree, out, manifest, args.reference)
     if not args.skip_e2e:
         gen_e2e(ddtree, out, manifest)
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)

@@ -60,6 +60,13 @@ def test_host_side_validation_rejects_bad_arguments():
     assert lib.ddt_compact_kv(ctypes.c_void_p(256), 64, ctypes.c_void_p(256), 2, 2, 128, 1024,
                               128, 2, 10, None) == -2
     assert lib.ddt_argmax(None, 2, 4, 4, 4, None, None) == -3
+    # sampled-chain trie: more chains than a tree budget holds is a capacity error
+    assert lib.ddt_chain_tree(p := ctypes.c_void_p(256), 2000, 15, 15, 64, p, p, p, p, p, 3,
+                              None, 0, None, None, None) == -2
+    assert lib.ddt_sample_chains(ctypes.c_void_p(256), 1, 21, 100, 100, 8, 1.0, 0, 0,
+                                 ctypes.c_void_p(256), None) == -2
+    assert lib.ddt_sample_chains(ctypes.c_void_p(256), 5, 4, 100, 100, 8, 1.0, 0, 0,
+                                 ctypes.c_void_p(256), None) == -3
     # the bounded-wait check takes limits from 100 us to 2 s and needs a status word
     p = ctypes.c_void_p(256)
     assert lib.ddt_tree_attn_wait_check(p, p, p, p, 65, 256, 32, 8, p, 3, 10, p, None) == -1

@@ -156,3 +156,29 @@ def test_random_tree_shape():
     for i in range(1, 513):
         depth[i] = depth[p[i]] + 1
     assert depth.max() <= 16
+
+
+@pytest.mark.parametrize("spec", gin.SAMPLED_CASES, ids=[c["name"] for c in gin.SAMPLED_CASES])
+def test_sampled_candidate_tree_matches_reference(golden, spec):
+    """build_sampled_candidate_tree (ddtree.py:169-224) restated: topology, tokens, depths and
+    visibility equal the reference's on chains with shared prefixes, budget cuts in the middle
+    of a chain, identical chains and the empty cases."""
+    name = spec["name"]
+    node_ids, depths, parents, child_maps, vis = oracle.build_sampled_candidate_tree(
+        gin.sampled_chains(spec), spec["budget"])
+    np.testing.assert_array_equal(node_ids.numpy(), golden[f"{name}/node_ids"])
+    np.testing.assert_array_equal(depths.numpy(), golden[f"{name}/depths"])
+    assert parents == golden[f"{name}/parents"].tolist()
+    n = len(parents)
+    g_vis = np.unpackbits(golden[f"{name}/visibility"], axis=-1, count=n).astype(bool)
+    np.testing.assert_array_equal(vis.numpy(), g_vis)
+    for i in range(1, n):
+        assert child_maps[parents[i]][int(node_ids[i - 1])] == i
+
+
+def test_greedy_chains_are_the_argmax_chain(golden):
+    spec = gin.GREEDY_CHAIN_CASE
+    logits = gin._logits(spec["seed"], spec["L"], spec["V"], "normal3")
+    chains = golden["greedy_chains/chains"]
+    assert chains.shape == (spec["S"], spec["L"])
+    np.testing.assert_array_equal(chains, np.tile(oracle.argmax(logits), (spec["S"], 1)))
