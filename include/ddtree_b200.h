@@ -27,6 +27,8 @@
  *                        (within one GPU, and across GPUs after an NCCL exchange)
  *   ddt_mask_to_bits     ddtree.py:262-264 read backwards: additive mask block ->
  *                        ancestor bitmasks, for callers that only hold the mask
+ *   ddt_lm_head_argmax   the verify forward's lm_head (ddtree.py:467-478) fused with
+ *                        sample() at temperature 0 (model/utils.py:28-30)
  *   ddt_sample_chains    mdflash.py:19-40 sample_candidate_chains
  *   ddt_chain_tree       ddtree.py:169-224 build_sampled_candidate_tree
  */
@@ -129,6 +131,22 @@ int ddt_chain_tree(const int64_t* chains, int64_t num_chains, int64_t depths,
  * index, NaN counts as the largest value. */
 int ddt_argmax(const void* logits, int dtype, int64_t rows, int64_t cols, int64_t row_stride,
                int64_t* out, void* stream);
+
+/* ---- fused lm_head -> greedy posterior ------------------------------------
+ * out[n] = argmax_v bf16(hidden[n] . weight[v]) for n < n_rows (ties to the lowest index,
+ * NaN largest), the logits being the bf16 rounding (nearest even) of fp32-accumulated dot
+ * products; hidden [n_rows, hidden_size] and weight [vocab, hidden_size] bf16, row strides
+ * hidden_ld / weight_ld elements, hidden_size a multiple of 64.  The [n_rows, vocab] logits
+ * are not written unless logits_out (bf16, row stride logits_ld) is given, a testing aid.
+ * Replaces the lm_head projection of the verify forward (ddtree.py:467-478) followed by
+ * sample() at temperature 0 (model/utils.py:28-30).  The workspace
+ * (ddt_lm_head_argmax_workspace_bytes) must be zero-filled before its first use; every
+ * launch leaves it zeroed.  status: as for ddt_tree_attn. */
+size_t ddt_lm_head_argmax_workspace_bytes(int64_t n_rows);
+int ddt_lm_head_argmax(const void* hidden, int64_t hidden_ld, const void* weight,
+                       int64_t weight_ld, int64_t n_rows, int64_t hidden_size, int64_t vocab,
+                       int64_t* out, void* logits_out, int64_t logits_ld, void* workspace,
+                       size_t workspace_bytes, int32_t* status, void* stream);
 
 /* ---- accept walk + KV compaction ----------------------------------------
  * KV cache: n_tensors tensors (K and V of every layer) whose device base pointers are in

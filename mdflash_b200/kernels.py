@@ -14,7 +14,7 @@ __all__ = [
     "DeviceTree", "expected_node_count", "topk_tree", "argmax", "accept_compact", "compact_kv",
     "tree_attention", "tree_attention_partial", "attn_merge", "mask_to_bits", "KvTable",
     "anc_words_for", "attention_status", "check_status", "tree_attention_wait_check",
-    "sample_chains", "chain_tree",
+    "sample_chains", "chain_tree", "lm_head_argmax",
 ]
 
 
@@ -256,6 +256,38 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
                                  out.data_ptr(), _stream(dev)), "ddt_argmax")
     STATS.launches += 1
     return out.view(logits.shape[:-1])
+
+
+def lm_head_argmax(hidden: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
+                   logits_out: torch.Tensor | None = None,
+                   status: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy posterior of the lm_head without materialising the logits: out[n] =
+    argmax_v bf16(hidden[n] . weight[v]) (ties to the lowest index).  hidden [N, H] and
+    weight [V, H] bf16 with unit inner stride; logits_out ([N, V] bf16), when given, receives
+    the bf16 logits the argmax was taken over."""
+    dev = _require_cuda(hidden, weight)
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("lm_head_argmax takes bf16 hidden states and weight")
+    h = hidden.reshape(-1, hidden.shape[-1])
+    if h.stride(1) != 1:
+        h = h.contiguous()
+    if weight.stride(1) != 1:
+        raise ValueError("weight rows must be contiguous")
+    n, H = h.shape
+    V = weight.shape[0]
+    if out is None:
+        out = torch.empty(n, dtype=torch.int64, device=dev)
+    if status is None:
+        status = attention_status(dev)
+    lib = _lib.load()
+    ws = WORKSPACES.get(dev, "lm_head_argmax", lib.ddt_lm_head_argmax_workspace_bytes(n))
+    lo_ptr, lo_ld = (None, 0) if logits_out is None else (logits_out.data_ptr(),
+                                                         logits_out.stride(0))
+    check(lib.ddt_lm_head_argmax(h.data_ptr(), h.stride(0), weight.data_ptr(), weight.stride(0),
+                                 n, H, V, out.data_ptr(), lo_ptr, lo_ld, ws.data_ptr(), ws.numel(),
+                                 status.data_ptr(), _stream(dev)), "ddt_lm_head_argmax")
+    STATS.launches += 1
+    return out
 
 
 class KvTable:

@@ -67,6 +67,12 @@ def test_host_side_validation_rejects_bad_arguments():
                                  ctypes.c_void_p(256), None) == -2
     assert lib.ddt_sample_chains(ctypes.c_void_p(256), 5, 4, 100, 100, 8, 1.0, 0, 0,
                                  ctypes.c_void_p(256), None) == -3
+    # fused lm_head -> argmax: hidden size a multiple of 64, a large enough workspace
+    assert lib.ddt_lm_head_argmax(p, 100, p, 100, 8, 100, 1000, p, None, 0, p, 4096, None,
+                                  None) == -2
+    assert lib.ddt_lm_head_argmax(p, 128, p, 128, 8, 128, 1000, p, None, 0, p, 16, None,
+                                  None) == -7
+    assert lib.ddt_lm_head_argmax_workspace_bytes(257) >= 257 * 8 + 4
     # the bounded-wait check takes limits from 100 us to 2 s and needs a status word
     p = ctypes.c_void_p(256)
     assert lib.ddt_tree_attn_wait_check(p, p, p, p, 65, 256, 32, 8, p, 3, 10, p, None) == -1
