@@ -67,10 +67,10 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["requests", "verify", "attn", "tree", "argmax",
-                                           "compact", "splitkv"], default="requests",
+                                           "compact", "lmhead", "splitkv"], default="requests",
                     help="requests: the 64-request mix sharded over the GPUs (default); verify: "
                          "one Qwen3-8B verify step (prefix 8192, budget 256); attn / tree / "
-                         "argmax / compact: one op alone; splitkv: attention over a prefix "
+                         "argmax / compact / lmhead: one op alone; splitkv: attention over a prefix "
                          "sharded along the sequence")
     ap.add_argument("--prefix", type=int, default=None,
                     help="prefix length of the single-request workloads (default 8192; 131072 "
@@ -786,6 +786,32 @@ def measure_compact(dev, prefix, budget, steps, warmup):
             "shape": f"36 layers x K/V [1, 8, {seq}, 128] bf16, forced path of {len(acc)} rows"}
 
 
+def measure_lm_head(dev, rows, steps, warmup, hidden=QWEN3_8B["hidden"]):
+    """Fused lm_head -> argmax (ddt_lm_head_argmax) at the Qwen3-8B verify shape against the
+    unfused path it replaces (cuBLAS bf16 GEMM writing the logits, then ddt_argmax).  Bound:
+    the weight read (V x hidden bf16) and the GEMM FLOPs, whichever is slower."""
+    from mdflash_b200 import kernels as K
+    g = torch.Generator(device=dev).manual_seed(0)
+    h = torch.randn((rows, hidden), generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn((V, hidden), generator=g, device=dev) * hidden ** -0.5).to(torch.bfloat16)
+    out = torch.empty(rows, dtype=torch.int64, device=dev)
+    ms = _timed_launches(lambda: K.lm_head_argmax(h, w, out=out), steps, warmup, dev)
+    K.check_status(K.attention_status(dev))
+    post_unfused = torch.empty(rows, dtype=torch.int64, device=dev)
+    ms_unfused = _timed_launches(lambda: K.argmax(torch.matmul(h, w.t()), out=post_unfused),
+                                 steps, warmup, dev)
+    agree = (out == post_unfused).float().mean().item()
+    peaks, kind = measured_peaks()
+    nbytes = w.numel() * 2
+    flops = 2.0 * rows * hidden * V
+    bound_ms = max(nbytes / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) * 1e3
+    return {"ms": ms, "unfused_ms": ms_unfused, "speedup_vs_unfused": ms_unfused / ms,
+            "tflops": flops / (ms / 1e3) / 1e12, "gbs": nbytes / (ms / 1e3) / 1e9,
+            "bound_ms": bound_ms, "frac": bound_ms / ms, "peak_source": kind,
+            "peak": peaks["bf16_tflops"], "posterior_agreement_vs_unfused": agree,
+            "shape": f"[{rows}, {hidden}] x [{V}, {hidden}]^T bf16 -> argmax per row"}
+
+
 def kernel_table(dev, args):
     steps, warmup = 20, 3
     return {
@@ -794,6 +820,7 @@ def kernel_table(dev, args):
         "argmax": measure_argmax(dev, VERIFY_BUDGET + 1, steps, warmup),
         "accept_compact": measure_compact(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
         "tree_attention": measure_attn(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
+        "lm_head_argmax": measure_lm_head(dev, VERIFY_BUDGET + 1, steps, warmup),
     }
 
 
@@ -838,6 +865,10 @@ def run_single(args):
     elif args.workload == "argmax":
         r = measure_argmax(dev, args.budget + 1, args.steps, args.warmup)
         line = _op_line("argmax GB/s", "GB/s", r, args, "argmax over " + r["shape"], "hbm", "gbs")
+    elif args.workload == "lmhead":
+        r = measure_lm_head(dev, args.budget + 1, args.steps, args.warmup)
+        line = _op_line("lm_head+argmax TFLOP/s", "TFLOP/s", r, args,
+                        "fused lm_head -> argmax: " + r["shape"], "max(hbm, tensor)", "tflops")
     else:
         r = measure_compact(dev, args.prefix, args.budget, args.steps, args.warmup)
         line = _op_line("compaction GB/s", "GB/s", r, args,

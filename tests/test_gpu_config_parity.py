@@ -16,7 +16,8 @@ caches are bit-exact.
          golden step produced by running the reference on the CPU (tests/golden)
   cfg 3  random-init Qwen3-8B shape (36 layers, bf16), prefix 8192, budget 256, against
          transformers' sdpa path (the reference's verify forward, ddtree.py:440-486) on the
-         same GPU and the same weights
+         same GPU and the same weights, with transformers' eager attention and an fp32 run as
+         the yardsticks of what bf16 rounding does over 36 layers (see the cfg-3 tests)
   cfg 5  split-KV attention at 131072 prefix keys and 513 tree rows (Qwen3-8B attention
          shape), sharded over 2 / 4 / 8 key ranges in one process, against the single-launch
          kernel and an fp32 reference on sampled rows; compaction on the owning shard
@@ -169,7 +170,12 @@ QWEN3_8B = dict(layers=36, hidden=4096, heads=32, kv_heads=8, head_dim=128, mlp=
 @pytest.fixture(scope="module")
 def cfg3(cuda_device):
     """Qwen3-8B-shaped random-init model in bf16, prefix 8192 prefilled by the reference path
-    (sdpa), and the reference tree-verify step of a 256-node tree (sdpa + additive mask)."""
+    (sdpa), and the reference tree-verify step of a 256-node tree (sdpa + additive mask) run
+    three ways on the same weights: sdpa in bf16 (the reference path), transformers' eager
+    attention in bf16 on the same prefix K/V (the reference's other attention), and sdpa in
+    fp32 (weights upcast, fp32 prefill: the exact computation the bf16 paths round)."""
+    import copy
+
     from transformers import DynamicCache, Qwen3Config, Qwen3ForCausalLM
     s = QWEN3_8B
     cfg = Qwen3Config(vocab_size=s["vocab"], hidden_size=s["hidden"], intermediate_size=s["mlp"],
@@ -189,41 +195,82 @@ def cfg3(cuda_device):
     ids = torch.from_numpy(rng.integers(0, s["vocab"], (1, P))).to(cuda_device)
     draft = torch.from_numpy(rng.standard_normal((L, s["vocab"])).astype(np.float32) *
                              np.float32(3.0)).to(torch.bfloat16).to(cuda_device)
-    model.config._attn_implementation = "sdpa"
-    ref_cache = DynamicCache()
+    tree = oracle.build_ddtree_tree(draft.cpu(), B)
+    node_ids, depths, parents, child_maps, vis, _ = tree
+    n = 1 + node_ids.numel()
+
+    def compile_(root, dtype):
+        vib = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        vpb = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+        amb = torch.zeros((1, 1, n, P + n), dtype=dtype, device=cuda_device)
+        tvb = torch.empty((n, n), dtype=torch.bool, device=cuda_device)
+        return oracle.compile_ddtree_tree(root, P, node_ids, depths, vis, P, dtype, cuda_device,
+                                          vib, vpb, amb, tvb, 0, 0)[:3]
+
+    def verify(m, impl, cache, vi, vp, am):
+        m.config._attn_implementation = impl
+        o = m(vi, position_ids=vp, attention_mask=am, past_key_values=cache, use_cache=True,
+              output_hidden_states=True)
+        return o.logits[0].float(), o.hidden_states[1][0].float()
+
     with torch.inference_mode():
+        model.config._attn_implementation = "sdpa"
+        ref_cache = DynamicCache()
         out = model(ids, position_ids=torch.arange(P, device=cuda_device)[None],
                     past_key_values=ref_cache, use_cache=True, logits_to_keep=1)
         root = out.logits[0, -1].argmax()
         del out
-        tree = oracle.build_ddtree_tree(draft.cpu(), B)
-        node_ids, depths, parents, child_maps, vis, _ = tree
-        n = 1 + node_ids.numel()
-        vib = torch.empty((1, n), dtype=torch.long, device=cuda_device)
-        vpb = torch.empty((1, n), dtype=torch.long, device=cuda_device)
-        amb = torch.zeros((1, 1, n, P + n), dtype=torch.bfloat16, device=cuda_device)
-        tvb = torch.empty((n, n), dtype=torch.bool, device=cuda_device)
-        vi, vp, am, _, _ = oracle.compile_ddtree_tree(root, P, node_ids, depths, vis, P,
-                                                      torch.bfloat16, cuda_device, vib, vpb, amb,
-                                                      tvb, 0, 0)
+        vi, vp, am = compile_(root, torch.bfloat16)
         # the prefix K / V before the verify step appends the tree rows
         prefix_kv = [(l.keys[..., :P, :].clone(), l.values[..., :P, :].clone())
                      for l in ref_cache.layers]
-        ref_logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=ref_cache,
-                           use_cache=True).logits[0]
-    top2 = torch.topk(ref_logits.float(), 2, dim=-1).values
+        r16, r16_h1 = verify(model, "sdpa", ref_cache, vi, vp, am)
+        eager_cache = DynamicCache()
+        for li, (k, v) in enumerate(prefix_kv):
+            eager_cache.update(k.clone(), v.clone(), li)
+        e16, e16_h1 = verify(model, "eager", eager_cache, vi, vp, am)
+        del eager_cache
+        m32 = copy.deepcopy(model).float()
+        m32.config._attn_implementation = "sdpa"
+        c32 = DynamicCache()
+        m32(ids, position_ids=torch.arange(P, device=cuda_device)[None], past_key_values=c32,
+            use_cache=True, logits_to_keep=1)
+        vi32, vp32, am32 = compile_(root, torch.float32)
+        r32, r32_h1 = verify(m32, "sdpa", c32, vi32, vp32, am32)
+        del m32, c32
+    model.config._attn_implementation = "sdpa"
+    torch.cuda.empty_cache()
+    top2 = torch.topk(r16, 2, dim=-1).values
+    spread = (e16 - r16).abs().max(-1).values  # the reference's own two attentions, per row
+    ref_bounds = dict(
+        norm32=max(norm_rel_err(r16, r32), norm_rel_err(e16, r32)),
+        elem32=max(elem_rel_err(r16, r32), elem_rel_err(e16, r32)),
+        agree32=min((r16.argmax(-1) == r32.argmax(-1)).float().mean().item(),
+                    (e16.argmax(-1) == r32.argmax(-1)).float().mean().item()),
+        norm16=norm_rel_err(e16, r16), elem16=elem_rel_err(e16, r16))
+    print(f"[cfg3 reference] sdpa16 vs fp32: norm {norm_rel_err(r16, r32):.3e} elem "
+          f"{elem_rel_err(r16, r32):.3e}; eager16 vs fp32: norm {norm_rel_err(e16, r32):.3e} "
+          f"elem {elem_rel_err(e16, r32):.3e}; eager16 vs sdpa16: norm {ref_bounds['norm16']:.3e} "
+          f"elem {ref_bounds['elem16']:.3e}; argmax vs fp32 >= {ref_bounds['agree32']:.4f}; "
+          f"layer-1 hidden eager vs sdpa norm {norm_rel_err(e16_h1, r16_h1):.3e}")
     return dict(model=model, P=P, B=B, L=L, root=root, draft=draft, tree=tree, n=n,
-                prefix_kv=prefix_kv, ref_logits=ref_logits, ref_post=ref_logits.argmax(-1),
-                ref_gap=(top2[:, 0] - top2[:, 1]).cpu().numpy(), ref_cache=ref_cache, vi=vi,
-                vp=vp)
+                prefix_kv=prefix_kv, ref_logits=r16, ref_post=r16.argmax(-1), r32=r32,
+                r16_h1=r16_h1, e16_h1=e16_h1, bounds=ref_bounds,
+                ref_gap=(top2[:, 0] - top2[:, 1]).cpu().numpy(),
+                spread=spread.cpu().numpy(), ref_cache=ref_cache, vi=vi, vp=vp)
 
 
-def _cfg3_tie_gap(ref_logits):
-    # both paths round the logits to bf16: 2 bf16 steps (2^-7 relative each) of the largest
-    # logit, plus the accumulated difference of the two forwards, as much again
-    return 4 * 2.0 ** -7 * ref_logits.float().abs().max().item()
-
-
+# Over 36 random-init layers bf16 rounding differences compound: transformers' own eager and
+# sdpa attentions give logits ~6% apart (normalised) and ~30% element-wise on this model, and
+# each is ~5-6% from the fp32 computation (measured on B200).  No bf16 implementation can
+# meet 2e-2 against another one at the logits here, so the config-level criteria are:
+#   * one decoder layer (no compounding): hidden states within 2e-2 of the sdpa path;
+#   * the logits are no farther from the fp32 computation than the reference's own bf16
+#     paths are (x 1.25), and no farther from the sdpa path than 2e-2 or than the eager path
+#     is from it (x 1.25);
+#   * argmax agreement with the fp32 computation no lower than the reference's bf16 paths'
+#     (- 2%); against the sdpa path >= 99.9% of the rows whose top-1 / top-2 gap exceeds twice
+#     the row's eager-vs-sdpa spread (rows within it are near-ties, logged).
 @pytest.mark.parametrize("fused", [True, False], ids=["fused_runner", "transformers_plugin"])
 def test_cfg3_verify_step_matches_sdpa(cfg3, cuda_device, fused):
     c = cfg3
@@ -241,6 +288,7 @@ def test_cfg3_verify_step_matches_sdpa(cfg3, cuda_device, fused):
     with torch.inference_mode():
         res = ver.step(c["draft"], c["root"].view(1), P)
         torch.cuda.synchronize()
+    model.config._attn_implementation = "sdpa"
     n = c["n"]
     o_ids, o_depths, o_par, o_cm, _, _ = c["tree"]
     assert res.n_nodes == n
@@ -249,16 +297,22 @@ def test_cfg3_verify_step_matches_sdpa(cfg3, cuda_device, fused):
     assert torch.equal(ver.tree.verify_ids[:n].view(1, n), c["vi"])
     assert torch.equal(ver.tree.verify_pos[:n].view(1, n), c["vp"])
     label = "cfg3 " + ("fused" if fused else "plugin")
-    e1, e2 = elem_rel_err(res.logits, c["ref_logits"]), norm_rel_err(res.logits, c["ref_logits"])
-    print(f"[{label}] logits: elem rel err {e1:.3e}, norm rel err {e2:.3e}")
-    assert e1 <= RTOL and e2 <= RTOL
-    # the tree rows' K / V written by the step, every layer
-    for li in (0, 17, 35):
-        ours = cache.layers[li].k_buf[0, :, P:P + n, :]
-        ref = c["ref_cache"].layers[li].keys[0, :, P:P + n, :]
-        assert elem_rel_err(ours, ref) <= RTOL, li
-    frac = posterior_agreement(label, res.posterior.cpu().numpy(), c["ref_post"].cpu().numpy(),
-                               c["ref_gap"], _cfg3_tie_gap(c["ref_logits"]))
+    o16, r16, r32, bd = res.logits.float(), c["ref_logits"], c["r32"], c["bounds"]
+    e_norm, e_elem = norm_rel_err(o16, r16), elem_rel_err(o16, r16)
+    e_norm32, e_elem32 = norm_rel_err(o16, r32), elem_rel_err(o16, r32)
+    agree32 = (o16.argmax(-1) == r32.argmax(-1)).float().mean().item()
+    print(f"[{label}] vs sdpa16: norm {e_norm:.3e} elem {e_elem:.3e}; vs fp32: norm "
+          f"{e_norm32:.3e} elem {e_elem32:.3e}; argmax vs fp32 {agree32:.4f}")
+    assert e_norm32 <= 1.25 * bd["norm32"] and e_elem32 <= 1.25 * bd["elem32"]
+    assert e_norm <= max(RTOL, 1.25 * bd["norm16"]) and e_elem <= max(RTOL, 1.25 * bd["elem16"])
+    assert agree32 >= bd["agree32"] - 0.02
+    # layer 0's tree-row K (the q/k-norm, rope and cache-write kernel on identical inputs)
+    ours = cache.layers[0].k_buf[0, :, P:P + n, :]
+    ref = c["ref_cache"].layers[0].keys[0, :, P:P + n, :]
+    assert elem_rel_err(ours, ref) <= RTOL
+    post = res.posterior.cpu().numpy()
+    ref_post = c["ref_post"].cpu().numpy()
+    frac = posterior_agreement(label, post, ref_post, c["ref_gap"], 2 * c["spread"])
     assert frac >= AGREE
     k = int(res.n_accepted.item())
     acc = res.accepted[:k].tolist()
@@ -269,6 +323,36 @@ def test_cfg3_verify_step_matches_sdpa(cfg3, cuda_device, fused):
     if walk_agrees(ref_acc, res.posterior.cpu(), c["ref_post"].cpu()):
         assert acc == ref_acc
     ver.commit(P, k)
+
+
+def test_cfg3_one_layer_within_tolerance(cfg3, cuda_device):
+    """One decoder layer through the ddtree_tree plug-in (tree attention kernel) on the sdpa
+    path's prefix: its output hidden states are within 2e-2 of the sdpa path's."""
+    from transformers import DynamicCache
+    c = cfg3
+    model, P = c["model"], c["P"]
+    cache = DynamicCache()
+    for li, (k, v) in enumerate(c["prefix_kv"]):
+        cache.update(k.clone(), v.clone(), li)
+    model.config._attn_implementation = A.ATTN_IMPLEMENTATION
+    node_ids, depths, parents, child_maps, vis, _ = D.build_ddtree_tree(c["draft"], c["B"])
+    n = len(parents)
+    vib = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+    vpb = torch.empty((1, n), dtype=torch.long, device=cuda_device)
+    amb = torch.zeros((1, 1, n, P + n), dtype=torch.bfloat16, device=cuda_device)
+    tvb = torch.empty((n, n), dtype=torch.bool, device=cuda_device)
+    with torch.inference_mode():
+        vi, vp, am, _, _ = D.compile_ddtree_tree(c["root"], P, node_ids, depths, vis, P,
+                                                 torch.bfloat16, cuda_device, vib, vpb, amb, tvb,
+                                                 0, 0)
+        h1 = model(vi, position_ids=vp, attention_mask=am, past_key_values=cache, use_cache=True,
+                   output_hidden_states=True).hidden_states[1][0].float()
+    model.config._attn_implementation = "sdpa"
+    A.clear_tree_context()
+    e = norm_rel_err(h1, c["r16_h1"])
+    print(f"[cfg3 layer 1] ours vs sdpa norm {e:.3e}, eager vs sdpa "
+          f"{norm_rel_err(c['e16_h1'], c['r16_h1']):.3e}")
+    assert e <= RTOL
 
 
 # ------------------------------------------------------------------------------ cfg 5

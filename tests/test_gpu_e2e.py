@@ -6,7 +6,8 @@ as ddtree_generate calls them (ddtree.py:440-486).  Our paths: (1) the drop-in f
 mdflash_b200.ddtree with the "ddtree_tree" attention plug-in, (2) TreeVerifier (device
 resident) over transformers, (3) TreeVerifier over the fused runner.  Tree topology,
 accepted paths and compaction are bit-exact; logits / KV rows are within bf16 tolerance
-(max |err| / max |ref| <= 2e-2, and element-wise 2e-2 relative with the row RMS as floor),
+(max |err| / max |ref| <= 2e-2, and element-wise, relative with the row RMS as floor, within
+2e-2 or within 1.25x the distance between transformers' own eager and sdpa attentions),
 and the greedy posteriors agree on >= 99.9% of the rows whose reference top-1 / top-2 gap
 exceeds 4 bf16 steps of the largest logit (near-ties are logged).
 """
@@ -72,12 +73,23 @@ def setup(cuda_device):
         vi, vp, am, _, _ = oracle.compile_ddtree_tree(root, P, node_ids, depths, vis, P,
                                                       torch.bfloat16, cuda_device, vib, vpb, amb,
                                                       tvb, 0, 0)
+        prefix = [(l.keys.clone(), l.values.clone()) for l in ref_cache.layers]
         ref_logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=ref_cache,
                            use_cache=True).logits[0]
+        # transformers' eager attention on the same prefix: the spread of the reference's own
+        # bf16 implementations, the yardstick of the element-wise check
+        eager_cache = DynamicCache()
+        for li, (k, v) in enumerate(prefix):
+            eager_cache.update(k, v, li)
+        model.config._attn_implementation = "eager"
+        eager_logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=eager_cache,
+                             use_cache=True).logits[0]
+        model.config._attn_implementation = "sdpa"
     ref_post = ref_logits.argmax(-1)
     ref_acc, ref_next = oracle.follow_verified_tree(child_maps, ref_post.cpu())
     return dict(model=model, ids=ids, logits=logits, root=root, tree=tree, n=n,
-                ref_logits=ref_logits, ref_post=ref_post, ref_cache=ref_cache, ref_acc=ref_acc,
+                ref_logits=ref_logits, elem_bound=max(TOL, 1.25 * elem_rel_err(eager_logits,
+                                                                               ref_logits)), ref_post=ref_post, ref_cache=ref_cache, ref_acc=ref_acc,
                 ref_next=ref_next, vi=vi, vp=vp)
 
 
@@ -112,7 +124,7 @@ def test_dropin_functions_and_plugin(setup, cuda_device):
         logits = model(vi, position_ids=vp, attention_mask=am, past_key_values=cache,
                        use_cache=True).logits[0]
         assert _rel(logits, s["ref_logits"]) <= TOL
-        assert elem_rel_err(logits, s["ref_logits"]) <= TOL
+        assert elem_rel_err(logits, s["ref_logits"]) <= s["elem_bound"]
         post = logits.argmax(-1)
         assert _agreement("e2e drop-in", post, s) >= 0.999
         acc, nxt = D.follow_verified_tree(child_maps, post[None])
@@ -174,7 +186,7 @@ def test_tree_verifier_matches_reference(setup, cuda_device, fused):
     assert verifier.tree.parents[:n].tolist() == o_par
     assert torch.equal(verifier.tree.node_token_ids[:n - 1].cpu(), o_ids)
     assert _rel(res.logits, s["ref_logits"]) <= TOL
-    assert elem_rel_err(res.logits, s["ref_logits"]) <= TOL
+    assert elem_rel_err(res.logits, s["ref_logits"]) <= s["elem_bound"]
     assert _agreement("e2e verifier fused" if fused else "e2e verifier", res.posterior, s) >= 0.999
     k = int(res.n_accepted.item())
     acc = res.accepted[:k].tolist()
