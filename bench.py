@@ -572,10 +572,12 @@ def verify_step(args, model, runner, dev, steps: int, warmup: int, prefix: int =
         cap.replay()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     ev0.record()
     for _ in range(steps):
         res = cap.replay()
     ev1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     verifier.check()
     ms = ev0.elapsed_time(ev1) / steps
