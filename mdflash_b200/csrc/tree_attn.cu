@@ -10,24 +10,19 @@
 // Work unit (one CTA): one KV head, two tiles of 128 query rows (256 rows), one key
 // split.  Query rows are (node, q head of the GQA group) pairs, node-major, so the whole
 // group shares every K/V tile.  Warp roles (12 warps, 3 warpgroups):
-//   warp 0      TMA producer: both Q tiles once, then K and V stages (128 keys x 128 dims,
+//   warp 0      TMA producer: both Q tiles once, then K and V tiles (128 keys x 128 dims,
 //               128-byte swizzle) into a 2-stage ring; never multicast.
-//   warp 1      allocates all 512 TMEM columns; with warp 3, issues tcgen05.mma (warp 1 for
-//               query tile 0, warp 3 for tile 1): S_q = Q_q K^T (SMEM x SMEM) and
-//               O_q += P_q V with P_q read from TMEM.
-//   warp 2      idle (it completes warpgroup 0, which gives its registers away)
+//   warp 1      allocates all 512 TMEM columns; one thread issues tcgen05.mma:
+//               S_q = Q_q K^T (SMEM x SMEM) and O_q += P_q V with P_q read from TMEM.
+//   warps 2-3   idle (they complete warpgroup 0, which gives its registers away)
 //   warps 4-7   softmax of query tile 0, warps 8-11 of query tile 1: thread t of a warp
-//               owns row 32 * (warp % 4) + t (the TMEM lane quarter of the warp).
-// Every stage is two 64-key sub-tiles.  Each query tile has two S buffers of 64 columns, one
-// per sub-tile of a stage: the softmax loads a sub-tile's S row, computes
-// P = exp2(S * scale - m) and writes P back as packed bf16 into the buffer's first 32
-// columns, where the P V MMA reads it; right behind that P V, the issuer computes the next
-// stage's S of the same sub-tile into the same buffer.  So the S of the next sub-tile is
-// ready before the softmax of the current one ends, and the softmax and the tensor pipe
-// overlap instead of taking turns.  O is rescaled in TMEM only when the row max grew by
-// more than 2^8.
-// TMEM columns: S0/P0 [0,128) O0 [128,256) S1/P1 [256,384) O1 [384,512); S buffer h of a
-// tile is the 64 columns [64 h, 64 h + 64) of its S region.
+//               owns row 32 * (warp % 4) + t (the TMEM lane quarter of the warp).  Pass 1 loads the S row and takes the masked max; pass 2
+//               reloads it, computes P = exp2(S * scale - m) and writes P back as packed
+//               bf16 into the first 64 columns of the tile's S region, where the P V MMA
+//               reads it.  O is rescaled in TMEM only when the row max grew by > 2^8.
+// The two softmax warpgroups work on different query tiles, so while one computes
+// exponentials the tensor pipe runs the other's MMAs.
+// TMEM columns: S0/P0 [0,128) O0 [128,256) S1/P1 [256,384) O1 [384,512).
 // Splits of the key range write fp32 partials (O, m, l) that ddt_attn_merge combines;
 // the same partial format is exchanged between GPUs for sequence-sharded prefixes.
 // Every mbarrier wait is bounded; a timeout sets *status and unwinds the CTA.  Every
@@ -43,7 +38,6 @@ namespace attn {
 
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
-constexpr int kSubN = 64;  // keys per S buffer / softmax pass (two per 128-key stage)
 constexpr int kHeadDim = 128;
 constexpr int kStages = 2;
 constexpr int kThreads = 384;
@@ -67,7 +61,7 @@ constexpr uint32_t kSmemK = kSmemQ + 2 * kTileBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
 constexpr uint32_t kSmemBytes = kSmemV + kStages * kTileBytes;  // 192 KB
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;               // + alignment slack
-constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kBlockM, kSubN, false, false);
+constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kBlockM, kBlockN, false, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kBlockM, kHeadDim, false, true);
 constexpr int kStatusTimeout = 1;
 // Pairs (of the 16 in each 32-column chunk of an S row) whose exponentials are computed by
@@ -156,17 +150,15 @@ __host__ __device__ inline UnitGeo unit_geo(const Params& p, int u) {
 }
 
 struct Bars {
-  // K and V stages are released separately: K_j once both issuers' S MMAs of stage j
-  // completed, V_j once both issuers' P V MMAs of stage j completed.
-  // q_empty: both issuers' last S MMAs of an item are done, Q may be replaced.
-  // Per query tile q and S buffer h (the 64-key half of a stage it holds): s_full[q][h]
-  // (S ready in TMEM), p_full[q][h] (P written back by the 4 softmax warps), o_ready[q][h]
-  // (the P V MMAs of sub-tile h of a stage, and every MMA before them, are complete).  Each
-  // is used once per stage, so a waiter on stage jg's phase (parity jg & 1) is never two
-  // phases behind: the MMA order (P V(jg - 1, h) before S(jg, h) before P V(jg, h)) keeps
-  // every earlier phase complete by the time the wait is issued.
+  // K and V stages are released separately: K_j once both S_q(j) MMAs completed, V_j once
+  // both P V MMAs of tile j completed, so the next K load starts a full tile earlier.
+  // q_empty: both S MMAs of an item's last tile are done, Q may be replaced.
   uint64_t q_full, q_empty, k_full[kStages], v_full[kStages], k_empty[kStages],
-      v_empty[kStages], s_full[2][2], p_full[2][2], o_ready[2][2], mma_done[2];
+      v_empty[kStages], s_full[2], p_half[2], p_full[2], o_ready[2], mma_done[2];
+  // MMA blocks issued per query tile (S_q(0), then P V(j) + S(j + 1) per tile): the two
+  // issuers take turns, tile 0 then tile 1, so the two softmax warpgroups stay half a
+  // period apart instead of competing for the same SM sub-partitions
+  uint32_t issued[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -258,11 +250,11 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       tc::mbar_init(&bars.v_empty[s], 2);
     }
     for (int q = 0; q < 2; ++q) {
-      for (int h = 0; h < 2; ++h) {
-        tc::mbar_init(&bars.s_full[q][h], 1);
-        tc::mbar_init(&bars.p_full[q][h], 4);  // one arrive per softmax warp
-        tc::mbar_init(&bars.o_ready[q][h], 1);
-      }
+      tc::mbar_init(&bars.s_full[q], 1);
+      tc::mbar_init(&bars.p_half[q], 4);  // one arrive per softmax warp
+      tc::mbar_init(&bars.p_full[q], 4);
+      bars.issued[q] = 0;
+      tc::mbar_init(&bars.o_ready[q], 1);
       tc::mbar_init(&bars.mma_done[q], 1);
     }
     bars.abort = 0;
@@ -351,17 +343,15 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
     } else if (warp == 1 || warp == 3) {
       // ---------------------------- MMA issuers, one per query tile ------------------
-      // Query tile 0's MMAs come from warp 1, tile 1's from warp 3.  Every 128-key stage is
-      // two 64-key sub-tiles, h = 0, 1; the S of sub-tile h goes to S buffer h of the tile
-      // (TMEM columns col_s(q) + 64 h), where the softmax writes its P back (first 32 columns,
-      // packed bf16).  The S of the NEXT stage's sub-tile h is issued right behind the P V of
-      // this stage's sub-tile h, so it is computed while the softmax works on sub-tile h ^ 1:
-      // the softmax of consecutive sub-tiles does not wait for the tensor pipe, which runs
-      // the two tiles' blocks back to back.
-      // An mbarrier wait (or any acquire) holds the waiting thread until its own MMAs in
-      // flight have drained, so the K / V waits of a stage come before its P waits, where
-      // this issuer's earlier MMAs are complete anyway.  The whole warp runs the loop
-      // (uniform control flow, warp-collective waits) and one elected lane issues.
+      // Query tile 0's MMAs come from warp 1, tile 1's from warp 3.  An mbarrier wait (or
+      // any acquire) holds the waiting thread until its own MMAs in flight have drained
+      // (measured ~180 cycles of idle tensor pipe per wait with a single issuer).  With one
+      // issuer per tile every wait falls where that tile's previous MMAs are complete anyway
+      // (P_q(j) ready implies S_q(j) done), while the other tile's MMAs keep the pipe busy.
+      // The whole warp runs the loop (uniform control flow, warp-collective waits) and one
+      // elected lane issues: a lone lane in a divergent branch issued one MMA per ~130
+      // cycles next to FMA-bound softmax warps on its sub-partition (measured), against
+      // the pipe's 64.
       const int q = warp == 1 ? 0 : 1;
       if (total > 0) {
         // descriptor low words of the Q, K and V tiles; every MMA adds a constant to them
@@ -370,33 +360,56 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const uint32_t k_lo = tc::desc_sw128_lo(tc::smem_u32(sK), 16);
         const uint32_t v_lo = tc::desc_sw128_lo(tc::smem_u32(sV), kHalfBytes);
         const uint32_t d_s = tmem + col_s(q), d_o = tmem + col_o(q);
-        // S_q(stage jg, sub-tile h) = Q_q K^T over keys [64 h, 64 h + 64) of the stage
-        // (K rows 64 h.., 64 rows of 128 bytes per 64-dim half)
-        auto issue_s = [&](int jg, int h) {
-          const uint32_t b = k_lo + (jg % kStages) * (kTileBytes >> 4) + h * (kSubN * 128 >> 4);
-          const uint32_t d = d_s + h * kSubN;
-          tc::mma_bf16_ss_w<0>(d, a_q, b, kDescHi, kIdescS);
+        volatile uint32_t* my_turns = &bars.issued[q];
+        const volatile uint32_t* other_turns = &bars.issued[q ^ 1];
+        // S_q = Q_q K^T of CTA tile jg into the S region of query tile q; the block's turn
+        // count `turn` is published right after its last MMA.  (Publishing it after half of
+        // the S MMAs, so the other issuer's block would queue behind this one, measured
+        // 5% slower: the two softmax warpgroups drift into each other.)
+        auto issue_s = [&](int jg, uint32_t turn) {
+          const uint32_t b = k_lo + (jg % kStages) * (kTileBytes >> 4);
+          tc::mma_bf16_ss_w<0>(d_s, a_q, b, kDescHi, kIdescS);
 #pragma unroll
           for (int kk = 1; kk < kHeadDim / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
-            tc::mma_bf16_ss_w<1>(d, a_q + off, b + off, kDescHi, kIdescS);
+            tc::mma_bf16_ss_w<1>(d_s, a_q + off, b + off, kDescHi, kIdescS);
+            if (kk == kHeadDim / 16 - 1) *my_turns = turn;
           }
-          tc::mma_commit(&bars.s_full[q][h]);
+          tc::mma_commit(&bars.s_full[q]);
         };
-        // O_q += P_q V over sub-tile h of stage jg; P from TMEM (8 columns per 16 keys)
-        auto issue_pv = [&](int jg, int h, bool first) {
+        // O_q += P_q V of tile jg (item tile j; j == 0 starts the item's O), P_q in TMEM
+        // (first 64 columns of the S region, 8 per K step), in two halves of 64 keys: the
+        // first runs while the softmax computes the second
+        auto issue_pv = [&](int jg, int j, int half) {
           const uint32_t b = v_lo + (jg % kStages) * (kTileBytes >> 4);
 #pragma unroll
-          for (int k4 = 0; k4 < kSubN / 16; ++k4) {
-            const int kk = h * (kSubN / 16) + k4;
-            tc::mma_bf16_ts_w(d_o, d_s + h * kSubN + k4 * 8, b + ((kk * 2048) >> 4), kDescHi,
-                              kIdescPV, (first && k4 == 0) ? 0u : 1u);
+          for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
+            const int kk = half * (kBlockN / 32) + k4;
+            tc::mma_bf16_ts_w(d_o, d_s + kk * 8, b + ((kk * 2048) >> 4), kDescHi, kIdescPV,
+                              (j > 0 || kk > 0) ? 1u : 0u);
           }
-          tc::mma_commit(&bars.o_ready[q][h]);
+          if (half) tc::mma_commit(&bars.o_ready[q]);
+        };
+        // Turn-taking on plain (volatile) loads and stores: an acquire or release here
+        // would wait for this thread's MMAs in flight, and the turns order only the issue
+        // of the two tiles' MMAs, no data.  Blocks per item: S of its first tile, then one
+        // per tile (P V(j) + S(j + 1)); `base` counts the blocks of earlier items.
+        auto wait_turn = [&](uint32_t target) {
+          uint64_t t0 = 0;
+          for (uint32_t it = 0;; ++it) {
+            if (__all_sync(DDT_FULL_MASK, *other_turns >= target)) return true;
+            if ((it & 255u) == 255u) {
+              const uint64_t now = global_timer_ns();
+              if (t0 == 0) t0 = now;
+              if (__any_sync(DDT_FULL_MASK, *abort_flag != 0 || now - t0 > p.timeout_ns))
+                return false;
+            }
+          }
         };
         // stage releases (k_empty / v_empty count one commit per issuer) are committed
         // only where the producer will wait for them
         bool ok = true;
+        uint32_t base = 0;
         int J = 0;
         for (int i = 0; ok && i < n_items; ++i) {
           int u, t0, nt, sl;
@@ -405,49 +418,48 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           if (!(ok = tc::mbar_wait_warp(&bars.k_full[J % kStages], (J / kStages) & 1, abort_flag,
                                         p.timeout_ns)))
             break;
+          if (!(ok = wait_turn(q == 0 ? base : base + 1))) break;
           tc::tc_fence_after();
           if (tc::elect_one()) {
-            issue_s(J, 0);
-            issue_s(J, 1);
+            issue_s(J, base + 1);
             if (J + kStages < total) tc::mma_commit(&bars.k_empty[J % kStages]);
-            // a one-stage item has issued all of its S MMAs
-            if (nt == 1 && i + 1 < n_items) tc::mma_commit(&bars.q_empty);
           }
           __syncwarp();
           for (int j = 0; j < nt; ++j) {
             const int jg = J + j;
             const int st = jg % kStages;
+            const int sn = (jg + 1) % kStages;
             const bool more = j + 1 < nt;
-            // V of this stage and K of the next one landed long before this stage's P
+            // K / V of the tile landed long before P_q(j): waited first, while the softmax runs
             if (!(ok = tc::mbar_wait_warp(&bars.v_full[st], (jg / kStages) & 1, abort_flag,
                                           p.timeout_ns)))
               break;
-            if (more && !(ok = tc::mbar_wait_warp(&bars.k_full[(jg + 1) % kStages],
-                                                  ((jg + 1) / kStages) & 1, abort_flag,
-                                                  p.timeout_ns)))
+            if (more && !(ok = tc::mbar_wait_warp(&bars.k_full[sn], ((jg + 1) / kStages) & 1,
+                                                  abort_flag, p.timeout_ns)))
               break;
-            for (int h = 0; h < 2; ++h) {
-              if (!(ok = tc::mbar_wait_warp(&bars.p_full[q][h], jg & 1, abort_flag, p.timeout_ns)))
-                break;
-              tc::tc_fence_after();
-              if (tc::elect_one()) {
-                issue_pv(jg, h, j == 0 && h == 0);
-                if (h == 1 && jg + kStages < total) tc::mma_commit(&bars.v_empty[st]);
-                if (more) {
-                  // S buffer h is free once the P V just issued has read P (in-order pipe)
-                  issue_s(jg + 1, h);
-                  if (h == 1) {
-                    if (jg + 1 + kStages < total)
-                      tc::mma_commit(&bars.k_empty[(jg + 1) % kStages]);
-                    // the item's last S MMAs are issued: Q may be replaced once they are done
-                    if (j + 2 == nt && i + 1 < n_items) tc::mma_commit(&bars.q_empty);
-                  }
-                }
+            if (!(ok = tc::mbar_wait_warp(&bars.p_half[q], jg & 1, abort_flag, p.timeout_ns))) break;
+            if (!(ok = wait_turn(q == 0 ? base + j + 1 : base + j + 2))) break;
+            tc::tc_fence_after();
+            if (tc::elect_one()) issue_pv(jg, j, 0);
+            __syncwarp();
+            if (!(ok = tc::mbar_wait_warp(&bars.p_full[q], jg & 1, abort_flag, p.timeout_ns))) break;
+            tc::tc_fence_after();
+            if (tc::elect_one()) {
+              issue_pv(jg, j, 1);
+              if (jg + kStages < total) tc::mma_commit(&bars.v_empty[st]);
+              if (more) {
+                issue_s(jg + 1, base + j + 2);  // reuses S_q / P_q: runs after the P V above
+                if (jg + 1 + kStages < total) tc::mma_commit(&bars.k_empty[sn]);
+              } else {
+                *my_turns = base + j + 2;
               }
-              __syncwarp();
             }
-            if (!ok) break;
+            __syncwarp();
           }
+          // the item's S MMAs are all issued: Q may be replaced once they are done
+          if (ok && i + 1 < n_items && tc::elect_one()) tc::mma_commit(&bars.q_empty);
+          __syncwarp();
+          base += nt + 1;
           J += nt;
         }
         if (!ok) {
@@ -482,7 +494,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const bool valid = R < rows;
       const int vnode = valid ? node : p.n_nodes - 1;
       const int g_end = g.g_end;
-      // the whole key range of a sub-tile is visible to this row (no mask needed) when it
+      // the whole key range of the tile is visible to this row (no mask needed) when it
       // ends before the tree window / the launch's last key
       const int full_end = p.mask_mode == DDT_MASK_NONE ? g_end
                            : p.mask_mode == DDT_MASK_CAUSAL
@@ -491,92 +503,90 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; ok && j < nt; ++j) {
         const int jg = J + j;
-        for (int h = 0; h < 2; ++h) {
-          if (!tc::mbar_wait_warp(&bars.s_full[q][h], jg & 1, abort_flag, p.timeout_ns)) {
+        if (!tc::mbar_wait_warp(&bars.s_full[q], jg & 1, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const int gk = p.key_lo + (t0 + j) * kBlockN;  // global key of column 0
+        const bool masked = __any_sync(DDT_FULL_MASK, gk + kBlockN > full_end);
+        uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) vis[c] = visible32(p, vnode, gk + c * 32, g_end);
+        }
+        // the whole S row (128 fp32) comes out of TMEM in one round trip
+        uint32_t sv[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + c * 32, sv[c]);
+        tc::tmem_wait_ld();
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (!((vis[c] >> e) & 1u)) sv[c][e] = __float_as_uint(-INFINITY);
+        }
+        // masked row max of the raw scores: three-input maxima in 8 independent chains
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            mx8[(e >> 1) & 7] = tc::fmax3(mx8[(e >> 1) & 7], __uint_as_float(sv[c][e]),
+                                          __uint_as_float(sv[c][e + 1]));
+        const float mx = tc::fmax3(tc::fmax3(mx8[0], mx8[1], mx8[2]),
+                                   tc::fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        bool rescale = false;
+        float alpha = 1.f;
+        if (mx > -INFINITY) {
+          const float ms = mx * sl2;
+          if (m_used == -INFINITY) {
+            m_used = ms;  // nothing accumulated yet: O and l are zero
+          } else if (ms > m_used + kRescaleLog2) {
+            alpha = tc::ex2_approx(m_used - ms);
+            m_used = ms;
+            rescale = true;
+          }
+        }
+        if (__any_sync(DDT_FULL_MASK, rescale)) {
+          // O_q is stable once the previous P V MMA of this item completed
+          if (j > 0 && !tc::mbar_wait_warp(&bars.o_ready[q], (jg - 1) & 1, abort_flag, p.timeout_ns)) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const int gk = p.key_lo + (t0 + j) * kBlockN + h * kSubN;  // global key of column 0
-          const bool masked = __any_sync(DDT_FULL_MASK, gk + kSubN > full_end);
-          uint32_t vis[2] = {~0u, ~0u};
-          if (masked) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c) vis[c] = visible32(p, vnode, gk + c * 32, g_end);
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tc::tmem_ld32(tO + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tc::tmem_st32(tO + c * 32, o);
           }
-          const uint32_t tSh = tS + h * kSubN;
-          // the sub-tile's S row (64 fp32) in one TMEM round trip
-          uint32_t sv[2][32];
+          l *= alpha;
+        }
+        const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
+        // P = exp2(S * scale - m), packed bf16 into columns [0, 64) of S_q (masked keys hold
+        // -inf and give 0, or 2^-126 on the polynomial lanes).  Scale and row sum run on
+        // packed fp32 pairs; the pairs selected by kPolyPairs take the polynomial
+        // exponential, the rest the MUFU one.
+        const uint64_t sl2x2 = tc::f2_pack(sl2, sl2), nmx2 = tc::f2_pack(nm, nm);
+        uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
+        // keys [0, 64) first: their P columns are stored and signalled (p_half) while the
+        // second half is computed, so the first four P V MMAs overlap it
+        uint32_t pk[2][32];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) tc::tmem_ld32(tSh + c * 32, sv[c]);
-          tc::tmem_wait_ld();
-          if (masked) {
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (!((vis[c] >> e) & 1u)) sv[c][e] = __float_as_uint(-INFINITY);
-          }
-          // masked row max of the raw scores: three-input maxima in 8 independent chains
-          float mx8[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; e += 2)
-              mx8[(e >> 1) & 7] = tc::fmax3(mx8[(e >> 1) & 7], __uint_as_float(sv[c][e]),
-                                            __uint_as_float(sv[c][e + 1]));
-          const float mx = tc::fmax3(tc::fmax3(mx8[0], mx8[1], mx8[2]),
-                                     tc::fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-          bool rescale = false;
-          float alpha = 1.f;
-          if (mx > -INFINITY) {
-            const float ms = mx * sl2;
-            if (m_used == -INFINITY) {
-              m_used = ms;  // nothing accumulated yet: O and l are zero
-            } else if (ms > m_used + kRescaleLog2) {
-              alpha = tc::ex2_approx(m_used - ms);
-              m_used = ms;
-              rescale = true;
-            }
-          }
-          if (__any_sync(DDT_FULL_MASK, rescale)) {
-            // O_q is stable once every P V MMA of the item before this sub-tile completed:
-            // the previous sub-tile's o_ready phase ((jg, 0) before (jg, 1), (jg - 1, 1)
-            // before (jg, 0))
-            if ((j > 0 || h > 0) &&
-                !tc::mbar_wait_warp(&bars.o_ready[q][h ^ 1], (h ? jg : jg - 1) & 1, abort_flag,
-                                    p.timeout_ns)) {
-              ok = false;
-              break;
-            }
-            tc::tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint32_t o[32];
-              tc::tmem_ld32(tO + c * 32, o);
-              tc::tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-              tc::tmem_st32(tO + c * 32, o);
-            }
-            l *= alpha;
-          }
-          const float nm = (m_used == -INFINITY) ? 0.f : -m_used;
-          // P = exp2(S * scale - m), packed bf16 into the first 32 columns of the S buffer
-          // (masked keys hold -inf and give 0, or 2^-126 on the polynomial lanes).  Scale and
-          // row sum run on packed fp32 pairs; the pairs selected by kPolyPairs take the
-          // polynomial exponential, the rest the MUFU one.
-          const uint64_t sl2x2 = tc::f2_pack(sl2, sl2), nmx2 = tc::f2_pack(nm, nm);
-          uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
-          uint32_t pk[32];
+        for (int hf = 0; hf < 2; ++hf) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const uint64_t x = tc::f2_fma(tc::f2_pack(__uint_as_float(sv[c][e]),
-                                                        __uint_as_float(sv[c][e + 1])),
+              const uint64_t x = tc::f2_fma(tc::f2_pack(__uint_as_float(sv[hf * 2 + c][e]),
+                                                        __uint_as_float(sv[hf * 2 + c][e + 1])),
                                             sl2x2, nmx2);
               float a, b;
               if ((kPolyPairs >> (e >> 1)) & 1u) {
@@ -588,23 +598,27 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                 b = tc::ex2_approx(x1);
               }
               ls2[(e >> 1) & 3] = tc::f2_add(ls2[(e >> 1) & 3], tc::f2_pack(a, b));
-              pk[c * 16 + e / 2] = tc::pack_bf16x2(a, b);
+              pk[hf][c * 16 + e / 2] = tc::pack_bf16x2(a, b);
             }
           }
-          tc::tmem_st32(tSh, pk);
-          float l0, l1, l2, l3;
-          tc::f2_unpack(tc::f2_add(ls2[0], ls2[1]), l0, l1);
-          tc::f2_unpack(tc::f2_add(ls2[2], ls2[3]), l2, l3);
-          l += (l0 + l1) + (l2 + l3);
-          tc::tmem_wait_st();
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&bars.p_full[q][h]);
+          if (hf == 0) tc::tmem_st32(tS, pk[0]);
         }
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars.p_half[q]);
+        tc::tmem_st32(tS + 32, pk[1]);
+        float l0, l1, l2, l3;
+        tc::f2_unpack(tc::f2_add(ls2[0], ls2[1]), l0, l1);
+        tc::f2_unpack(tc::f2_add(ls2[2], ls2[3]), l2, l3);
+        l += (l0 + l1) + (l2 + l3);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars.p_full[q]);
       }
-      // the item's last P V: sub-tile 1 of stage J + nt - 1
       if (ok && nt > 0 &&
-          !tc::mbar_wait_warp(&bars.o_ready[q][1], (J + nt - 1) & 1, abort_flag, p.timeout_ns))
+          !tc::mbar_wait_warp(&bars.o_ready[q], (J + nt - 1) & 1, abort_flag, p.timeout_ns))
         ok = false;
       const bool have = ok && nt > 0;  // warp-uniform
       if (have) tc::tc_fence_after();
@@ -698,7 +712,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
       }
       // the O columns are read: the next item's first P V MMA may overwrite them (it waits
-      // for this warpgroup's first p_full of that item, which comes after this point)
+      // for this warpgroup's p_half of that item, which comes after this point)
       tc::tc_fence_before();
       J += nt;
       if (!ok) break;
