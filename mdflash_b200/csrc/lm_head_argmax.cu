@@ -171,27 +171,39 @@ lm_head_argmax_kernel(const __grid_constant__ CUtensorMap tm_w,
         if (it > 0 && !(ok = tc::mbar_wait_warp(&bars.d_empty[q], (it - 1) & 1, abort_flag,
                                                 kTimeoutNs)))
           break;
-        for (int kc = 0; kc < p.k_chunks; ++kc, ++gi) {
-          const int s = gi % kStages;
-          if (!(ok = tc::mbar_wait_warp(&bars.full[s], (gi / kStages) & 1, abort_flag, kTimeoutNs)))
-            break;
+        // stages are consumed two at a time: both waits come first (the second one finds no
+        // MMA of this warp in flight), then 8 MMAs, so a wait that drains this warp's MMAs
+        // comes once per 8 MMAs instead of once per 4
+        for (int kc = 0; kc < p.k_chunks; kc += 2) {
+          const int nk = kc + 1 < p.k_chunks ? 2 : 1;
+          for (int x = 0; x < nk; ++x) {
+            const int s = (gi + x) % kStages;
+            if (!(ok = tc::mbar_wait_warp(&bars.full[s], ((gi + x) / kStages) & 1, abort_flag,
+                                          kTimeoutNs)))
+              break;
+          }
+          if (!ok) break;
           tc::tc_fence_after();
           if (tc::elect_one()) {
-            if (n_mma > 0) {
-              const uint32_t so = (s * kStageBytes) >> 4;
+            for (int x = 0; x < nk; ++x) {
+              const int s = (gi + x) % kStages;
+              if (n_mma > 0) {
+                const uint32_t so = (s * kStageBytes) >> 4;
 #pragma unroll
-              for (int k = 0; k < kK / 16; ++k) {
-                const uint32_t off = so + ((k * 32) >> 4);
-                if (kc == 0 && k == 0)
-                  tc::mma_bf16_ss_w<0>(d, a_lo + off, b_lo + off, kDescHi, idesc);
-                else
-                  tc::mma_bf16_ss_w<1>(d, a_lo + off, b_lo + off, kDescHi, idesc);
+                for (int k = 0; k < kK / 16; ++k) {
+                  const uint32_t off = so + ((k * 32) >> 4);
+                  if (kc + x == 0 && k == 0)
+                    tc::mma_bf16_ss_w<0>(d, a_lo + off, b_lo + off, kDescHi, idesc);
+                  else
+                    tc::mma_bf16_ss_w<1>(d, a_lo + off, b_lo + off, kDescHi, idesc);
+                }
               }
+              tc::mma_commit(&bars.empty[s]);
             }
-            tc::mma_commit(&bars.empty[s]);
-            if (kc == p.k_chunks - 1) tc::mma_commit(&bars.d_full[q]);
+            if (kc + nk == p.k_chunks) tc::mma_commit(&bars.d_full[q]);
           }
           __syncwarp();
+          gi += nk;
         }
       }
       if (!ok) {
