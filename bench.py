@@ -712,14 +712,21 @@ def measure_argmax(dev, rows, steps, warmup):
     logits = torch.randn((rows, V), generator=g, device=dev).mul_(3).to(torch.bfloat16)
     out = torch.empty(rows, dtype=torch.int64, device=dev)
     ms = _timed_launches(lambda: K.argmax(logits, out=out), steps, warmup, dev)
+    # what a plain device copy of the same bytes reaches, timed the same way: the stream
+    # ceiling of a launch this size (copy bytes counted read + write, as the HBM peak is)
+    dst = torch.empty_like(logits)
+    ms_copy = _timed_launches(lambda: dst.copy_(logits), steps, warmup, dev)
     ref = logits.float().argmax(-1)
     if not torch.equal(out, ref):
         raise RuntimeError("argmax disagrees with torch.argmax on the bench data")
     nbytes = logits.numel() * logits.element_size()
     peaks, kind = measured_peaks()
     gbs = nbytes / (ms / 1e3) / 1e9
+    copy_gbs = 2 * nbytes / (ms_copy / 1e3) / 1e9
     return {"ms": ms, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
             "peak_source": kind, "bytes_per_launch": nbytes,
+            "same_size_copy": {"ms": ms_copy, "gbs": copy_gbs,
+                               "frac": copy_gbs / peaks["hbm_gbs"]},
             "shape": f"[{rows}, {V}] bf16 verify logits, N(0,1)*3"}
 
 
