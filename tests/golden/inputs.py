@@ -254,3 +254,55 @@ def sampled_chains(spec: dict) -> torch.Tensor:
 
 # sample_candidate_chains at temperature 0 (mdflash.py:19-40): the argmax chain repeated
 GREEDY_CHAIN_CASE = dict(name="greedy_chains", seed=410, L=15, V=V_QWEN3, S=16)
+
+
+# A few rounds of ddtree_generate (ddtree.py:338-530) on a tiny fp32 target with a
+# deterministic stand-in for the DFlash drafter.  The vocabulary is small (16) so that the
+# tree's depth-1 candidates often hold the target's greedy token and rounds accept several
+# tokens; the weights are large (initializer_range 0.2) so that greedy choices have wide
+# margins.
+LOOP_CASE = dict(name="loop_tiny", layers=2, hidden=256, heads=4, kv_heads=2, head_dim=128,
+                 mlp=512, vocab=16, rope_theta=1e6, prompt=24, block_size=8, budget=64,
+                 max_new_tokens=40, model_seed=3, input_seed=4, mask_token_id=15)
+
+
+def loop_target(spec: dict):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    cfg = Qwen3Config(vocab_size=spec["vocab"], hidden_size=spec["hidden"],
+                      intermediate_size=spec["mlp"], num_hidden_layers=spec["layers"],
+                      num_attention_heads=spec["heads"], num_key_value_heads=spec["kv_heads"],
+                      head_dim=spec["head_dim"], rope_theta=spec["rope_theta"],
+                      max_position_embeddings=4096, tie_word_embeddings=False,
+                      initializer_range=0.2, attn_implementation="sdpa")
+    torch.manual_seed(spec["model_seed"])
+    return Qwen3ForCausalLM(cfg).eval()
+
+
+class StubDrafter(torch.nn.Module):
+    """Stands in for DFlashDraftModel in ddtree_generate: the same call signature, hidden
+    states [1, block, hidden] from the noise embedding of the block and the last context
+    feature through a fixed random map.  Deterministic; ignores its KV cache."""
+
+    def __init__(self, hidden: int, seed: int = 5):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        # small weights: nearly flat draft logits, so the best-first tree takes every depth-1
+        # token before going deeper and rounds accept two or more tokens
+        self.proj = torch.nn.Parameter(torch.randn((hidden, hidden), generator=g) *
+                                       (0.002 * hidden ** -0.5), requires_grad=False)
+        self.target_layer_ids = [0]
+        self.hidden = hidden
+
+    @property
+    def device(self):
+        return self.proj.device
+
+    def forward(self, target_hidden, noise_embedding, position_ids=None, past_key_values=None,
+                use_cache=True, is_causal=False):
+        ctx = target_hidden[:, -1:, :self.hidden].to(noise_embedding.dtype)
+        return (noise_embedding + ctx) @ self.proj.to(noise_embedding.dtype)
+
+
+def loop_inputs(spec: dict) -> torch.Tensor:
+    rng = np.random.default_rng(spec["input_seed"])
+    return torch.from_numpy(rng.integers(0, spec["vocab"] - 1, (1, spec["prompt"])).astype(np.int64))

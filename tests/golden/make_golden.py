@@ -230,6 +230,22 @@ def gen_sampled(ddtree, out: dict, manifest: dict, reference: str):
     manifest["greedy_chains"] = dict(spec)
 
 
+def gen_loop(ddtree, out: dict, manifest: dict):
+    """The reference's own decode loop, ddtree_generate (ddtree.py:338-530), for a few rounds
+    on the tiny fp32 target with the stub drafter: output ids and per-round acceptance."""
+    spec = gin.LOOP_CASE
+    target = gin.loop_target(spec)
+    drafter = gin.StubDrafter(spec["hidden"])
+    ids = gin.loop_inputs(spec)
+    res = ddtree.ddtree_generate(drafter, target, ids, spec["mask_token_id"],
+                                 spec["max_new_tokens"], spec["block_size"], None, 0.0,
+                                 spec["budget"])
+    out["loop/output_ids"] = res.output_ids.numpy().astype(np.int64)
+    out["loop/acceptance_lengths"] = np.asarray(res.acceptance_lengths, np.int64)
+    manifest["loop"] = dict(spec)
+    print("loop acceptance", res.acceptance_lengths)
+
+
 def gen_e2e(ddtree, out: dict, manifest: dict):
     """One DDTree verify step on the CPU-runnable Qwen3-0.6B-shaped target (fp32)."""
     from transformers import DynamicCache
@@ -289,7 +305,7 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("DDTREE_REFERENCE"),
                     help="checkout of the DDTree research code (default: $DDTREE_REFERENCE)")
     ap.add_argument("--only", default="",
-                    help="comma-separated groups to regenerate (e2e, sampled), keeping the other "
+                    help="comma-separated groups to regenerate (e2e, sampled, loop), keeping the other "
                          "arrays of golden.npz")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--no-cpp", action="store_true")
@@ -307,7 +323,8 @@ def main():
         groups = set(args.only.split(","))
         prefixes = {"e2e": ("e2e/",),
                     "sampled": tuple(f"{c['name']}/" for c in gin.SAMPLED_CASES) +
-                    ("greedy_chains/",)}
+                    ("greedy_chains/",),
+                    "loop": ("loop/",)}
         drop = tuple(p for g in groups for p in prefixes[g])
         old = np.load(os.path.join(HERE, "golden.npz"))
         out = {k: old[k] for k in old.files if not k.startswith(drop)}
@@ -317,6 +334,8 @@ def main():
             gen_e2e(ddtree, out, manifest)
         if "sampled" in groups:
             gen_sampled(ddtree, out, manifest, args.reference)
+        if "loop" in groups:
+            gen_loop(ddtree, out, manifest)
         np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)
         with open(os.path.join(HERE, "manifest.json"), "w") as f:
             json.dump(manifest, f, indent=1, sort_keys=True)
@@ -328,6 +347,7 @@ def main():
     gen_compact(ddtree, out, manifest, use_cpp=not args.no_cpp)
     gen_attention(ddtree, out, manifest)
     gen_sampled(ddtree, out, manifest, args.reference)
+    gen_loop(ddtree, out, manifest)
     if not args.skip_e2e:
         gen_e2e(ddtree, out, manifest)
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)
