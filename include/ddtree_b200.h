@@ -268,7 +268,7 @@ int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_pa
 /* ---- fused elementwise stages of the Qwen3 verify forward (bf16) ----------
  * ddt_add_rmsnorm: r = x + delta (delta may be NULL), writes r to residual_out (may be
  *   NULL, may alias x) and weight * rmsnorm(r) to norm_out; rows x hidden, hidden a
- *   multiple of 8 up to 8192.  Replaces the residual add of Qwen3DecoderLayer and
+ *   multiple of 8 up to 16384.  Replaces the residual add of Qwen3DecoderLayer and
  *   Qwen3RMSNorm.forward (transformers/models/qwen3/modeling_qwen3.py:59-64).
  * ddt_qk_norm_rope_cache: from the fused projection qkv [n_tokens, (q_heads + 2 kv_heads),
  *   head_dim], applies q_norm / k_norm and the rotary embedding at positions (device i64),
@@ -276,6 +276,12 @@ int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_pa
  *   caches ([kv_heads, seq, head_dim] at the given strides).  Replaces
  *   modeling_qwen3.py:263-271 (q/k norm, apply_rotary_pos_emb :151-181, cos / sin of
  *   Qwen3RotaryEmbedding :137-147) and DynamicLayer.update (cache_utils.py:102-121).
+ * ddt_rope_table: the bf16 cos / sin of the rotary embedding at positions (device i64) for
+ *   the head_dim / 2 frequencies inv_freq, times rope_scale (Qwen3RotaryEmbedding.forward,
+ *   modeling_qwen3.py:137-147), as table[n_tokens, head_dim / 2] of 32-bit words
+ *   (cos | sin << 16); table 16-byte aligned.  Built once per forward.
+ * ddt_qk_norm_rope_cache_table: ddt_qk_norm_rope_cache with cos / sin read from that table
+ *   (bit-identical results).
  * ddt_silu_mul: out[r, i] = silu(gate_up[r, i]) * gate_up[r, inter + i]; Qwen3MLP.forward
  *   (modeling_qwen3.py:81-83) between its projections. */
 int ddt_add_rmsnorm(const void* x, const void* delta, const void* weight, int64_t rows,
@@ -285,6 +291,13 @@ int ddt_qk_norm_rope_cache(const void* qkv, int64_t n_tokens, int64_t q_heads, i
                            const int64_t* positions, const float* inv_freq, float rope_scale,
                            void* q_out, void* k_cache, void* v_cache, int64_t head_stride,
                            int64_t seq_stride, int64_t past_length, void* stream);
+int ddt_rope_table(const int64_t* positions, int64_t n_tokens, const float* inv_freq,
+                   int64_t head_dim, float rope_scale, void* table, void* stream);
+int ddt_qk_norm_rope_cache_table(const void* qkv, int64_t n_tokens, int64_t q_heads,
+                                 int64_t kv_heads, int64_t head_dim, const void* q_norm_w,
+                                 const void* k_norm_w, float eps, const void* rope_table,
+                                 void* q_out, void* k_cache, void* v_cache, int64_t head_stride,
+                                 int64_t seq_stride, int64_t past_length, void* stream);
 int ddt_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* out, void* stream);
 
 /* additive mask block [n_nodes, n_nodes] (row stride in elements; 0 = visible) ->

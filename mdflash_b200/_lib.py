@@ -62,6 +62,9 @@ SIGNATURES = {
     "ddt_add_rmsnorm": (_i, [_P, _P, _P, _I, _I, _F, _P, _P, _P]),
     "ddt_qk_norm_rope_cache": (_i, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _F, _P, _P, _P, _I, _I,
                                     _I, _P]),
+    "ddt_rope_table": (_i, [_P, _I, _P, _I, _F, _P, _P]),
+    "ddt_qk_norm_rope_cache_table": (_i, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _P, _I, _I,
+                                          _I, _P]),
     "ddt_silu_mul": (_i, [_P, _I, _I, _P, _P]),
 }
 

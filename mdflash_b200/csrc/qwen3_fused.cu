@@ -12,7 +12,9 @@
 //                            fp32 and casts them to bf16; apply_rotary_pos_emb :151-181
 //                            rounds q*cos, rotate_half(q)*sin and their sum to bf16),
 //                            and the KV-cache write that DynamicLayer.update does with
-//                            torch.cat (cache_utils.py:119-120), in place at rows past + i
+//                            torch.cat (cache_utils.py:119-120), in place at rows past + i;
+//                            the _table form reads cos / sin from ddt_rope_table's table,
+//                            built once per forward (the same values)
 //   ddt_silu_mul             Qwen3MLP.forward (:81-83): bf16(silu(gate)) * up in bf16
 #include <cuda_bf16.h>
 
@@ -29,11 +31,15 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// One CTA per row (up to 256 threads); each thread owns 8 consecutive elements per pass,
-// at most 4 passes.
-constexpr int kNormThreads = 256;
+// One CTA per row: hidden / 8 vectors of 8 elements, spread over at most 512 threads in
+// kPasses <= 4 passes.  The weight vectors are loaded together with the row, before the
+// reduction, so that their latency overlaps it.
+constexpr int kNormThreads = 512;
 constexpr int kNormMaxPasses = 4;
 
+__device__ __forceinline__ uint4 ld16(const __nv_bfloat16* p) { return *reinterpret_cast<const uint4*>(p); }
+
+template <int kPasses>
 __global__ void __launch_bounds__(kNormThreads)
 add_rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* __restrict__ delta,
                    const __nv_bfloat16* __restrict__ w, int hidden, float eps,
@@ -41,21 +47,28 @@ add_rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* __restrict__ del
   // residual_out may alias x: each thread reads its elements before it writes them
   const long long row = blockIdx.x;
   const int tid = threadIdx.x;
+  const int nthr = blockDim.x;
+  const int vecs = hidden >> 3;
   const __nv_bfloat16* xr = x + row * hidden;
   const __nv_bfloat16* dr = delta ? delta + row * hidden : nullptr;
-  const int nthr = blockDim.x;
-  const int passes = hidden / (nthr * 8);
-  float v[kNormMaxPasses * 8];
+  uint4 xv[kPasses], dv[kPasses], wv[kPasses];
+#pragma unroll
+  for (int c = 0; c < kPasses; ++c) {
+    const int vi = c * nthr + tid;
+    xv[c] = dv[c] = wv[c] = make_uint4(0, 0, 0, 0);
+    if (vi < vecs) {
+      xv[c] = ld16(xr + vi * 8);
+      if (dr) dv[c] = ld16(dr + vi * 8);
+      wv[c] = ld16(w + vi * 8);
+    }
+  }
+  float v[kPasses * 8];
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kNormMaxPasses; ++c) {
-    if (c >= passes) break;
-    const int base = (c * nthr + tid) * 8;
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + base);
-    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
-    uint4 dv = make_uint4(0, 0, 0, 0);
-    if (dr) dv = *reinterpret_cast<const uint4*>(dr + base);
-    const __nv_bfloat16* de = reinterpret_cast<const __nv_bfloat16*>(&dv);
+  for (int c = 0; c < kPasses; ++c) {
+    const int vi = c * nthr + tid;
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[c]);
+    const __nv_bfloat16* de = reinterpret_cast<const __nv_bfloat16*>(&dv[c]);
     uint4 rv;
     __nv_bfloat16* re = reinterpret_cast<__nv_bfloat16*>(&rv);
 #pragma unroll
@@ -64,9 +77,10 @@ add_rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* __restrict__ del
                          : __bfloat162float(xe[e]);
       re[e] = __float2bfloat16_rn(r);
       v[c * 8 + e] = r;
-      ss += r * r;
+      ss += r * r;  // padding vectors hold zeros
     }
-    if (residual_out) *reinterpret_cast<uint4*>(residual_out + row * hidden + base) = rv;
+    if (residual_out && vi < vecs)
+      *reinterpret_cast<uint4*>(residual_out + row * hidden + vi * 8) = rv;
   }
   __shared__ float red[kNormThreads / 32];
   ss = warp_sum(ss);
@@ -76,31 +90,53 @@ add_rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* __restrict__ del
   for (int i = 0; i < (nthr >> 5); ++i) tot += red[i];
   const float inv = rsqrtf(tot / static_cast<float>(hidden) + eps);
 #pragma unroll
-  for (int c = 0; c < kNormMaxPasses; ++c) {
-    if (c >= passes) break;
-    const int base = (c * nthr + tid) * 8;
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + base);
-    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+  for (int c = 0; c < kPasses; ++c) {
+    const int vi = c * nthr + tid;
+    if (vi >= vecs) break;
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[c]);
     uint4 ov;
     __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&ov);
 #pragma unroll
     for (int e = 0; e < 8; ++e) oe[e] = __float2bfloat16_rn(__bfloat162float(we[e]) * bf(v[c * 8 + e] * inv));
-    *reinterpret_cast<uint4*>(norm_out + row * hidden + base) = ov;
+    *reinterpret_cast<uint4*>(norm_out + row * hidden + vi * 8) = ov;
   }
 }
 
+// cos / sin of the rotary embedding for every (token, frequency): the bf16 values that
+// Qwen3RotaryEmbedding.forward produces (fp32 inv_freq * position, cos / sin in fp32, times
+// attention_scaling, cast to bf16), packed as (cos | sin << 16) in one 32-bit word.  Built
+// once per forward and read by every layer's q/k rotary embedding.
+__global__ void rope_table_kernel(const int64_t* __restrict__ positions, int n_tokens,
+                                  const float* __restrict__ inv_freq, int half, float rope_scale,
+                                  uint32_t* __restrict__ table) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_tokens * half) return;
+  const int tok = i / half, fi = i - tok * half;
+  const float f = inv_freq[fi] * static_cast<float>(positions[tok]);
+  const __nv_bfloat16 c = __float2bfloat16_rn(cosf(f) * rope_scale);
+  const __nv_bfloat16 s = __float2bfloat16_rn(sinf(f) * rope_scale);
+  table[i] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&c)) |
+             (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&s)) << 16);
+}
+
 // One warp per (token, head) of the fused qkv projection; head_dim 128, lane owns
-// elements [4 lane, 4 lane + 4), the rotate_half partner lives in lane ^ 16.
+// elements [4 lane, 4 lane + 4), the rotate_half partner lives in lane ^ 16.  kTable: cos /
+// sin come from the rope table (16 bytes per lane), else they are computed here.
 constexpr int kHeadDim = 128;
 
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+template <bool kTable>
 __global__ void __launch_bounds__(256)
 qk_norm_rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, int n_tokens, int q_heads,
                           int kv_heads, const __nv_bfloat16* __restrict__ qw,
                           const __nv_bfloat16* __restrict__ kw, float eps,
                           const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
-                          float rope_scale, __nv_bfloat16* __restrict__ q_out,
-                          __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
-                          long long head_stride, long long seq_stride, long long past) {
+                          float rope_scale, const uint32_t* __restrict__ table,
+                          __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
+                          __nv_bfloat16* __restrict__ v_cache, long long head_stride,
+                          long long seq_stride, long long past) {
   const int warps = blockDim.x >> 5;
   const long long gw = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -118,6 +154,13 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, int n_tokens, i
   }
   const bool is_q = hh < q_heads;
   const __nv_bfloat16* nw = is_q ? qw : kw;
+  const uint2 wraw = *reinterpret_cast<const uint2*>(nw + lane * 4);
+  const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wraw);
+  uint4 cs = make_uint4(0, 0, 0, 0);
+  if (kTable)  // emb = cat(freqs, freqs): lanes l and l ^ 16 share frequencies 4 (l & 15) ..
+    cs = *reinterpret_cast<const uint4*>(table + static_cast<long long>(tok) * (kHeadDim / 2) +
+                                         (lane & 15) * 4);
+  const uint32_t* csw = reinterpret_cast<const uint32_t*>(&cs);
   float x[4];
   float ss = 0.f;
 #pragma unroll
@@ -129,21 +172,25 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, int n_tokens, i
   const float inv = rsqrtf(ss / static_cast<float>(kHeadDim) + eps);
   float n[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) n[e] = bf(__bfloat162float(nw[lane * 4 + e]) * bf(x[e] * inv));
+  for (int e = 0; e < 4; ++e) n[e] = bf(__bfloat162float(we[e]) * bf(x[e] * inv));
   // rotate_half: first half takes -x[d + 64], second half x[d - 64] (lane ^ 16)
   float partner[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) partner[e] = __shfl_xor_sync(DDT_FULL_MASK, n[e], 16);
-  const float pos = static_cast<float>(positions[tok]);
   uint2 outv;
   __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&outv);
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int d = lane * 4 + e;
-    const int fi = d & 63;  // emb = cat(freqs, freqs)
-    const float f = inv_freq[fi] * pos;
-    const float c = bf(cosf(f) * rope_scale);
-    const float s = bf(sinf(f) * rope_scale);
+    float c, s;
+    if (kTable) {
+      c = bf_lo(csw[e]);
+      s = bf_hi(csw[e]);
+    } else {
+      const float f = inv_freq[d & 63] * static_cast<float>(positions[tok]);
+      c = bf(cosf(f) * rope_scale);
+      s = bf(sinf(f) * rope_scale);
+    }
     const float rot = d < 64 ? -partner[e] : partner[e];
     oe[e] = __float2bfloat16_rn(bf(n[e] * c) + bf(rot * s));
   }
@@ -155,15 +202,9 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, int n_tokens, i
   }
 }
 
-__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, long long rows, int inter,
-                                __nv_bfloat16* __restrict__ out) {
-  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
-  const long long total = rows * inter;
-  if (i >= total) return;
-  const long long r = i / inter;
-  const int c = static_cast<int>(i % inter);
-  const uint4 gv = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + c);
-  const uint4 uv = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter + c);
+// Two 8-element vectors per thread (vector i and i + half the vectors), both loaded before
+// either is computed, so that the grid is one wave at verify size.
+__device__ __forceinline__ uint4 silu_mul8(uint4 gv, uint4 uv) {
   const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
   const __nv_bfloat16* ue = reinterpret_cast<const __nv_bfloat16*>(&uv);
   uint4 ov;
@@ -174,7 +215,30 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, long long 
     const float s = bf(g / (1.f + expf(-g)));
     oe[e] = __float2bfloat16_rn(s * __bfloat162float(ue[e]));
   }
-  *reinterpret_cast<uint4*>(out + i) = ov;
+  return ov;
+}
+
+__global__ void __launch_bounds__(256)
+silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, long long rows, int inter,
+                __nv_bfloat16* __restrict__ out) {
+  const long long vecs = rows * (inter >> 3);
+  const long long half = (vecs + 1) >> 1;
+  const long long v0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (v0 >= half) return;
+  const long long v1 = v0 + half;
+  const int per_row = inter >> 3;
+  const long long r0 = v0 / per_row, r1 = v1 / per_row;
+  const int c0 = static_cast<int>(v0 - r0 * per_row) * 8, c1 = static_cast<int>(v1 - r1 * per_row) * 8;
+  const bool two = v1 < vecs;
+  const uint4 g0 = ld16(gu + r0 * 2 * inter + c0);
+  const uint4 u0 = ld16(gu + r0 * 2 * inter + inter + c0);
+  uint4 g1 = make_uint4(0, 0, 0, 0), u1 = g1;
+  if (two) {
+    g1 = ld16(gu + r1 * 2 * inter + c1);
+    u1 = ld16(gu + r1 * 2 * inter + inter + c1);
+  }
+  *reinterpret_cast<uint4*>(out + r0 * inter + c0) = silu_mul8(g0, u0);
+  if (two) *reinterpret_cast<uint4*>(out + r1 * inter + c1) = silu_mul8(g1, u1);
 }
 
 }  // namespace fused
@@ -182,24 +246,96 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, long long 
 
 using namespace ddt;
 
+namespace {
+
+// hidden / 8 vectors in at most kNormMaxPasses passes of at most kNormThreads threads.
+bool norm_shape(int64_t hidden, int& nthr) {
+  if (hidden <= 0 || hidden % 8) return false;
+  const int64_t vecs = hidden / 8;
+  const int64_t passes = (vecs + fused::kNormThreads - 1) / fused::kNormThreads;
+  if (passes > fused::kNormMaxPasses) return false;
+  const int64_t per = (vecs + passes - 1) / passes;
+  nthr = static_cast<int>((per + 31) / 32 * 32);
+  return true;
+}
+
+int qk_norm_rope_launch(const void* qkv, int64_t n_tokens, int64_t q_heads, int64_t kv_heads,
+                        int64_t head_dim, const void* q_norm_w, const void* k_norm_w, float eps,
+                        const int64_t* positions, const float* inv_freq, float rope_scale,
+                        const void* table, void* q_out, void* k_cache, void* v_cache,
+                        int64_t head_stride, int64_t seq_stride, int64_t past_length,
+                        void* stream) {
+  if (!qkv || !q_norm_w || !k_norm_w || !q_out || !k_cache || !v_cache) return DDT_ERR_INVALID;
+  if (!table && (!positions || !inv_freq)) return DDT_ERR_INVALID;
+  if (head_dim != fused::kHeadDim) return DDT_ERR_CAPACITY;
+  if (n_tokens < 0 || q_heads <= 0 || kv_heads <= 0 || past_length < 0) return DDT_ERR_INVALID;
+  if (!aligned(qkv, 8) || !aligned(q_out, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) ||
+      !aligned(q_norm_w, 8) || !aligned(k_norm_w, 8) || (table && !aligned(table, 16)) ||
+      (head_stride * 2) % 8 || (seq_stride * 2) % 8)
+    return DDT_ERR_ALIGN;
+  if (n_tokens == 0) return DDT_OK;
+  const long long warps = n_tokens * (q_heads + 2 * kv_heads);
+  const dim3 grid(static_cast<unsigned>((warps + 7) / 8));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const auto* in = static_cast<const __nv_bfloat16*>(qkv);
+  const auto* qw = static_cast<const __nv_bfloat16*>(q_norm_w);
+  const auto* kw = static_cast<const __nv_bfloat16*>(k_norm_w);
+  auto* qo = static_cast<__nv_bfloat16*>(q_out);
+  auto* kc = static_cast<__nv_bfloat16*>(k_cache);
+  auto* vc = static_cast<__nv_bfloat16*>(v_cache);
+  if (table)
+    fused::qk_norm_rope_cache_kernel<true><<<grid, 256, 0, st>>>(
+        in, static_cast<int>(n_tokens), static_cast<int>(q_heads), static_cast<int>(kv_heads), qw,
+        kw, eps, nullptr, nullptr, 1.f, static_cast<const uint32_t*>(table), qo, kc, vc,
+        head_stride, seq_stride, past_length);
+  else
+    fused::qk_norm_rope_cache_kernel<false><<<grid, 256, 0, st>>>(
+        in, static_cast<int>(n_tokens), static_cast<int>(q_heads), static_cast<int>(kv_heads), qw,
+        kw, eps, positions, inv_freq, rope_scale, nullptr, qo, kc, vc, head_stride, seq_stride,
+        past_length);
+  return launch_status();
+}
+
+}  // namespace
+
 extern "C" int ddt_add_rmsnorm(const void* x, const void* delta, const void* weight, int64_t rows,
                                int64_t hidden, float eps, void* residual_out, void* norm_out,
                                void* stream) {
   if (!x || !weight || !norm_out || rows < 0) return DDT_ERR_INVALID;
-  int nthr = static_cast<int>(hidden / 8);
-  if (nthr > fused::kNormThreads) nthr = fused::kNormThreads;
-  nthr &= ~31;
-  if (nthr < 32 || hidden % (nthr * 8) || hidden / (nthr * 8) > fused::kNormMaxPasses)
-    return DDT_ERR_CAPACITY;
+  int nthr = 0;
+  if (!norm_shape(hidden, nthr)) return DDT_ERR_CAPACITY;
   if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(norm_out, 16) ||
       (delta && !aligned(delta, 16)) || (residual_out && !aligned(residual_out, 16)))
     return DDT_ERR_ALIGN;
   if (rows == 0) return DDT_OK;
-  fused::add_rmsnorm_kernel<<<static_cast<unsigned>(rows), nthr, 0,
-                              static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(delta),
-      static_cast<const __nv_bfloat16*>(weight), static_cast<int>(hidden), eps,
-      static_cast<__nv_bfloat16*>(residual_out), static_cast<__nv_bfloat16*>(norm_out));
+  const auto* xp = static_cast<const __nv_bfloat16*>(x);
+  const auto* dp = static_cast<const __nv_bfloat16*>(delta);
+  const auto* wp = static_cast<const __nv_bfloat16*>(weight);
+  auto* rp = static_cast<__nv_bfloat16*>(residual_out);
+  auto* np = static_cast<__nv_bfloat16*>(norm_out);
+  const int h = static_cast<int>(hidden);
+  const dim3 grid(static_cast<unsigned>(rows));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch ((hidden / 8 + nthr - 1) / nthr) {
+    case 1: fused::add_rmsnorm_kernel<1><<<grid, nthr, 0, st>>>(xp, dp, wp, h, eps, rp, np); break;
+    case 2: fused::add_rmsnorm_kernel<2><<<grid, nthr, 0, st>>>(xp, dp, wp, h, eps, rp, np); break;
+    case 3: fused::add_rmsnorm_kernel<3><<<grid, nthr, 0, st>>>(xp, dp, wp, h, eps, rp, np); break;
+    default: fused::add_rmsnorm_kernel<4><<<grid, nthr, 0, st>>>(xp, dp, wp, h, eps, rp, np); break;
+  }
+  return launch_status();
+}
+
+extern "C" int ddt_rope_table(const int64_t* positions, int64_t n_tokens, const float* inv_freq,
+                              int64_t head_dim, float rope_scale, void* table, void* stream) {
+  if (!positions || !inv_freq || !table || n_tokens < 0) return DDT_ERR_INVALID;
+  if (head_dim != fused::kHeadDim) return DDT_ERR_CAPACITY;
+  if (!aligned(table, 16)) return DDT_ERR_ALIGN;
+  if (n_tokens == 0) return DDT_OK;
+  const long long n = n_tokens * (head_dim / 2);
+  fused::rope_table_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                             static_cast<cudaStream_t>(stream)>>>(
+      positions, static_cast<int>(n_tokens), inv_freq, static_cast<int>(head_dim / 2), rope_scale,
+      static_cast<uint32_t*>(table));
   return launch_status();
 }
 
@@ -209,23 +345,22 @@ extern "C" int ddt_qk_norm_rope_cache(const void* qkv, int64_t n_tokens, int64_t
                                       const float* inv_freq, float rope_scale, void* q_out,
                                       void* k_cache, void* v_cache, int64_t head_stride,
                                       int64_t seq_stride, int64_t past_length, void* stream) {
-  if (!qkv || !q_norm_w || !k_norm_w || !positions || !inv_freq || !q_out || !k_cache || !v_cache)
-    return DDT_ERR_INVALID;
-  if (head_dim != fused::kHeadDim) return DDT_ERR_CAPACITY;
-  if (n_tokens < 0 || q_heads <= 0 || kv_heads <= 0 || past_length < 0) return DDT_ERR_INVALID;
-  if (!aligned(qkv, 8) || !aligned(q_out, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) ||
-      (head_stride * 2) % 8 || (seq_stride * 2) % 8)
-    return DDT_ERR_ALIGN;
-  if (n_tokens == 0) return DDT_OK;
-  const long long warps = n_tokens * (q_heads + 2 * kv_heads);
-  fused::qk_norm_rope_cache_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0,
-                                     static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(qkv), static_cast<int>(n_tokens), static_cast<int>(q_heads),
-      static_cast<int>(kv_heads), static_cast<const __nv_bfloat16*>(q_norm_w),
-      static_cast<const __nv_bfloat16*>(k_norm_w), eps, positions, inv_freq, rope_scale,
-      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
-      static_cast<__nv_bfloat16*>(v_cache), head_stride, seq_stride, past_length);
-  return launch_status();
+  if (!positions || !inv_freq) return DDT_ERR_INVALID;
+  return qk_norm_rope_launch(qkv, n_tokens, q_heads, kv_heads, head_dim, q_norm_w, k_norm_w, eps,
+                             positions, inv_freq, rope_scale, nullptr, q_out, k_cache, v_cache,
+                             head_stride, seq_stride, past_length, stream);
+}
+
+extern "C" int ddt_qk_norm_rope_cache_table(const void* qkv, int64_t n_tokens, int64_t q_heads,
+                                            int64_t kv_heads, int64_t head_dim,
+                                            const void* q_norm_w, const void* k_norm_w, float eps,
+                                            const void* rope_table, void* q_out, void* k_cache,
+                                            void* v_cache, int64_t head_stride, int64_t seq_stride,
+                                            int64_t past_length, void* stream) {
+  if (!rope_table) return DDT_ERR_INVALID;
+  return qk_norm_rope_launch(qkv, n_tokens, q_heads, kv_heads, head_dim, q_norm_w, k_norm_w, eps,
+                             nullptr, nullptr, 1.f, rope_table, q_out, k_cache, v_cache,
+                             head_stride, seq_stride, past_length, stream);
 }
 
 extern "C" int ddt_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* out,
@@ -233,8 +368,8 @@ extern "C" int ddt_silu_mul(const void* gate_up, int64_t rows, int64_t inter, vo
   if (!gate_up || !out || rows < 0 || inter <= 0) return DDT_ERR_INVALID;
   if (inter % 8 || !aligned(gate_up, 16) || !aligned(out, 16)) return DDT_ERR_ALIGN;
   if (rows == 0) return DDT_OK;
-  const long long vecs = rows * inter / 8;
-  fused::silu_mul_kernel<<<static_cast<unsigned>((vecs + 255) / 256), 256, 0,
+  const long long half = (rows * inter / 8 + 1) / 2;
+  fused::silu_mul_kernel<<<static_cast<unsigned>((half + 255) / 256), 256, 0,
                            static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(gate_up), rows, static_cast<int>(inter),
       static_cast<__nv_bfloat16*>(out));

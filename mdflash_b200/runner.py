@@ -7,7 +7,8 @@ its bf16 rounding points but runs each layer as
 
     ddt_add_rmsnorm          residual add + input_layernorm
     GEMM                     q/k/v projections (one cuBLAS GEMM on the concatenated weight)
-    ddt_qk_norm_rope_cache   q_norm / k_norm, rotary embedding, K/V written into the cache
+    ddt_qk_norm_rope_cache_table
+                             q_norm / k_norm, rotary embedding, K/V written into the cache
     ddt_tree_attn            tree attention (tcgen05)
     GEMM                     o_proj
     ddt_add_rmsnorm          residual add + post_attention_layernorm
@@ -15,7 +16,8 @@ its bf16 rounding points but runs each layer as
     ddt_silu_mul             SiLU(gate) * up
     GEMM                     down_proj
 
-followed by the final norm and lm_head.  It is used by TreeVerifier(fused=True).
+followed by the final norm and lm_head.  The rotary cos / sin of the forward's positions are
+built once (ddt_rope_table) and read by every layer.  It is used by TreeVerifier(fused=True).
 """
 from __future__ import annotations
 
@@ -78,6 +80,10 @@ class Qwen3VerifyRunner:
         h = torch.empty_like(x)
         q = torch.empty((n, hq, d), dtype=x.dtype, device=x.device)
         act = torch.empty((n, self.inter), dtype=x.dtype, device=x.device)
+        rope = torch.empty((n, d // 2), dtype=torch.int32, device=x.device)
+        check(lib.ddt_rope_table(positions.data_ptr(), n, self.inv_freq.data_ptr(), d,
+                                 self.rope_scale, rope.data_ptr(), st), "ddt_rope_table")
+        K.STATS.launches += 1
         delta = None
         for li, w in enumerate(self.layers):
             layer = cache.layers[li]
@@ -86,12 +92,12 @@ class Qwen3VerifyRunner:
                                       w["ln1"].data_ptr(), n, H, self.eps, x.data_ptr(),
                                       h.data_ptr(), st), "ddt_add_rmsnorm")
             qkv = torch.matmul(h, w["w_qkv"].t())
-            check(lib.ddt_qk_norm_rope_cache(qkv.data_ptr(), n, hq, hkv, d, w["qn"].data_ptr(),
-                                             w["kn"].data_ptr(), self.eps, positions.data_ptr(),
-                                             self.inv_freq.data_ptr(), self.rope_scale,
-                                             q.data_ptr(), kbuf.data_ptr(), vbuf.data_ptr(),
-                                             kbuf.stride(0), kbuf.stride(1), past_length, st),
-                  "ddt_qk_norm_rope_cache")
+            check(lib.ddt_qk_norm_rope_cache_table(qkv.data_ptr(), n, hq, hkv, d,
+                                                   w["qn"].data_ptr(), w["kn"].data_ptr(),
+                                                   self.eps, rope.data_ptr(), q.data_ptr(),
+                                                   kbuf.data_ptr(), vbuf.data_ptr(),
+                                                   kbuf.stride(0), kbuf.stride(1), past_length,
+                                                   st), "ddt_qk_norm_rope_cache_table")
             K.STATS.launches += 3
             s = past_length + n
             attn = K.tree_attention(q, kbuf[:, :s], vbuf[:, :s], anc_bits, past_length,

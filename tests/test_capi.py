@@ -73,6 +73,18 @@ def test_host_side_validation_rejects_bad_arguments():
     assert lib.ddt_lm_head_argmax(p, 128, p, 128, 8, 128, 1000, p, None, 0, p, 16, None,
                                   None) == -7
     assert lib.ddt_lm_head_argmax_workspace_bytes(257) >= 257 * 8 + 4
+    # fused elementwise stages: head_dim 128 only, a 16-byte aligned rope table, hidden up to
+    # 16384 in multiples of 8
+    assert lib.ddt_rope_table(p, 4, p, 64, 1.0, p, None) == -2
+    assert lib.ddt_rope_table(p, 4, p, 128, 1.0, ctypes.c_void_p(260), None) == -4
+    assert lib.ddt_rope_table(None, 4, p, 128, 1.0, p, None) == -1
+    assert lib.ddt_qk_norm_rope_cache_table(p, 4, 32, 8, 128, p, p, 1e-6, None, p, p, p, 1024,
+                                            128, 0, None) == -1
+    assert lib.ddt_qk_norm_rope_cache_table(p, 4, 32, 8, 128, p, p, 1e-6, ctypes.c_void_p(264),
+                                            p, p, p, 1024, 128, 0, None) == -4
+    assert lib.ddt_add_rmsnorm(p, None, p, 4, 16392, 1e-6, None, p, None) == -2
+    assert lib.ddt_add_rmsnorm(p, None, p, 4, 100, 1e-6, None, p, None) == -2
+    assert lib.ddt_add_rmsnorm(p, None, p, 0, 5120, 1e-6, None, p, None) == 0
     # the bounded-wait check takes limits from 100 us to 2 s and needs a status word
     p = ctypes.c_void_p(256)
     assert lib.ddt_tree_attn_wait_check(p, p, p, p, 65, 256, 32, 8, p, 3, 10, p, None) == -1
