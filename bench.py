@@ -86,6 +86,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="skip the verify_step / kernels sub-records")
+    ap.add_argument("--tree-build", choices=["batched", "per-request"], default="batched",
+                    help="requests workload: one batched tree-build launch for all of a rank's "
+                         "requests per step (default), or one tree build inside each request's "
+                         "graph")
     ap.add_argument("--fused", type=int, default=1,
                     help="1: verify forward through the fused Qwen3 runner (default); 0: through "
                          "transformers' Qwen3 with the ddtree_tree attention plug-in")
@@ -419,29 +423,46 @@ def run_requests(args):
     pool = torch.cuda.graph_pool_handle()
     caps = []
     g = torch.Generator(device=dev).manual_seed(rank)
-    for i in mine:
+    batched = args.tree_build == "batched"
+    # every request's drafter logits and root token, pinned on the host and resident on the
+    # device ([R, depths, V]); the batched build reads them all in one launch
+    host_logits = torch.stack([request_logits(specs[i].seed).to(torch.bfloat16)
+                               for i in mine]).pin_memory() if mine else None
+    host_roots = torch.tensor([int(np.random.default_rng(specs[i].seed).integers(0, V))
+                               for i in mine], dtype=torch.int64).pin_memory()
+    dev_logits = host_logits.to(dev) if mine else None
+    trees = K.TreeBatch.allocate(dev, [specs[i].budget for i in mine], DEPTHS, V) if mine else None
+    if mine:
+        trees.starts.copy_(torch.tensor([specs[i].prefix for i in mine]))
+        trees.root_tokens.copy_(host_roots)
+        if batched:
+            K.topk_tree_batched(dev_logits, trees)  # the trees the captured steps start from
+    for j, i in enumerate(mine):
         sp = specs[i]
         cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
             QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
         _fill_prefix(cache, sp.prefix, g)  # the verify work does not depend on the K / V values
         ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
-        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pool)
-        host = request_logits(sp.seed).to(torch.bfloat16).pin_memory()
-        root = torch.tensor([int(np.random.default_rng(sp.seed).integers(0, V))],
-                            dtype=torch.int64).pin_memory()
-        cap.draft_logits.copy_(host)
-        cap.root_token.copy_(root)
-        caps.append((sp, cap, host, root))
+        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pool,
+                           tree=trees.tree(j) if batched else None)
+        cap.draft_logits.copy_(dev_logits[j])
+        cap.root_token.copy_(trees.root_tokens[j:j + 1])
+        caps.append((sp, cap))
     records = torch.full((len(caps), S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
-    for j, (sp, cap, _, _) in enumerate(caps):
+    for j, (sp, cap) in enumerate(caps):
         records[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
         records[j, 5] = 0
 
     def one_step(e2e: bool):
-        for j, (sp, cap, host, root) in enumerate(caps):
-            if e2e:
-                cap.draft_logits.copy_(host, non_blocking=True)
-                cap.root_token.copy_(root, non_blocking=True)
+        if e2e and batched and caps:  # this step's inputs from pinned host memory
+            dev_logits.copy_(host_logits, non_blocking=True)
+            trees.root_tokens.copy_(host_roots, non_blocking=True)
+        if batched and caps:
+            K.topk_tree_batched(dev_logits, trees)
+        for j, (sp, cap) in enumerate(caps):
+            if e2e and not batched:
+                cap.draft_logits.copy_(host_logits[j], non_blocking=True)
+                cap.root_token.copy_(host_roots[j:j + 1], non_blocking=True)
             r = cap.replay()
             # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
             records[j, 3] = r.n_accepted[0]
@@ -451,7 +472,7 @@ def run_requests(args):
         return S.gather_results(records)
 
     def check_statuses():
-        st = torch.stack([cap.verifier.status for _, cap, _, _ in caps])
+        st = torch.stack([cap.verifier.status for _, cap in caps])
         if int(st.abs().sum().item()) != 0:
             raise RuntimeError("a tree-attention launch reported a bounded-wait timeout")
 
@@ -491,9 +512,10 @@ def run_requests(args):
     e2e_ms, e2e_rec = timed(True)
     e2e_tokens = int((e2e_rec[:, 2] + e2e_rec[:, 3]).sum())
     check_statuses()
-    h2d = sum(h.numel() * h.element_size() + 8 for _, _, h, _ in caps)
+    h2d = (host_logits.numel() * host_logits.element_size() + host_roots.numel() * 8) if caps else 0
     d2h = int(allrec.numel()) * 8
-    launches = sum(cap.launches_per_replay for _, cap, _, _ in caps) * args.steps
+    launches = (sum(cap.launches_per_replay for _, cap in caps) + (1 if batched and caps else 0)) \
+        * args.steps
     sums = torch.tensor([float(h2d), float(launches)], device=dev)
     if world > 1:
         dist.all_reduce(sums, op=dist.ReduceOp.SUM)
@@ -517,8 +539,13 @@ def run_requests(args):
         "step_roofline": {"bound": "max(HBM: weights + prefix K/V once, bf16 FLOPs) per request, "
                                    "the slowest rank's requests back to back",
                           "ms": bound, "frac": bound / ms, "peak_source": peak_kind},
-        "execution": "one CUDA-graph replay per request (tree build, 36-layer fused verify "
-                     "forward, argmax, accept walk + compaction), records all-gathered per step",
+        "execution": ("one batched tree-build launch for the rank's requests, then "
+                      "one CUDA-graph replay per request (36-layer fused verify forward, argmax, "
+                      "accept walk + compaction)" if batched else
+                      "one CUDA-graph replay per request (tree build, 36-layer fused verify "
+                      "forward, argmax, accept walk + compaction)") +
+                     "; records all-gathered per step",
+        "tree_build": args.tree_build,
     }
     del caps
     torch.cuda.synchronize()

@@ -86,6 +86,31 @@ int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths, int64_t v
                   int64_t* verify_ids, int64_t* verify_pos, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Batched tree build: the trees of n_requests independent requests (the same depths and
+ * vocabulary) in one launch, each exactly what ddt_topk_tree gives for that request.  No
+ * counterpart in the reference, which builds one tree per ddtree_generate call
+ * (ddtree.py:440); it serves a server that verifies many requests per step.
+ *   draft_logits: request r, depth d at draft_logits + r * request_stride + d * row_stride
+ *   budgets: i32 [n_requests] on the device, each in [0, max_budget] (larger values are
+ *     clamped to max_budget; 0 gives the root-only tree)
+ *   outputs per request at fixed strides: node_token_ids / node_depths [n_requests,
+ *     max_budget]; parents / verify_ids / verify_pos [n_requests, max_budget + 1];
+ *     anc_bits [n_requests, max_budget + 1, anc_words]; node_count i32 [n_requests]
+ *   root_tokens i64 [n_requests] (may be NULL: root token 0), starts i64 [n_requests]
+ *     (may be NULL: every start 0); verify_ids / verify_pos may be NULL
+ * The workspace (ddt_topk_tree_batched_workspace_bytes) must be zero-filled before its first
+ * use; every launch leaves its counters at zero again. */
+size_t ddt_topk_tree_batched_workspace_bytes(int64_t n_requests, int64_t depths, int64_t vocab,
+                                             int64_t max_budget);
+int ddt_topk_tree_batched(const void* draft_logits, int dtype, int64_t n_requests,
+                          int64_t depths, int64_t vocab, int64_t row_stride,
+                          int64_t request_stride, const int32_t* budgets, int64_t max_budget,
+                          int64_t* node_token_ids, int64_t* node_depths, int32_t* parents,
+                          int32_t* node_count, uint32_t* anc_bits, int64_t anc_words,
+                          const int64_t* root_tokens, const int64_t* starts,
+                          int64_t* verify_ids, int64_t* verify_pos, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* Tree build that allocates nothing and takes no workspace.  No counterpart in the
  * reference: it serves callers that cannot allocate device memory when they call (a
  * serving stack that owns all device memory in its own pool after start-up, or a plugin

@@ -35,6 +35,9 @@ SIGNATURES = {
     "ddt_topk_tree_workspace_bytes": (_S, [_I, _I, _I]),
     "ddt_topk_tree": (_i, [_P, _i, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P,
                            _P, _S, _P]),
+    "ddt_topk_tree_batched_workspace_bytes": (_S, [_I, _I, _I, _I]),
+    "ddt_topk_tree_batched": (_i, [_P, _i, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _I, _P,
+                                   _P, _P, _P, _P, _S, _P]),
     "ddt_topk_tree_noalloc": (_i, [_P, _i, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I,
                                    _P, _P, _P]),
     "ddt_sample_chains": (_i, [_P, _i, _I, _I, _I, _I, _F, ctypes.c_uint64, ctypes.c_uint64, _P,

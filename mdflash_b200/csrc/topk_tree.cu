@@ -526,6 +526,20 @@ __device__ int heap_build(const float* lp, int L, int k, int budget, Frontier f,
   return count;
 }
 
+// Per-request strides of a batched launch (all zero / null for a single tree): request r
+// reads logits + r * logits, writes its nodes at r * nodes (node_token_ids, node_depths) and
+// r * (nodes + 1) (parents, verify ids / positions, rows of anc_bits), its count at
+// node_count + r, and uses workspace slice r of ws_bytes.  budgets / starts / root tokens
+// are per-request device arrays when given.
+struct Batch {
+  int64_t logits;
+  int64_t nodes;
+  size_t ws_bytes;
+  int kmax;
+  const int32_t* budgets;
+  const int64_t* starts;
+};
+
 template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
 topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_stride, int k,
@@ -535,14 +549,45 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
                  uint32_t* __restrict__ anc_bits, int anc_words,
                  const int64_t* __restrict__ root_token, int64_t start,
                  int64_t* __restrict__ verify_ids, int64_t* __restrict__ verify_pos,
-                 unsigned char* __restrict__ ws, int vec_ok) {
+                 unsigned char* __restrict__ ws, int vec_ok, const Batch batch) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ RadixShared rs;
-  const int C = gridDim.x / L;
-  const int d = blockIdx.x / C;
-  const int c = blockIdx.x % C;
   const int tid = threadIdx.x;
-  const WsLayout wl = ws_layout(L, V, k);
+  const int C = num_chunks(V);
+  const int r = blockIdx.x / (L * C);
+  const int d = (blockIdx.x / C) % L;
+  const int c = blockIdx.x % C;
+  int kmax = k;
+  if (batch.budgets) {  // request r of a batched launch
+    budget = batch.budgets[r];
+    if (budget > batch.nodes) budget = static_cast<int>(batch.nodes);  // stays in its slice
+    k = budget < V ? budget : static_cast<int>(V);
+    kmax = batch.kmax;
+    const int64_t nodes1 = batch.nodes + 1;
+    if (kBF16) logits = static_cast<const uint16_t*>(logits) + r * batch.logits;
+    else logits = static_cast<const float*>(logits) + r * batch.logits;
+    node_token_ids += r * batch.nodes;
+    node_depths += r * batch.nodes;
+    parents += r * nodes1;
+    node_count += r;
+    anc_bits += r * nodes1 * anc_words;
+    if (root_token) root_token += r;
+    if (batch.starts) start = batch.starts[r];
+    if (verify_ids) verify_ids += r * nodes1;
+    if (verify_pos) verify_pos += r * nodes1;
+    ws += r * batch.ws_bytes;
+    if (budget <= 0) {  // the empty tree (root only), written by the request's first CTA
+      if (d == 0 && c == 0 && tid == 0) {
+        parents[0] = -1;
+        *node_count = 0;
+        for (int w = 0; w < anc_words; ++w) anc_bits[w] = (w == 0) ? 1u : 0u;
+        if (verify_ids) verify_ids[0] = root_token ? *root_token : 0;
+        if (verify_pos) verify_pos[0] = start;
+      }
+      return;
+    }
+  }
+  const WsLayout wl = ws_layout(L, V, kmax);
   uint32_t* counters = reinterpret_cast<uint32_t*>(ws + wl.counters);
   float* chunk_max = reinterpret_cast<float*>(ws + wl.chunk_max);
   double* chunk_sum = reinterpret_cast<double*>(ws + wl.chunk_sum);
@@ -856,7 +901,7 @@ extern "C" int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths
         draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(k),
         static_cast<int>(budget), top_log_probs, top_token_ids, node_token_ids, node_depths,
         parents, node_count, anc_bits, static_cast<int>(anc_words), root_token, start,
-        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok);
+        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok, topk::Batch{});
   } else {
     auto kern = topk::topk_tree_kernel<false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -866,8 +911,67 @@ extern "C" int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths
         draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(k),
         static_cast<int>(budget), top_log_probs, top_token_ids, node_token_ids, node_depths,
         parents, node_count, anc_bits, static_cast<int>(anc_words), root_token, start,
-        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok);
+        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok, topk::Batch{});
   }
+  return launch_status();
+}
+
+// ---- batched: one launch builds the trees of many requests -----------------------------
+namespace {
+size_t batched_ws_slice(int64_t depths, int64_t vocab, int64_t max_budget) {
+  const int64_t k = max_budget < vocab ? max_budget : vocab;
+  return topk::align_up(topk::ws_layout(depths, vocab, k).total, 256);
+}
+}  // namespace
+
+extern "C" size_t ddt_topk_tree_batched_workspace_bytes(int64_t n_requests, int64_t depths,
+                                                        int64_t vocab, int64_t max_budget) {
+  if (n_requests <= 0 || depths <= 0 || vocab <= 0 || max_budget <= 0) return 256;
+  return static_cast<size_t>(n_requests) * batched_ws_slice(depths, vocab, max_budget);
+}
+
+extern "C" int ddt_topk_tree_batched(const void* draft_logits, int dtype, int64_t n_requests,
+                                     int64_t depths, int64_t vocab, int64_t row_stride,
+                                     int64_t request_stride, const int32_t* budgets,
+                                     int64_t max_budget, int64_t* node_token_ids,
+                                     int64_t* node_depths, int32_t* parents, int32_t* node_count,
+                                     uint32_t* anc_bits, int64_t anc_words,
+                                     const int64_t* root_tokens, const int64_t* starts,
+                                     int64_t* verify_ids, int64_t* verify_pos, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype != DDT_F32 && dtype != DDT_BF16) return DDT_ERR_DTYPE;
+  if (!draft_logits || !budgets || !node_token_ids || !node_depths || !parents || !node_count ||
+      !anc_bits || !workspace || n_requests < 0 || depths <= 0 || vocab <= 0 || max_budget <= 0)
+    return DDT_ERR_INVALID;
+  if (max_budget > DDT_MAX_BUDGET || depths > DDT_MAX_DEPTH) return DDT_ERR_CAPACITY;
+  if (anc_words * 32 < max_budget + 1) return DDT_ERR_INVALID;
+  if (row_stride < vocab || request_stride < depths * row_stride ||
+      vocab >= (int64_t(1) << 31))
+    return DDT_ERR_INVALID;
+  const int64_t kmax = max_budget < vocab ? max_budget : vocab;
+  const int C = topk::num_chunks(vocab);
+  if (static_cast<int64_t>(C) * kmax > topk::kMaxCand) return DDT_ERR_CAPACITY;
+  const size_t slice = batched_ws_slice(depths, vocab, max_budget);
+  if (workspace_bytes < slice * static_cast<size_t>(n_requests)) return DDT_ERR_WORKSPACE;
+  if (n_requests == 0) return DDT_OK;
+  if (static_cast<int64_t>(n_requests) * depths * C > 0x7fffffffLL) return DDT_ERR_CAPACITY;
+  const size_t esz = dtype == DDT_BF16 ? 2 : 4;
+  const int vec_ok = aligned(draft_logits, 16) && ((row_stride * esz) % 16 == 0) &&
+                     ((request_stride * esz) % 16 == 0) && ((vocab * esz) % 16 == 0);
+  const size_t smem = topk::smem_bytes(depths, kmax, max_budget);
+  const dim3 grid(static_cast<unsigned>(n_requests * depths * C));
+  const topk::Batch batch{request_stride, max_budget, slice, static_cast<int>(kmax), budgets,
+                          starts};
+  auto kern = dtype == DDT_BF16 ? topk::topk_tree_kernel<true> : topk::topk_tree_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return DDT_ERR_CUDA;
+  kern<<<grid, topk::kThreads, smem, st>>>(
+      draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(kmax),
+      static_cast<int>(max_budget), nullptr, nullptr, node_token_ids, node_depths, parents,
+      node_count, anc_bits, static_cast<int>(anc_words), root_tokens, 0, verify_ids, verify_pos,
+      static_cast<unsigned char*>(workspace), vec_ok, batch);
   return launch_status();
 }
 

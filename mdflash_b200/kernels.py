@@ -13,7 +13,7 @@ from ._lib import DDT_BF16, DDT_F32, DDT_MASK_CAUSAL, DDT_MASK_NONE, DDT_MASK_TR
 __all__ = [
     "DeviceTree", "expected_node_count", "topk_tree", "argmax", "accept_compact", "compact_kv",
     "tree_attention", "tree_attention_partial", "attn_merge", "mask_to_bits", "KvTable",
-    "anc_words_for", "attention_status", "check_status", "tree_attention_wait_check",
+    "anc_words_for", "TreeBatch", "topk_tree_batched", "attention_status", "check_status", "tree_attention_wait_check",
     "sample_chains", "chain_tree", "lm_head_argmax",
 ]
 
@@ -189,6 +189,86 @@ def topk_tree(draft_logits: torch.Tensor, budget: int, root_token: torch.Tensor 
     check(rc, "ddt_topk_tree")
     STATS.launches += 1
     return tree
+
+
+@dataclass
+class TreeBatch:
+    """The trees of a batched build (ddt_topk_tree_batched): request r's outputs are row r of
+    each [n_requests, ...] tensor; ``tree(r)`` views them as a DeviceTree."""
+    budgets: list[int]             # per request (host copy; the device copy is budgets_dev)
+    max_budget: int
+    depths: int
+    vocab: int
+    budgets_dev: torch.Tensor      # i32 [R]
+    starts: torch.Tensor           # i64 [R]
+    root_tokens: torch.Tensor      # i64 [R]
+    node_count: torch.Tensor       # i32 [R]
+    node_token_ids: torch.Tensor   # i64 [R, max_budget]
+    node_depths: torch.Tensor      # i64 [R, max_budget]
+    parents: torch.Tensor          # i32 [R, max_budget + 1]
+    anc_bits: torch.Tensor         # i32 [R, max_budget + 1, anc_words]
+    verify_ids: torch.Tensor       # i64 [R, max_budget + 1]
+    verify_pos: torch.Tensor       # i64 [R, max_budget + 1]
+
+    @staticmethod
+    def allocate(device, budgets: list[int], depths: int, vocab: int) -> "TreeBatch":
+        R = len(budgets)
+        mb = max([max(int(b), 0) for b in budgets] + [1])
+        i64 = dict(dtype=torch.int64, device=device)
+        return TreeBatch(
+            budgets=[max(int(b), 0) for b in budgets], max_budget=mb, depths=depths, vocab=vocab,
+            budgets_dev=torch.tensor([max(int(b), 0) for b in budgets], dtype=torch.int32,
+                                     device=device),
+            starts=torch.zeros(R, **i64), root_tokens=torch.zeros(R, **i64),
+            node_count=torch.zeros(R, dtype=torch.int32, device=device),
+            node_token_ids=torch.zeros((R, mb), **i64), node_depths=torch.zeros((R, mb), **i64),
+            parents=torch.zeros((R, mb + 1), dtype=torch.int32, device=device),
+            anc_bits=torch.zeros((R, mb + 1, anc_words_for(mb + 1)), dtype=torch.int32,
+                                 device=device),
+            verify_ids=torch.zeros((R, mb + 1), **i64), verify_pos=torch.zeros((R, mb + 1), **i64))
+
+    def tree(self, r: int) -> DeviceTree:
+        b = self.budgets[r]
+        k = min(b, self.vocab) if b > 0 else 0
+        dev = self.parents.device
+        return DeviceTree(
+            budget=b, depths=self.depths, k=k,
+            n_nodes=1 + expected_node_count(self.depths, self.vocab, b),
+            node_count=self.node_count[r:r + 1], node_token_ids=self.node_token_ids[r, :max(b, 1)],
+            node_depths=self.node_depths[r, :max(b, 1)], parents=self.parents[r, :b + 1],
+            anc_bits=self.anc_bits[r, :b + 1], verify_ids=self.verify_ids[r, :b + 1],
+            verify_pos=self.verify_pos[r, :b + 1],
+            # the batched build keeps no per-depth top-k tables
+            top_log_probs=torch.zeros((max(self.depths, 1), 0), dtype=torch.float32, device=dev),
+            top_token_ids=torch.zeros((max(self.depths, 1), 0), dtype=torch.int64, device=dev))
+
+
+def topk_tree_batched(draft_logits: torch.Tensor, out: TreeBatch) -> TreeBatch:
+    """ddt_topk_tree_batched: the tree of every request of ``draft_logits`` [R, depths, vocab]
+    in one launch, with out.budgets_dev, out.root_tokens and out.starts as inputs (fill them
+    before the call); request r's tree equals topk_tree(draft_logits[r], budgets[r],
+    root_tokens[r], starts[r])."""
+    if draft_logits.dim() != 3:
+        raise ValueError("draft_logits must be [requests, depths, vocab]")
+    dev = _require_cuda(draft_logits)
+    R, L, V = draft_logits.shape
+    if draft_logits.stride(2) != 1:
+        draft_logits = draft_logits.contiguous()
+    if R != len(out.budgets) or L != out.depths or V != out.vocab:
+        raise ValueError("TreeBatch was allocated for another request count / depth / vocabulary")
+    lib = _lib.load()
+    ws_bytes = lib.ddt_topk_tree_batched_workspace_bytes(R, L, V, out.max_budget)
+    ws = WORKSPACES.get(dev, "topk_tree_batched", ws_bytes)
+    check(lib.ddt_topk_tree_batched(
+        draft_logits.data_ptr(), _dtype_code(draft_logits), R, L, V, draft_logits.stride(1),
+        draft_logits.stride(0), out.budgets_dev.data_ptr(), out.max_budget,
+        out.node_token_ids.data_ptr(), out.node_depths.data_ptr(), out.parents.data_ptr(),
+        out.node_count.data_ptr(), out.anc_bits.data_ptr(), out.anc_bits.shape[2],
+        out.root_tokens.data_ptr(), out.starts.data_ptr(), out.verify_ids.data_ptr(),
+        out.verify_pos.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev)),
+        "ddt_topk_tree_batched")
+    STATS.launches += 1
+    return out
 
 
 def sample_chains(draft_logits: torch.Tensor, num_samples: int, temperature: float, seed: int,

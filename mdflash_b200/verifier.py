@@ -71,6 +71,14 @@ class TreeVerifier:
         if self.cache.get_seq_length() != start:
             raise RuntimeError(f"cache holds {self.cache.get_seq_length()} rows, expected {start}")
         tree = K.topk_tree(draft_logits, self.budget, root_token, start, out=self.tree)
+        return self.verify_tree(tree, start)
+
+    @torch.inference_mode()
+    def verify_tree(self, tree: K.DeviceTree, start: int) -> StepResult:
+        """The step after the tree build, for a tree built elsewhere (for instance one
+        request's tree of a batched build, K.topk_tree_batched) over the same prefix."""
+        if self.cache.get_seq_length() != start:
+            raise RuntimeError(f"cache holds {self.cache.get_seq_length()} rows, expected {start}")
         n = tree.n_nodes
         ids = tree.verify_ids[:n].view(1, n)
         pos = tree.verify_pos[:n].view(1, n)
@@ -108,24 +116,33 @@ class CapturedStep:
     object: copy new values in before ``replay``); outputs land in ``result``."""
 
     def __init__(self, verifier: TreeVerifier, start: int, warmup: int = 2,
-                 time_attention: bool = False, pool=None):
+                 time_attention: bool = False, pool=None, tree: K.DeviceTree | None = None):
+        """tree=None records the whole step (tree build from ``draft_logits``); a given tree
+        (built by the caller before each replay, e.g. by one batched build for many
+        requests) records the step from that tree on."""
         self.verifier = verifier
         self.start = start
         v = verifier
         self.draft_logits = torch.zeros((v.depths, v.vocab), dtype=torch.bfloat16, device=v.device)
         self.root_token = torch.zeros(1, dtype=torch.int64, device=v.device)
+
+        def run():
+            if tree is None:
+                return v.step(self.draft_logits, self.root_token, start)
+            return v.verify_tree(tree, start)
+
         side = torch.cuda.Stream(v.device)
         side.wait_stream(torch.cuda.current_stream(v.device))
         with torch.cuda.stream(side):
             for _ in range(warmup):
-                v.step(self.draft_logits, self.root_token, start)
+                run()
                 v.cache.crop(start)
         torch.cuda.current_stream(v.device).wait_stream(side)
         torch.cuda.synchronize(v.device)
         self.graph = torch.cuda.CUDAGraph()
         K.STATS.reset(time_attention=time_attention)
         with torch.cuda.graph(self.graph, pool=pool):
-            self.result = v.step(self.draft_logits, self.root_token, start)
+            self.result = run()
         self.launches_per_replay = K.STATS.launches
         self.attn_events = list(K.STATS.attn_events)
         K.STATS.reset()

@@ -73,6 +73,22 @@ def test_host_side_validation_rejects_bad_arguments():
     assert lib.ddt_lm_head_argmax(p, 128, p, 128, 8, 128, 1000, p, None, 0, p, 16, None,
                                   None) == -7
     assert lib.ddt_lm_head_argmax_workspace_bytes(257) >= 257 * 8 + 4
+    # batched tree build: budget / depth limits, per-request budgets required, a workspace of
+    # one slice per request
+    bt = lib.ddt_topk_tree_batched
+    assert bt(p, 1, 4, 15, 1000, 1000, 15000, p, 2000, p, p, p, p, p, 63, None, None, None,
+              None, p, 1 << 30, None) == -2
+    assert bt(p, 1, 4, 15, 1000, 1000, 15000, None, 64, p, p, p, p, p, 3, None, None, None,
+              None, p, 1 << 30, None) == -1
+    assert bt(p, 1, 4, 15, 1000, 1000, 100, p, 64, p, p, p, p, p, 3, None, None, None,
+              None, p, 1 << 30, None) == -1  # requests overlap
+    ws1 = lib.ddt_topk_tree_batched_workspace_bytes(1, 15, 1000, 64)
+    assert lib.ddt_topk_tree_batched_workspace_bytes(4, 15, 1000, 64) == 4 * ws1
+    assert ws1 >= lib.ddt_topk_tree_workspace_bytes(15, 1000, 64)
+    assert bt(p, 1, 4, 15, 1000, 1000, 15000, p, 64, p, p, p, p, p, 3, None, None, None,
+              None, p, 4 * ws1 - 1, None) == -7
+    assert bt(p, 1, 0, 15, 1000, 1000, 15000, p, 64, p, p, p, p, p, 3, None, None, None,
+              None, p, 0, None) == 0
     # fused elementwise stages: head_dim 128 only, a 16-byte aligned rope table, hidden up to
     # 16384 in multiples of 8
     assert lib.ddt_rope_table(p, 4, p, 64, 1.0, p, None) == -2
