@@ -98,8 +98,8 @@ int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths, int64_t v
  *     anc_bits [n_requests, max_budget + 1, anc_words]; node_count i32 [n_requests]
  *   root_tokens i64 [n_requests] (may be NULL: root token 0), starts i64 [n_requests]
  *     (may be NULL: every start 0); verify_ids / verify_pos may be NULL
- * The workspace (ddt_topk_tree_batched_workspace_bytes) must be zero-filled before its first
- * use; every launch leaves its counters at zero again. */
+ * The workspace (ddt_topk_tree_batched_workspace_bytes) needs no initialisation: the call
+ * zero-fills its per-request tickets (one cudaMemsetAsync on the stream) before the launch. */
 size_t ddt_topk_tree_batched_workspace_bytes(int64_t n_requests, int64_t depths, int64_t vocab,
                                              int64_t max_budget);
 int ddt_topk_tree_batched(const void* draft_logits, int dtype, int64_t n_requests,

@@ -531,6 +531,9 @@ __device__ int heap_build(const float* lp, int L, int k, int budget, Frontier f,
 // r * (nodes + 1) (parents, verify ids / positions, rows of anc_bits), its count at
 // node_count + r, and uses workspace slice r of ws_bytes.  budgets / starts / root tokens
 // are per-request device arrays when given.
+// The atomic tickets of all requests sit together at the start of the workspace
+// (counters + r * (depths + 1)); the entry point zero-fills them before every launch, so a
+// workspace can be reused whatever the shape of the previous launch.
 struct Batch {
   int64_t logits;
   int64_t nodes;
@@ -538,6 +541,7 @@ struct Batch {
   int kmax;
   const int32_t* budgets;
   const int64_t* starts;
+  uint32_t* counters;
 };
 
 template <bool kBF16>
@@ -588,7 +592,8 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
     }
   }
   const WsLayout wl = ws_layout(L, V, kmax);
-  uint32_t* counters = reinterpret_cast<uint32_t*>(ws + wl.counters);
+  uint32_t* counters = batch.budgets ? batch.counters + r * (L + 1)
+                                     : reinterpret_cast<uint32_t*>(ws + wl.counters);
   float* chunk_max = reinterpret_cast<float*>(ws + wl.chunk_max);
   double* chunk_sum = reinterpret_cast<double*>(ws + wl.chunk_sum);
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(ws + wl.cand);
@@ -922,12 +927,16 @@ size_t batched_ws_slice(int64_t depths, int64_t vocab, int64_t max_budget) {
   const int64_t k = max_budget < vocab ? max_budget : vocab;
   return topk::align_up(topk::ws_layout(depths, vocab, k).total, 256);
 }
+size_t batched_counter_bytes(int64_t n_requests, int64_t depths) {
+  return topk::align_up(sizeof(uint32_t) * static_cast<size_t>(n_requests * (depths + 1)), 256);
+}
 }  // namespace
 
 extern "C" size_t ddt_topk_tree_batched_workspace_bytes(int64_t n_requests, int64_t depths,
                                                         int64_t vocab, int64_t max_budget) {
   if (n_requests <= 0 || depths <= 0 || vocab <= 0 || max_budget <= 0) return 256;
-  return static_cast<size_t>(n_requests) * batched_ws_slice(depths, vocab, max_budget);
+  return batched_counter_bytes(n_requests, depths) +
+         static_cast<size_t>(n_requests) * batched_ws_slice(depths, vocab, max_budget);
 }
 
 extern "C" int ddt_topk_tree_batched(const void* draft_logits, int dtype, int64_t n_requests,
@@ -953,25 +962,28 @@ extern "C" int ddt_topk_tree_batched(const void* draft_logits, int dtype, int64_
   const int C = topk::num_chunks(vocab);
   if (static_cast<int64_t>(C) * kmax > topk::kMaxCand) return DDT_ERR_CAPACITY;
   const size_t slice = batched_ws_slice(depths, vocab, max_budget);
-  if (workspace_bytes < slice * static_cast<size_t>(n_requests)) return DDT_ERR_WORKSPACE;
+  const size_t cbytes = batched_counter_bytes(n_requests, depths);
   if (n_requests == 0) return DDT_OK;
+  if (workspace_bytes < cbytes + slice * static_cast<size_t>(n_requests)) return DDT_ERR_WORKSPACE;
   if (static_cast<int64_t>(n_requests) * depths * C > 0x7fffffffLL) return DDT_ERR_CAPACITY;
   const size_t esz = dtype == DDT_BF16 ? 2 : 4;
   const int vec_ok = aligned(draft_logits, 16) && ((row_stride * esz) % 16 == 0) &&
                      ((request_stride * esz) % 16 == 0) && ((vocab * esz) % 16 == 0);
   const size_t smem = topk::smem_bytes(depths, kmax, max_budget);
   const dim3 grid(static_cast<unsigned>(n_requests * depths * C));
+  unsigned char* wsb = static_cast<unsigned char*>(workspace);
   const topk::Batch batch{request_stride, max_budget, slice, static_cast<int>(kmax), budgets,
-                          starts};
+                          starts, reinterpret_cast<uint32_t*>(wsb)};
   auto kern = dtype == DDT_BF16 ? topk::topk_tree_kernel<true> : topk::topk_tree_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return DDT_ERR_CUDA;
+  if (cudaMemsetAsync(wsb, 0, cbytes, st) != cudaSuccess) return DDT_ERR_CUDA;
   kern<<<grid, topk::kThreads, smem, st>>>(
       draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(kmax),
       static_cast<int>(max_budget), nullptr, nullptr, node_token_ids, node_depths, parents,
       node_count, anc_bits, static_cast<int>(anc_words), root_tokens, 0, verify_ids, verify_pos,
-      static_cast<unsigned char*>(workspace), vec_ok, batch);
+      wsb + cbytes, vec_ok, batch);
   return launch_status();
 }
 
