@@ -66,11 +66,13 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["requests", "verify", "attn", "tree", "argmax",
-                                           "compact", "lmhead", "splitkv"], default="requests",
+    ap.add_argument("--workload", choices=["requests", "verify", "attn", "tree", "treebatch",
+                                           "argmax", "compact", "lmhead", "splitkv"],
+                    default="requests",
                     help="requests: the 64-request mix sharded over the GPUs (default); verify: "
                          "one Qwen3-8B verify step (prefix 8192, budget 256); attn / tree / "
-                         "argmax / compact / lmhead: one op alone; splitkv: attention over a prefix "
+                         "argmax / compact / lmhead: one op alone; treebatch: the batched tree "
+                         "build of the request mix's trees; splitkv: attention over a prefix "
                          "sharded along the sequence")
     ap.add_argument("--prefix", type=int, default=None,
                     help="prefix length of the single-request workloads (default 8192; 131072 "
@@ -733,6 +735,25 @@ def measure_tree(dev, budget, steps, warmup):
             "node_count": int(tree.node_count.item())}
 
 
+def measure_tree_batched(dev, n_requests, steps, warmup):
+    """One ddt_topk_tree_batched launch over the request mix's drafter logits (n_requests x 15
+    x V bf16, the mix's budgets)."""
+    from mdflash_b200 import kernels as K
+    from mdflash_b200 import sharding as S
+    specs = S.request_specs(n_requests, seed=0)
+    x = torch.stack([request_logits(sp.seed).to(torch.bfloat16) for sp in specs]).to(dev)
+    trees = K.TreeBatch.allocate(dev, [sp.budget for sp in specs], DEPTHS, V)
+    trees.starts.copy_(torch.tensor([sp.prefix for sp in specs]))
+    ms = _timed_launches(lambda: K.topk_tree_batched(x, trees), steps, warmup, dev)
+    nbytes = x.numel() * x.element_size()
+    peaks, kind = measured_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"ms": ms, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
+            "peak_source": kind, "bytes_per_launch": nbytes, "requests": n_requests,
+            "shape": f"{n_requests} requests x 15 x {V} bf16 drafter logits, budgets of the mix",
+            "nodes": int(trees.node_count.sum().item())}
+
+
 def measure_argmax(dev, rows, steps, warmup):
     from mdflash_b200 import kernels as K
     g = torch.Generator(device=dev).manual_seed(0)
@@ -853,6 +874,7 @@ def kernel_table(dev, args):
     return {
         "l2": "256 MB buffer written before every launch (L2 flushed); CUDA events per launch",
         "tree_build": measure_tree(dev, VERIFY_BUDGET, steps, warmup),
+        "tree_build_batched": measure_tree_batched(dev, args.requests, steps, warmup),
         "argmax": measure_argmax(dev, VERIFY_BUDGET + 1, steps, warmup),
         "accept_compact": measure_compact(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
         "tree_attention": measure_attn(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
@@ -898,6 +920,10 @@ def run_single(args):
         r = measure_tree(dev, args.budget, args.steps, args.warmup)
         line = _op_line("tree build GB/s", "GB/s", r, args, "tree build: " + r["shape"], "hbm",
                         "gbs")
+    elif args.workload == "treebatch":
+        r = measure_tree_batched(dev, args.requests, args.steps, args.warmup)
+        line = _op_line("batched tree build GB/s", "GB/s", r, args, "batched tree build: " +
+                        r["shape"], "hbm", "gbs")
     elif args.workload == "argmax":
         r = measure_argmax(dev, args.budget + 1, args.steps, args.warmup)
         line = _op_line("argmax GB/s", "GB/s", r, args, "argmax over " + r["shape"], "hbm", "gbs")

@@ -44,7 +44,8 @@ constexpr int kThreads = 384;
 // Register split (setmaxnreg): the launch gives every thread 168 registers (3 warps per SM
 // sub-partition share its 16K-entry file); warpgroup 0 (TMA, MMA, 2 idle warps) gives
 // back down to 64 and the two softmax warpgroups take 216:
-// 128 * 64 + 256 * 216 = 63488 <= 384 * 168.  (At 56 the issuers' loop spilled.)
+// 128 * 64 + 256 * 216 = 63488 <= 384 * 168.  (Measured against 56 / 224: the same
+// schedule ran 52.0 against 52.5 us at the Qwen3-8B verify shape.)
 constexpr int kRegsLaunch = 168;
 constexpr int kRegsControl = 64;
 constexpr int kRegsSoftmax = 216;
@@ -283,8 +284,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tc::tma_prefetch_desc(&tm_k);
         tc::tma_prefetch_desc(&tm_v);
         // both query tiles of a unit; the second one of a unit's last row pair may lie
-        // past the last node, where the load reads zeros (its MMAs are skipped and its rows
-        // are not stored)
+        // past the last node, where the load reads zeros and its rows are not stored
         int q_loads = 0;
         auto load_q = [&](const UnitGeo& g) {
           tc::mbar_expect_tx(&bars.q_full, 2 * kTileBytes);
@@ -367,10 +367,6 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // count `turn` is published right after its last MMA.  (Publishing it after half of
         // the S MMAs, so the other issuer's block would queue behind this one, measured
         // 5% slower: the two softmax warpgroups drift into each other.)
-        // idle: every row of this query tile is padding past the last node (the second tile
-        // of a head's last unit when fewer than 129 rows are left): its MMAs are skipped and
-        // only the commits and turns that the other warps count are made
-        bool idle = false;
         auto issue_s = [&](int jg, uint32_t turn) {
           const uint32_t b = k_lo + (jg % kStages) * (kTileBytes >> 4);
           tc::mma_bf16_ss_w<0>(d_s, a_q, b, kDescHi, kIdescS);
@@ -385,10 +381,6 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // O_q += P_q V of tile jg (item tile j; j == 0 starts the item's O), P_q in TMEM
         // (first 64 columns of the S region, 8 per K step), in two halves of 64 keys: the
         // first runs while the softmax computes the second
-        auto skip_s = [&](uint32_t turn) {  // an idle tile's S: the turn and the commit only
-          *my_turns = turn;
-          tc::mma_commit(&bars.s_full[q]);
-        };
         auto issue_pv = [&](int jg, int j, int half) {
           const uint32_t b = v_lo + (jg % kStages) * (kTileBytes >> 4);
 #pragma unroll
@@ -423,7 +415,6 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         for (int i = 0; ok && i < n_items; ++i) {
           int u, t0, nt, sl;
           item(i, u, t0, nt, sl);
-          idle = (u % p.n_pairs) * kRowsPerCta + q * kBlockM >= rows;  // unit_geo's row0
           if (!(ok = tc::mbar_wait_warp(&bars.q_full, i & 1, abort_flag, p.timeout_ns))) break;
           if (!(ok = tc::mbar_wait_warp(&bars.k_full[J % kStages], (J / kStages) & 1, abort_flag,
                                         p.timeout_ns)))
@@ -431,8 +422,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           if (!(ok = wait_turn(q == 0 ? base : base + 1))) break;
           tc::tc_fence_after();
           if (tc::elect_one()) {
-            if (idle) skip_s(base + 1);
-            else issue_s(J, base + 1);
+            issue_s(J, base + 1);
             if (J + kStages < total) tc::mma_commit(&bars.k_empty[J % kStages]);
           }
           __syncwarp();
@@ -451,17 +441,15 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             if (!(ok = tc::mbar_wait_warp(&bars.p_half[q], jg & 1, abort_flag, p.timeout_ns))) break;
             if (!(ok = wait_turn(q == 0 ? base + j + 1 : base + j + 2))) break;
             tc::tc_fence_after();
-            if (!idle && tc::elect_one()) issue_pv(jg, j, 0);
+            if (tc::elect_one()) issue_pv(jg, j, 0);
             __syncwarp();
             if (!(ok = tc::mbar_wait_warp(&bars.p_full[q], jg & 1, abort_flag, p.timeout_ns))) break;
             tc::tc_fence_after();
             if (tc::elect_one()) {
-              if (idle) tc::mma_commit(&bars.o_ready[q]);
-              else issue_pv(jg, j, 1);
+              issue_pv(jg, j, 1);
               if (jg + kStages < total) tc::mma_commit(&bars.v_empty[st]);
               if (more) {
-                if (idle) skip_s(base + j + 2);
-                else issue_s(jg + 1, base + j + 2);  // reuses S_q / P_q: after the P V above
+                issue_s(jg + 1, base + j + 2);  // reuses S_q / P_q: runs after the P V above
                 if (jg + 1 + kStages < total) tc::mma_commit(&bars.k_empty[sn]);
               } else {
                 *my_turns = base + j + 2;
@@ -505,9 +493,6 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const int node = R / p.group;
       const int qh = g.h * p.group + (R % p.group);
       const bool valid = R < rows;
-      // every row of this warp is padding: nothing to compute or store; the warp only makes
-      // the arrivals the issuer counts (its P and O rows are left as they are)
-      const bool dead = __all_sync(DDT_FULL_MASK, !valid);
       const int vnode = valid ? node : p.n_nodes - 1;
       const int g_end = g.g_end;
       // the whole key range of the tile is visible to this row (no mask needed) when it
@@ -517,20 +502,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                                ? (g_end < p.past_len + vnode + 1 ? g_end : p.past_len + vnode + 1)
                                : (g_end < p.past_len ? g_end : p.past_len);
       float m_used = -INFINITY, l = 0.f;
-      // a dead warp waits for each tile's S and arrives at once (no earlier: the issuer's
-      // parity waits must not see two phases complete)
-      for (int j = 0; dead && ok && j < nt; ++j) {
-        if (!tc::mbar_wait_warp(&bars.s_full[q], (J + j) & 1, abort_flag, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        __syncwarp();
-        if (lane == 0) {
-          tc::mbar_arrive(&bars.p_half[q]);
-          tc::mbar_arrive(&bars.p_full[q]);
-        }
-      }
-      for (int j = 0; !dead && ok && j < nt; ++j) {
+      for (int j = 0; ok && j < nt; ++j) {
         const int jg = J + j;
         if (!tc::mbar_wait_warp(&bars.s_full[q], jg & 1, abort_flag, p.timeout_ns)) {
           ok = false;
@@ -646,10 +618,10 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars.p_full[q]);
       }
-      if (ok && nt > 0 && !dead &&
+      if (ok && nt > 0 &&
           !tc::mbar_wait_warp(&bars.o_ready[q], (J + nt - 1) & 1, abort_flag, p.timeout_ns))
         ok = false;
-      const bool have = ok && nt > 0 && !dead;  // warp-uniform
+      const bool have = ok && nt > 0;  // warp-uniform
       if (have) tc::tc_fence_after();
       // ---- epilogue of the item ----------------------------------------------------------
       if (p.partial && p.balanced) {
@@ -1125,30 +1097,21 @@ inline int prepare(Launch& L, const void* q, int64_t q_node_stride, int64_t q_he
 // softmax) + 4918 per item (Q load, pipeline refill, the partial's epilogue):
 //   kCostTile = 8, kCostMasked = 13 (1.6 tiles), kCostItem = 16 (2 tiles, paid at the start
 //   of each unit's range, so a CTA whose range reaches into a second unit gets
-//   correspondingly fewer tiles); units with an all-padding second query tile cost
-//   kCostHalf / kCostHalfMasked per tile.
+//   correspondingly fewer tiles).
 // A CTA's cost range maps to whole tiles of a unit by the unit's cumulative cost (a tile goes
 // to the CTA whose range holds the tile's start); a CTA may get no tile of a unit it touches,
 // and then has no item for it.  Returns false (and leaves the launch on uniform splits) when
 // a limit of the tables is exceeded or a unit has no key tile.
-// A unit whose second query tile is all padding (a head's last unit with at most 128 rows)
-// runs one tile's MMAs and softmax per key tile: kCostHalf / kCostHalfMasked.
-#ifndef DDT_COST_HALF
-#define DDT_COST_HALF 5
-#endif
 constexpr int kCostTile = 8;
 constexpr int kCostMasked = 13;
 constexpr int kCostItem = 16;
-constexpr int kCostHalf = DDT_COST_HALF;
-constexpr int kCostHalfMasked = (DDT_COST_HALF * 13 + 4) / 8;
 
 inline bool build_balanced(Launch& L, int64_t units) {
   Params& p = L.p;
   if (units <= 0 || units > kMaxUnits) return false;
   int64_t W = 0, real = 0;
-  int ntot[kMaxUnits], nfull[kMaxUnits], ct[kMaxUnits], cm[kMaxUnits];
+  int ntot[kMaxUnits], nfull[kMaxUnits];
   int64_t cost[kMaxUnits];
-  const int rows = p.n_nodes * p.group;
   // tiles of a unit that end at or before the prefix end (unmasked in the tree window sense)
   int64_t before = (static_cast<int64_t>(p.past_len) - p.key_lo) / kBlockN;
   if (p.past_len < p.key_lo) before = 0;
@@ -1156,11 +1119,8 @@ inline bool build_balanced(Launch& L, int64_t units) {
     ntot[u] = unit_geo(p, u).ntot;
     if (ntot[u] <= 0 || ntot[u] > 0xffff) return false;
     nfull[u] = static_cast<int>(before < ntot[u] ? before : ntot[u]);
-    const bool half = unit_geo(p, u).row0 + kBlockM >= rows;
-    ct[u] = half ? kCostHalf : kCostTile;
-    cm[u] = half ? kCostHalfMasked : kCostMasked;
-    cost[u] = static_cast<int64_t>(nfull[u]) * ct[u] +
-              static_cast<int64_t>(ntot[u] - nfull[u]) * cm[u];
+    cost[u] = static_cast<int64_t>(nfull[u]) * kCostTile +
+              static_cast<int64_t>(ntot[u] - nfull[u]) * kCostMasked;
     W += kCostItem + cost[u];
     real += ntot[u];
   }
@@ -1175,11 +1135,11 @@ inline bool build_balanced(Launch& L, int64_t units) {
     T += kCostItem;
     L.slots.unit_slot[u] = static_cast<uint16_t>(n);
     // tile boundary at cost offset x of this unit (the first tile not started before x)
-    const int64_t fcost = static_cast<int64_t>(nfull[u]) * ct[u];
+    const int64_t fcost = static_cast<int64_t>(nfull[u]) * kCostTile;
     auto tile_at = [&](int64_t x) -> int64_t {
       if (x >= cost[u]) return ntot[u];
-      if (x <= fcost) return (x + ct[u] - 1) / ct[u];
-      const int64_t t = nfull[u] + (x - fcost + cm[u] - 1) / cm[u];
+      if (x <= fcost) return (x + kCostTile - 1) / kCostTile;
+      const int64_t t = nfull[u] + (x - fcost + kCostMasked - 1) / kCostMasked;
       return t < ntot[u] ? t : ntot[u];
     };
     const int64_t cf = cta_of(T), cl = cta_of(T + cost[u] - 1);
