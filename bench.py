@@ -36,6 +36,7 @@ the mix per step, as many steps as fit a time budget (reported).
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -92,6 +93,10 @@ def parse_args():
                     help="requests workload: one batched tree-build launch for all of a rank's "
                          "requests per step (default), or one tree build inside each request's "
                          "graph")
+    ap.add_argument("--lanes", type=int, default=1,
+                    help="requests workload: replay the per-request graphs on this many streams "
+                         "at once (request j on stream j mod lanes; each lane has its own graph "
+                         "pool and scratch buffers)")
     ap.add_argument("--fused", type=int, default=1,
                     help="1: verify forward through the fused Qwen3 runner (default); 0: through "
                          "transformers' Qwen3 with the ddtree_tree attention plug-in")
@@ -422,7 +427,10 @@ def run_requests(args):
     specs = S.request_specs(args.requests, seed=0)
     assignment = S.assign_requests([S.request_cost(s) for s in specs], world)
     mine = assignment[rank]
-    pool = torch.cuda.graph_pool_handle()
+    lanes = max(1, args.lanes)
+    pools = [torch.cuda.graph_pool_handle() for _ in range(lanes)]
+    streams = [torch.cuda.Stream(dev) for _ in range(lanes)] if lanes > 1 else None
+    cap_streams = [torch.cuda.Stream(dev) for _ in range(lanes)] if lanes > 1 else None
     caps = []
     g = torch.Generator(device=dev).manual_seed(rank)
     batched = args.tree_build == "batched"
@@ -445,8 +453,9 @@ def run_requests(args):
             QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
         _fill_prefix(cache, sp.prefix, g)  # the verify work does not depend on the K / V values
         ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
-        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pool,
-                           tree=trees.tree(j) if batched else None)
+        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pools[j % lanes],
+                           tree=trees.tree(j) if batched else None, lane=j % lanes,
+                           capture_stream=cap_streams[j % lanes] if cap_streams else None)
         cap.draft_logits.copy_(dev_logits[j])
         cap.root_token.copy_(trees.root_tokens[j:j + 1])
         caps.append((sp, cap))
@@ -461,16 +470,24 @@ def run_requests(args):
             trees.root_tokens.copy_(host_roots, non_blocking=True)
         if batched and caps:
             K.topk_tree_batched(dev_logits, trees)
+        main = torch.cuda.current_stream(dev)
+        if streams:
+            for st in streams:
+                st.wait_stream(main)
         for j, (sp, cap) in enumerate(caps):
-            if e2e and not batched:
-                cap.draft_logits.copy_(host_logits[j], non_blocking=True)
-                cap.root_token.copy_(host_roots[j:j + 1], non_blocking=True)
-            r = cap.replay()
-            # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
-            records[j, 3] = r.n_accepted[0]
-            records[j, 4] = r.next_token[0]
-            m = min(S.MAX_PATH, r.n_nodes)
-            records[j, 6:6 + m] = r.accepted[:m]
+            with torch.cuda.stream(streams[j % lanes] if streams else main):
+                if e2e and not batched:
+                    cap.draft_logits.copy_(host_logits[j], non_blocking=True)
+                    cap.root_token.copy_(host_roots[j:j + 1], non_blocking=True)
+                r = cap.replay()
+                # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
+                records[j, 3] = r.n_accepted[0]
+                records[j, 4] = r.next_token[0]
+                m = min(S.MAX_PATH, r.n_nodes)
+                records[j, 6:6 + m] = r.accepted[:m]
+        if streams:
+            for st in streams:
+                main.wait_stream(st)
         return S.gather_results(records)
 
     def check_statuses():
@@ -537,6 +554,9 @@ def run_requests(args):
                 "ms_per_step": e2e_ms},
         "gpu_launches": int(sums[1].item()),
         "tokens_per_step": tokens,
+        # digest of the gathered result records (accepted paths, next tokens): equal across
+        # --lanes / --tree-build settings, since every request's step is deterministic
+        "records_digest": hashlib.sha1(allrec.numpy().tobytes()).hexdigest()[:16],
         "requests_per_rank": [len(a) for a in assignment],
         "step_roofline": {"bound": "max(HBM: weights + prefix K/V once, bf16 FLOPs) per request, "
                                    "the slowest rank's requests back to back",
@@ -548,6 +568,7 @@ def run_requests(args):
                       "forward, argmax, accept walk + compaction)") +
                      "; records all-gathered per step",
         "tree_build": args.tree_build,
+        "lanes": lanes,
     }
     del caps
     torch.cuda.synchronize()

@@ -2,6 +2,7 @@
 the current CUDA stream of the tensors' device and never synchronise the host."""
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 
@@ -63,21 +64,38 @@ def _require_cuda(*ts: torch.Tensor) -> torch.device:
 
 
 class _Workspaces:
-    """Per-device scratch buffers, grown on demand and zero-filled when (re)allocated."""
+    """Per-device scratch buffers, grown on demand and zero-filled when (re)allocated.
+
+    A buffer that is outgrown is kept alive, not freed: CUDA graphs captured earlier still
+    hold its address, and freed memory could be handed to another tensor.  Buffers are also
+    keyed by the current lane (``lane``): graphs that may replay concurrently on different
+    streams are captured in different lanes, so they share no scratch."""
 
     def __init__(self):
-        self._bufs: dict[tuple[int, str], torch.Tensor] = {}
+        self._bufs: dict[tuple[int, str, int], torch.Tensor] = {}
+        self._retired: list[torch.Tensor] = []
+        self.current_lane = 0
 
     def get(self, device: torch.device, name: str, nbytes: int) -> torch.Tensor:
-        key = (device.index if device.index is not None else torch.cuda.current_device(), name)
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        key = (idx, name, self.current_lane)
         buf = self._bufs.get(key)
         if buf is None or buf.numel() < nbytes:
             nb = max(nbytes, 256)
             if buf is not None:
                 nb = max(nb, 2 * buf.numel())
+                self._retired.append(buf)
             buf = torch.zeros(nb, dtype=torch.uint8, device=device)
             self._bufs[key] = buf
         return buf
+
+    @contextlib.contextmanager
+    def lane(self, lane: int):
+        prev, self.current_lane = self.current_lane, int(lane)
+        try:
+            yield
+        finally:
+            self.current_lane = prev
 
 
 WORKSPACES = _Workspaces()
@@ -86,7 +104,8 @@ WORKSPACES = _Workspaces()
 def attention_status(device: torch.device) -> torch.Tensor:
     """The device's default status word (i32 [1]) of tree-attention launches that are given
     none: a bounded wait of the kernel that ran out sets it non-zero."""
-    return WORKSPACES.get(device, "attn_status", 256)[:4].view(torch.int32)
+    with WORKSPACES.lane(0):  # one status word per device, whatever lane a launch runs in
+        return WORKSPACES.get(device, "attn_status", 256)[:4].view(torch.int32)
 
 
 def check_status(status: torch.Tensor, what: str = "ddt_tree_attn") -> None:

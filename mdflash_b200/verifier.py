@@ -116,10 +116,14 @@ class CapturedStep:
     object: copy new values in before ``replay``); outputs land in ``result``."""
 
     def __init__(self, verifier: TreeVerifier, start: int, warmup: int = 2,
-                 time_attention: bool = False, pool=None, tree: K.DeviceTree | None = None):
+                 time_attention: bool = False, pool=None, tree: K.DeviceTree | None = None,
+                 lane: int = 0, capture_stream: torch.cuda.Stream | None = None):
         """tree=None records the whole step (tree build from ``draft_logits``); a given tree
         (built by the caller before each replay, e.g. by one batched build for many
-        requests) records the step from that tree on."""
+        requests) records the step from that tree on.  Steps that may replay concurrently
+        (on different streams) need different ``lane`` numbers, graph pools and capture
+        streams: the lane selects this package's scratch buffers, the capture stream the
+        library GEMMs' (cuBLAS keeps one workspace per stream)."""
         self.verifier = verifier
         self.start = start
         v = verifier
@@ -133,16 +137,17 @@ class CapturedStep:
 
         side = torch.cuda.Stream(v.device)
         side.wait_stream(torch.cuda.current_stream(v.device))
-        with torch.cuda.stream(side):
-            for _ in range(warmup):
-                run()
-                v.cache.crop(start)
-        torch.cuda.current_stream(v.device).wait_stream(side)
-        torch.cuda.synchronize(v.device)
-        self.graph = torch.cuda.CUDAGraph()
-        K.STATS.reset(time_attention=time_attention)
-        with torch.cuda.graph(self.graph, pool=pool):
-            self.result = run()
+        with K.WORKSPACES.lane(lane):
+            with torch.cuda.stream(side):
+                for _ in range(warmup):
+                    run()
+                    v.cache.crop(start)
+            torch.cuda.current_stream(v.device).wait_stream(side)
+            torch.cuda.synchronize(v.device)
+            self.graph = torch.cuda.CUDAGraph()
+            K.STATS.reset(time_attention=time_attention)
+            with torch.cuda.graph(self.graph, pool=pool, stream=capture_stream):
+                self.result = run()
         self.launches_per_replay = K.STATS.launches
         self.attn_events = list(K.STATS.attn_events)
         K.STATS.reset()
