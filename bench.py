@@ -5,10 +5,13 @@ Default workload, at every GPU count (one process per GPU under torchrun): a bat
 independent requests on a random-init Qwen3-8B-shaped target (36 layers, hidden 4096,
 32 q / 8 kv heads, head_dim 128, MLP 12288, vocab 151936, bf16).  Prefix lengths are
 log-uniform in 1k..32k, tree budgets uniform over {64, 128, 256, 512}, drafter logits
-seeded per request (15 depths of N(0,1)*3).  A "step" verifies every request once: tree
-build -> tree-attention verify forward -> greedy posterior -> accept walk -> KV compaction,
-one CUDA-graph replay per request, then the result records are all-gathered.  Requests are
-assigned to ranks by longest-processing-time first; there is no other cross-GPU traffic.
+seeded per request (15 depths of N(0,1)*3).  A "step" verifies every request once: one
+batched tree-build launch for all of the rank's requests, then per request a CUDA-graph
+replay of the tree-attention verify forward -> greedy posterior -> accept walk -> KV
+compaction, the replays spread over 4 streams (--lanes) so that one request's launch gaps
+and kernel tails are filled by another's work; then the result records are all-gathered.
+Requests are assigned to ranks by longest-processing-time first; there is no other
+cross-GPU traffic.
 Metric: verified + accepted tokens per second over all GPUs.
 
   value      inputs resident in HBM; K steps bracketed by a barrier + synchronize, CUDA
@@ -31,7 +34,8 @@ Metric: verified + accepted tokens per second over all GPUs.
 
 --impl reference: that CPU path alone on this host's cores (rank 0 only), one request of
 the mix per step, as many steps as fit a time budget (reported).
---workload verify / attn / tree / argmax / compact / splitkv: one sub-workload alone.
+--workload verify / attn / tree / treebatch / argmax / compact / lmhead / splitkv: one
+sub-workload alone.
 """
 from __future__ import annotations
 
@@ -93,7 +97,7 @@ def parse_args():
                     help="requests workload: one batched tree-build launch for all of a rank's "
                          "requests per step (default), or one tree build inside each request's "
                          "graph")
-    ap.add_argument("--lanes", type=int, default=1,
+    ap.add_argument("--lanes", type=int, default=4,
                     help="requests workload: replay the per-request graphs on this many streams "
                          "at once (request j on stream j mod lanes; each lane has its own graph "
                          "pool and scratch buffers)")
