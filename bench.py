@@ -101,6 +101,9 @@ def parse_args():
                     help="requests workload: replay the per-request graphs on this many streams "
                          "at once (request j on stream j mod lanes; each lane has its own graph "
                          "pool and scratch buffers)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="splitkv workload: partials travel over NVLink peer memory "
+                         "(PeerExchange, default) or in an NCCL all-gather")
     ap.add_argument("--fused", type=int, default=1,
                     help="1: verify forward through the fused Qwen3 runner (default); 0: through "
                          "transformers' Qwen3 with the ddtree_tree attention plug-in")
@@ -967,9 +970,9 @@ def run_single(args):
 def run_splitkv(args):
     """Tree attention over one 131072-key prefix (Hq 32 / Hkv 8, D 128, 513 tree rows of a
     seeded random tree) whose K/V are sharded along the sequence across the GPUs: each rank
-    computes the partial (O, m, l) of its shard, one NCCL all-gather exchanges them and
-    ddt_attn_merge combines them; the last rank owns the tree keys and compacts the accepted
-    path inside its shard.  The exchange and merge are timed apart from the shard's
+    computes the partial (O, m, l) of its shard, the partials are exchanged (NVLink peer
+    stores into every rank's buffer, or --exchange nccl: one all-gather) and merged; the last
+    rank owns the tree keys and compacts the accepted path inside its shard.  The exchange and merge are timed apart from the shard's
     attention (CUDA events on the step stream)."""
     import torch.distributed as dist
 
@@ -1001,6 +1004,7 @@ def run_splitkv(args):
         path.append(int(parents[path[-1]]))
     keep = torch.tensor(path[::-1], dtype=torch.int64, device=dev)
     table = K.KvTable([k, v])
+    xchg = S.PeerExchange(n, 32, dev) if args.exchange == "peer" else None
 
     def step(events=None):
         if events:
@@ -1008,8 +1012,11 @@ def run_splitkv(args):
         o, m, l = K.tree_attention_partial_merged(q, k, v, kb, ke, bits, P)
         if events:
             events[1].record()
-        og, mg, lg = S.gather_partials(o, m, l)
-        K.attn_merge(og, mg, lg, n, 32, out=out)
+        if xchg is not None:
+            xchg.exchange_merge(o, m, l, out=out)
+        else:
+            og, mg, lg = S.gather_partials(o, m, l)
+            K.attn_merge(og, mg, lg, n, 32, out=out)
         if events:
             events[2].record()
         if owner:  # compaction of the accepted path on the rank holding the tree keys
@@ -1051,7 +1058,10 @@ def run_splitkv(args):
         "config": {"workload": f"split-KV tree attention: prefix {P} sharded over {world} GPUs, "
                                f"{n} tree rows, Hq 32 / Hkv 8, D 128; compaction of a "
                                f"{len(path)}-row path on the owner shard",
-                   "exchange": "NCCL all-gather of fp32 (O, m, l) partials + ddt_attn_merge",
+                   "exchange": ("NVLink peer stores of fp32 (O, m, l) partials into every "
+                                "rank's buffer (ddt_peer_push) + counter wait and merge "
+                                "(ddt_peer_merge)" if xchg is not None else
+                                "NCCL all-gather of fp32 (O, m, l) partials + ddt_attn_merge"),
                    "partial_bytes_received_per_rank": link_bytes},
         "split": {"shard_attention_ms": shard_ms, "exchange_and_merge_ms": xchg_ms,
                   "note": "max over ranks of each part; the rest of ms_per_step is the owner's "
@@ -1060,6 +1070,8 @@ def run_splitkv(args):
                      "unit": "TFLOP/s per GPU", "frac": tflops / world / peaks["bf16_tflops"],
                      "peak_source": f"{kind} bf16 burst", "flops_per_step": flops},
     }
+    if xchg is not None:
+        xchg.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -290,6 +290,30 @@ int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_pa
                    int64_t n_parts, int64_t n_nodes, int64_t q_heads, int64_t head_dim,
                    void* out, int64_t o_node_stride, int64_t o_head_stride, void* stream);
 
+/* ---- split-KV exchange over NVLink peer memory (one node, up to 8 ranks) --------------
+ * No counterpart in the reference.  Replaces the NCCL all-gather of the ranks' partials:
+ * every rank allocates one receive buffer (ddt_peer_alloc: cudaMalloc, zeroed, and its
+ * 64-byte CUDA IPC handle), the handles are exchanged over the process group, and every rank
+ * opens the others' (ddt_peer_open).  Per call (epoch e = 1, 2, ..., the same on all ranks):
+ * ddt_peer_push writes this rank's partial (O fp32 [rows, 128], m, l; rows = n_nodes *
+ * q_heads) into slot `rank` of every buffer (peer_bases: host array of world pointers, this
+ * rank's own buffer at index rank) and then bumps counter `rank` of each; ticket is a device
+ * u32, zero before the first call, that every push leaves at zero.  ddt_peer_merge waits until
+ * every rank's counter in the local buffer has reached e (bounded by timeout_ns, 100 us to
+ * 2 s; on expiry it sets *status non-zero and the output is incomplete), then merges the world
+ * partials like ddt_attn_merge.  Two parities of the buffer alternate between calls. */
+size_t ddt_peer_buffer_bytes(int64_t world, int64_t n_nodes, int64_t q_heads, int64_t head_dim);
+int ddt_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int ddt_peer_open(const void* ipc_handle, void** ptr);
+int ddt_peer_close(void* ptr);
+int ddt_peer_free(void* ptr);
+int ddt_peer_push(const float* o, const float* m, const float* l, int64_t n_nodes,
+                  int64_t q_heads, int64_t head_dim, void* const* peer_bases, int64_t world,
+                  int64_t rank, uint32_t epoch, uint32_t* ticket, void* stream);
+int ddt_peer_merge(const void* local_base, int64_t world, int64_t n_nodes, int64_t q_heads,
+                   int64_t head_dim, uint32_t epoch, void* out, int64_t o_node_stride,
+                   int64_t o_head_stride, int32_t* status, uint64_t timeout_ns, void* stream);
+
 /* ---- fused elementwise stages of the Qwen3 verify forward (bf16) ----------
  * ddt_add_rmsnorm: r = x + delta (delta may be NULL), writes r to residual_out (may be
  *   NULL, may alias x) and weight * rmsnorm(r) to norm_out; rows x hidden, hidden a

@@ -61,6 +61,14 @@ SIGNATURES = {
     "ddt_tree_attn_wait_check": (_i, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _I, ctypes.c_uint64, _P,
                                       _P]),
     "ddt_attn_merge": (_i, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P]),
+    "ddt_peer_buffer_bytes": (_S, [_I, _I, _I, _I]),
+    "ddt_peer_alloc": (_i, [_S, _P, _P]),
+    "ddt_peer_open": (_i, [_P, _P]),
+    "ddt_peer_close": (_i, [_P]),
+    "ddt_peer_free": (_i, [_P]),
+    "ddt_peer_push": (_i, [_P, _P, _P, _I, _I, _I, _P, _I, _I, ctypes.c_uint32, _P, _P]),
+    "ddt_peer_merge": (_i, [_P, _I, _I, _I, _I, ctypes.c_uint32, _P, _I, _I, _P, ctypes.c_uint64,
+                            _P]),
     "ddt_mask_to_bits": (_i, [_P, _i, _I, _I, _P, _I, _P]),
     "ddt_add_rmsnorm": (_i, [_P, _P, _P, _I, _I, _F, _P, _P, _P]),
     "ddt_qk_norm_rope_cache": (_i, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _F, _P, _P, _P, _I, _I,

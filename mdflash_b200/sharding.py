@@ -13,11 +13,15 @@ split-KV exchange:
   contiguous, 128-key-aligned shards; the last rank also owns the tree rows (so it is the
   rank that runs the compaction).  Every rank computes one partial (O, m, l) per row over
   its keys with ``ddt_tree_attn_partial_merged`` (the shard's tiles spread over all SMs and
-  merged in-GPU); all-gathers straight into the merge layout and ``ddt_attn_merge`` give
-  every rank the full attention output.
+  merged in-GPU).  The partials then travel over NVLink peer memory (``PeerExchange``: every
+  rank stores its partial straight into every rank's receive buffer and bumps a counter
+  there; each rank waits for all counters and merges) or, without one, in an NCCL
+  all-gather straight into the merge layout; ``ddt_attn_merge`` gives every rank the full
+  attention output.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -183,16 +187,112 @@ def gather_partials(o: torch.Tensor, m: torch.Tensor, l: torch.Tensor, group=Non
     return tuple(out)
 
 
+class PeerExchange:
+    """Receive buffers in NVLink peer memory for the split-KV partials of ``n_nodes`` tree
+    rows x ``q_heads`` heads, one per rank of ``group`` (all on one node, at most 8), opened by
+    every other rank through CUDA IPC handles that travel over the process group.
+
+    ``exchange_merge(o, m, l)`` pushes this rank's partial into every rank's buffer
+    (ddt_peer_push: 16-byte stores over NVLink, then one counter increment per buffer) and
+    merges the world partials of its own buffer once every rank's push has landed
+    (ddt_peer_merge, a bounded wait).  Every rank makes the same calls in the same order.
+    Without an initialised process group the world is this one rank."""
+
+    def __init__(self, n_nodes: int, q_heads: int, device, head_dim: int = 128, group=None,
+                 timeout_ns: int = 2_000_000_000):
+        from . import _lib
+        from . import kernels as K
+        self._lib = _lib.load()
+        self.device = torch.device(device)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.n_nodes, self.q_heads, self.head_dim = n_nodes, q_heads, head_dim
+        self.timeout_ns = int(timeout_ns)
+        nbytes = self._lib.ddt_peer_buffer_bytes(self.world, n_nodes, q_heads, head_dim)
+        if nbytes == 0:
+            raise ValueError("peer exchange: unsupported world size or shape")
+        with torch.cuda.device(self.device):
+            ptr = ctypes.c_void_p()
+            handle = (ctypes.c_char * 64)()
+            _lib.check(self._lib.ddt_peer_alloc(nbytes, ctypes.byref(ptr), handle),
+                       "ddt_peer_alloc")
+            self.local = ptr.value
+            handles = [bytes(handle)]
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            self.peers, self._opened = [], []
+            try:
+                for r in range(self.world):
+                    if r == self.rank:
+                        self.peers.append(self.local)
+                        continue
+                    pp = ctypes.c_void_p()
+                    buf = (ctypes.c_char * 64).from_buffer_copy(handles[r])
+                    _lib.check(self._lib.ddt_peer_open(buf, ctypes.byref(pp)), "ddt_peer_open")
+                    self.peers.append(pp.value)
+                    self._opened.append(pp.value)
+            except Exception:
+                self.close()
+                raise
+        self._bases = (ctypes.c_void_p * self.world)(*self.peers)
+        self.ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status = K.attention_status(self.device)
+        self.epoch = 0
+        if self.world > 1:
+            dist.barrier(group=group)  # every buffer is open before the first push
+
+    def exchange_merge(self, o: torch.Tensor, m: torch.Tensor, l: torch.Tensor,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        from . import kernels as K
+        from ._lib import check
+        n, hq, d = self.n_nodes, self.q_heads, self.head_dim
+        if out is None:
+            out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=self.device)
+        o, m, l = o.contiguous(), m.contiguous(), l.contiguous()
+        self.epoch += 1
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        check(self._lib.ddt_peer_push(o.data_ptr(), m.data_ptr(), l.data_ptr(), n, hq, d,
+                                      ctypes.cast(self._bases, ctypes.c_void_p), self.world,
+                                      self.rank, self.epoch & 0xffffffff, self.ticket.data_ptr(),
+                                      st), "ddt_peer_push")
+        check(self._lib.ddt_peer_merge(self.local, self.world, n, hq, d, self.epoch & 0xffffffff,
+                                       out.data_ptr(), out.stride(0), out.stride(1),
+                                       self.status.data_ptr(), self.timeout_ns, st),
+              "ddt_peer_merge")
+        K.STATS.launches += 3
+        return out
+
+    def close(self) -> None:
+        """Releases the IPC mappings and the buffer (after a barrier, so that no peer still
+        writes into it)."""
+        if getattr(self, "local", None) is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1 and dist.is_initialized():
+            dist.barrier(group=self.group)
+        for p in getattr(self, "_opened", []):
+            self._lib.ddt_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        self._lib.ddt_peer_free(ctypes.c_void_p(self.local))
+        self.local = None
+
+
 def splitkv_attention(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
                       key_begin: int, key_end: int, anc_bits: torch.Tensor | None,
                       past_length: int, scale: float | None = None, group=None,
-                      out: torch.Tensor | None = None) -> torch.Tensor:
+                      out: torch.Tensor | None = None,
+                      exchange: PeerExchange | None = None) -> torch.Tensor:
     """Tree attention over a sequence-sharded prefix: this rank's keys spread over all of its
-    SMs and merged in-GPU to one partial per row, one all-gather of the partials, merge.
-    Returns the bf16 output [N, Hq, D] on every rank."""
+    SMs and merged in-GPU to one partial per row, the partials of all ranks exchanged (over
+    NVLink peer memory with ``exchange``, else one NCCL all-gather), merge.  Returns the bf16
+    output [N, Hq, D] on every rank."""
     from . import kernels as K
     n, hq = q.shape[0], q.shape[1]
     o, m, l = K.tree_attention_partial_merged(q, k_shard, v_shard, key_begin, key_end, anc_bits,
                                               past_length, scale=scale)
+    if exchange is not None:
+        return exchange.exchange_merge(o, m, l, out=out)
     og, mg, lg = gather_partials(o, m, l, group)
     return K.attn_merge(og, mg, lg, n, hq, out=out)

@@ -102,6 +102,18 @@ def test_host_side_validation_rejects_bad_arguments():
     assert lib.ddt_add_rmsnorm(p, None, p, 4, 16392, 1e-6, None, p, None) == -2
     assert lib.ddt_add_rmsnorm(p, None, p, 4, 100, 1e-6, None, p, None) == -2
     assert lib.ddt_add_rmsnorm(p, None, p, 0, 5120, 1e-6, None, p, None) == 0
+    # NVLink peer exchange: at most 8 ranks, head_dim 128, epochs from 1, bounded waits
+    assert lib.ddt_peer_buffer_bytes(9, 513, 32, 128) == 0
+    assert lib.ddt_peer_buffer_bytes(2, 513, 32, 64) == 0
+    assert lib.ddt_peer_buffer_bytes(2, 513, 32, 128) > 2 * 2 * 513 * 32 * 130 * 4
+    bases = (ctypes.c_void_p * 2)(256, 512)
+    pb = ctypes.cast(bases, ctypes.c_void_p)
+    assert lib.ddt_peer_push(p, p, p, 513, 32, 128, pb, 9, 0, 1, p, None) == -2
+    assert lib.ddt_peer_push(p, p, p, 513, 32, 128, pb, 2, 2, 1, p, None) == -1
+    assert lib.ddt_peer_push(p, p, p, 513, 32, 128, pb, 2, 0, 0, p, None) == -1
+    assert lib.ddt_peer_merge(p, 2, 513, 32, 128, 1, p, 4096, 128, p, 10, None) == -1
+    assert lib.ddt_peer_merge(p, 2, 513, 32, 128, 1, p, 4096, 128, None, 10**6, None) == -1
+    assert lib.ddt_peer_alloc(0, None, None) == -1
     # the bounded-wait check takes limits from 100 us to 2 s and needs a status word
     p = ctypes.c_void_p(256)
     assert lib.ddt_tree_attn_wait_check(p, p, p, p, 65, 256, 32, 8, p, 3, 10, p, None) == -1

@@ -1,7 +1,8 @@
 """Split-KV (sequence-sharded prefix) attention on GPUs: partials of every shard, the
 exchange and ddt_attn_merge must reproduce the single-GPU tree attention.  With one GPU the
-shards run in one process (the exchange is a stack); with two or more GPUs the shards run in
-NCCL processes, one per GPU."""
+shards run in one process (the exchange is a stack, or the peer exchange of a single rank);
+with two or more GPUs the shards run in NCCL processes, one per GPU, and the exchange over
+NVLink peer memory (PeerExchange) must give exactly the NCCL all-gather's output."""
 import os
 import socket
 
@@ -66,6 +67,29 @@ def test_merged_partials_per_shard(cuda_device, world):
     assert _rel(merged, full) <= 1e-2
 
 
+def test_peer_exchange_one_rank(cuda_device):
+    """PeerExchange without a process group (world 1): the push into its own buffer and the
+    counter-waiting merge give exactly ddt_attn_merge's output, call after call (the two
+    buffer parities alternate)."""
+    q, k, v, bits = _data(cuda_device)
+    full = K.tree_attention(q, k, v, bits, P)
+    x = S.PeerExchange(N, 32, cuda_device)
+    try:
+        for _ in range(3):
+            o, m, l = K.tree_attention_partial_merged(q, k, v, 0, P + N, bits, P)
+            ref = K.attn_merge(o[None], m[None], l[None], N, 32)
+            got = x.exchange_merge(o, m, l)
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref)
+            assert _rel(got, full) <= 1e-2
+            assert int(x.status.item()) == 0
+            again = S.splitkv_attention(q, k, v, 0, P + N, bits, P, exchange=x)
+            torch.cuda.synchronize()
+            assert torch.equal(again, ref)
+    finally:
+        x.close()
+
+
 def _port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -81,11 +105,21 @@ def _worker(rank, world, port, q_out):
     try:
         q, k, v, bits = _data(dev)
         kb, ke = S.shard_range(P, N, world, rank)
-        out = S.splitkv_attention(q, k[:, kb:ke].contiguous(), v[:, kb:ke].contiguous(), kb, ke,
-                                  bits, P)
+        ks, vs = k[:, kb:ke].contiguous(), v[:, kb:ke].contiguous()
+        out = S.splitkv_attention(q, ks, vs, kb, ke, bits, P)
         full = K.tree_attention(q, k, v, bits, P)
+        # the same exchange over NVLink peer memory: identical output, several calls in a row
+        x = S.PeerExchange(N, 32, dev)
+        same = True
+        try:
+            for _ in range(3):
+                peer = S.splitkv_attention(q, ks, vs, kb, ke, bits, P, exchange=x)
+                torch.cuda.synchronize()
+                same = same and torch.equal(peer, out) and int(x.status.item()) == 0
+        finally:
+            x.close()
         torch.cuda.synchronize()
-        q_out.put((rank, _rel(out, full)))
+        q_out.put((rank, _rel(out, full) if same else 1.0))
     finally:
         dist.destroy_process_group()
 
