@@ -40,8 +40,6 @@ struct RadixShared {
   unsigned long long prefix;
   unsigned long long mask;
   uint32_t remaining;
-  uint32_t bin_count;  // elements in the bin the last pass chose
-  uint32_t list_n;     // elements in the shared list (0: passes read the registers)
   int done;
   uint32_t out_count;
   int is_last;
@@ -78,9 +76,7 @@ __host__ __device__ inline WsLayout ws_layout(int64_t L, int64_t V, int64_t k) {
   return w;
 }
 
-constexpr size_t kRadixListBytes = 32768;  // 4096 composites
-
-// dynamic shared memory: max over the merge phase, the heap phase and the radix list
+// dynamic shared memory: max over the merge phase and the heap phase
 __host__ inline size_t smem_bytes(int64_t L, int64_t k, int64_t budget) {
   int64_t kpad = 1;
   while (kpad < k) kpad <<= 1;
@@ -90,9 +86,7 @@ __host__ inline size_t smem_bytes(int64_t L, int64_t k, int64_t budget) {
                 sizeof(double) * fcap + sizeof(double) * budget +
                 4 * sizeof(unsigned long long) * fcap + sizeof(uint32_t) * fcap +
                 sizeof(uint32_t) * budget;
-  size_t need = merge > heap ? merge : heap;
-  if (need < kRadixListBytes) need = kRadixListBytes;  // the radix select's element list
-  return align_up(need, 16);
+  return align_up(merge > heap ? merge : heap, 16);
 }
 
 // ---- exp in double for the log-partition sum ------------------------------------------
@@ -143,13 +137,8 @@ __device__ __forceinline__ int pass_shift(int p) {
 template <bool kBF16>
 __device__ __forceinline__ int num_passes() { return kBF16 ? 6 : 8; }
 
-// After a pass, when the chosen bin holds at most `cap` elements, they are copied to the
-// shared `list` and the later passes read only the list: the first pass (sign and 7 exponent
-// bits of the key) typically leaves a few percent of a chunk's elements, so the later passes
-// no longer visit every register-held element.  The passes and so the result are unchanged.
 template <int EPT, bool kBF16>
-__device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, RadixShared& s,
-                             unsigned long long* list, uint32_t cap) {
+__device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, RadixShared& s) {
   const int npass = num_passes<kBF16>();
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -158,7 +147,6 @@ __device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, 
     s.mask = 0ull;
     s.remaining = k;
     s.done = 0;
-    s.list_n = 0;
   }
   __syncthreads();
   for (int p = 0; p < npass; ++p) {
@@ -169,29 +157,14 @@ __device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, 
     // read the pass state before the barrier that precedes its update
     const unsigned long long prefix = s.prefix, mask = s.mask;
     const uint32_t rem = s.remaining;
-    const uint32_t ln = s.list_n;
-    if (ln == 0) {
 #pragma unroll
-      for (int j = 0; j < EPT; ++j) {
-        const bool act = comp[j] != 0ull && (comp[j] & mask) == prefix;
-        const uint32_t digit = static_cast<uint32_t>(comp[j] >> sh) & 255u;
-        const unsigned am = __ballot_sync(DDT_FULL_MASK, act);
-        if (act) {
-          const unsigned peers = __match_any_sync(am, digit);
-          if (lane == __ffs(peers) - 1) atomicAdd(&s.hist[digit], static_cast<uint32_t>(__popc(peers)));
-        }
-      }
-    } else {
-      for (uint32_t i0 = tid - lane; i0 < ln; i0 += blockDim.x) {  // warp-uniform trip count
-        const uint32_t i = i0 + lane;
-        const unsigned long long c = i < ln ? list[i] : 0ull;
-        const bool act = c != 0ull && (c & mask) == prefix;
-        const uint32_t digit = static_cast<uint32_t>(c >> sh) & 255u;
-        const unsigned am = __ballot_sync(DDT_FULL_MASK, act);
-        if (act) {
-          const unsigned peers = __match_any_sync(am, digit);
-          if (lane == __ffs(peers) - 1) atomicAdd(&s.hist[digit], static_cast<uint32_t>(__popc(peers)));
-        }
+    for (int j = 0; j < EPT; ++j) {
+      const bool act = comp[j] != 0ull && (comp[j] & mask) == prefix;
+      const uint32_t digit = static_cast<uint32_t>(comp[j] >> sh) & 255u;
+      const unsigned am = __ballot_sync(DDT_FULL_MASK, act);
+      if (act) {
+        const unsigned peers = __match_any_sync(am, digit);
+        if (lane == __ffs(peers) - 1) atomicAdd(&s.hist[digit], static_cast<uint32_t>(__popc(peers)));
       }
     }
     __syncthreads();
@@ -218,26 +191,10 @@ __device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, 
         s.prefix = prefix | (static_cast<unsigned long long>(b) << sh);
         s.mask = mask | (255ull << sh);
         s.remaining = nrem;
-        s.bin_count = v;
         if (v == nrem) s.done = 1;
       }
     }
     __syncthreads();
-    if (ln == 0 && list != nullptr && !s.done && p + 1 < npass && s.bin_count <= cap) {
-      // copy the chosen bin's elements to the list (order irrelevant; list_n is 0 here)
-      const unsigned long long np = s.prefix, nm = s.mask;
-#pragma unroll
-      for (int j = 0; j < EPT; ++j) {
-        const bool act = comp[j] != 0ull && (comp[j] & nm) == np;
-        const unsigned m = __ballot_sync(DDT_FULL_MASK, act);
-        if (m == 0u) continue;
-        uint32_t base = 0;
-        if (lane == __ffs(m) - 1) base = atomicAdd(&s.list_n, static_cast<uint32_t>(__popc(m)));
-        base = __shfl_sync(DDT_FULL_MASK, base, __ffs(m) - 1);
-        if (act) list[base + __popc(m & ((1u << lane) - 1u))] = comp[j];
-      }
-      __syncthreads();
-    }
   }
 }
 
@@ -596,8 +553,7 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
                  uint32_t* __restrict__ anc_bits, int anc_words,
                  const int64_t* __restrict__ root_token, int64_t start,
                  int64_t* __restrict__ verify_ids, int64_t* __restrict__ verify_pos,
-                 unsigned char* __restrict__ ws, int vec_ok, const Batch batch,
-                 uint32_t list_cap) {
+                 unsigned char* __restrict__ ws, int vec_ok, const Batch batch) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ RadixShared rs;
   const int tid = threadIdx.x;
@@ -728,8 +684,7 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
   // exact top-k of the chunk
   const int kk = static_cast<int>(n < k ? n : k);
   if (kk < n) {
-    radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(kk), rs,
-                              reinterpret_cast<unsigned long long*>(smem), list_cap);
+    radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(kk), rs);
   } else if (tid == 0) {
     rs.prefix = 0ull;
     rs.mask = 0ull;
@@ -778,8 +733,7 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
     const int i = j * kThreads + tid;
     comp[j] = i < ncand ? __ldcg(&row_cand[i]) : 0ull;
   }
-  radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(k), rs,
-                            reinterpret_cast<unsigned long long*>(smem), list_cap);
+  radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(k), rs);
   if (tid == 0) rs.out_count = 0;
   __syncthreads();
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem);
@@ -952,8 +906,7 @@ extern "C" int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths
         draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(k),
         static_cast<int>(budget), top_log_probs, top_token_ids, node_token_ids, node_depths,
         parents, node_count, anc_bits, static_cast<int>(anc_words), root_token, start,
-        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok, topk::Batch{},
-        static_cast<uint32_t>(smem / 8));
+        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok, topk::Batch{});
   } else {
     auto kern = topk::topk_tree_kernel<false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -963,8 +916,7 @@ extern "C" int ddt_topk_tree(const void* draft_logits, int dtype, int64_t depths
         draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(k),
         static_cast<int>(budget), top_log_probs, top_token_ids, node_token_ids, node_depths,
         parents, node_count, anc_bits, static_cast<int>(anc_words), root_token, start,
-        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok, topk::Batch{},
-        static_cast<uint32_t>(smem / 8));
+        verify_ids, verify_pos, static_cast<unsigned char*>(workspace), vec_ok, topk::Batch{});
   }
   return launch_status();
 }
@@ -1031,7 +983,7 @@ extern "C" int ddt_topk_tree_batched(const void* draft_logits, int dtype, int64_
       draft_logits, static_cast<int>(depths), vocab, row_stride, static_cast<int>(kmax),
       static_cast<int>(max_budget), nullptr, nullptr, node_token_ids, node_depths, parents,
       node_count, anc_bits, static_cast<int>(anc_words), root_tokens, 0, verify_ids, verify_pos,
-      wsb + cbytes, vec_ok, batch, static_cast<uint32_t>(smem / 8));
+      wsb + cbytes, vec_ok, batch);
   return launch_status();
 }
 
