@@ -581,10 +581,12 @@ def run_requests(args):
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     if rank == 0 and not args.no_subrecords:
-        sub = verify_step(args, model, runner, dev, steps=max(3, min(args.steps, 20)),
-                          warmup=args.warmup)
+        with ClockSampler(_gpu_index(local)) as sub_clocks:
+            sub = verify_step(args, model, runner, dev, steps=max(3, min(args.steps, 20)),
+                              warmup=args.warmup)
+        sub["clocks"] = sub_clocks.summary()
         line["verify_step"] = sub
-        line["roofline"] = sub["roofline"]
+        line["roofline"] = dict(sub["roofline"], clocks=sub["clocks"])
         if world == 1:
             line["kernels"] = kernel_table(dev, args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
