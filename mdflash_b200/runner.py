@@ -72,6 +72,20 @@ class Qwen3VerifyRunner:
         (a TreeKVCache) at [past_length, past_length + N) and returns logits [N, V] (bf16).
         Tree mode attends with anc_bits; causal=True attends causally (prefill).  Attention
         timeouts go to `status` (default: the device's status word)."""
+        h = self._final_hidden(ids, positions, cache, past_length, anc_bits, causal, status)
+        return torch.matmul(h, self.lm_head.t())
+
+    def forward_posterior(self, ids: torch.Tensor, positions: torch.Tensor, cache,
+                          past_length: int, anc_bits: torch.Tensor | None,
+                          out: torch.Tensor | None = None,
+                          status: torch.Tensor | None = None) -> torch.Tensor:
+        """The greedy posterior (i64 [N]) of the verify rows without the [N, V] logits: the
+        final hidden states go through the fused lm_head -> argmax kernel
+        (ddt_lm_head_argmax).  Same cache effects as forward."""
+        h = self._final_hidden(ids, positions, cache, past_length, anc_bits, False, status)
+        return K.lm_head_argmax(h, self.lm_head, out=out)
+
+    def _final_hidden(self, ids, positions, cache, past_length, anc_bits, causal, status):
         lib = _lib.load()
         st = self._stream()
         n = ids.numel()
@@ -117,4 +131,4 @@ class Qwen3VerifyRunner:
             layer.length = past_length + n
             layer.keys = layer.k_buf[..., :layer.length, :]
             layer.values = layer.v_buf[..., :layer.length, :]
-        return torch.matmul(h, self.lm_head.t())
+        return h

@@ -40,10 +40,13 @@ class StepResult:
 class TreeVerifier:
     def __init__(self, target: torch.nn.Module, cache: TreeKVCache, budget: int, depths: int,
                  vocab: int, device: torch.device | str = "cuda", keep_logits: bool = False,
-                 fused: bool = False, runner=None):
+                 fused: bool = False, runner=None, fused_head: bool = False):
         """fused=False runs the transformers model with attn_implementation="ddtree_tree";
         fused=True runs its weights through Qwen3VerifyRunner (fused elementwise stages); a
-        runner can be shared between verifiers of the same model (runner=...)."""
+        runner can be shared between verifiers of the same model (runner=...).  With a
+        runner, fused_head=True takes the greedy posterior from the fused lm_head -> argmax
+        kernel instead of cuBLAS logits + ddt_argmax (no logits then, even with
+        keep_logits)."""
         self.target = target
         self.runner = runner
         if fused and runner is None:
@@ -55,6 +58,7 @@ class TreeVerifier:
         self.vocab = vocab
         self.device = torch.device(device)
         self.keep_logits = keep_logits
+        self.fused_head = bool(fused_head)
         self.tree = K.DeviceTree.allocate(self.device, budget, depths, vocab)
         n_cap = budget + 1
         self.posterior = torch.zeros(n_cap, dtype=torch.int64, device=self.device)
@@ -82,19 +86,26 @@ class TreeVerifier:
         n = tree.n_nodes
         ids = tree.verify_ids[:n].view(1, n)
         pos = tree.verify_pos[:n].view(1, n)
-        if self.runner is not None:
-            logits = self.runner.forward(tree.verify_ids[:n], tree.verify_pos[:n], self.cache,
-                                         start, tree.anc_bits, status=self.status)
+        logits = None
+        if self.runner is not None and self.fused_head:
+            post = self.runner.forward_posterior(tree.verify_ids[:n], tree.verify_pos[:n],
+                                                 self.cache, start, tree.anc_bits,
+                                                 out=self.posterior[:n], status=self.status)
         else:
-            with A.tree_verify(tree, start, n, status=self.status):
-                out = self.target(ids, position_ids=pos, past_key_values=self.cache,
-                                  use_cache=True)
-            logits = out.logits[0]
-        post = K.argmax(logits, out=self.posterior[:n])
+            if self.runner is not None:
+                logits = self.runner.forward(tree.verify_ids[:n], tree.verify_pos[:n],
+                                             self.cache, start, tree.anc_bits,
+                                             status=self.status)
+            else:
+                with A.tree_verify(tree, start, n, status=self.status):
+                    out = self.target(ids, position_ids=pos, past_key_values=self.cache,
+                                      use_cache=True)
+                logits = out.logits[0]
+            post = K.argmax(logits, out=self.posterior[:n])
         K.accept_compact(post, tree, self.cache.kv_table(), start, accepted=self.accepted,
                          n_accepted=self.n_accepted, next_token=self.next_token, n_nodes=n)
         return StepResult(n, self.accepted, self.n_accepted, self.next_token, post, self.status,
-                          logits if self.keep_logits else None)
+                          logits if self.keep_logits and logits is not None else None)
 
     def check(self) -> None:
         """Raises DDTreeError (DDT_ERR_TIMEOUT) if an attention launch of the steps since the

@@ -199,6 +199,29 @@ def test_tree_verifier_matches_reference(setup, cuda_device, fused):
     assert cache.get_seq_length() == P + k
 
 
+def test_tree_verifier_fused_lm_head(setup, cuda_device):
+    """The fused runner with the fused lm_head -> argmax kernel (no logits): same tree, the
+    posterior within the reference's near-ties, and the walk of that posterior."""
+    s = setup
+    model = s["model"]
+    cache = TreeKVCache(2, P + BUDGET + 8).allocate(2, 128, torch.bfloat16, cuda_device)
+    verifier = TreeVerifier(model, cache, BUDGET, DEPTHS, V, cuda_device, fused=True,
+                            fused_head=True)
+    with torch.inference_mode():
+        verifier.runner.forward(s["ids"][0], torch.arange(P, device=cuda_device), cache, 0, None,
+                                causal=True)
+        res = verifier.step(s["logits"].to(cuda_device), s["root"].view(1), P)
+        torch.cuda.synchronize()
+    o_ids, o_depths, o_par, _, _, _ = s["tree"]
+    assert res.n_nodes == s["n"] and res.logits is None
+    verifier.check()
+    assert _agreement("e2e verifier fused lm_head", res.posterior, s) >= 0.999
+    k = int(res.n_accepted.item())
+    o_acc, o_next = oracle.follow_verified_tree((np.asarray(o_par, np.int32), o_ids.numpy()),
+                                                res.posterior.cpu())
+    assert res.accepted[:k].tolist() == o_acc and int(res.next_token.item()) == o_next
+
+
 def test_follow_verified_tree_on_a_foreign_tree(setup, cuda_device):
     """child_maps that are not the tree build_ddtree_tree just built (here: the oracle's tree
     of other logits) are walked on the device too, with the reference's result."""
