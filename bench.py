@@ -99,7 +99,8 @@ def parse_args():
                          "graph")
     ap.add_argument("--lanes", type=int, default=4,
                     help="requests workload: replay the per-request graphs on this many streams "
-                         "at once (request j on stream j mod lanes; each lane has its own graph "
+                         "at once (requests split over the lanes by predicted cost; each lane "
+                         "has its own graph "
                          "pool and scratch buffers)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="splitkv workload: partials travel over NVLink peer memory "
@@ -454,18 +455,32 @@ def run_requests(args):
         trees.root_tokens.copy_(host_roots)
         if batched:
             K.topk_tree_batched(dev_logits, trees)  # the trees the captured steps start from
-    for j, i in enumerate(mine):
-        sp = specs[i]
+    # lanes get equal shares of the predicted work (longest-processing-time first over the
+    # request cost model); within a lane the longest requests go first, and the replay order
+    # interleaves the lanes so that all of them start at once.  A lane's graphs share one
+    # pool, so they are captured in the order they are replayed.
+    lane_lists = S.assign_requests([S.request_cost(specs[i]) for i in mine], lanes)
+    lane_of = {}
+    for ln, lst in enumerate(lane_lists):
+        lst.sort(key=lambda j: (-S.request_cost(specs[mine[j]]), j))
+        for j in lst:
+            lane_of[j] = ln
+    order = [lst[t] for t in range(max((len(x) for x in lane_lists), default=0))
+             for lst in lane_lists if t < len(lst)]
+    caps = [None] * len(mine)
+    for j in order:
+        sp = specs[mine[j]]
+        ln = lane_of[j]
         cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
             QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
         _fill_prefix(cache, sp.prefix, g)  # the verify work does not depend on the K / V values
         ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
-        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pools[j % lanes],
-                           tree=trees.tree(j) if batched else None, lane=j % lanes,
-                           capture_stream=cap_streams[j % lanes] if cap_streams else None)
+        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pools[ln],
+                           tree=trees.tree(j) if batched else None, lane=ln,
+                           capture_stream=cap_streams[ln] if cap_streams else None)
         cap.draft_logits.copy_(dev_logits[j])
         cap.root_token.copy_(trees.root_tokens[j:j + 1])
-        caps.append((sp, cap))
+        caps[j] = (sp, cap)
     records = torch.full((len(caps), S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
     for j, (sp, cap) in enumerate(caps):
         records[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
@@ -481,8 +496,9 @@ def run_requests(args):
         if streams:
             for st in streams:
                 st.wait_stream(main)
-        for j, (sp, cap) in enumerate(caps):
-            with torch.cuda.stream(streams[j % lanes] if streams else main):
+        for j in order:
+            sp, cap = caps[j]
+            with torch.cuda.stream(streams[lane_of[j]] if streams else main):
                 if e2e and not batched:
                     cap.draft_logits.copy_(host_logits[j], non_blocking=True)
                     cap.root_token.copy_(host_roots[j:j + 1], non_blocking=True)
