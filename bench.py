@@ -440,7 +440,7 @@ def run_requests(args):
     streams = [torch.cuda.Stream(dev) for _ in range(lanes)] if lanes > 1 else None
     cap_streams = [torch.cuda.Stream(dev) for _ in range(lanes)] if lanes > 1 else None
     caps = []
-    g = torch.Generator(device=dev).manual_seed(rank)
+    g = torch.Generator(device=dev)
     batched = args.tree_build == "batched"
     # every request's drafter logits and root token, pinned on the host and resident on the
     # device ([R, depths, V]); the batched build reads them all in one launch
@@ -473,7 +473,9 @@ def run_requests(args):
         ln = lane_of[j]
         cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
             QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
-        _fill_prefix(cache, sp.prefix, g)  # the verify work does not depend on the K / V values
+        # random prefix K / V seeded per request (the verify work does not depend on the
+        # values; the results then do not depend on the rank or the capture order)
+        _fill_prefix(cache, sp.prefix, g.manual_seed(1000 + sp.index))
         ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
         cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pools[ln],
                            tree=trees.tree(j) if batched else None, lane=ln,
