@@ -579,9 +579,11 @@ def run_requests(args):
                 "ms_per_step": e2e_ms},
         "gpu_launches": int(sums[1].item()),
         "tokens_per_step": tokens,
-        # digest of the gathered result records (accepted paths, next tokens): equal across
-        # --lanes / --tree-build settings, since every request's step is deterministic
-        "records_digest": hashlib.sha1(allrec.numpy().tobytes()).hexdigest()[:16],
+        # digest of the gathered result records (accepted paths, next tokens) without their
+        # rank field: the same at every GPU count and --lanes / --tree-build setting, since
+        # every request's step is deterministic
+        "records_digest": hashlib.sha1(
+            allrec.index_fill(1, torch.tensor([1]), 0).numpy().tobytes()).hexdigest()[:16],
         "requests_per_rank": [len(a) for a in assignment],
         "step_roofline": {"bound": "max(HBM: weights + prefix K/V once, bf16 FLOPs) per request, "
                                    "the slowest rank's requests back to back",
