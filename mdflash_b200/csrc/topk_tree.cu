@@ -31,6 +31,7 @@ constexpr int kEPT = 40;                    // elements per thread held in regis
 constexpr int kChunk = kThreads * kEPT;     // max elements per chunk (20480): 8 chunks of
                                             // a 151936 vocabulary, 120 CTAs for 15 depths
 constexpr int kMaxCand = kThreads * kEPT;   // max candidates merged per row
+constexpr int kEPTMerge = 16;               // candidates per thread when at most 8192
 constexpr int kRankBits = 12;               // bits per level in the packed rank tuple
 constexpr int kLevelsPerWord = 5;
 
@@ -544,6 +545,23 @@ struct Batch {
   uint32_t* counters;
 };
 
+// Top k of a row's merged candidates (ncand composites at row_cand, EPT per thread) into
+// sel[0, kpad) in arbitrary order.
+template <int EPT, bool kBF16>
+__device__ __forceinline__ void merge_select(const unsigned long long* row_cand, int ncand, int k,
+                                             RadixShared& rs, unsigned long long* sel, int kpad) {
+  unsigned long long c[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int i = j * kThreads + threadIdx.x;
+    c[j] = i < ncand ? __ldcg(&row_cand[i]) : 0ull;
+  }
+  radix_select<EPT, kBF16>(c, static_cast<uint32_t>(k), rs);
+  if (threadIdx.x == 0) rs.out_count = 0;
+  __syncthreads();
+  append_selected<EPT>(c, rs, sel, static_cast<uint32_t>(kpad));
+}
+
 template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
 topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_stride, int k,
@@ -725,21 +743,17 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
            exp_neg_d(static_cast<double>(__ldcg(&chunk_max[d * C + i])) - static_cast<double>(M));
     s_logz = static_cast<float>(static_cast<double>(M) + log(S));
   }
-  // candidates of the row: C * k composites, 0 = empty
+  // candidates of the row: C * k composites, 0 = empty; up to 8192 of them (budgets to 1024
+  // at 8 chunks) are held 16 per thread, so the radix passes visit 16 slots, not 40
   const unsigned long long* row_cand = cand + static_cast<int64_t>(d) * C * k;
   const int ncand = C * k;
-#pragma unroll
-  for (int j = 0; j < kEPT; ++j) {
-    const int i = j * kThreads + tid;
-    comp[j] = i < ncand ? __ldcg(&row_cand[i]) : 0ull;
-  }
-  radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(k), rs);
-  if (tid == 0) rs.out_count = 0;
-  __syncthreads();
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem);
   int kpad = 1;
   while (kpad < k) kpad <<= 1;
-  append_selected<kEPT>(comp, rs, sel, static_cast<uint32_t>(kpad));
+  if (ncand <= kThreads * kEPTMerge)
+    merge_select<kEPTMerge, kBF16>(row_cand, ncand, k, rs, sel, kpad);
+  else
+    merge_select<kEPT, kBF16>(row_cand, ncand, k, rs, sel, kpad);
   __syncthreads();
   for (int i = k + tid; i < kpad; i += kThreads) sel[i] = 0ull;
   __syncthreads();
