@@ -138,8 +138,12 @@ __device__ __forceinline__ int pass_shift(int p) {
 template <bool kBF16>
 __device__ __forceinline__ int num_passes() { return kBF16 ? 6 : 8; }
 
+// small_index: every index is below 2^24, so the top byte of ~index is 0xff for every element
+// and the pass over it (the first index pass) would choose bin 0xff with all active elements;
+// it is applied without counting.
 template <int EPT, bool kBF16>
-__device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, RadixShared& s) {
+__device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, RadixShared& s,
+                             bool small_index) {
   const int npass = num_passes<kBF16>();
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -153,6 +157,14 @@ __device__ void radix_select(const unsigned long long (&comp)[EPT], uint32_t k, 
   for (int p = 0; p < npass; ++p) {
     if (s.done) break;
     const int sh = pass_shift<kBF16>(p);
+    if (small_index && sh == 24) {
+      if (tid == 0) {
+        s.prefix |= 0xffull << 24;
+        s.mask |= 0xffull << 24;
+      }
+      __syncthreads();
+      continue;
+    }
     if (tid < 256) s.hist[tid] = 0;
     __syncthreads();
     // read the pass state before the barrier that precedes its update
@@ -549,14 +561,15 @@ struct Batch {
 // sel[0, kpad) in arbitrary order.
 template <int EPT, bool kBF16>
 __device__ __forceinline__ void merge_select(const unsigned long long* row_cand, int ncand, int k,
-                                             RadixShared& rs, unsigned long long* sel, int kpad) {
+                                             RadixShared& rs, unsigned long long* sel, int kpad,
+                                             bool small_index) {
   unsigned long long c[EPT];
 #pragma unroll
   for (int j = 0; j < EPT; ++j) {
     const int i = j * kThreads + threadIdx.x;
     c[j] = i < ncand ? __ldcg(&row_cand[i]) : 0ull;
   }
-  radix_select<EPT, kBF16>(c, static_cast<uint32_t>(k), rs);
+  radix_select<EPT, kBF16>(c, static_cast<uint32_t>(k), rs, small_index);
   if (threadIdx.x == 0) rs.out_count = 0;
   __syncthreads();
   append_selected<EPT>(c, rs, sel, static_cast<uint32_t>(kpad));
@@ -702,7 +715,7 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
   // exact top-k of the chunk
   const int kk = static_cast<int>(n < k ? n : k);
   if (kk < n) {
-    radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(kk), rs);
+    radix_select<kEPT, kBF16>(comp, static_cast<uint32_t>(kk), rs, V <= (int64_t(1) << 24));
   } else if (tid == 0) {
     rs.prefix = 0ull;
     rs.mask = 0ull;
@@ -750,10 +763,11 @@ topk_tree_kernel(const void* __restrict__ logits, int L, int64_t V, int64_t row_
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem);
   int kpad = 1;
   while (kpad < k) kpad <<= 1;
+  const bool small_index = V <= (int64_t(1) << 24);
   if (ncand <= kThreads * kEPTMerge)
-    merge_select<kEPTMerge, kBF16>(row_cand, ncand, k, rs, sel, kpad);
+    merge_select<kEPTMerge, kBF16>(row_cand, ncand, k, rs, sel, kpad, small_index);
   else
-    merge_select<kEPT, kBF16>(row_cand, ncand, k, rs, sel, kpad);
+    merge_select<kEPT, kBF16>(row_cand, ncand, k, rs, sel, kpad, small_index);
   __syncthreads();
   for (int i = k + tid; i < kpad; i += kThreads) sel[i] = 0ull;
   __syncthreads();
