@@ -72,7 +72,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["requests", "verify", "attn", "tree", "treebatch",
-                                           "argmax", "compact", "lmhead", "splitkv"],
+                                           "argmax", "compact", "compactbatch", "lmhead",
+                                           "splitkv"],
                     default="requests",
                     help="requests: the 64-request mix sharded over the GPUs (default); verify: "
                          "one Qwen3-8B verify step (prefix 8192, budget 256); attn / tree / "
@@ -893,6 +894,74 @@ def measure_compact(dev, prefix, budget, steps, warmup):
             "shape": f"36 layers x K/V [1, 8, {seq}, 128] bf16, forced path of {len(acc)} rows"}
 
 
+def measure_compact_batched(dev, n_requests, steps, warmup, prefix=1024):
+    """The batched walk + compaction (ddt_accept_compact_batched) over the request mix's trees
+    (budgets of the mix, drafter logits with one lifted token per depth as in
+    measure_compact), each request's posterior forced along the path to its deepest node, on
+    Qwen3-8B-shaped caches (36 layers x K, V [8, prefix + budget + 1, 128] bf16, one cache per
+    request).  GB/s of the algorithmic bytes (read + write of every moved row)."""
+    from mdflash_b200 import kernels as K
+    from mdflash_b200 import sharding as S
+    layers, hkv, d = 36, 8, 128
+    specs = S.request_specs(n_requests, seed=0)
+    rng = np.random.default_rng(7)
+    lg = torch.stack([request_logits(sp.seed) for sp in specs])
+    for r in range(n_requests):
+        for dep in range(lg.shape[1]):
+            lg[r, dep, int(rng.integers(V))] = 16.4
+    x = lg.to(torch.bfloat16).to(dev)
+    trees = K.TreeBatch.allocate(dev, [sp.budget for sp in specs], DEPTHS, V)
+    trees.starts.fill_(prefix)
+    K.topk_tree_batched(x, trees)
+    mn = trees.max_budget + 1
+    post = np.zeros((n_requests, mn), np.int64)
+    paths, moved = [], 0
+    for r in range(n_requests):
+        t = trees.tree(r)
+        n = t.n_nodes
+        parents = t.parents[:n].cpu().numpy()
+        tokens = t.verify_ids[:n].cpu().numpy()
+        depth = np.zeros(n, np.int64)
+        for i in range(1, n):
+            depth[i] = depth[parents[i]] + 1
+        target = int(np.flatnonzero(depth == depth.max())[-1])
+        path = [target]
+        while path[-1] != 0:
+            path.append(int(parents[path[-1]]))
+        path = path[::-1]
+        for a, b in zip(path[:-1], path[1:]):
+            post[r, a] = tokens[b]
+        post[r, target] = V  # no node carries it: the walk ends at the target
+        paths.append(path)
+        moved += sum(1 for i, a in enumerate(path) if a != i)
+    posterior = torch.from_numpy(post).to(dev)
+    tables = []
+    for sp in specs:
+        seq = prefix + sp.budget + 1
+        tables.append(K.KvTable([torch.empty((hkv, seq, d), dtype=torch.bfloat16, device=dev)
+                                 for _ in range(2 * layers)]))
+    kvb = K.KvBatch(tables)
+    pasts = [prefix] * n_requests
+    out = (torch.zeros((n_requests, mn), dtype=torch.int64, device=dev),
+           torch.zeros(n_requests, dtype=torch.int32, device=dev),
+           torch.zeros(n_requests, dtype=torch.int64, device=dev))
+    ms = _timed_launches(lambda: K.accept_compact_batched(posterior, trees, kvb, pasts, *out),
+                         steps, warmup, dev)
+    K.check_status(K.attention_status(dev))
+    acc, nacc = out[0].cpu(), out[1].cpu()
+    for r in range(n_requests):
+        if acc[r, :int(nacc[r])].tolist() != paths[r]:
+            raise RuntimeError(f"request {r}: forced path not accepted")
+    nbytes = 2 * layers * hkv * moved * d * 2 * 2
+    peaks, kind = measured_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"ms": ms, "gbs": gbs, "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
+            "peak_source": kind, "bytes_per_launch": nbytes, "requests": n_requests,
+            "moved_rows_per_tensor_total": moved,
+            "shape": f"{n_requests} requests, 36 layers x K/V [8, {prefix} + budget + 1, 128] "
+                     f"bf16, forced paths to the deepest node"}
+
+
 def measure_lm_head(dev, rows, steps, warmup, hidden=QWEN3_8B["hidden"]):
     """Fused lm_head -> argmax (ddt_lm_head_argmax) at the Qwen3-8B verify shape against the
     unfused path it replaces (cuBLAS bf16 GEMM writing the logits, then ddt_argmax).  Bound:
@@ -927,6 +996,7 @@ def kernel_table(dev, args):
         "tree_build_batched": measure_tree_batched(dev, args.requests, steps, warmup),
         "argmax": measure_argmax(dev, VERIFY_BUDGET + 1, steps, warmup),
         "accept_compact": measure_compact(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
+        "accept_compact_batched": measure_compact_batched(dev, args.requests, steps, warmup),
         "tree_attention": measure_attn(dev, VERIFY_PREFIX, VERIFY_BUDGET, steps, warmup),
         "lm_head_argmax": measure_lm_head(dev, VERIFY_BUDGET + 1, steps, warmup),
     }
@@ -974,6 +1044,10 @@ def run_single(args):
         r = measure_tree_batched(dev, args.requests, args.steps, args.warmup)
         line = _op_line("batched tree build GB/s", "GB/s", r, args, "batched tree build: " +
                         r["shape"], "hbm", "gbs")
+    elif args.workload == "compactbatch":
+        r = measure_compact_batched(dev, args.requests, args.steps, args.warmup)
+        line = _op_line("batched compaction GB/s", "GB/s", r, args,
+                        "batched accept walk + KV compaction: " + r["shape"], "hbm", "gbs")
     elif args.workload == "argmax":
         r = measure_argmax(dev, args.budget + 1, args.steps, args.warmup)
         line = _op_line("argmax GB/s", "GB/s", r, args, "argmax over " + r["shape"], "hbm", "gbs")

@@ -192,6 +192,23 @@ int ddt_accept_compact(const int64_t* posterior, const int32_t* parents,
 int ddt_compact_kv(const int64_t* keep, int64_t keep_count, void* const* kv_ptrs,
                    int64_t n_tensors, int64_t heads, int64_t head_dim, int64_t head_stride,
                    int64_t seq_stride, int64_t elem_bytes, int64_t past_length, void* stream);
+/* Batched walk + compaction: request r's tree (node_counts[r] + 1 nodes; parents,
+ * node_token_ids and posterior rows at the given strides, as ddt_topk_tree_batched writes
+ * them) is walked and its cache compacted exactly like ddt_accept_compact, all requests in one
+ * launch.  kv_ptrs: device array [n_requests, n_tensors] of K/V bases; head_strides,
+ * past_lengths: device i64 [n_requests] (a head stride that is not a whole number of 16-byte
+ * vectors moves nothing and sets *status non-zero); outputs accepted [n_requests, acc_stride],
+ * n_accepted i32 [n_requests], next_token i64 [n_requests].  No counterpart in the reference,
+ * which compacts one request's cache per ddtree_generate round (ddtree.py:284-335). */
+int ddt_accept_compact_batched(int64_t n_requests, const int64_t* posterior, int64_t post_stride,
+                               const int32_t* parents, int64_t par_stride,
+                               const int64_t* node_token_ids, int64_t ids_stride,
+                               const int32_t* node_counts, int64_t max_nodes,
+                               void* const* kv_ptrs, int64_t n_tensors, int64_t heads,
+                               int64_t head_dim, const int64_t* head_strides, int64_t seq_stride,
+                               int64_t elem_bytes, const int64_t* past_lengths, int64_t* accepted,
+                               int64_t acc_stride, int32_t* n_accepted, int64_t* next_token,
+                               int32_t* status, void* stream);
 
 /* ---- tree attention -----------------------------------------------------
  * q: [n_nodes, q_heads, head_dim] bf16 at element strides (q_node_stride, q_head_stride);

@@ -47,6 +47,8 @@ SIGNATURES = {
     "ddt_lm_head_argmax_workspace_bytes": (_S, [_I]),
     "ddt_lm_head_argmax": (_i, [_P, _I, _P, _I, _I, _I, _I, _P, _P, _I, _P, _S, _P, _P]),
     "ddt_accept_compact": (_i, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "ddt_accept_compact_batched": (_i, [_I, _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _I, _P, _I,
+                                        _I, _P, _P, _I, _P, _P, _P, _P]),
     "ddt_compact_kv": (_i, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "ddt_tree_attn_workspace_bytes": (_S, [_I, _I, _I, _I]),
     "ddt_tree_attn": (_i, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _i,

@@ -302,6 +302,101 @@ compact_kernel(const int64_t* __restrict__ keep, int cnt, KvDesc kv) {
     move_slice(kv, sl, s_keep, cnt, lane);
 }
 
+// Batched walk + compaction: G CTAs per request.  Request r's tree (node_counts[r] + 1 nodes:
+// parents, node tokens, posterior at fixed strides) is walked by each of its CTAs, whose warps
+// then move its (tensor, head) slices: tensors kv_ptrs[r * n_tensors + t], rows of
+// head_strides[r] elements per head, prefix past[r].  A request whose head stride is not a
+// whole number of 16-byte vectors (checked here, since the strides live on the device) moves
+// nothing and sets *status.
+struct KvBatch {
+  void* const* ptrs;
+  const int64_t* head_strides;
+  const int64_t* past;
+  int64_t n_tensors, heads, seq_stride;
+  int elem_bytes, vec_per_row;
+};
+
+__global__ void __launch_bounds__(kCompactWarps * 32)
+accept_compact_batched_kernel(const int64_t* __restrict__ posterior, int64_t post_stride,
+                              const int32_t* __restrict__ parents, int64_t par_stride,
+                              const int64_t* __restrict__ node_ids, int64_t ids_stride,
+                              const int32_t* __restrict__ node_counts, int max_nodes, KvBatch kb,
+                              int G, int64_t* __restrict__ accepted, int64_t acc_stride,
+                              int32_t* __restrict__ n_accepted, int64_t* __restrict__ next_token,
+                              int* status) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  int32_t* s_par = reinterpret_cast<int32_t*>(smem);
+  int64_t* s_tok = reinterpret_cast<int64_t*>(smem + ((sizeof(int32_t) * max_nodes + 15) / 16) * 16);
+  int64_t* s_post = s_tok + max_nodes;
+  __shared__ int64_t s_acc[kMaxRows];
+  __shared__ int s_cnt;
+  __shared__ int64_t s_next;
+  const int tid = threadIdx.x;
+  const int r = blockIdx.x / G, g = blockIdx.x % G;
+  int n_nodes = node_counts[r] + 1;
+  if (n_nodes > max_nodes) n_nodes = max_nodes;
+  if (n_nodes < 1) n_nodes = 1;
+  const int32_t* par = parents + r * par_stride;
+  const int64_t* ids = node_ids + r * ids_stride;
+  const int64_t* post = posterior + r * post_stride;
+  for (int i = tid; i < n_nodes; i += blockDim.x) {
+    s_par[i] = par[i];
+    s_tok[i] = i > 0 ? ids[i - 1] : -1;
+    s_post[i] = post[i];
+  }
+  __syncthreads();
+  if (tid < 32) {
+    const int lane = tid;
+    int cur = 0, cnt = 1;
+    if (lane == 0) s_acc[0] = 0;
+    int64_t tok = s_post[0];
+    for (;;) {
+      int found = -1;
+      for (int i = 1 + lane; i < n_nodes; i += 32)
+        if (s_par[i] == cur && s_tok[i] == tok) found = i;  // last match, like a dict overwrite
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(DDT_FULL_MASK, found, o));
+      if (found < 0 || cnt >= kMaxRows) break;
+      cur = found;
+      if (lane == 0) s_acc[cnt] = cur;
+      ++cnt;
+      tok = s_post[cur];
+    }
+    if (lane == 0) {
+      s_cnt = cnt;
+      s_next = tok;
+    }
+  }
+  __syncthreads();
+  const int cnt = s_cnt;
+  if (g == 0) {
+    for (int i = tid; i < cnt; i += blockDim.x) accepted[r * acc_stride + i] = s_acc[i];
+    if (tid == 0) {
+      n_accepted[r] = cnt;
+      next_token[r] = s_next;
+    }
+  }
+  const int64_t hs = kb.head_strides[r];
+  if ((hs * kb.elem_bytes) % 16 != 0) {
+    if (g == 0 && tid == 0 && status) atomicOr(status, 2);
+    return;
+  }
+  KvDesc kv;
+  kv.ptrs = kb.ptrs + r * kb.n_tensors;
+  kv.n_tensors = kb.n_tensors;
+  kv.heads = kb.heads;
+  kv.head_stride = hs;
+  kv.seq_stride = kb.seq_stride;
+  kv.elem_bytes = kb.elem_bytes;
+  kv.vec_per_row = kb.vec_per_row;
+  kv.past_length = kb.past[r];
+  const int lane = tid & 31;
+  const int64_t nslices = kv.n_tensors * kv.heads;
+  for (int64_t sl = static_cast<int64_t>(g) * kCompactWarps + (tid >> 5); sl < nslices;
+       sl += static_cast<int64_t>(G) * kCompactWarps)
+    move_slice(kv, sl, s_acc, cnt, lane);
+}
+
 inline int make_desc(void* const* kv_ptrs, int64_t n_tensors, int64_t heads, int64_t head_dim,
                      int64_t head_stride, int64_t seq_stride, int64_t elem_bytes,
                      int64_t past_length, KvDesc* d) {
@@ -396,5 +491,39 @@ extern "C" int ddt_compact_kv(const int64_t* keep, int64_t keep_count, void* con
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   accept::compact_kernel<<<accept::compact_grid(n_tensors, heads), accept::kCompactWarps * 32, 0,
                            st>>>(keep, static_cast<int>(keep_count), kv);
+  return launch_status();
+}
+
+extern "C" int ddt_accept_compact_batched(
+    int64_t n_requests, const int64_t* posterior, int64_t post_stride, const int32_t* parents,
+    int64_t par_stride, const int64_t* node_token_ids, int64_t ids_stride,
+    const int32_t* node_counts, int64_t max_nodes, void* const* kv_ptrs, int64_t n_tensors,
+    int64_t heads, int64_t head_dim, const int64_t* head_strides, int64_t seq_stride,
+    int64_t elem_bytes, const int64_t* past_lengths, int64_t* accepted, int64_t acc_stride,
+    int32_t* n_accepted, int64_t* next_token, int32_t* status, void* stream) {
+  if (n_requests < 0 || !posterior || !parents || !node_token_ids || !node_counts ||
+      !head_strides || !past_lengths || !accepted || !n_accepted || !next_token)
+    return DDT_ERR_INVALID;
+  if (max_nodes < 1 || post_stride < max_nodes || par_stride < max_nodes ||
+      ids_stride < max_nodes - 1 || acc_stride < 1)
+    return DDT_ERR_INVALID;
+  if (max_nodes > DDT_MAX_NODES) return DDT_ERR_CAPACITY;
+  accept::KvDesc d;
+  int rc = accept::make_desc(kv_ptrs, n_tensors, heads, head_dim, 0, seq_stride, elem_bytes, 0, &d);
+  if (rc != DDT_OK) return rc;
+  if (acc_stride < accept::kMaxRows && acc_stride < max_nodes) return DDT_ERR_INVALID;
+  if (n_requests == 0) return DDT_OK;
+  const unsigned per = accept::compact_grid(n_tensors, heads) / 4 > 0
+                           ? (accept::compact_grid(n_tensors, heads) + 3) / 4 : 1u;
+  if (static_cast<int64_t>(per) * n_requests > 0x7fffffffLL) return DDT_ERR_CAPACITY;
+  accept::KvBatch kb{kv_ptrs, head_strides, past_lengths, n_tensors, heads, seq_stride,
+                     d.elem_bytes, d.vec_per_row};
+  const size_t smem = ((sizeof(int32_t) * max_nodes + 15) / 16) * 16 + 2 * sizeof(int64_t) * max_nodes;
+  accept::accept_compact_batched_kernel<<<static_cast<unsigned>(per * n_requests),
+                                          accept::kCompactWarps * 32, smem,
+                                          static_cast<cudaStream_t>(stream)>>>(
+      posterior, post_stride, parents, par_stride, node_token_ids, ids_stride, node_counts,
+      static_cast<int>(max_nodes), kb, static_cast<int>(per), accepted, acc_stride, n_accepted,
+      next_token, status);
   return launch_status();
 }

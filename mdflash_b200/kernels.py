@@ -14,7 +14,8 @@ from ._lib import DDT_BF16, DDT_F32, DDT_MASK_CAUSAL, DDT_MASK_NONE, DDT_MASK_TR
 __all__ = [
     "DeviceTree", "expected_node_count", "topk_tree", "argmax", "accept_compact", "compact_kv",
     "tree_attention", "tree_attention_partial", "attn_merge", "mask_to_bits", "KvTable",
-    "anc_words_for", "TreeBatch", "topk_tree_batched", "attention_status", "check_status", "tree_attention_wait_check",
+    "anc_words_for", "TreeBatch", "topk_tree_batched", "KvBatch", "accept_compact_batched",
+    "attention_status", "check_status", "tree_attention_wait_check",
     "sample_chains", "chain_tree", "lm_head_argmax",
 ]
 
@@ -440,6 +441,71 @@ def accept_compact(posterior: torch.Tensor, tree: DeviceTree, kv: KvTable, past_
         kv.ptrs.data_ptr(), kv.n, kv.heads, kv.head_dim, kv.head_stride, kv.seq_stride,
         kv.elem_bytes, past_length, accepted.data_ptr(), n_accepted.data_ptr(),
         next_token.data_ptr(), _stream(dev)), "ddt_accept_compact")
+    STATS.launches += 1
+    return accepted, n_accepted, next_token
+
+
+class KvBatch:
+    """The K/V tables of several requests for the batched walk + compaction: the tables share
+    tensor count, heads, head_dim, sequence stride and dtype; their capacities (head strides)
+    may differ."""
+
+    def __init__(self, tables: list[KvTable]):
+        if not tables:
+            raise ValueError("empty KV batch")
+        t0 = tables[0]
+        for t in tables:
+            if (t.n, t.heads, t.head_dim, t.seq_stride, t.elem_bytes) != \
+                    (t0.n, t0.heads, t0.head_dim, t0.seq_stride, t0.elem_bytes):
+                raise ValueError("KV tables of a batch must share layout and dtype")
+        self.tables = tables
+        self.device = t0.device
+        self.n, self.heads, self.head_dim = t0.n, t0.heads, t0.head_dim
+        self.seq_stride, self.elem_bytes = t0.seq_stride, t0.elem_bytes
+        self.capacity = [t.seq for t in tables]
+        self.ptrs = torch.cat([t.ptrs for t in tables])
+        self.head_strides = torch.tensor([t.head_stride for t in tables], dtype=torch.int64,
+                                         device=self.device)
+
+
+def accept_compact_batched(posteriors: torch.Tensor, trees: TreeBatch, kvb: KvBatch,
+                           past_lengths, accepted: torch.Tensor | None = None,
+                           n_accepted: torch.Tensor | None = None,
+                           next_token: torch.Tensor | None = None,
+                           status: torch.Tensor | None = None):
+    """ddt_accept_compact_batched: the greedy walk of every request's tree (trees, one row per
+    request) under its posterior row (posteriors [R, max_budget + 1] i64) and the compaction of
+    its cache, one launch.  Returns (accepted [R, max_budget + 1], n_accepted i32 [R],
+    next_token i64 [R])."""
+    dev = _require_cuda(posteriors)
+    R = len(trees.budgets)
+    mn = trees.max_budget + 1
+    if posteriors.shape != (R, mn) or posteriors.dtype != torch.int64 or posteriors.stride(1) != 1:
+        raise ValueError("posteriors must be i64 [requests, max_budget + 1] with unit stride")
+    if len(kvb.tables) != R:
+        raise ValueError("one KV table per request")
+    past = [int(x) for x in past_lengths]
+    for r in range(R):
+        n = 1 + expected_node_count(trees.depths, trees.vocab, trees.budgets[r])
+        if past[r] < 0 or past[r] + n > kvb.capacity[r]:
+            raise ValueError(f"request {r}: cache holds {kvb.capacity[r]} rows, the tree window "
+                             f"needs {past[r] + n}")
+    if accepted is None:
+        accepted = torch.zeros((R, mn), dtype=torch.int64, device=dev)
+    if n_accepted is None:
+        n_accepted = torch.zeros(R, dtype=torch.int32, device=dev)
+    if next_token is None:
+        next_token = torch.zeros(R, dtype=torch.int64, device=dev)
+    if status is None:
+        status = attention_status(dev)
+    past_dev = torch.tensor(past, dtype=torch.int64, device=dev)
+    check(_lib.load().ddt_accept_compact_batched(
+        R, posteriors.data_ptr(), posteriors.stride(0), trees.parents.data_ptr(),
+        trees.parents.stride(0), trees.node_token_ids.data_ptr(), trees.node_token_ids.stride(0),
+        trees.node_count.data_ptr(), mn, kvb.ptrs.data_ptr(), kvb.n, kvb.heads, kvb.head_dim,
+        kvb.head_strides.data_ptr(), kvb.seq_stride, kvb.elem_bytes, past_dev.data_ptr(),
+        accepted.data_ptr(), accepted.stride(0), n_accepted.data_ptr(), next_token.data_ptr(),
+        status.data_ptr(), _stream(dev)), "ddt_accept_compact_batched")
     STATS.launches += 1
     return accepted, n_accepted, next_token
 
