@@ -302,12 +302,60 @@ compact_kernel(const int64_t* __restrict__ keep, int cnt, KvDesc kv) {
     move_slice(kv, sl, s_keep, cnt, lane);
 }
 
-// Batched walk + compaction: G CTAs per request.  Request r's tree (node_counts[r] + 1 nodes:
-// parents, node tokens, posterior at fixed strides) is walked by each of its CTAs, whose warps
-// then move its (tensor, head) slices: tensors kv_ptrs[r * n_tensors + t], rows of
-// head_strides[r] elements per head, prefix past[r].  A request whose head stride is not a
-// whole number of 16-byte vectors (checked here, since the strides live on the device) moves
-// nothing and sets *status.
+// ---- batched: the walks of all requests, then all their compactions (two launches) ----
+// Walk of request blockIdx.x (one warp): its tree is staged in shared memory, then walked
+// as in accept_compact_kernel; writes accepted[r], n_accepted[r], next_token[r].
+__global__ void __launch_bounds__(32)
+accept_walk_batched_kernel(const int64_t* __restrict__ posterior, int64_t post_stride,
+                           const int32_t* __restrict__ parents, int64_t par_stride,
+                           const int64_t* __restrict__ node_ids, int64_t ids_stride,
+                           const int32_t* __restrict__ node_counts, int max_nodes,
+                           int64_t* __restrict__ accepted, int64_t acc_stride,
+                           int32_t* __restrict__ n_accepted, int64_t* __restrict__ next_token) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  int32_t* s_par = reinterpret_cast<int32_t*>(smem);
+  int64_t* s_tok = reinterpret_cast<int64_t*>(smem + ((sizeof(int32_t) * max_nodes + 15) / 16) * 16);
+  int64_t* s_post = s_tok + max_nodes;
+  const int lane = threadIdx.x;
+  const int r = blockIdx.x;
+  int n_nodes = node_counts[r] + 1;
+  if (n_nodes > max_nodes) n_nodes = max_nodes;
+  if (n_nodes < 1) n_nodes = 1;
+  const int32_t* par = parents + r * par_stride;
+  const int64_t* ids = node_ids + r * ids_stride;
+  const int64_t* post = posterior + r * post_stride;
+  for (int i = lane; i < n_nodes; i += 32) {
+    s_par[i] = par[i];
+    s_tok[i] = i > 0 ? ids[i - 1] : -1;
+    s_post[i] = post[i];
+  }
+  __syncwarp();
+  int64_t* acc = accepted + r * acc_stride;
+  int cur = 0, cnt = 1;
+  if (lane == 0) acc[0] = 0;
+  int64_t tok = s_post[0];
+  for (;;) {
+    int found = -1;
+    for (int i = 1 + lane; i < n_nodes; i += 32)
+      if (s_par[i] == cur && s_tok[i] == tok) found = i;  // last match, like a dict overwrite
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(DDT_FULL_MASK, found, o));
+    if (found < 0 || cnt >= kMaxRows) break;
+    cur = found;
+    if (lane == 0) acc[cnt] = cur;
+    ++cnt;
+    tok = s_post[cur];
+  }
+  if (lane == 0) {
+    n_accepted[r] = cnt;
+    next_token[r] = tok;
+  }
+}
+
+// Compaction of every request's cache after accept_walk_batched_kernel: G CTAs per request;
+// request r's tensors are kv_ptrs[r * n_tensors + t], with head_strides[r] elements per head
+// and prefix past[r].  A request whose head stride is not a whole number of 16-byte vectors
+// (checked here, since the strides live on the device) moves nothing and sets *status.
 struct KvBatch {
   void* const* ptrs;
   const int64_t* head_strides;
@@ -317,65 +365,15 @@ struct KvBatch {
 };
 
 __global__ void __launch_bounds__(kCompactWarps * 32)
-accept_compact_batched_kernel(const int64_t* __restrict__ posterior, int64_t post_stride,
-                              const int32_t* __restrict__ parents, int64_t par_stride,
-                              const int64_t* __restrict__ node_ids, int64_t ids_stride,
-                              const int32_t* __restrict__ node_counts, int max_nodes, KvBatch kb,
-                              int G, int64_t* __restrict__ accepted, int64_t acc_stride,
-                              int32_t* __restrict__ n_accepted, int64_t* __restrict__ next_token,
-                              int* status) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  int32_t* s_par = reinterpret_cast<int32_t*>(smem);
-  int64_t* s_tok = reinterpret_cast<int64_t*>(smem + ((sizeof(int32_t) * max_nodes + 15) / 16) * 16);
-  int64_t* s_post = s_tok + max_nodes;
+compact_batched_kernel(const int64_t* __restrict__ accepted, int64_t acc_stride,
+                       const int32_t* __restrict__ n_accepted, KvBatch kb, int G, int* status) {
   __shared__ int64_t s_acc[kMaxRows];
-  __shared__ int s_cnt;
-  __shared__ int64_t s_next;
   const int tid = threadIdx.x;
   const int r = blockIdx.x / G, g = blockIdx.x % G;
-  int n_nodes = node_counts[r] + 1;
-  if (n_nodes > max_nodes) n_nodes = max_nodes;
-  if (n_nodes < 1) n_nodes = 1;
-  const int32_t* par = parents + r * par_stride;
-  const int64_t* ids = node_ids + r * ids_stride;
-  const int64_t* post = posterior + r * post_stride;
-  for (int i = tid; i < n_nodes; i += blockDim.x) {
-    s_par[i] = par[i];
-    s_tok[i] = i > 0 ? ids[i - 1] : -1;
-    s_post[i] = post[i];
-  }
+  int cnt = n_accepted[r];
+  cnt = cnt < 0 ? 0 : (cnt > kMaxRows ? kMaxRows : cnt);
+  if (tid < cnt) s_acc[tid] = accepted[r * acc_stride + tid];
   __syncthreads();
-  if (tid < 32) {
-    const int lane = tid;
-    int cur = 0, cnt = 1;
-    if (lane == 0) s_acc[0] = 0;
-    int64_t tok = s_post[0];
-    for (;;) {
-      int found = -1;
-      for (int i = 1 + lane; i < n_nodes; i += 32)
-        if (s_par[i] == cur && s_tok[i] == tok) found = i;  // last match, like a dict overwrite
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(DDT_FULL_MASK, found, o));
-      if (found < 0 || cnt >= kMaxRows) break;
-      cur = found;
-      if (lane == 0) s_acc[cnt] = cur;
-      ++cnt;
-      tok = s_post[cur];
-    }
-    if (lane == 0) {
-      s_cnt = cnt;
-      s_next = tok;
-    }
-  }
-  __syncthreads();
-  const int cnt = s_cnt;
-  if (g == 0) {
-    for (int i = tid; i < cnt; i += blockDim.x) accepted[r * acc_stride + i] = s_acc[i];
-    if (tid == 0) {
-      n_accepted[r] = cnt;
-      next_token[r] = s_next;
-    }
-  }
   const int64_t hs = kb.head_strides[r];
   if ((hs * kb.elem_bytes) % 16 != 0) {
     if (g == 0 && tid == 0 && status) atomicOr(status, 2);
@@ -518,12 +516,15 @@ extern "C" int ddt_accept_compact_batched(
   if (static_cast<int64_t>(per) * n_requests > 0x7fffffffLL) return DDT_ERR_CAPACITY;
   accept::KvBatch kb{kv_ptrs, head_strides, past_lengths, n_tensors, heads, seq_stride,
                      d.elem_bytes, d.vec_per_row};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t smem = ((sizeof(int32_t) * max_nodes + 15) / 16) * 16 + 2 * sizeof(int64_t) * max_nodes;
-  accept::accept_compact_batched_kernel<<<static_cast<unsigned>(per * n_requests),
-                                          accept::kCompactWarps * 32, smem,
-                                          static_cast<cudaStream_t>(stream)>>>(
+  accept::accept_walk_batched_kernel<<<static_cast<unsigned>(n_requests), 32, smem, st>>>(
       posterior, post_stride, parents, par_stride, node_token_ids, ids_stride, node_counts,
-      static_cast<int>(max_nodes), kb, static_cast<int>(per), accepted, acc_stride, n_accepted,
-      next_token, status);
+      static_cast<int>(max_nodes), accepted, acc_stride, n_accepted, next_token);
+  rc = launch_status();
+  if (rc != DDT_OK || n_tensors == 0) return rc;
+  accept::compact_batched_kernel<<<static_cast<unsigned>(per * n_requests),
+                                   accept::kCompactWarps * 32, 0, st>>>(
+      accepted, acc_stride, n_accepted, kb, static_cast<int>(per), status);
   return launch_status();
 }
