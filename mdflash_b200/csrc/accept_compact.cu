@@ -303,6 +303,30 @@ compact_kernel(const int64_t* __restrict__ keep, int cnt, KvDesc kv) {
 }
 
 // ---- batched: the walks of all requests, then all their compactions (two launches) ----
+
+// move_slice with the slice staged in shared memory (stage: this warp's kMaxRows x
+// vec_per_row vectors) instead of registers, so a CTA needs few registers and many warps
+// per SM keep loads in flight.
+__device__ __forceinline__ void move_slice_smem(const KvDesc& kv, int64_t slice,
+                                                const int64_t* keep, int cnt, int lane,
+                                                uint4* stage) {
+  const int64_t t = slice / kv.heads;
+  const int64_t h = slice % kv.heads;
+  unsigned char* base = static_cast<unsigned char*>(kv.ptrs[t]) +
+                        (h * kv.head_stride + kv.past_length * kv.seq_stride) * kv.elem_bytes;
+  const int64_t row_bytes = kv.seq_stride * kv.elem_bytes;
+  const int total = cnt * kv.vec_per_row;
+  for (int v = lane; v < total; v += 32) {
+    const int j = v / kv.vec_per_row, c = v % kv.vec_per_row;
+    if (keep[j] != j) stage[v] = *reinterpret_cast<const uint4*>(base + keep[j] * row_bytes + c * 16);
+  }
+  __syncwarp();
+  for (int v = lane; v < total; v += 32) {
+    const int j = v / kv.vec_per_row, c = v % kv.vec_per_row;
+    if (keep[j] != j) *reinterpret_cast<uint4*>(base + j * row_bytes + c * 16) = stage[v];
+  }
+  __syncwarp();  // the stage is reused for the warp's next slice
+}
 // Walk of request blockIdx.x (one warp): its tree is staged in shared memory, then walked
 // as in accept_compact_kernel; writes accepted[r], n_accepted[r], next_token[r].
 __global__ void __launch_bounds__(32)
@@ -367,6 +391,7 @@ struct KvBatch {
 __global__ void __launch_bounds__(kCompactWarps * 32)
 compact_batched_kernel(const int64_t* __restrict__ accepted, int64_t acc_stride,
                        const int32_t* __restrict__ n_accepted, KvBatch kb, int G, int* status) {
+  extern __shared__ __align__(16) unsigned char stage_raw[];
   __shared__ int64_t s_acc[kMaxRows];
   const int tid = threadIdx.x;
   const int r = blockIdx.x / G, g = blockIdx.x % G;
@@ -389,10 +414,11 @@ compact_batched_kernel(const int64_t* __restrict__ accepted, int64_t acc_stride,
   kv.vec_per_row = kb.vec_per_row;
   kv.past_length = kb.past[r];
   const int lane = tid & 31;
+  uint4* stage = reinterpret_cast<uint4*>(stage_raw) + (tid >> 5) * kMaxRows * kb.vec_per_row;
   const int64_t nslices = kv.n_tensors * kv.heads;
   for (int64_t sl = static_cast<int64_t>(g) * kCompactWarps + (tid >> 5); sl < nslices;
        sl += static_cast<int64_t>(G) * kCompactWarps)
-    move_slice(kv, sl, s_acc, cnt, lane);
+    move_slice_smem(kv, sl, s_acc, cnt, lane, stage);
 }
 
 inline int make_desc(void* const* kv_ptrs, int64_t n_tensors, int64_t heads, int64_t head_dim,
@@ -523,8 +549,14 @@ extern "C" int ddt_accept_compact_batched(
       static_cast<int>(max_nodes), accepted, acc_stride, n_accepted, next_token);
   rc = launch_status();
   if (rc != DDT_OK || n_tensors == 0) return rc;
+  const size_t stage = static_cast<size_t>(accept::kCompactWarps) * accept::kMaxRows *
+                       d.vec_per_row * 16;
+  if (cudaFuncSetAttribute(accept::compact_batched_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(stage)) != cudaSuccess)
+    return DDT_ERR_CUDA;
   accept::compact_batched_kernel<<<static_cast<unsigned>(per * n_requests),
-                                   accept::kCompactWarps * 32, 0, st>>>(
+                                   accept::kCompactWarps * 32, stage, st>>>(
       accepted, acc_stride, n_accepted, kb, static_cast<int>(per), status);
   return launch_status();
 }
