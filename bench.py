@@ -941,7 +941,8 @@ def measure_compact_batched(dev, n_requests, steps, warmup, prefix=1024):
         tables.append(K.KvTable([torch.empty((hkv, seq, d), dtype=torch.bfloat16, device=dev)
                                  for _ in range(2 * layers)]))
     kvb = K.KvBatch(tables)
-    pasts = [prefix] * n_requests
+    K.accept_compact_batched(posterior, trees, kvb, [prefix] * n_requests)  # checks the windows
+    pasts = torch.full((n_requests,), prefix, dtype=torch.int64, device=dev)
     out = (torch.zeros((n_requests, mn), dtype=torch.int64, device=dev),
            torch.zeros(n_requests, dtype=torch.int32, device=dev),
            torch.zeros(n_requests, dtype=torch.int64, device=dev))

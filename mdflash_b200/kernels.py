@@ -475,8 +475,9 @@ def accept_compact_batched(posteriors: torch.Tensor, trees: TreeBatch, kvb: KvBa
                            status: torch.Tensor | None = None):
     """ddt_accept_compact_batched: the greedy walk of every request's tree (trees, one row per
     request) under its posterior row (posteriors [R, max_budget + 1] i64) and the compaction of
-    its cache, one launch.  Returns (accepted [R, max_budget + 1], n_accepted i32 [R],
-    next_token i64 [R])."""
+    its cache.  past_lengths: a host list (checked against every cache's capacity) or a device
+    i64 tensor (trusted, no host work per call).  Returns (accepted [R, max_budget + 1],
+    n_accepted i32 [R], next_token i64 [R])."""
     dev = _require_cuda(posteriors)
     R = len(trees.budgets)
     mn = trees.max_budget + 1
@@ -484,12 +485,18 @@ def accept_compact_batched(posteriors: torch.Tensor, trees: TreeBatch, kvb: KvBa
         raise ValueError("posteriors must be i64 [requests, max_budget + 1] with unit stride")
     if len(kvb.tables) != R:
         raise ValueError("one KV table per request")
-    past = [int(x) for x in past_lengths]
-    for r in range(R):
-        n = 1 + expected_node_count(trees.depths, trees.vocab, trees.budgets[r])
-        if past[r] < 0 or past[r] + n > kvb.capacity[r]:
-            raise ValueError(f"request {r}: cache holds {kvb.capacity[r]} rows, the tree window "
-                             f"needs {past[r] + n}")
+    if isinstance(past_lengths, torch.Tensor) and past_lengths.is_cuda:
+        if past_lengths.dtype != torch.int64 or past_lengths.numel() != R:
+            raise ValueError("past_lengths must be i64 [requests]")
+        past_dev = past_lengths.contiguous()
+    else:
+        past = [int(x) for x in past_lengths]
+        for r in range(R):
+            n = 1 + expected_node_count(trees.depths, trees.vocab, trees.budgets[r])
+            if past[r] < 0 or past[r] + n > kvb.capacity[r]:
+                raise ValueError(f"request {r}: cache holds {kvb.capacity[r]} rows, the tree "
+                                 f"window needs {past[r] + n}")
+        past_dev = torch.tensor(past, dtype=torch.int64, device=dev)
     if accepted is None:
         accepted = torch.zeros((R, mn), dtype=torch.int64, device=dev)
     if n_accepted is None:
@@ -498,7 +505,6 @@ def accept_compact_batched(posteriors: torch.Tensor, trees: TreeBatch, kvb: KvBa
         next_token = torch.zeros(R, dtype=torch.int64, device=dev)
     if status is None:
         status = attention_status(dev)
-    past_dev = torch.tensor(past, dtype=torch.int64, device=dev)
     check(_lib.load().ddt_accept_compact_batched(
         R, posteriors.data_ptr(), posteriors.stride(0), trees.parents.data_ptr(),
         trees.parents.stride(0), trees.node_token_ids.data_ptr(), trees.node_token_ids.stride(0),
