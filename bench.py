@@ -24,8 +24,9 @@ Metric: verified + accepted tokens per second over all GPUs.
              launch time measured with CUDA events inside the step's graph, against the
              measured bf16 burst peak
   verify_step   sub-record: that single-request step alone (rank 0)
-  kernels    sub-record (N = 1): op-level tree build, argmax, compaction and attention at
-             the same shape, L2 flushed between launches
+  kernels    sub-record (N = 1): op-level tree build (single and batched over the mix),
+             argmax, compaction (single and batched over the mix), attention and the fused
+             lm_head at the same shape, L2 flushed between launches
   cpu_baseline  (N = 1) the CPU path of the reference restated (oracle): C tree build,
              torch CPU Qwen3 forward with SDPA + additive mask (fp32, all 36 layers; the
              layers share one set of weights to bound host memory, which leaves the
@@ -34,8 +35,8 @@ Metric: verified + accepted tokens per second over all GPUs.
 
 --impl reference: that CPU path alone on this host's cores (rank 0 only), one request of
 the mix per step, as many steps as fit a time budget (reported).
---workload verify / attn / tree / treebatch / argmax / compact / lmhead / splitkv: one
-sub-workload alone.
+--workload verify / attn / tree / treebatch / argmax / compact / compactbatch / lmhead /
+splitkv: one sub-workload alone.
 """
 from __future__ import annotations
 
