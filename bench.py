@@ -99,6 +99,10 @@ def parse_args():
                     help="requests workload: one batched tree-build launch for all of a rank's "
                          "requests per step (default), or one tree build inside each request's "
                          "graph")
+    ap.add_argument("--compaction", choices=["batched", "per-request"], default="batched",
+                    help="requests workload: one batched walk + compaction of all of the rank's "
+                         "requests after their verify replays (default), or each request's walk "
+                         "and compaction inside its graph")
     ap.add_argument("--lanes", type=int, default=4,
                     help="requests workload: replay the per-request graphs on this many streams "
                          "at once (requests split over the lanes by predicted cost; each lane "
@@ -469,6 +473,10 @@ def run_requests(args):
             lane_of[j] = ln
     order = [lst[t] for t in range(max((len(x) for x in lane_lists), default=0))
              for lst in lane_lists if t < len(lst)]
+    # the batched walk reads the batched build's trees
+    bcompact = args.compaction == "batched" and batched
+    posteriors = (torch.zeros((len(mine), trees.max_budget + 1), dtype=torch.int64, device=dev)
+                  if mine else None)
     caps = [None] * len(mine)
     for j in order:
         sp = specs[mine[j]]
@@ -478,7 +486,8 @@ def run_requests(args):
         # random prefix K / V seeded per request (the verify work does not depend on the
         # values; the results then do not depend on the rank or the capture order)
         _fill_prefix(cache, sp.prefix, g.manual_seed(1000 + sp.index))
-        ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner)
+        ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner,
+                           posterior=posteriors[j] if bcompact else None, walk=not bcompact)
         cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pools[ln],
                            tree=trees.tree(j) if batched else None, lane=ln,
                            capture_stream=cap_streams[ln] if cap_streams else None)
@@ -489,6 +498,17 @@ def run_requests(args):
     for j, (sp, cap) in enumerate(caps):
         records[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
         records[j, 5] = 0
+    if bcompact and caps:
+        kvb = K.KvBatch([cap.verifier.cache.kv_table() for _, cap in caps])
+        K.accept_compact_batched(posteriors, trees, kvb, [sp.prefix for sp, _ in caps])
+        past_dev = torch.tensor([sp.prefix for sp, _ in caps], dtype=torch.int64, device=dev)
+        b_acc = torch.zeros((len(caps), trees.max_budget + 1), dtype=torch.int64, device=dev)
+        b_n = torch.zeros(len(caps), dtype=torch.int32, device=dev)
+        b_next = torch.zeros(len(caps), dtype=torch.int64, device=dev)
+        m_path = min(S.MAX_PATH, trees.max_budget + 1)
+        # path columns a request's record holds: min(MAX_PATH, its node count), the rest -1
+        nn = torch.tensor([cap.result.n_nodes for _, cap in caps], device=dev)
+        path_cols = torch.arange(m_path, device=dev)[None, :] < nn[:, None]
 
     def one_step(e2e: bool):
         if e2e and batched and caps:  # this step's inputs from pinned host memory
@@ -507,14 +527,21 @@ def run_requests(args):
                     cap.draft_logits.copy_(host_logits[j], non_blocking=True)
                     cap.root_token.copy_(host_roots[j:j + 1], non_blocking=True)
                 r = cap.replay()
-                # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
-                records[j, 3] = r.n_accepted[0]
-                records[j, 4] = r.next_token[0]
-                m = min(S.MAX_PATH, r.n_nodes)
-                records[j, 6:6 + m] = r.accepted[:m]
+                if not bcompact:
+                    # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
+                    records[j, 3] = r.n_accepted[0]
+                    records[j, 4] = r.next_token[0]
+                    m = min(S.MAX_PATH, r.n_nodes)
+                    records[j, 6:6 + m] = r.accepted[:m]
         if streams:
             for st in streams:
                 main.wait_stream(st)
+        if bcompact and caps:
+            # every request's walk and compaction in one batched launch after the replays
+            K.accept_compact_batched(posteriors, trees, kvb, past_dev, b_acc, b_n, b_next)
+            records[:, 3] = b_n
+            records[:, 4] = b_next
+            records[:, 6:6 + m_path] = torch.where(path_cols, b_acc[:, :m_path], -1)
         return S.gather_results(records)
 
     def check_statuses():
@@ -560,8 +587,8 @@ def run_requests(args):
     check_statuses()
     h2d = (host_logits.numel() * host_logits.element_size() + host_roots.numel() * 8) if caps else 0
     d2h = int(allrec.numel()) * 8
-    launches = (sum(cap.launches_per_replay for _, cap in caps) + (1 if batched and caps else 0)) \
-        * args.steps
+    launches = (sum(cap.launches_per_replay for _, cap in caps) + (1 if batched and caps else 0)
+                + (2 if bcompact and caps else 0)) * args.steps
     sums = torch.tensor([float(h2d), float(launches)], device=dev)
     if world > 1:
         dist.all_reduce(sums, op=dist.ReduceOp.SUM)
@@ -591,12 +618,14 @@ def run_requests(args):
                                    "the slowest rank's requests back to back",
                           "ms": bound, "frac": bound / ms, "peak_source": peak_kind},
         "execution": ("one batched tree-build launch for the rank's requests, then "
-                      "one CUDA-graph replay per request (36-layer fused verify forward, argmax, "
-                      "accept walk + compaction)" if batched else
+                      "one CUDA-graph replay per request (36-layer fused verify forward, argmax"
+                      + (f") on {lanes} lanes, then one batched walk + compaction" if bcompact else
+                         ", accept walk + compaction)") if batched else
                       "one CUDA-graph replay per request (tree build, 36-layer fused verify "
                       "forward, argmax, accept walk + compaction)") +
                      "; records all-gathered per step",
         "tree_build": args.tree_build,
+        "compaction": "batched" if bcompact else "per-request",
         "lanes": lanes,
     }
     del caps

@@ -40,13 +40,17 @@ class StepResult:
 class TreeVerifier:
     def __init__(self, target: torch.nn.Module, cache: TreeKVCache, budget: int, depths: int,
                  vocab: int, device: torch.device | str = "cuda", keep_logits: bool = False,
-                 fused: bool = False, runner=None, fused_head: bool = False):
+                 fused: bool = False, runner=None, fused_head: bool = False,
+                 posterior: torch.Tensor | None = None, walk: bool = True):
         """fused=False runs the transformers model with attn_implementation="ddtree_tree";
         fused=True runs its weights through Qwen3VerifyRunner (fused elementwise stages); a
         runner can be shared between verifiers of the same model (runner=...).  With a
         runner, fused_head=True takes the greedy posterior from the fused lm_head -> argmax
         kernel instead of cuBLAS logits + ddt_argmax (no logits then, even with
-        keep_logits)."""
+        keep_logits).  posterior: an i64 buffer (>= budget + 1) to write the greedy posterior
+        into, e.g. one row of a batch; walk=False stops the step after the posterior (the
+        caller walks and compacts, for instance all requests at once with
+        K.accept_compact_batched)."""
         self.target = target
         self.runner = runner
         if fused and runner is None:
@@ -61,7 +65,11 @@ class TreeVerifier:
         self.fused_head = bool(fused_head)
         self.tree = K.DeviceTree.allocate(self.device, budget, depths, vocab)
         n_cap = budget + 1
-        self.posterior = torch.zeros(n_cap, dtype=torch.int64, device=self.device)
+        if posterior is not None and (posterior.numel() < n_cap or posterior.dtype != torch.int64):
+            raise ValueError("posterior buffer must be i64 with budget + 1 entries")
+        self.posterior = (posterior.view(-1) if posterior is not None else
+                          torch.zeros(n_cap, dtype=torch.int64, device=self.device))
+        self.walk = bool(walk)
         self.accepted = torch.zeros(n_cap, dtype=torch.int64, device=self.device)
         self.n_accepted = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.next_token = torch.zeros(1, dtype=torch.int64, device=self.device)
@@ -102,8 +110,9 @@ class TreeVerifier:
                                       use_cache=True)
                 logits = out.logits[0]
             post = K.argmax(logits, out=self.posterior[:n])
-        K.accept_compact(post, tree, self.cache.kv_table(), start, accepted=self.accepted,
-                         n_accepted=self.n_accepted, next_token=self.next_token, n_nodes=n)
+        if self.walk:
+            K.accept_compact(post, tree, self.cache.kv_table(), start, accepted=self.accepted,
+                             n_accepted=self.n_accepted, next_token=self.next_token, n_nodes=n)
         return StepResult(n, self.accepted, self.n_accepted, self.next_token, post, self.status,
                           logits if self.keep_logits and logits is not None else None)
 
