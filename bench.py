@@ -7,9 +7,10 @@ independent requests on a random-init Qwen3-8B-shaped target (36 layers, hidden 
 log-uniform in 1k..32k, tree budgets uniform over {64, 128, 256, 512}, drafter logits
 seeded per request (15 depths of N(0,1)*3).  A "step" verifies every request once: one
 batched tree-build launch for all of the rank's requests, then per request a CUDA-graph
-replay of the tree-attention verify forward -> greedy posterior -> accept walk -> KV
-compaction, the replays spread over 4 streams (--lanes) so that one request's launch gaps
-and kernel tails are filled by another's work; then the result records are all-gathered.
+replay of the tree-attention verify forward -> greedy posterior, the replays spread over 4
+streams (--lanes) so that one request's launch gaps and kernel tails are filled by another's
+work, then one batched accept walk + KV compaction of all the requests; then the result
+records are all-gathered.
 Requests are assigned to ranks by longest-processing-time first; there is no other
 cross-GPU traffic.
 Metric: verified + accepted tokens per second over all GPUs.
