@@ -232,6 +232,35 @@ __device__ __forceinline__ void move_slice(const KvDesc& kv, int64_t slice, cons
   }
 }
 
+// follow_verified_tree (ddtree.py:270-281) by one warp over a tree staged in shared memory
+// (s_par: parents, s_tok: node tokens with -1 for the root, s_post: posterior): from the root,
+// repeatedly the child whose token is the posterior of the current node (the last such child
+// in node order, as a dict built in node order keeps), at most kMaxRows nodes.  Lane 0 writes
+// the accepted node indices to acc; returns their count and sets next (the posterior of the
+// last accepted node) on every lane.
+__device__ __forceinline__ int walk_tree(const int32_t* s_par, const int64_t* s_tok,
+                                         const int64_t* s_post, int n_nodes, int64_t* acc,
+                                         int64_t& next) {
+  const int lane = threadIdx.x & 31;
+  int cur = 0, cnt = 1;
+  if (lane == 0) acc[0] = 0;
+  int64_t tok = s_post[0];
+  for (;;) {
+    int found = -1;
+    for (int i = 1 + lane; i < n_nodes; i += 32)
+      if (s_par[i] == cur && s_tok[i] == tok) found = i;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(DDT_FULL_MASK, found, o));
+    if (found < 0 || cnt >= kMaxRows) break;
+    cur = found;
+    if (lane == 0) acc[cnt] = cur;
+    ++cnt;
+    tok = s_post[cur];
+  }
+  next = tok;
+  return cnt;
+}
+
 // walk + compaction; every CTA replays the walk (it is a few shared-memory steps).
 __global__ void __launch_bounds__(kCompactWarps * 32)
 accept_compact_kernel(const int64_t* __restrict__ posterior, const int32_t* __restrict__ parents,
@@ -253,23 +282,9 @@ accept_compact_kernel(const int64_t* __restrict__ posterior, const int32_t* __re
   }
   __syncthreads();
   if (tid < 32) {
-    const int lane = tid;
-    int cur = 0, cnt = 1;
-    if (lane == 0) s_acc[0] = 0;
-    int64_t tok = s_post[0];
-    for (;;) {
-      int found = -1;
-      for (int i = 1 + lane; i < n_nodes; i += 32)
-        if (s_par[i] == cur && s_tok[i] == tok) found = i;  // last match, like a dict overwrite
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(DDT_FULL_MASK, found, o));
-      if (found < 0 || cnt >= kMaxRows) break;
-      cur = found;
-      if (lane == 0) s_acc[cnt] = cur;
-      ++cnt;
-      tok = s_post[cur];
-    }
-    if (lane == 0) {
+    int64_t tok;
+    const int cnt = walk_tree(s_par, s_tok, s_post, n_nodes, s_acc, tok);
+    if (tid == 0) {
       s_cnt = cnt;
       s_next = tok;
     }
@@ -354,22 +369,8 @@ accept_walk_batched_kernel(const int64_t* __restrict__ posterior, int64_t post_s
     s_post[i] = post[i];
   }
   __syncwarp();
-  int64_t* acc = accepted + r * acc_stride;
-  int cur = 0, cnt = 1;
-  if (lane == 0) acc[0] = 0;
-  int64_t tok = s_post[0];
-  for (;;) {
-    int found = -1;
-    for (int i = 1 + lane; i < n_nodes; i += 32)
-      if (s_par[i] == cur && s_tok[i] == tok) found = i;  // last match, like a dict overwrite
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) found = max(found, __shfl_xor_sync(DDT_FULL_MASK, found, o));
-    if (found < 0 || cnt >= kMaxRows) break;
-    cur = found;
-    if (lane == 0) acc[cnt] = cur;
-    ++cnt;
-    tok = s_post[cur];
-  }
+  int64_t tok;
+  const int cnt = walk_tree(s_par, s_tok, s_post, n_nodes, accepted + r * acc_stride, tok);
   if (lane == 0) {
     n_accepted[r] = cnt;
     next_token[r] = tok;
