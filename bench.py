@@ -1137,11 +1137,14 @@ def run_splitkv(args):
     def step(events=None):
         if events:
             events[0].record()
-        o, m, l = K.tree_attention_partial_merged(q, k, v, kb, ke, bits, P)
+        if xchg is not None:  # the merge of the shard's splits stores into every rank's buffer
+            xchg.attend_push(q, k, v, kb, ke, bits, P)
+        else:
+            o, m, l = K.tree_attention_partial_merged(q, k, v, kb, ke, bits, P)
         if events:
             events[1].record()
         if xchg is not None:
-            xchg.exchange_merge(o, m, l, out=out)
+            xchg.merge(out)
         else:
             og, mg, lg = S.gather_partials(o, m, l)
             K.attn_merge(og, mg, lg, n, 32, out=out)
@@ -1186,9 +1189,9 @@ def run_splitkv(args):
         "config": {"workload": f"split-KV tree attention: prefix {P} sharded over {world} GPUs, "
                                f"{n} tree rows, Hq 32 / Hkv 8, D 128; compaction of a "
                                f"{len(path)}-row path on the owner shard",
-                   "exchange": ("NVLink peer stores of fp32 (O, m, l) partials into every "
-                                "rank's buffer (ddt_peer_push) + counter wait and merge "
-                                "(ddt_peer_merge)" if xchg is not None else
+                   "exchange": ("the shard's split merge stores the fp32 (O, m, l) partial "
+                                "into every rank's buffer over NVLink (ddt_tree_attn_partial_push)"
+                                "; counter wait and merge (ddt_peer_merge)" if xchg is not None else
                                 "NCCL all-gather of fp32 (O, m, l) partials + ddt_attn_merge"),
                    "partial_bytes_received_per_rank": link_bytes},
         "split": {"shard_attention_ms": shard_ms, "exchange_and_merge_ms": xchg_ms,

@@ -320,6 +320,22 @@ int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_pa
  * 2 s; on expiry it sets *status non-zero and the output is incomplete), then merges the world
  * partials like ddt_attn_merge.  Two parities of the buffer alternate between calls. */
 size_t ddt_peer_buffer_bytes(int64_t world, int64_t n_nodes, int64_t q_heads, int64_t head_dim);
+/* ddt_tree_attn_partial_merged and ddt_peer_push in one call: this rank's shard attention,
+ * whose merge of the shard's key splits (when K / V exceed L2, the uniform-split plan) stores
+ * the merged partial straight into every rank's receive buffer and bumps the counters; other
+ * plans merge into the workspace and push with a copy kernel.  Workspace:
+ * ddt_tree_attn_partial_push_workspace_bytes. */
+size_t ddt_tree_attn_partial_push_workspace_bytes(int64_t n_nodes, int64_t q_heads,
+                                                  int64_t head_dim);
+int ddt_tree_attn_partial_push(const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                               const void* k, const void* v, int64_t kv_head_stride,
+                               int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
+                               int64_t n_nodes, int64_t past_length, int64_t q_heads,
+                               int64_t kv_heads, int64_t head_dim, const uint32_t* anc_bits,
+                               int64_t anc_words, int mask_mode, float scale,
+                               void* const* peer_bases, int64_t world, int64_t rank,
+                               uint32_t epoch, uint32_t* ticket, void* workspace,
+                               size_t workspace_bytes, int32_t* status, void* stream);
 int ddt_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
 int ddt_peer_open(const void* ipc_handle, void** ptr);
 int ddt_peer_close(void* ptr);

@@ -64,6 +64,10 @@ SIGNATURES = {
                                       _P]),
     "ddt_attn_merge": (_i, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P]),
     "ddt_peer_buffer_bytes": (_S, [_I, _I, _I, _I]),
+    "ddt_tree_attn_partial_push_workspace_bytes": (_S, [_I, _I, _I]),
+    "ddt_tree_attn_partial_push": (_i, [_P, _I, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I,
+                                        _P, _I, _i, _F, _P, _I, _I, ctypes.c_uint32, _P, _P, _S,
+                                        _P, _P]),
     "ddt_peer_alloc": (_i, [_S, _P, _P]),
     "ddt_peer_open": (_i, [_P, _P]),
     "ddt_peer_close": (_i, [_P]),

@@ -21,34 +21,12 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace ddt {
 namespace peer {
 
-constexpr int kMaxWorld = 8;  // ranks of one node
-constexpr int kHeadDim = 128;
 constexpr int kStatusTimeout = 1;
-
-struct Layout {
-  size_t o[2], m[2], l[2], total;
-};
-
-inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
-
-inline Layout layout(int64_t world, int64_t rows) {
-  Layout L;
-  size_t off = 256;  // counters
-  for (int p = 0; p < 2; ++p) {
-    L.o[p] = off;
-    off = align256(off + sizeof(float) * static_cast<size_t>(world * rows * kHeadDim));
-    L.m[p] = off;
-    off = align256(off + sizeof(float) * static_cast<size_t>(world * rows));
-    L.l[p] = off;
-    off = align256(off + sizeof(float) * static_cast<size_t>(world * rows));
-  }
-  L.total = off;
-  return L;
-}
 
 struct Dests {
   unsigned char* base[kMaxWorld];

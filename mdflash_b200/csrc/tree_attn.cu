@@ -31,6 +31,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "tc.cuh"
 
 namespace ddt {
@@ -820,31 +821,58 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ o_parts,
   }
 }
 
+// push.world > 0 (split-KV over NVLink peer memory): the merged partial goes to slot
+// push.rank of every rank's receive buffer instead of o_merged / m_merged / l_merged, and the
+// grid's last CTA (ticket), after a system-scope fence, bumps counter push.rank in each.
 __global__ void merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ m_parts,
                              const float* __restrict__ l_parts, int n_parts, long long rows,
                              int q_heads, __nv_bfloat16* __restrict__ out, long long o_node_stride,
                              long long o_head_stride, float* __restrict__ o_merged,
-                             float* __restrict__ m_merged, float* __restrict__ l_merged) {
+                             float* __restrict__ m_merged, float* __restrict__ l_merged,
+                             const __grid_constant__ peer::Push push) {
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  float4 acc;
-  float M, L;
-  merge_row(o_parts, m_parts, l_parts, n_parts,
-            [&](int i) { return static_cast<long long>(i) * rows + row; }, lane, acc, M, L);
-  if (out) {
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const long long node = row / q_heads, qh = row % q_heads;
-    __nv_bfloat16* orow = out + node * o_node_stride + qh * o_head_stride + lane * 4;
-    uint2 v;
-    v.x = tc::pack_bf16x2(acc.x * inv, acc.y * inv);
-    v.y = tc::pack_bf16x2(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(orow) = v;
-  } else {
-    *reinterpret_cast<float4*>(o_merged + row * kHeadDim + lane * 4) = acc;
-    if (lane == 0) {
-      m_merged[row] = M;
-      l_merged[row] = L;
+  if (row < rows) {  // warp-uniform
+    float4 acc;
+    float M, L;
+    merge_row(o_parts, m_parts, l_parts, n_parts,
+              [&](int i) { return static_cast<long long>(i) * rows + row; }, lane, acc, M, L);
+    if (out) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      const long long node = row / q_heads, qh = row % q_heads;
+      __nv_bfloat16* orow = out + node * o_node_stride + qh * o_head_stride + lane * 4;
+      uint2 v;
+      v.x = tc::pack_bf16x2(acc.x * inv, acc.y * inv);
+      v.y = tc::pack_bf16x2(acc.z * inv, acc.w * inv);
+      *reinterpret_cast<uint2*>(orow) = v;
+    } else if (push.world > 0) {
+      const long long slot = static_cast<long long>(push.rank) * rows + row;
+      for (int w = 0; w < push.world; ++w) {
+        reinterpret_cast<float4*>(push.base[w] + push.o_off)[slot * (kHeadDim / 4) + lane] = acc;
+        if (lane == 0) {
+          reinterpret_cast<float*>(push.base[w] + push.m_off)[slot] = M;
+          reinterpret_cast<float*>(push.base[w] + push.l_off)[slot] = L;
+        }
+      }
+    } else {
+      *reinterpret_cast<float4*>(o_merged + row * kHeadDim + lane * 4) = acc;
+      if (lane == 0) {
+        m_merged[row] = M;
+        l_merged[row] = L;
+      }
+    }
+  }
+  if (push.world > 0) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned int t = atomicAdd(push.ticket, 1u);
+      if (t == gridDim.x - 1) {
+        __threadfence_system();
+        for (int w = 0; w < push.world; ++w)
+          atomicAdd_system(reinterpret_cast<unsigned int*>(push.base[w]) + push.rank, 1u);
+        atomicExch(push.ticket, 0u);
+      }
     }
   }
 }
@@ -1263,7 +1291,8 @@ inline size_t plan_workspace(const Launch& L, int kind) {
 // row in (node, q head) order: o_merged [rows, 128], m_merged / l_merged [rows].
 inline int run(Launch& L, int kind, int64_t kv_heads, void* workspace, size_t workspace_bytes,
                __nv_bfloat16* out, int64_t o_node_stride, int64_t o_head_stride, float* o_merged,
-               float* m_merged, float* l_merged, cudaStream_t st) {
+               float* m_merged, float* l_merged, cudaStream_t st,
+               const peer::Push& push = peer::Push{}) {
   Params& p = L.p;
   const int64_t rows = static_cast<int64_t>(p.n_nodes) * p.q_heads;
   if (kind == kPlanSingle) {
@@ -1306,7 +1335,7 @@ inline int run(Launch& L, int kind, int64_t kv_heads, void* workspace, size_t wo
   const int wpb = 8;
   merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0, st>>>(
       op, mp, lp, p.n_splits, rows, p.q_heads, out, o_node_stride, o_head_stride, o_merged,
-      m_merged, l_merged);
+      m_merged, l_merged, push);
   return launch_status();
 }
 
@@ -1469,6 +1498,71 @@ extern "C" int ddt_tree_attn_partial_merged(
                    l_part, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int ddt_peer_push(const float* o, const float* m, const float* l, int64_t n_nodes,
+                             int64_t q_heads, int64_t head_dim, void* const* peer_bases,
+                             int64_t world, int64_t rank, uint32_t epoch, uint32_t* ticket,
+                             void* stream);
+
+// rows x (128 + 2) fp32 after the partials, for plans whose merge is not the uniform one
+extern "C" size_t ddt_tree_attn_partial_push_workspace_bytes(int64_t n_nodes, int64_t q_heads,
+                                                             int64_t head_dim) {
+  const size_t rows = static_cast<size_t>(n_nodes > 0 ? n_nodes : 0) *
+                      static_cast<size_t>(q_heads > 0 ? q_heads : 0);
+  return peer::align256(ddt_tree_attn_workspace_bytes(n_nodes, q_heads, head_dim, 0)) +
+         peer::align256(rows * (attn::kHeadDim + 2) * sizeof(float));
+}
+
+extern "C" int ddt_tree_attn_partial_push(
+    const void* q, int64_t q_node_stride, int64_t q_head_stride, const void* k, const void* v,
+    int64_t kv_head_stride, int64_t kv_seq_stride, int64_t key_begin, int64_t key_end,
+    int64_t n_nodes, int64_t past_length, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+    const uint32_t* anc_bits, int64_t anc_words, int mask_mode, float scale,
+    void* const* peer_bases, int64_t world, int64_t rank, uint32_t epoch, uint32_t* ticket,
+    void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!peer_bases || !ticket || epoch == 0 || !workspace) return DDT_ERR_INVALID;
+  if (world <= 0 || world > peer::kMaxWorld) return DDT_ERR_CAPACITY;
+  if (rank < 0 || rank >= world) return DDT_ERR_INVALID;
+  for (int w = 0; w < world; ++w)
+    if (!peer_bases[w] || !aligned(peer_bases[w], 256)) return DDT_ERR_INVALID;
+  attn::Launch L;
+  int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride,
+                         key_begin, key_end, n_nodes, past_length, q_heads, kv_heads, head_dim,
+                         anc_bits, anc_words, mask_mode, scale);
+  if (rc) return rc;
+  int kind = 0;
+  rc = attn::choose_plan(L, kv_heads, 0, true, kind);
+  if (rc) return rc;
+  L.p.status = status;
+  const int64_t rows = n_nodes * q_heads;
+  const size_t part = peer::align256(attn::plan_workspace(L, kind));
+  const size_t local = peer::align256(static_cast<size_t>(rows) * (attn::kHeadDim + 2) * sizeof(float));
+  if (workspace_bytes < part + local) return DDT_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (kind == attn::kPlanUniform) {
+    // the merge of the shard's key splits stores straight into every rank's buffer
+    const peer::Layout lay = peer::layout(world, rows);
+    const int par = static_cast<int>(epoch & 1u);
+    peer::Push push{};
+    for (int w = 0; w < world; ++w) push.base[w] = static_cast<unsigned char*>(peer_bases[w]);
+    push.world = static_cast<int>(world);
+    push.rank = static_cast<int>(rank);
+    push.o_off = lay.o[par];
+    push.m_off = lay.m[par];
+    push.l_off = lay.l[par];
+    push.ticket = ticket;
+    return attn::run(L, kind, kv_heads, workspace, workspace_bytes, nullptr, 0, 0, nullptr,
+                     nullptr, nullptr, st, push);
+  }
+  // balanced shards (K / V within L2): merged locally, then pushed by a copy kernel
+  float* o = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + part);
+  float* m = o + static_cast<size_t>(rows) * attn::kHeadDim;
+  float* l = m + rows;
+  rc = attn::run(L, kind, kv_heads, workspace, part, nullptr, 0, 0, o, m, l, st);
+  if (rc) return rc;
+  return ddt_peer_push(o, m, l, n_nodes, q_heads, head_dim, peer_bases, world, rank, epoch,
+                       ticket, stream);
+}
+
 extern "C" int ddt_attn_merge(const float* o_parts, const float* m_parts, const float* l_parts,
                               int64_t n_parts, int64_t n_nodes, int64_t q_heads, int64_t head_dim,
                               void* out, int64_t o_node_stride, int64_t o_head_stride,
@@ -1483,7 +1577,8 @@ extern "C" int ddt_attn_merge(const float* o_parts, const float* m_parts, const 
   attn::merge_kernel<<<static_cast<unsigned>((rows + wpb - 1) / wpb), wpb * 32, 0,
                        static_cast<cudaStream_t>(stream)>>>(
       o_parts, m_parts, l_parts, static_cast<int>(n_parts), rows, static_cast<int>(q_heads),
-      static_cast<__nv_bfloat16*>(out), o_node_stride, o_head_stride, nullptr, nullptr, nullptr);
+      static_cast<__nv_bfloat16*>(out), o_node_stride, o_head_stride, nullptr, nullptr, nullptr,
+      peer::Push{});
   return launch_status();
 }
 

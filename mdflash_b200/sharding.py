@@ -264,6 +264,58 @@ class PeerExchange:
         K.STATS.launches += 3
         return out
 
+    def attend(self, q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
+               key_begin: int, key_end: int, anc_bits: torch.Tensor | None, past_length: int,
+               scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's shard attention whose merge stores the partial straight into every
+        rank's buffer (ddt_tree_attn_partial_push, one call), then the counter-waiting merge
+        of all ranks' partials (ddt_peer_merge).  Returns the bf16 output [N, Hq, D]."""
+        self.attend_push(q, k_shard, v_shard, key_begin, key_end, anc_bits, past_length, scale)
+        return self.merge(out)
+
+    def attend_push(self, q, k_shard, v_shard, key_begin: int, key_end: int, anc_bits,
+                    past_length: int, scale: float | None = None) -> None:
+        """The first half of attend: shard attention + push of this call's partial."""
+        from . import kernels as K
+        from ._lib import DDT_MASK_TREE, check
+        n, hq, qns, qhs = K._q_view(q)
+        hkv, s_local, khs, kss = K._kv_view(k_shard)
+        d = q.shape[-1]
+        if (n, hq, d) != (self.n_nodes, self.q_heads, self.head_dim):
+            raise ValueError("query shape differs from the exchange's")
+        if s_local < key_end - key_begin:
+            raise ValueError("shard shorter than its key range")
+        if scale is None:
+            scale = 1.0 / math.sqrt(d)
+        ws_bytes = self._lib.ddt_tree_attn_partial_push_workspace_bytes(n, hq, d)
+        ws = K.WORKSPACES.get(self.device, "attn_partial_push", ws_bytes)
+        words = anc_bits.shape[1] if anc_bits is not None else 0
+        self.epoch += 1
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        check(self._lib.ddt_tree_attn_partial_push(
+            q.data_ptr(), qns, qhs, k_shard.data_ptr(), v_shard.data_ptr(), khs, kss, key_begin,
+            key_end, n, past_length, hq, hkv, d,
+            anc_bits.data_ptr() if anc_bits is not None else None, words, DDT_MASK_TREE,
+            float(scale), ctypes.cast(self._bases, ctypes.c_void_p), self.world, self.rank,
+            self.epoch & 0xffffffff, self.ticket.data_ptr(), ws.data_ptr(), ws.numel(),
+            self.status.data_ptr(), st), "ddt_tree_attn_partial_push")
+        K.STATS.launches += 2
+
+    def merge(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The second half of attend: wait for every rank's push of the current call, merge."""
+        from . import kernels as K
+        from ._lib import check
+        n, hq, d = self.n_nodes, self.q_heads, self.head_dim
+        if out is None:
+            out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=self.device)
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        check(self._lib.ddt_peer_merge(self.local, self.world, n, hq, d, self.epoch & 0xffffffff,
+                                       out.data_ptr(), out.stride(0), out.stride(1),
+                                       self.status.data_ptr(), self.timeout_ns, st),
+              "ddt_peer_merge")
+        K.STATS.launches += 2
+        return out
+
     def close(self) -> None:
         """Releases the IPC mappings and the buffer (after a barrier, so that no peer still
         writes into it)."""
@@ -285,14 +337,16 @@ def splitkv_attention(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Ten
                       out: torch.Tensor | None = None,
                       exchange: PeerExchange | None = None) -> torch.Tensor:
     """Tree attention over a sequence-sharded prefix: this rank's keys spread over all of its
-    SMs and merged in-GPU to one partial per row, the partials of all ranks exchanged (over
-    NVLink peer memory with ``exchange``, else one NCCL all-gather), merge.  Returns the bf16
-    output [N, Hq, D] on every rank."""
+    SMs and merged in-GPU to one partial per row, the partials of all ranks exchanged, merge.
+    With ``exchange`` the in-GPU merge itself stores the partial into every rank's buffer over
+    NVLink (PeerExchange.attend); without, one NCCL all-gather.  Returns the bf16 output
+    [N, Hq, D] on every rank."""
     from . import kernels as K
     n, hq = q.shape[0], q.shape[1]
+    if exchange is not None:
+        return exchange.attend(q, k_shard, v_shard, key_begin, key_end, anc_bits, past_length,
+                               scale=scale, out=out)
     o, m, l = K.tree_attention_partial_merged(q, k_shard, v_shard, key_begin, key_end, anc_bits,
                                               past_length, scale=scale)
-    if exchange is not None:
-        return exchange.exchange_merge(o, m, l, out=out)
     og, mg, lg = gather_partials(o, m, l, group)
     return K.attn_merge(og, mg, lg, n, hq, out=out)

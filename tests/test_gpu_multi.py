@@ -83,9 +83,37 @@ def test_peer_exchange_one_rank(cuda_device):
             assert torch.equal(got, ref)
             assert _rel(got, full) <= 1e-2
             assert int(x.status.item()) == 0
-            again = S.splitkv_attention(q, k, v, 0, P + N, bits, P, exchange=x)
+            again = x.attend(q, k, v, 0, P + N, bits, P)
             torch.cuda.synchronize()
             assert torch.equal(again, ref)
+    finally:
+        x.close()
+
+
+@pytest.mark.parametrize("past", [4096, 20000])
+def test_peer_exchange_fused_merge_one_rank(cuda_device, past):
+    """PeerExchange.attend (world 1): the shard attention's own merge stores into the receive
+    buffer.  At 20000 keys the K / V exceed L2 and the shard runs the uniform-split plan,
+    whose merge kernel pushes; at 4096 the balanced plan merges locally and a copy kernel
+    pushes.  Both equal partial_merged + ddt_attn_merge exactly, call after call."""
+    g = torch.Generator().manual_seed(1)
+    sc = 128 ** -0.5
+    q = (torch.randn((N, 32, 128), generator=g) * sc).to(torch.bfloat16).to(cuda_device)
+    k = (torch.randn((8, past + N, 128), generator=g) * sc).to(torch.bfloat16).to(cuda_device)
+    v = torch.randn((8, past + N, 128), generator=g).to(torch.bfloat16).to(cuda_device)
+    bits = torch.from_numpy(oracle.ancestor_bits(gin.random_tree(N, 4)).view(np.int32)).to(
+        cuda_device)
+    o, m, l = K.tree_attention_partial_merged(q, k, v, 0, past + N, bits, past)
+    ref = K.attn_merge(o[None], m[None], l[None], N, 32)
+    full = K.tree_attention(q, k, v, bits, past)
+    x = S.PeerExchange(N, 32, cuda_device)
+    try:
+        for _ in range(3):
+            got = S.splitkv_attention(q, k, v, 0, past + N, bits, past, exchange=x)
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref)
+            assert int(x.status.item()) == 0
+        assert _rel(got, full) <= 1e-2
     finally:
         x.close()
 
