@@ -24,7 +24,9 @@ Metric: verified + accepted tokens per second over all GPUs.
              shape (prefix 8192, 257 tree rows): algorithmic FLOPs per launch over the
              launch time measured with CUDA events inside the step's graph, against the
              measured bf16 burst peak
-  verify_step   sub-record: that single-request step alone (rank 0)
+  verify_step   sub-record: that single-request step alone (rank 0), and its decode_loop:
+             16 rounds of a decode loop that replay ONE graph recorded with the prefix
+             length in device memory (start advances by the accepted count every round)
   kernels    sub-record (N = 1): op-level tree build (single and batched over the mix),
              argmax, compaction (single and batched over the mix), attention and the fused
              lm_head at the same shape, L2 flushed between launches
@@ -65,6 +67,7 @@ QWEN3_8B = dict(layers=36, hidden=4096, heads=32, kv_heads=8, head_dim=128, mlp=
 PARAMS_8B = 8.19e9
 METRIC = "verified+accepted tokens/s"
 VERIFY_PREFIX, VERIFY_BUDGET = 8192, 256
+LOOP_ROUNDS = 16  # decode-loop rounds replayed on one graph (verify_step's decode_loop)
 
 
 def parse_args():
@@ -663,7 +666,7 @@ def verify_step(args, model, runner, dev, steps: int, warmup: int, prefix: int =
     from mdflash_b200.verifier import CapturedStep, TreeVerifier
     ids, logits = single_request_inputs(prefix)
     P, B = prefix, budget
-    cache = TreeKVCache(QWEN3_8B["layers"], P + B + 1 + 64).allocate(
+    cache = TreeKVCache(QWEN3_8B["layers"], P + B + 1 + LOOP_ROUNDS * (DEPTHS + 1)).allocate(
         QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
     verifier = TreeVerifier(model, cache, B, DEPTHS, V, dev, runner=runner)
     with torch.inference_mode():
@@ -704,6 +707,7 @@ def verify_step(args, model, runner, dev, steps: int, warmup: int, prefix: int =
     step_bound = step_roofline_ms(P, n_nodes, peaks)
     launches = cap.launches_per_replay
     del cap
+    loop = decode_loop(verifier, draft_dev, root_dev, P, LOOP_ROUNDS, warmup, ms)
     return {
         "workload": f"Qwen3-8B-shaped verify step: 36 layers, prefix {P}, {B}-node best-first tree "
                     "(15 depths), bf16, one CUDA-graph replay per step",
@@ -721,7 +725,51 @@ def verify_step(args, model, runner, dev, steps: int, warmup: int, prefix: int =
                      "flops_per_launch": flops, "launch_ms": attn_mean,
                      "launches_timed": len(attn_ms),
                      "traffic": traffic.get("bytes_per_launch") if traffic else None},
+        "decode_loop": loop,
     }
+
+
+def decode_loop(verifier, draft_dev, root_dev, P: int, rounds: int, warmup: int,
+                fixed_ms: float) -> dict:
+    """`rounds` rounds of a decode loop (ddtree.py:417-506) on ONE CUDA graph recorded with
+    the prefix length in device memory (CapturedStep(max_start=...)): each round replays it at
+    the current start, reads the accepted count (the loop's one host sync per round),
+    commits, advances start by the accepted count and feeds the next token back as the root.
+    Timed with CUDA events around all rounds, host gaps included; the cache is restored to
+    the prefix afterwards."""
+    from mdflash_b200.verifier import CapturedStep
+    cache = verifier.cache
+    max_start = P + rounds * (DEPTHS + 1)
+    cap = CapturedStep(verifier, P, warmup=1, max_start=max_start)
+    cap.draft_logits.copy_(draft_dev)
+
+    def run():
+        cap.root_token.copy_(root_dev)
+        start, acc = P, []
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(rounds):
+            res = cap.replay(start)
+            k = int(res.n_accepted.item())
+            verifier.commit(start, k)
+            acc.append(k)
+            start += k
+            cap.root_token.copy_(res.next_token)
+        ev1.record()
+        torch.cuda.synchronize()
+        cache.set_seq_length(P)
+        return ev0.elapsed_time(ev1), acc, res.n_nodes
+
+    for _ in range(warmup):
+        run()
+    total_ms, acc, n_nodes = run()
+    del cap
+    ms = total_ms / rounds
+    return {"rounds": rounds, "graphs_recorded": 1, "max_start": max_start,
+            "start_first": P, "start_last": P + sum(acc) - acc[-1],
+            "accepted_per_round": float(np.mean(acc)), "ms_per_round": ms,
+            "value": (rounds * n_nodes + sum(acc)) / (total_ms / 1e3), "unit": "tokens/s",
+            "vs_fixed_prefix_step": ms / fixed_ms}
 
 
 # ------------------------------------------------------------ op-level measurements

@@ -238,6 +238,25 @@ int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_head_stride, c
                   int64_t kv_splits, void* workspace, size_t workspace_bytes, int32_t* status,
                   void* stream);
 
+/* ddt_tree_attn with the prefix length in device memory: *past_length_dev (i64, 8-byte
+ * aligned) is read when the kernel runs, so that one launch recorded in a CUDA graph serves
+ * every prefix length up to max_past_length (a decode loop whose prefix grows every round).
+ * k, v: [kv_heads, max_past_length + n_nodes, head_dim] views; the tree's rows sit at
+ * [live, live + n_nodes) and every key after them is masked.  The plan is the one of
+ * ddt_tree_attn at max_past_length, and so is the cost.  mask_mode DDT_MASK_TREE or
+ * DDT_MASK_CAUSAL; status is required: a live length outside [0, max_past_length] sets bit
+ * 4 (the launch then runs at max_past_length, in bounds, and its output is not meaningful),
+ * an expired wait bit 1.  Replaces the same call as ddt_tree_attn (sdpa_attention.py:92 via
+ * ddtree.py:467), where the reference's prefix length is host state. */
+int ddt_tree_attn_device_past(const void* q, int64_t q_node_stride, int64_t q_head_stride,
+                              const void* k, const void* v, int64_t kv_head_stride,
+                              int64_t kv_seq_stride, void* out, int64_t o_node_stride,
+                              int64_t o_head_stride, int64_t n_nodes, int64_t max_past_length,
+                              const int64_t* past_length_dev, int64_t q_heads, int64_t kv_heads,
+                              int64_t head_dim, const uint32_t* anc_bits, int64_t anc_words,
+                              int mask_mode, float scale, int64_t kv_splits, void* workspace,
+                              size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Host-only query of the launch plan ddt_tree_attn uses for these sizes (key_end < 0, e.g.
  * -1), or ddt_tree_attn_partial_merged for the key shard [key_begin, key_end) (key_end >= 0;
  * an empty shard [b, b) included), computed by the same host function those entry points
@@ -364,6 +383,12 @@ int ddt_peer_merge(const void* local_base, int64_t world, int64_t n_nodes, int64
  *   (cos | sin << 16); table 16-byte aligned.  Built once per forward.
  * ddt_qk_norm_rope_cache_table: ddt_qk_norm_rope_cache with cos / sin read from that table
  *   (bit-identical results).
+ * ddt_qk_norm_rope_cache_table_device_past: the table form with the prefix length read from
+ *   device memory (*past_length_dev, i64, 8-byte aligned) when the kernel runs, so that a
+ *   recorded verify step serves every prefix length; the caches must hold max_past_length +
+ *   n_tokens rows, and a value outside [0, max_past_length] writes nothing (the step's
+ *   ddt_tree_attn_device_past reports it).  No counterpart in the reference, whose cache
+ *   length is host state (cache_utils.py:102-121).
  * ddt_silu_mul: out[r, i] = silu(gate_up[r, i]) * gate_up[r, inter + i]; Qwen3MLP.forward
  *   (modeling_qwen3.py:81-83) between its projections. */
 int ddt_add_rmsnorm(const void* x, const void* delta, const void* weight, int64_t rows,
@@ -380,6 +405,13 @@ int ddt_qk_norm_rope_cache_table(const void* qkv, int64_t n_tokens, int64_t q_he
                                  const void* k_norm_w, float eps, const void* rope_table,
                                  void* q_out, void* k_cache, void* v_cache, int64_t head_stride,
                                  int64_t seq_stride, int64_t past_length, void* stream);
+int ddt_qk_norm_rope_cache_table_device_past(const void* qkv, int64_t n_tokens, int64_t q_heads,
+                                             int64_t kv_heads, int64_t head_dim,
+                                             const void* q_norm_w, const void* k_norm_w,
+                                             float eps, const void* rope_table, void* q_out,
+                                             void* k_cache, void* v_cache, int64_t head_stride,
+                                             int64_t seq_stride, int64_t max_past_length,
+                                             const int64_t* past_length_dev, void* stream);
 int ddt_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* out, void* stream);
 
 /* additive mask block [n_nodes, n_nodes] (row stride in elements; 0 = visible) ->

@@ -53,6 +53,8 @@ SIGNATURES = {
     "ddt_tree_attn_workspace_bytes": (_S, [_I, _I, _I, _I]),
     "ddt_tree_attn": (_i, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _i,
                            _F, _I, _P, _S, _P, _P]),
+    "ddt_tree_attn_device_past": (_i, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _I, _I, _I, _P, _I, _I,
+                                       _I, _P, _I, _i, _F, _I, _P, _S, _P, _P]),
     "ddt_tree_attn_partial_splits": (_I, [_I, _I, _I, _I]),
     "ddt_tree_attn_plan": (_i, [_I, _I, _I, _I, _I, _I, _I, _P]),
     "ddt_tree_attn_partial": (_i, [_P, _I, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I,
@@ -82,6 +84,8 @@ SIGNATURES = {
     "ddt_rope_table": (_i, [_P, _I, _P, _I, _F, _P, _P]),
     "ddt_qk_norm_rope_cache_table": (_i, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _P, _I, _I,
                                           _I, _P]),
+    "ddt_qk_norm_rope_cache_table_device_past": (_i, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P,
+                                                      _P, _I, _I, _I, _P, _P]),
     "ddt_silu_mul": (_i, [_P, _I, _I, _P, _P]),
 }
 

@@ -17,12 +17,41 @@ from . import kernels as K
 
 
 class TreeKVLayer(DynamicLayer):
+    """``keys`` / ``values`` are views of the live rows, built when read: a decode loop sets
+    the length every round, and building two views per layer there cost ~5 us each on the
+    host (0.35 ms per round at 36 layers)."""
+
     def __init__(self, capacity: int):
         super().__init__()
         self.capacity = int(capacity)
         self.length = 0
         self.k_buf: torch.Tensor | None = None
         self.v_buf: torch.Tensor | None = None
+        self._views: tuple[int, torch.Tensor, torch.Tensor] | None = None
+
+    def _live(self, i: int):
+        if getattr(self, "k_buf", None) is None:
+            return self.__dict__.get("_unset_kv", (None, None))[i]
+        if self._views is None or self._views[0] != self.length:
+            self._views = (self.length, self.k_buf[..., :self.length, :],
+                           self.v_buf[..., :self.length, :])
+        return self._views[1 + i]
+
+    @property
+    def keys(self):
+        return self._live(0)
+
+    @keys.setter
+    def keys(self, t):  # before the buffers exist (the base class sets None)
+        self.__dict__["_unset_kv"] = (t, self.__dict__.get("_unset_kv", (None, None))[1])
+
+    @property
+    def values(self):
+        return self._live(1)
+
+    @values.setter
+    def values(self, t):
+        self.__dict__["_unset_kv"] = (self.__dict__.get("_unset_kv", (None, None))[0], t)
 
     def lazy_initialization(self, key_states: torch.Tensor, value_states: torch.Tensor) -> None:
         self.dtype, self.device = key_states.dtype, key_states.device
@@ -31,8 +60,6 @@ class TreeKVLayer(DynamicLayer):
         self.v_buf = torch.zeros((b, h, self.capacity, value_states.shape[-1]), dtype=self.dtype,
                                  device=self.device)
         self.length = 0
-        self.keys = self.k_buf[..., :0, :]
-        self.values = self.v_buf[..., :0, :]
         self.is_initialized = True
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, *args, **kwargs):
@@ -45,8 +72,6 @@ class TreeKVLayer(DynamicLayer):
         self.k_buf[..., self.length:end, :].copy_(key_states)
         self.v_buf[..., self.length:end, :].copy_(value_states)
         self.length = end
-        self.keys = self.k_buf[..., :end, :]
-        self.values = self.v_buf[..., :end, :]
         return self.keys, self.values
 
     def get_seq_length(self) -> int:
@@ -61,14 +86,18 @@ class TreeKVLayer(DynamicLayer):
         if not self.is_initialized or self.length <= max_length:
             return
         self.length = max(0, max_length)
-        self.keys = self.k_buf[..., :self.length, :]
-        self.values = self.v_buf[..., :self.length, :]
+
+    def set_length(self, length: int) -> None:
+        """Sets the live row count (shorter or longer), for rows that a device-side step
+        wrote without telling the host (a step recorded with a device prefix length)."""
+        if not self.is_initialized:
+            raise RuntimeError("cache layer is not initialised yet")
+        if not 0 <= length <= self.capacity:
+            raise ValueError(f"length {length} outside [0, {self.capacity}]")
+        self.length = int(length)
 
     def reset(self) -> None:
         self.length = 0
-        if self.is_initialized:
-            self.keys = self.k_buf[..., :0, :]
-            self.values = self.v_buf[..., :0, :]
 
 
 class TreeKVCache(DynamicCache):
@@ -88,6 +117,15 @@ class TreeKVCache(DynamicCache):
             if not layer.is_initialized:
                 layer.lazy_initialization(proto, proto)
         return self
+
+    def set_seq_length(self, length: int) -> None:
+        """TreeKVLayer.set_length on every layer."""
+        for layer in self.layers:
+            layer.set_length(length)
+
+    @property
+    def capacity(self) -> int:
+        return self.layers[0].capacity
 
     def kv_table(self) -> K.KvTable:
         """Pointer table of every layer's K and V buffers (stable across steps)."""

@@ -136,7 +136,15 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, int n_tokens, i
                           float rope_scale, const uint32_t* __restrict__ table,
                           __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                           __nv_bfloat16* __restrict__ v_cache, long long head_stride,
-                          long long seq_stride, long long past) {
+                          long long seq_stride, long long past,
+                          const int64_t* __restrict__ past_dev) {
+  if (past_dev) {
+    // device-side prefix length, at most `past` (the rows the caller sized the cache for);
+    // outside [0, past] nothing is written (the attention launch of the step reports it)
+    const long long live = *past_dev;
+    if (live < 0 || live > past) return;
+    past = live;
+  }
   const int warps = blockDim.x >> 5;
   const long long gw = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -254,11 +262,12 @@ int qk_norm_rope_launch(const void* qkv, int64_t n_tokens, int64_t q_heads, int6
                         const int64_t* positions, const float* inv_freq, float rope_scale,
                         const void* table, void* q_out, void* k_cache, void* v_cache,
                         int64_t head_stride, int64_t seq_stride, int64_t past_length,
-                        void* stream) {
+                        const int64_t* past_dev, void* stream) {
   if (!qkv || !q_norm_w || !k_norm_w || !q_out || !k_cache || !v_cache) return DDT_ERR_INVALID;
   if (!table && (!positions || !inv_freq)) return DDT_ERR_INVALID;
   if (head_dim != fused::kHeadDim) return DDT_ERR_CAPACITY;
   if (n_tokens < 0 || q_heads <= 0 || kv_heads <= 0 || past_length < 0) return DDT_ERR_INVALID;
+  if (past_dev && !aligned(past_dev, 8)) return DDT_ERR_ALIGN;
   if (!aligned(qkv, 8) || !aligned(q_out, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) ||
       !aligned(q_norm_w, 8) || !aligned(k_norm_w, 8) || (table && !aligned(table, 16)) ||
       (head_stride * 2) % 8 || (seq_stride * 2) % 8)
@@ -277,12 +286,12 @@ int qk_norm_rope_launch(const void* qkv, int64_t n_tokens, int64_t q_heads, int6
     fused::qk_norm_rope_cache_kernel<true><<<grid, 256, 0, st>>>(
         in, static_cast<int>(n_tokens), static_cast<int>(q_heads), static_cast<int>(kv_heads), qw,
         kw, eps, nullptr, nullptr, 1.f, static_cast<const uint32_t*>(table), qo, kc, vc,
-        head_stride, seq_stride, past_length);
+        head_stride, seq_stride, past_length, past_dev);
   else
     fused::qk_norm_rope_cache_kernel<false><<<grid, 256, 0, st>>>(
         in, static_cast<int>(n_tokens), static_cast<int>(q_heads), static_cast<int>(kv_heads), qw,
         kw, eps, positions, inv_freq, rope_scale, nullptr, qo, kc, vc, head_stride, seq_stride,
-        past_length);
+        past_length, past_dev);
   return launch_status();
 }
 
@@ -338,7 +347,7 @@ extern "C" int ddt_qk_norm_rope_cache(const void* qkv, int64_t n_tokens, int64_t
   if (!positions || !inv_freq) return DDT_ERR_INVALID;
   return qk_norm_rope_launch(qkv, n_tokens, q_heads, kv_heads, head_dim, q_norm_w, k_norm_w, eps,
                              positions, inv_freq, rope_scale, nullptr, q_out, k_cache, v_cache,
-                             head_stride, seq_stride, past_length, stream);
+                             head_stride, seq_stride, past_length, nullptr, stream);
 }
 
 extern "C" int ddt_qk_norm_rope_cache_table(const void* qkv, int64_t n_tokens, int64_t q_heads,
@@ -350,7 +359,21 @@ extern "C" int ddt_qk_norm_rope_cache_table(const void* qkv, int64_t n_tokens, i
   if (!rope_table) return DDT_ERR_INVALID;
   return qk_norm_rope_launch(qkv, n_tokens, q_heads, kv_heads, head_dim, q_norm_w, k_norm_w, eps,
                              nullptr, nullptr, 1.f, rope_table, q_out, k_cache, v_cache,
-                             head_stride, seq_stride, past_length, stream);
+                             head_stride, seq_stride, past_length, nullptr, stream);
+}
+
+// The table form with the prefix length in device memory (*past_length_dev, at most
+// max_past_length: the cache must hold max_past_length + n_tokens rows), for a verify step
+// recorded once and replayed at every prefix length.
+extern "C" int ddt_qk_norm_rope_cache_table_device_past(
+    const void* qkv, int64_t n_tokens, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+    const void* q_norm_w, const void* k_norm_w, float eps, const void* rope_table, void* q_out,
+    void* k_cache, void* v_cache, int64_t head_stride, int64_t seq_stride,
+    int64_t max_past_length, const int64_t* past_length_dev, void* stream) {
+  if (!rope_table || !past_length_dev) return DDT_ERR_INVALID;
+  return qk_norm_rope_launch(qkv, n_tokens, q_heads, kv_heads, head_dim, q_norm_w, k_norm_w, eps,
+                             nullptr, nullptr, 1.f, rope_table, q_out, k_cache, v_cache,
+                             head_stride, seq_stride, max_past_length, past_length_dev, stream);
 }
 
 extern "C" int ddt_silu_mul(const void* gate_up, int64_t rows, int64_t inter, void* out,

@@ -66,6 +66,9 @@ constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;               // + alignment 
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kBlockM, kBlockN, false, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kBlockM, kHeadDim, false, true);
 constexpr int kStatusTimeout = 1;
+// a launch with a device-side prefix length found it outside [0, planned prefix]: it ran with
+// the planned length instead (every access stays in bounds; the output is not meaningful)
+constexpr int kStatusPastRange = 4;
 // Pairs (of the 16 in each 32-column chunk of an S row) whose exponentials are computed by
 // the FMA-pipe polynomial instead of MUFU: pairs 0, 3, 6, 9 and 12, 10 of every 32
 // exponentials.  Measured per-CTA cycles against MUFU alone: -10% (prefix 8192, 257 rows),
@@ -101,6 +104,10 @@ struct Params {
   // diagnostic launches only (ddt_tree_attn_wait_check): the producer issues no load, so the
   // first wait of every consumer runs out after timeout_ns and the kernel unwinds
   int withhold_loads;
+  // ddt_tree_attn_device_past: the live prefix length, read by the kernel (past_len is then
+  // the planned maximum: the schedule, the tile counts and the tensor maps cover past_len +
+  // n_nodes keys, and keys at or beyond live + node + 1 are masked); null otherwise
+  const int64_t* past_dev;
 };
 
 // Balanced schedule ("stream-K" over the key tiles): the flattened (work unit, key tile)
@@ -137,7 +144,9 @@ struct SlotTable {
 struct UnitGeo {
   int h, row0, g_end, ntot;
 };
-__host__ __device__ inline UnitGeo unit_geo(const Params& p, int u) {
+// `past` is the prefix length the mask uses: p.past_len, or the live length of a device-past
+// launch (its tile count ntot then still covers the planned p.past_len).
+__host__ __device__ inline UnitGeo unit_geo(const Params& p, int u, int past) {
   UnitGeo g;
   g.h = u / p.n_pairs;
   g.row0 = (u % p.n_pairs) * kRowsPerCta;
@@ -145,10 +154,16 @@ __host__ __device__ inline UnitGeo unit_geo(const Params& p, int u) {
   if (node_hi > p.n_nodes - 1) node_hi = p.n_nodes - 1;
   // keys beyond past + node_hi are invisible to every row of the unit (tree and causal
   // masks); without a mask every row sees every key
-  g.g_end = p.mask_mode == DDT_MASK_NONE ? p.key_hi : p.past_len + node_hi + 1;
+  const int plan_end = p.mask_mode == DDT_MASK_NONE ? p.key_hi : p.past_len + node_hi + 1;
+  g.g_end = p.mask_mode == DDT_MASK_NONE ? p.key_hi : past + node_hi + 1;
   if (g.g_end > p.key_hi) g.g_end = p.key_hi;
-  g.ntot = g.g_end > p.key_lo ? (g.g_end - p.key_lo + kBlockN - 1) / kBlockN : 0;
+  g.ntot = plan_end > p.key_lo
+               ? ((plan_end < p.key_hi ? plan_end : p.key_hi) - p.key_lo + kBlockN - 1) / kBlockN
+               : 0;
   return g;
+}
+__host__ __device__ inline UnitGeo unit_geo(const Params& p, int u) {
+  return unit_geo(p, u, p.past_len);
 }
 
 struct Bars {
@@ -171,7 +186,8 @@ __device__ __forceinline__ void raise_abort(Bars& b, int* status) {
 }
 
 // Visibility mask of 32 consecutive keys starting at global key g0 for one node.
-__device__ __forceinline__ uint32_t visible32(const Params& p, int node, int g0, int g_end) {
+__device__ __forceinline__ uint32_t visible32(const Params& p, int node, int g0, int g_end,
+                                              int past) {
   uint32_t m = 0xffffffffu;
   // keys at or beyond g_end (other shard / past the window) are invisible
   const int n_ok = g_end - g0;
@@ -179,12 +195,12 @@ __device__ __forceinline__ uint32_t visible32(const Params& p, int node, int g0,
   if (n_ok < 32) m = (1u << n_ok) - 1u;
   if (p.mask_mode == DDT_MASK_NONE) return m;
   if (p.mask_mode == DDT_MASK_CAUSAL) {
-    const int lim = p.past_len + node + 1 - g0;  // keys < lim visible
+    const int lim = past + node + 1 - g0;  // keys < lim visible
     if (lim <= 0) return 0u;
     if (lim < 32) m &= (1u << lim) - 1u;
     return m;
   }
-  const int o0 = g0 - p.past_len;  // tree offset of the first key
+  const int o0 = g0 - past;  // tree offset of the first key
   if (o0 + 32 <= 0) return m;      // all prefix
   uint32_t tree;
   const uint32_t* row = p.anc + static_cast<long long>(node) * p.anc_words;
@@ -202,6 +218,7 @@ __device__ __forceinline__ uint32_t visible32(const Params& p, int node, int g0,
   return m & tree;
 }
 
+template <bool kLivePast>
 __global__ void __launch_bounds__(kThreads, 1)
 tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params p,
@@ -484,12 +501,20 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const uint32_t tO = tl + col_o(q);
     const float sl2 = p.scale_log2;
     const tc::Exp2Poly exp2_poly;
+    // the prefix length of the mask: the launch's, or the one in device memory (a value
+    // outside [0, planned] is reported and replaced by the planned length)
+    int past = p.past_len;
+    if (kLivePast) {
+      const int64_t live = *p.past_dev;
+      if (live >= 0 && live <= p.past_len) past = static_cast<int>(live);
+      else if (warp == 4 && lane == 0 && p.status) atomicOr(p.status, kStatusPastRange);
+    }
     bool ok = true;
     int J = 0;
     for (int i = 0; i < n_items; ++i) {
       int u, t0, nt, slot;
       item(i, u, t0, nt, slot);
-      const UnitGeo g = unit_geo(p, u);
+      const UnitGeo g = unit_geo(p, u, past);
       const int R = g.row0 + q * kBlockM + r;
       const int node = R / p.group;
       const int qh = g.h * p.group + (R % p.group);
@@ -500,8 +525,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // ends before the tree window / the launch's last key
       const int full_end = p.mask_mode == DDT_MASK_NONE ? g_end
                            : p.mask_mode == DDT_MASK_CAUSAL
-                               ? (g_end < p.past_len + vnode + 1 ? g_end : p.past_len + vnode + 1)
-                               : (g_end < p.past_len ? g_end : p.past_len);
+                               ? (g_end < past + vnode + 1 ? g_end : past + vnode + 1)
+                               : (g_end < past ? g_end : past);
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; ok && j < nt; ++j) {
         const int jg = J + j;
@@ -515,7 +540,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
         if (masked) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) vis[c] = visible32(p, vnode, gk + c * 32, g_end);
+          for (int c = 0; c < 4; ++c) vis[c] = visible32(p, vnode, gk + c * 32, g_end, past);
         }
         // the whole S row (128 fp32) comes out of TMEM in one round trip
         uint32_t sv[4][32];
@@ -1078,6 +1103,7 @@ inline int prepare_sizes(Params& p, int64_t n_nodes, int64_t past_length, int64_
   p.status = nullptr;
   p.timeout_ns = kTimeoutNs;
   p.withhold_loads = 0;
+  p.past_dev = nullptr;
   return DDT_OK;
 }
 
@@ -1231,12 +1257,12 @@ inline SlotPtrs slot_ptrs(void* ws, int64_t parts) {
 inline int launch(const Launch& L, int64_t kv_heads, cudaStream_t st) {
   // the attribute belongs to the current device: set on every launch (it costs a host call),
   // so a process that uses several GPUs, from several threads, needs no per-device state
-  if (cudaFuncSetAttribute(tree_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kSmemAlloc) != cudaSuccess)
+  auto kern = L.p.past_dev ? tree_attn_kernel<true> : tree_attn_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc) !=
+      cudaSuccess)
     return DDT_ERR_CUDA;
   const int64_t grid = L.p.balanced ? L.grid : kv_heads * L.p.n_pairs * L.p.n_splits;
-  tree_attn_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, st>>>(L.q, L.k, L.v, L.p,
-                                                                             L.sched);
+  kern<<<static_cast<unsigned>(grid), kThreads, kSmemAlloc, st>>>(L.q, L.k, L.v, L.p, L.sched);
   return launch_status();
 }
 
@@ -1377,6 +1403,42 @@ extern "C" int ddt_tree_attn(const void* q, int64_t q_node_stride, int64_t q_hea
   rc = attn::choose_plan(L, kv_heads, kv_splits, false, kind);
   if (rc) return rc;
   L.p.status = status;
+  return attn::run(L, kind, kv_heads, workspace, workspace_bytes, static_cast<__nv_bfloat16*>(out),
+                   o_node_stride, o_head_stride, nullptr, nullptr, nullptr,
+                   static_cast<cudaStream_t>(stream));
+}
+
+// ddt_tree_attn with the prefix length in device memory, so that one launch (one CUDA graph
+// node) serves every prefix length up to max_past_length.  The plan, the schedule and the
+// tensor maps are made for max_past_length: K / V hold max_past_length + n_nodes rows, the
+// tree's rows sit at [live, live + n_nodes) and the keys after them are masked, so the launch
+// costs what a launch at max_past_length costs.
+extern "C" int ddt_tree_attn_device_past(const void* q, int64_t q_node_stride,
+                                         int64_t q_head_stride, const void* k, const void* v,
+                                         int64_t kv_head_stride, int64_t kv_seq_stride, void* out,
+                                         int64_t o_node_stride, int64_t o_head_stride,
+                                         int64_t n_nodes, int64_t max_past_length,
+                                         const int64_t* past_length_dev, int64_t q_heads,
+                                         int64_t kv_heads, int64_t head_dim,
+                                         const uint32_t* anc_bits, int64_t anc_words,
+                                         int mask_mode, float scale, int64_t kv_splits,
+                                         void* workspace, size_t workspace_bytes, int32_t* status,
+                                         void* stream) {
+  if (!out || !past_length_dev || !status) return DDT_ERR_INVALID;
+  // every row sees every key without a mask, including the rows after the live window
+  if (mask_mode == DDT_MASK_NONE) return DDT_ERR_INVALID;
+  if (!aligned(past_length_dev, 8)) return DDT_ERR_ALIGN;
+  if (!aligned(out, 16) || (o_node_stride * 2) % 16 || (o_head_stride * 2) % 16) return DDT_ERR_ALIGN;
+  attn::Launch L;
+  int rc = attn::prepare(L, q, q_node_stride, q_head_stride, k, v, kv_head_stride, kv_seq_stride, 0,
+                         max_past_length + n_nodes, n_nodes, max_past_length, q_heads, kv_heads,
+                         head_dim, anc_bits, anc_words, mask_mode, scale);
+  if (rc) return rc;
+  int kind = 0;
+  rc = attn::choose_plan(L, kv_heads, kv_splits, false, kind);
+  if (rc) return rc;
+  L.p.status = status;
+  L.p.past_dev = past_length_dev;
   return attn::run(L, kind, kv_heads, workspace, workspace_bytes, static_cast<__nv_bfloat16*>(out),
                    o_node_stride, o_head_stride, nullptr, nullptr, nullptr,
                    static_cast<cudaStream_t>(stream));

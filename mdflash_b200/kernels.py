@@ -109,14 +109,23 @@ def attention_status(device: torch.device) -> torch.Tensor:
         return WORKSPACES.get(device, "attn_status", 256)[:4].view(torch.int32)
 
 
+STATUS_TIMEOUT = 1      # a bounded wait of a kernel ran out
+STATUS_LAYOUT = 2       # a batched compaction met a head stride it cannot move
+STATUS_PAST_RANGE = 4   # a device-side prefix length was outside [0, planned maximum]
+
+
 def check_status(status: torch.Tensor, what: str = "ddt_tree_attn") -> None:
-    """Reads a status word (this syncs with its stream) and raises DDTreeError with
-    DDT_ERR_TIMEOUT when a launch that wrote to it gave up a bounded wait; the word is
-    cleared first, so the next launches start clean."""
+    """Reads a status word (this syncs with its stream) and raises DDTreeError when a launch
+    that wrote to it reported an error: DDT_ERR_TIMEOUT when a bounded wait ran out,
+    DDT_ERR_INVALID for a device-side prefix length out of range or a layout the batched
+    compaction cannot move.  The word is cleared first, so the next launches start clean."""
     v = int(status.reshape(-1)[0].item())
     if v != 0:
         status.zero_()
-        check(_lib.DDT_ERR_TIMEOUT, what)
+        if v & STATUS_TIMEOUT:
+            check(_lib.DDT_ERR_TIMEOUT, what)
+        why = "prefix length out of range" if v & STATUS_PAST_RANGE else "invalid KV layout"
+        raise _lib.DDTreeError(f"{what}: device status {v:#x} ({why})")
 
 
 def anc_words_for(n_nodes: int) -> int:
@@ -565,17 +574,29 @@ def _mask_mode(causal: bool, unmasked: bool) -> int:
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    anc_bits: torch.Tensor | None, past_length: int, scale: float | None = None,
                    causal: bool = False, out: torch.Tensor | None = None, kv_splits: int = 0,
-                   status: torch.Tensor | None = None, unmasked: bool = False) -> torch.Tensor:
+                   status: torch.Tensor | None = None, unmasked: bool = False,
+                   past_dev: torch.Tensor | None = None) -> torch.Tensor:
     """softmax(Q K^T * scale, tree / causal mask) V on tcgen05.  q: [N, Hq, D] (or HF
     [1, Hq, N, D]); k, v: [Hkv, past_length + N, D] (or [1, ...]); returns [N, Hq, D].
     Mask: the tree (anc_bits), causal=True (node i sees keys < past_length + i + 1), or
     unmasked=True (every row sees every key: the drafter's non-causal attention).
 
+    past_dev (i64 [1], device): the prefix length is read from it when the kernel runs
+    (ddt_tree_attn_device_past), past_length is then its maximum and k / v cover
+    past_length + N rows; a recorded launch serves every prefix length up to past_length.
+
     The kernel computes in bf16 (fp32 accumulation).  fp32 inputs (an fp32 model) are rounded
     to bf16 for the kernel and the output is returned in fp32: the result is within the bf16
     tolerance of fp32 attention, not fp32-exact."""
     dev = _require_cuda(q, k, v)
+    if past_dev is not None:
+        if unmasked:
+            raise ValueError("a device-side prefix length needs the tree or causal mask")
+        if past_dev.dtype != torch.int64 or not past_dev.is_cuda or past_dev.numel() != 1:
+            raise ValueError("past_dev must be a device i64 [1]")
     if q.dtype == torch.float32 and k.dtype == torch.float32 and v.dtype == torch.float32:
+        if past_dev is not None:
+            raise TypeError("a device-side prefix length takes bf16 q / k / v")
         res = tree_attention(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16),
                              anc_bits, past_length, scale=scale, causal=causal,
                              kv_splits=kv_splits, status=status, unmasked=unmasked)
@@ -613,12 +634,20 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         ev = (torch.cuda.Event(enable_timing=True, external=True),
               torch.cuda.Event(enable_timing=True, external=True))
         ev[0].record()
-    rc = lib.ddt_tree_attn(
-        q.data_ptr(), qns, qhs, k.data_ptr(), v.data_ptr(), khs, kss, out.data_ptr(),
-        out.stride(0), out.stride(1), n, past_length, hq, hkv, d,
-        anc_bits.data_ptr() if anc_bits is not None else None, words, mode, float(scale),
-        kv_splits, ws.data_ptr(), ws.numel(), status.data_ptr(), stream)
-    check(rc, "ddt_tree_attn")
+    if past_dev is not None:
+        rc = lib.ddt_tree_attn_device_past(
+            q.data_ptr(), qns, qhs, k.data_ptr(), v.data_ptr(), khs, kss, out.data_ptr(),
+            out.stride(0), out.stride(1), n, past_length, past_dev.data_ptr(), hq, hkv, d,
+            anc_bits.data_ptr() if anc_bits is not None else None, words, mode, float(scale),
+            kv_splits, ws.data_ptr(), ws.numel(), status.data_ptr(), stream)
+        check(rc, "ddt_tree_attn_device_past")
+    else:
+        rc = lib.ddt_tree_attn(
+            q.data_ptr(), qns, qhs, k.data_ptr(), v.data_ptr(), khs, kss, out.data_ptr(),
+            out.stride(0), out.stride(1), n, past_length, hq, hkv, d,
+            anc_bits.data_ptr() if anc_bits is not None else None, words, mode, float(scale),
+            kv_splits, ws.data_ptr(), ws.numel(), status.data_ptr(), stream)
+        check(rc, "ddt_tree_attn")
     if STATS.time_attention:
         ev[1].record()
         STATS.attn_events.append(ev)

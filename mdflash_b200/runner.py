@@ -67,25 +67,34 @@ class Qwen3VerifyRunner:
 
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, cache, past_length: int,
                 anc_bits: torch.Tensor | None, causal: bool = False,
-                status: torch.Tensor | None = None) -> torch.Tensor:
+                status: torch.Tensor | None = None,
+                past_dev: torch.Tensor | None = None) -> torch.Tensor:
         """ids, positions: i64 [N] (device).  Writes the N new K/V rows into `cache`
         (a TreeKVCache) at [past_length, past_length + N) and returns logits [N, V] (bf16).
         Tree mode attends with anc_bits; causal=True attends causally (prefill).  Attention
-        timeouts go to `status` (default: the device's status word)."""
-        h = self._final_hidden(ids, positions, cache, past_length, anc_bits, causal, status)
+        timeouts go to `status` (default: the device's status word).
+
+        past_dev (i64 [1], device): the prefix length is read from it by the kernels, so that
+        a recorded forward serves every prefix length up to past_length (the cache must hold
+        past_length + N rows); the cache's host-side length is then left to the caller."""
+        h = self._final_hidden(ids, positions, cache, past_length, anc_bits, causal, status,
+                               past_dev)
         return torch.matmul(h, self.lm_head.t())
 
     def forward_posterior(self, ids: torch.Tensor, positions: torch.Tensor, cache,
                           past_length: int, anc_bits: torch.Tensor | None,
                           out: torch.Tensor | None = None,
-                          status: torch.Tensor | None = None) -> torch.Tensor:
+                          status: torch.Tensor | None = None,
+                          past_dev: torch.Tensor | None = None) -> torch.Tensor:
         """The greedy posterior (i64 [N]) of the verify rows without the [N, V] logits: the
         final hidden states go through the fused lm_head -> argmax kernel
-        (ddt_lm_head_argmax).  Same cache effects as forward."""
-        h = self._final_hidden(ids, positions, cache, past_length, anc_bits, False, status)
+        (ddt_lm_head_argmax).  Same cache effects (and past_dev) as forward."""
+        h = self._final_hidden(ids, positions, cache, past_length, anc_bits, False, status,
+                               past_dev)
         return K.lm_head_argmax(h, self.lm_head, out=out)
 
-    def _final_hidden(self, ids, positions, cache, past_length, anc_bits, causal, status):
+    def _final_hidden(self, ids, positions, cache, past_length, anc_bits, causal, status,
+                      past_dev=None):
         lib = _lib.load()
         st = self._stream()
         n = ids.numel()
@@ -106,16 +115,23 @@ class Qwen3VerifyRunner:
                                       w["ln1"].data_ptr(), n, H, self.eps, x.data_ptr(),
                                       h.data_ptr(), st), "ddt_add_rmsnorm")
             qkv = torch.matmul(h, w["w_qkv"].t())
-            check(lib.ddt_qk_norm_rope_cache_table(qkv.data_ptr(), n, hq, hkv, d,
-                                                   w["qn"].data_ptr(), w["kn"].data_ptr(),
-                                                   self.eps, rope.data_ptr(), q.data_ptr(),
-                                                   kbuf.data_ptr(), vbuf.data_ptr(),
-                                                   kbuf.stride(0), kbuf.stride(1), past_length,
-                                                   st), "ddt_qk_norm_rope_cache_table")
+            if past_dev is None:
+                check(lib.ddt_qk_norm_rope_cache_table(
+                    qkv.data_ptr(), n, hq, hkv, d, w["qn"].data_ptr(), w["kn"].data_ptr(),
+                    self.eps, rope.data_ptr(), q.data_ptr(), kbuf.data_ptr(), vbuf.data_ptr(),
+                    kbuf.stride(0), kbuf.stride(1), past_length, st),
+                    "ddt_qk_norm_rope_cache_table")
+            else:
+                check(lib.ddt_qk_norm_rope_cache_table_device_past(
+                    qkv.data_ptr(), n, hq, hkv, d, w["qn"].data_ptr(), w["kn"].data_ptr(),
+                    self.eps, rope.data_ptr(), q.data_ptr(), kbuf.data_ptr(), vbuf.data_ptr(),
+                    kbuf.stride(0), kbuf.stride(1), past_length, past_dev.data_ptr(), st),
+                    "ddt_qk_norm_rope_cache_table_device_past")
             K.STATS.launches += 3
             s = past_length + n
             attn = K.tree_attention(q, kbuf[:, :s], vbuf[:, :s], anc_bits, past_length,
-                                    scale=self.scaling, causal=causal, status=status)
+                                    scale=self.scaling, causal=causal, status=status,
+                                    past_dev=past_dev)
             o = torch.matmul(attn.view(n, hq * d), w["w_o"].t())
             check(lib.ddt_add_rmsnorm(x.data_ptr(), o.data_ptr(), w["ln2"].data_ptr(), n, H,
                                       self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")
@@ -127,8 +143,8 @@ class Qwen3VerifyRunner:
         check(lib.ddt_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.final_norm.data_ptr(), n, H,
                                   self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")
         K.STATS.launches += 1
+        if past_dev is not None:
+            return h
         for layer in cache.layers:
             layer.length = past_length + n
-            layer.keys = layer.k_buf[..., :layer.length, :]
-            layer.values = layer.v_buf[..., :layer.length, :]
         return h

@@ -10,13 +10,16 @@ without the host round trips of the reference).
 Nothing in ``step`` synchronises the host; the caller reads the (small) result when it
 needs it, then calls ``commit`` to set the cache length to past + accepted.
 
-``capture`` records one step for a fixed (prefix length, budget) into a CUDA graph; a
-replay re-runs every kernel of the step (tree build from the current contents of the
-draft-logit buffer, the 36-layer forward, argmax, walk, compaction) with one launch
-from the host, which removes the Python / launch overhead of the forward.
+``CapturedStep`` records one step into a CUDA graph; a replay re-runs every kernel of the
+step (tree build from the current contents of the draft-logit buffer, the 36-layer forward,
+argmax, walk, compaction) with one launch from the host, which removes the Python / launch
+overhead of the forward.  Recorded for one prefix length, or (``max_start``) with the prefix
+length in device memory, so that one graph serves every round of a decode loop whose prefix
+grows (``step_device_past``).
 """
 from __future__ import annotations
 
+import dataclasses
 from dataclasses import dataclass
 
 import torch
@@ -74,6 +77,8 @@ class TreeVerifier:
         self.n_accepted = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.next_token = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._dtrees: K.TreeBatch | None = None  # one-request batch of step_device_past
+        self._kvb: K.KvBatch | None = None
 
     @torch.inference_mode()
     def step(self, draft_logits: torch.Tensor, root_token: torch.Tensor, start: int) -> StepResult:
@@ -116,6 +121,57 @@ class TreeVerifier:
         return StepResult(n, self.accepted, self.n_accepted, self.next_token, post, self.status,
                           logits if self.keep_logits and logits is not None else None)
 
+    @torch.inference_mode()
+    def step_device_past(self, draft_logits: torch.Tensor, root_token: torch.Tensor,
+                         past_dev: torch.Tensor, max_past: int) -> StepResult:
+        """One verify step whose prefix length is read from device memory (past_dev, i64 [1],
+        at most max_past) by every kernel that depends on it: the tree build's verify
+        positions (ddt_topk_tree_batched with one request), the K/V rows the forward writes
+        (ddt_qk_norm_rope_cache_table_device_past), the attention mask
+        (ddt_tree_attn_device_past, planned for max_past) and the compaction
+        (ddt_accept_compact_batched).  Nothing in it depends on the host value, so a graph
+        recorded from it serves every prefix length up to max_past.  Needs the fused runner
+        and a cache of at least max_past + budget + 1 rows; the cache's host-side length is
+        left as it is (``commit`` sets it)."""
+        if self.runner is None:
+            raise RuntimeError("a device-side prefix length needs the fused runner (fused=True)")
+        n_cap = self.budget + 1
+        if max_past < 0 or max_past + n_cap > self.cache.capacity:
+            raise ValueError(f"cache holds {self.cache.capacity} rows, max_past {max_past} + "
+                             f"tree window {n_cap} does not fit")
+        if past_dev.dtype != torch.int64 or past_dev.numel() != 1 or not past_dev.is_cuda:
+            raise ValueError("past_dev must be a device i64 [1]")
+        if self._dtrees is None:
+            self._dtrees = K.TreeBatch.allocate(self.device, [self.budget], self.depths,
+                                                self.vocab)
+            self._kvb = K.KvBatch([self.cache.kv_table()])
+        root = root_token.reshape(-1)[:1]
+        if root.dtype != torch.int64:
+            raise ValueError("root_token must be i64")
+        trees = dataclasses.replace(self._dtrees, starts=past_dev.reshape(1), root_tokens=root)
+        K.topk_tree_batched(draft_logits.reshape(1, self.depths, self.vocab), trees)
+        tree = trees.tree(0)
+        n = tree.n_nodes
+        logits = None
+        if self.fused_head:
+            post = self.runner.forward_posterior(tree.verify_ids[:n], tree.verify_pos[:n],
+                                                 self.cache, max_past, tree.anc_bits,
+                                                 out=self.posterior[:n], status=self.status,
+                                                 past_dev=past_dev)
+        else:
+            logits = self.runner.forward(tree.verify_ids[:n], tree.verify_pos[:n], self.cache,
+                                         max_past, tree.anc_bits, status=self.status,
+                                         past_dev=past_dev)
+            post = K.argmax(logits, out=self.posterior[:n])
+        if self.walk:
+            K.accept_compact_batched(self.posterior[:n_cap].view(1, n_cap), trees, self._kvb,
+                                     past_dev.reshape(1), accepted=self.accepted.view(1, n_cap),
+                                     n_accepted=self.n_accepted, next_token=self.next_token,
+                                     status=self.status)
+        self.tree_device_past = tree
+        return StepResult(n, self.accepted, self.n_accepted, self.next_token, post, self.status,
+                          logits if self.keep_logits and logits is not None else None)
+
     def check(self) -> None:
         """Raises DDTreeError (DDT_ERR_TIMEOUT) if an attention launch of the steps since the
         last check gave up a bounded wait (its output, and so the step's result, is then
@@ -126,31 +182,49 @@ class TreeVerifier:
         """Sets the cache length to start + n_accepted after the caller read the count, and
         raises if the step's attention reported a timeout (the caller has synced already)."""
         self.check()
-        self.cache.crop(start + n_accepted)
+        self.cache.set_seq_length(start + n_accepted)
 
 
 class CapturedStep:
-    """A verify step recorded in a CUDA graph for one prefix length.
+    """A verify step recorded in a CUDA graph, for one prefix length or (``max_start``) for
+    every prefix length up to a maximum.
 
     Inputs are read from ``draft_logits`` / ``root_token`` (device buffers owned by this
     object: copy new values in before ``replay``); outputs land in ``result``."""
 
     def __init__(self, verifier: TreeVerifier, start: int, warmup: int = 2,
                  time_attention: bool = False, pool=None, tree: K.DeviceTree | None = None,
-                 lane: int = 0, capture_stream: torch.cuda.Stream | None = None):
+                 lane: int = 0, capture_stream: torch.cuda.Stream | None = None,
+                 max_start: int | None = None):
         """tree=None records the whole step (tree build from ``draft_logits``); a given tree
         (built by the caller before each replay, e.g. by one batched build for many
         requests) records the step from that tree on.  Steps that may replay concurrently
         (on different streams) need different ``lane`` numbers, graph pools and capture
         streams: the lane selects this package's scratch buffers, the capture stream the
-        library GEMMs' (cuBLAS keeps one workspace per stream)."""
+        library GEMMs' (cuBLAS keeps one workspace per stream).
+
+        max_start: record TreeVerifier.step_device_past instead, with the prefix length in
+        ``start_dev``; ``replay(start)`` then runs the step at any start in [0, max_start]
+        (fused runner only; the attention costs what it costs at max_start, so a decode loop
+        records a new step when its prefix outgrows the bucket)."""
         self.verifier = verifier
         self.start = start
+        self.max_start = max_start
         v = verifier
         self.draft_logits = torch.zeros((v.depths, v.vocab), dtype=torch.bfloat16, device=v.device)
         self.root_token = torch.zeros(1, dtype=torch.int64, device=v.device)
+        self.start_dev = None
+        if max_start is not None:
+            if tree is not None:
+                raise ValueError("a device-side prefix length records the whole step (tree=None)")
+            if not 0 <= start <= max_start:
+                raise ValueError(f"start {start} outside [0, {max_start}]")
+            self.start_dev = torch.full((1,), start, dtype=torch.int64, device=v.device)
 
         def run():
+            if max_start is not None:
+                return v.step_device_past(self.draft_logits, self.root_token, self.start_dev,
+                                          max_start)
             if tree is None:
                 return v.step(self.draft_logits, self.root_token, start)
             return v.verify_tree(tree, start)
@@ -173,7 +247,21 @@ class CapturedStep:
         K.STATS.reset()
         v.cache.crop(start)
 
-    def replay(self) -> StepResult:
+    def replay(self, start: int | None = None) -> StepResult:
+        """Runs the recorded step.  With max_start, ``start`` (default: the recording's) is
+        the prefix length of this round: the cache must hold exactly that many rows, and
+        ``commit(start, n_accepted)`` afterwards sets its new length."""
+        if start is not None and start != self.start:
+            if self.max_start is None:
+                raise ValueError(f"step recorded for start {self.start}, not {start}")
+            if not 0 <= start <= self.max_start:
+                raise ValueError(f"start {start} outside [0, {self.max_start}]")
+        if self.start_dev is not None:
+            s = self.start if start is None else start
+            if self.verifier.cache.get_seq_length() != s:
+                raise RuntimeError(f"cache holds {self.verifier.cache.get_seq_length()} rows, "
+                                   f"expected {s}")
+            self.start_dev.fill_(s)
         self.graph.replay()
         return self.result
 
