@@ -736,11 +736,12 @@ def decode_loop(verifier, draft_dev, root_dev, P: int, rounds: int, warmup: int,
     the current start, reads the accepted count (the loop's one host sync per round),
     commits, advances start by the accepted count and feeds the next token back as the root.
     Timed with CUDA events around all rounds, host gaps included; the cache is restored to
-    the prefix afterwards."""
+    the prefix afterwards.  Then the same rounds enqueued back to back with one host sync
+    (the recorded step advances its own start and root on the device, ddt_advance_round)."""
     from mdflash_b200.verifier import CapturedStep
     cache = verifier.cache
     max_start = P + rounds * (DEPTHS + 1)
-    cap = CapturedStep(verifier, P, warmup=1, max_start=max_start)
+    cap = CapturedStep(verifier, P, warmup=1, max_start=max_start, advance=True)
     cap.draft_logits.copy_(draft_dev)
 
     def run():
@@ -760,16 +761,31 @@ def decode_loop(verifier, draft_dev, root_dev, P: int, rounds: int, warmup: int,
         cache.set_seq_length(P)
         return ev0.elapsed_time(ev1), acc, res.n_nodes
 
+    def run_device():
+        cap.begin(P, root_dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        cap.run_rounds(rounds)
+        ev1.record()
+        _, lengths = cap.finish()
+        cache.set_seq_length(P)
+        return ev0.elapsed_time(ev1), lengths
+
     for _ in range(warmup):
         run()
+        run_device()
     total_ms, acc, n_nodes = run()
+    dev_ms, dev_acc = run_device()
     del cap
     ms = total_ms / rounds
     return {"rounds": rounds, "graphs_recorded": 1, "max_start": max_start,
             "start_first": P, "start_last": P + sum(acc) - acc[-1],
             "accepted_per_round": float(np.mean(acc)), "ms_per_round": ms,
             "value": (rounds * n_nodes + sum(acc)) / (total_ms / 1e3), "unit": "tokens/s",
-            "vs_fixed_prefix_step": ms / fixed_ms}
+            "vs_fixed_prefix_step": ms / fixed_ms,
+            "device_advanced": {"ms_per_round": dev_ms / rounds, "host_syncs": 1,
+                                "vs_fixed_prefix_step": dev_ms / rounds / fixed_ms,
+                                "same_acceptance_as_host_loop": dev_acc == acc}}
 
 
 # ------------------------------------------------------------ op-level measurements

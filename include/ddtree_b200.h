@@ -210,6 +210,22 @@ int ddt_accept_compact_batched(int64_t n_requests, const int64_t* posterior, int
                                int64_t acc_stride, int32_t* n_accepted, int64_t* next_token,
                                int32_t* status, void* stream);
 
+/* One decode-loop round's bookkeeping on the device, after the walk, for each request r
+ * (one warp each), as ddtree.py:488-498 does on the host:
+ *   output_ids[r, starts[r] + i] = verify_ids[r, accepted[r, i]]   for i < n_accepted[r]
+ *   output_ids[r, starts[r] + n_accepted[r]] = next_token[r]
+ *   root_tokens[r] = next_token[r]  (the next round's root, output_ids[start] there)
+ *   acceptance[r, rounds[r]] = n_accepted[r]; rounds[r] += 1; starts[r] += n_accepted[r].
+ * With it a recorded verify step advances its own device-side prefix length, so a host can
+ * enqueue several rounds and sync once.  Writes at or beyond out_capacity / len_capacity
+ * are dropped and set *status bit 8 (status may be null). */
+int ddt_advance_round(int64_t n_requests, int64_t* starts, int32_t* rounds,
+                      const int32_t* n_accepted, const int64_t* accepted, int64_t acc_stride,
+                      const int64_t* verify_ids, int64_t ids_stride, int64_t max_nodes,
+                      const int64_t* next_token, int64_t* root_tokens, int64_t* output_ids,
+                      int64_t out_stride, int64_t out_capacity, int32_t* acceptance,
+                      int64_t len_stride, int64_t len_capacity, int32_t* status, void* stream);
+
 /* ---- tree attention -----------------------------------------------------
  * q: [n_nodes, q_heads, head_dim] bf16 at element strides (q_node_stride, q_head_stride);
  * k, v: [kv_heads, past_length + n_nodes, head_dim] bf16 at (kv_head_stride,

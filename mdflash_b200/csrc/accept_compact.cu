@@ -452,6 +452,55 @@ inline unsigned compact_grid(int64_t n_tensors, int64_t heads) {
   return static_cast<unsigned>(g);
 }
 
+// One decode-loop round's bookkeeping on the device, after the walk (ddtree.py:488-498): the
+// accepted tokens and the next token go to the output row at the round's start, the next
+// token becomes the next round's root, the acceptance length is logged and the start
+// advances.  One warp per request; writes beyond a buffer's capacity are dropped and set
+// status bit 8.
+constexpr int kStatusLogFull = 8;
+
+__global__ void advance_round_kernel(int64_t* __restrict__ starts, int32_t* __restrict__ rounds,
+                                     const int32_t* __restrict__ n_accepted,
+                                     const int64_t* __restrict__ accepted, int64_t acc_stride,
+                                     const int64_t* __restrict__ verify_ids, int64_t ids_stride,
+                                     const int64_t* __restrict__ next_token,
+                                     int64_t* __restrict__ root_tokens,
+                                     int64_t* __restrict__ output_ids, int64_t out_stride,
+                                     int64_t out_capacity, int32_t* __restrict__ acceptance,
+                                     int64_t len_stride, int64_t len_capacity, int max_nodes,
+                                     int* status) {
+  const int r = blockIdx.x;
+  const int lane = threadIdx.x;
+  const int64_t start = starts[r];
+  int k = n_accepted[r];
+  k = k < 0 ? 0 : (k > max_nodes ? max_nodes : k);
+  const int64_t tok = next_token[r];
+  bool dropped = false;
+  for (int i = lane; i <= k; i += 32) {
+    const int64_t pos = start + i;
+    if (pos < 0 || pos >= out_capacity) {
+      dropped = true;
+      continue;
+    }
+    int64_t t = tok;
+    if (i < k) {
+      const int64_t node = accepted[r * acc_stride + i];
+      t = (node >= 0 && node < max_nodes) ? verify_ids[r * ids_stride + node] : -1;
+    }
+    output_ids[r * out_stride + pos] = t;
+  }
+  dropped = __any_sync(DDT_FULL_MASK, dropped);
+  if (lane == 0) {
+    const int32_t round = rounds[r];
+    if (round >= 0 && round < len_capacity) acceptance[r * len_stride + round] = k;
+    else dropped = true;
+    rounds[r] = round + 1;
+    starts[r] = start + k;
+    root_tokens[r] = tok;
+    if (dropped && status) atomicOr(status, kStatusLogFull);
+  }
+}
+
 }  // namespace accept
 }  // namespace ddt
 
@@ -559,5 +608,30 @@ extern "C" int ddt_accept_compact_batched(
   accept::compact_batched_kernel<<<static_cast<unsigned>(per * n_requests),
                                    accept::kCompactWarps * 32, stage, st>>>(
       accepted, acc_stride, n_accepted, kb, static_cast<int>(per), status);
+  return launch_status();
+}
+
+extern "C" int ddt_advance_round(int64_t n_requests, int64_t* starts, int32_t* rounds,
+                                 const int32_t* n_accepted, const int64_t* accepted,
+                                 int64_t acc_stride, const int64_t* verify_ids,
+                                 int64_t ids_stride, int64_t max_nodes,
+                                 const int64_t* next_token, int64_t* root_tokens,
+                                 int64_t* output_ids, int64_t out_stride, int64_t out_capacity,
+                                 int32_t* acceptance, int64_t len_stride, int64_t len_capacity,
+                                 int32_t* status, void* stream) {
+  if (n_requests < 0 || !starts || !rounds || !n_accepted || !accepted || !verify_ids ||
+      !next_token || !root_tokens || !output_ids || !acceptance)
+    return DDT_ERR_INVALID;
+  if (max_nodes < 1 || max_nodes > DDT_MAX_NODES || acc_stride < 1 || ids_stride < max_nodes ||
+      out_capacity < 1 || out_stride < out_capacity || len_capacity < 1 ||
+      len_stride < len_capacity)
+    return DDT_ERR_INVALID;
+  if (n_requests == 0) return DDT_OK;
+  if (n_requests > 0x7fffffffLL) return DDT_ERR_CAPACITY;
+  accept::advance_round_kernel<<<static_cast<unsigned>(n_requests), 32, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(
+      starts, rounds, n_accepted, accepted, acc_stride, verify_ids, ids_stride, next_token,
+      root_tokens, output_ids, out_stride, out_capacity, acceptance, len_stride, len_capacity,
+      static_cast<int>(max_nodes), status);
   return launch_status();
 }

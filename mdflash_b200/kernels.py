@@ -112,6 +112,7 @@ def attention_status(device: torch.device) -> torch.Tensor:
 STATUS_TIMEOUT = 1      # a bounded wait of a kernel ran out
 STATUS_LAYOUT = 2       # a batched compaction met a head stride it cannot move
 STATUS_PAST_RANGE = 4   # a device-side prefix length was outside [0, planned maximum]
+STATUS_LOG_FULL = 8     # a decode-loop round found its output or length log full
 
 
 def check_status(status: torch.Tensor, what: str = "ddt_tree_attn") -> None:
@@ -124,7 +125,8 @@ def check_status(status: torch.Tensor, what: str = "ddt_tree_attn") -> None:
         status.zero_()
         if v & STATUS_TIMEOUT:
             check(_lib.DDT_ERR_TIMEOUT, what)
-        why = "prefix length out of range" if v & STATUS_PAST_RANGE else "invalid KV layout"
+        why = ("prefix length out of range" if v & STATUS_PAST_RANGE else
+               "decode-loop log full" if v & STATUS_LOG_FULL else "invalid KV layout")
         raise _lib.DDTreeError(f"{what}: device status {v:#x} ({why})")
 
 
@@ -523,6 +525,42 @@ def accept_compact_batched(posteriors: torch.Tensor, trees: TreeBatch, kvb: KvBa
         status.data_ptr(), _stream(dev)), "ddt_accept_compact_batched")
     STATS.launches += 1
     return accepted, n_accepted, next_token
+
+
+def advance_round(starts: torch.Tensor, rounds: torch.Tensor, n_accepted: torch.Tensor,
+                  accepted: torch.Tensor, verify_ids: torch.Tensor, next_token: torch.Tensor,
+                  root_tokens: torch.Tensor, output_ids: torch.Tensor, acceptance: torch.Tensor,
+                  status: torch.Tensor | None = None) -> None:
+    """ddt_advance_round: one decode-loop round's bookkeeping on the device for R requests
+    (ddtree.py:488-498): the accepted tokens and the next token into output_ids [R, cap] at
+    starts[r], the next token into root_tokens[r], n_accepted[r] into acceptance[R, rounds]
+    at rounds[r]; then rounds[r] += 1 and starts[r] += n_accepted[r].  starts / root_tokens /
+    next_token i64 [R], rounds / n_accepted i32 [R], accepted / verify_ids i64 [R, nodes]."""
+    dev = _require_cuda(starts)
+    R = starts.numel()
+    for t, dt, name in ((starts, torch.int64, "starts"), (rounds, torch.int32, "rounds"),
+                        (n_accepted, torch.int32, "n_accepted"),
+                        (next_token, torch.int64, "next_token"),
+                        (root_tokens, torch.int64, "root_tokens")):
+        if t.dtype != dt or t.numel() != R or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous {dt} [{R}]")
+    acc = accepted.reshape(R, -1)
+    vid = verify_ids.reshape(R, -1)
+    out = output_ids.reshape(R, -1)
+    lens = acceptance.reshape(R, -1)
+    if acc.dtype != torch.int64 or vid.dtype != torch.int64 or out.dtype != torch.int64 or \
+            lens.dtype != torch.int32:
+        raise ValueError("accepted / verify_ids / output_ids must be i64, acceptance i32")
+    if any(t.stride(1) != 1 for t in (acc, vid, out, lens)):
+        raise ValueError("rows must have unit stride")
+    if status is None:
+        status = attention_status(dev)
+    check(_lib.load().ddt_advance_round(
+        R, starts.data_ptr(), rounds.data_ptr(), n_accepted.data_ptr(), acc.data_ptr(),
+        acc.stride(0), vid.data_ptr(), vid.stride(0), vid.shape[1], next_token.data_ptr(),
+        root_tokens.data_ptr(), out.data_ptr(), out.stride(0), out.shape[1], lens.data_ptr(),
+        lens.stride(0), lens.shape[1], status.data_ptr(), _stream(dev)), "ddt_advance_round")
+    STATS.launches += 1
 
 
 def compact_kv(keep, kv: KvTable, past_length: int) -> None:

@@ -195,7 +195,7 @@ class CapturedStep:
     def __init__(self, verifier: TreeVerifier, start: int, warmup: int = 2,
                  time_attention: bool = False, pool=None, tree: K.DeviceTree | None = None,
                  lane: int = 0, capture_stream: torch.cuda.Stream | None = None,
-                 max_start: int | None = None):
+                 max_start: int | None = None, advance: bool = False):
         """tree=None records the whole step (tree build from ``draft_logits``); a given tree
         (built by the caller before each replay, e.g. by one batched build for many
         requests) records the step from that tree on.  Steps that may replay concurrently
@@ -206,7 +206,12 @@ class CapturedStep:
         max_start: record TreeVerifier.step_device_past instead, with the prefix length in
         ``start_dev``; ``replay(start)`` then runs the step at any start in [0, max_start]
         (fused runner only; the attention costs what it costs at max_start, so a decode loop
-        records a new step when its prefix outgrows the bucket)."""
+        records a new step when its prefix outgrows the bucket).
+
+        advance (with max_start): the graph also ends with ddt_advance_round, which writes the
+        round's accepted tokens and next token into ``output_ids`` at the device start, logs
+        the acceptance length, advances the start and makes the next token the next root:
+        ``begin`` / ``run_rounds`` / ``finish`` then run several rounds with one host sync."""
         self.verifier = verifier
         self.start = start
         self.max_start = max_start
@@ -220,11 +225,28 @@ class CapturedStep:
             if not 0 <= start <= max_start:
                 raise ValueError(f"start {start} outside [0, {max_start}]")
             self.start_dev = torch.full((1,), start, dtype=torch.int64, device=v.device)
+        if advance and max_start is None:
+            raise ValueError("advance needs max_start")
+        self.advance = advance
+        if advance:
+            # start + accepted + 1 <= max_start + depths + 2 positions; >= 1 token per round
+            self.output_ids = torch.zeros((1, max_start + v.depths + 2), dtype=torch.int64,
+                                          device=v.device)
+            self.acceptance = torch.zeros((1, max_start + 1), dtype=torch.int32, device=v.device)
+            self.rounds_dev = torch.zeros(1, dtype=torch.int32, device=v.device)
+            self._begin_start = start
+            self._enqueued = 0
 
         def run():
             if max_start is not None:
-                return v.step_device_past(self.draft_logits, self.root_token, self.start_dev,
-                                          max_start)
+                res = v.step_device_past(self.draft_logits, self.root_token, self.start_dev,
+                                         max_start)
+                if advance:
+                    K.advance_round(self.start_dev, self.rounds_dev, res.n_accepted,
+                                    res.accepted, v.tree_device_past.verify_ids,
+                                    res.next_token, self.root_token, self.output_ids,
+                                    self.acceptance, status=res.status)
+                return res
             if tree is None:
                 return v.step(self.draft_logits, self.root_token, start)
             return v.verify_tree(tree, start)
@@ -234,6 +256,8 @@ class CapturedStep:
         with K.WORKSPACES.lane(lane):
             with torch.cuda.stream(side):
                 for _ in range(warmup):
+                    if self.start_dev is not None:  # an advancing step moved it
+                        self.start_dev.fill_(start)
                     run()
                     v.cache.crop(start)
             torch.cuda.current_stream(v.device).wait_stream(side)
@@ -246,6 +270,8 @@ class CapturedStep:
         self.attn_events = list(K.STATS.attn_events)
         K.STATS.reset()
         v.cache.crop(start)
+        if self.start_dev is not None:
+            self.start_dev.fill_(start)
 
     def replay(self, start: int | None = None) -> StepResult:
         """Runs the recorded step.  With max_start, ``start`` (default: the recording's) is
@@ -264,6 +290,55 @@ class CapturedStep:
             self.start_dev.fill_(s)
         self.graph.replay()
         return self.result
+
+    def begin(self, start: int, root_token: torch.Tensor | int) -> None:
+        """advance mode: the loop's first round starts at ``start`` (the cache holds exactly
+        that many rows) with ``root_token``; clears the round counter."""
+        if not self.advance:
+            raise RuntimeError("begin / run_rounds / finish need a step recorded with advance")
+        if not 0 <= start <= self.max_start:
+            raise ValueError(f"start {start} outside [0, {self.max_start}]")
+        if self.verifier.cache.get_seq_length() != start:
+            raise RuntimeError(f"cache holds {self.verifier.cache.get_seq_length()} rows, "
+                               f"expected {start}")
+        self.start_dev.fill_(start)
+        self.rounds_dev.zero_()
+        if isinstance(root_token, torch.Tensor):
+            self.root_token.copy_(root_token.reshape(-1)[:1])
+        else:
+            self.root_token.fill_(int(root_token))
+        self._begin_start = start
+        self._enqueued = 0
+
+    def run_rounds(self, n: int) -> None:
+        """advance mode: enqueues n rounds back to back (no host sync); every round reads the
+        start and root the previous one left on the device.  Refuses (on the host) a count
+        that could carry the start past max_start, at depths + 1 tokens per round."""
+        if not self.advance:
+            raise RuntimeError("begin / run_rounds / finish need a step recorded with advance")
+        worst = self._begin_start + (self._enqueued + n) * (self.verifier.depths + 1)
+        if worst > self.max_start:
+            raise ValueError(f"{self._enqueued + n} rounds from start {self._begin_start} may "
+                             f"pass max_start {self.max_start}")
+        for _ in range(n):
+            self.graph.replay()
+        self._enqueued += n
+
+    def finish(self) -> tuple[int, list[int]]:
+        """advance mode: one sync; returns the start after the rounds run since ``begin`` and
+        their acceptance lengths, sets the cache's length and raises if a kernel reported an
+        error.  The committed tokens are ``output_ids[0, begin start : start + 1]`` (the last
+        one is the next round's root)."""
+        if not self.advance:
+            raise RuntimeError("begin / run_rounds / finish need a step recorded with advance")
+        start = int(self.start_dev.item())
+        rounds = int(self.rounds_dev.item())
+        lengths = self.acceptance[0, :rounds].tolist()
+        self.verifier.commit(start, 0)
+        self._begin_start = start
+        self._enqueued = 0
+        self.rounds_dev.zero_()
+        return start, lengths
 
     def attention_ms(self) -> list[float]:
         """Device time of each tree-attention call of the most recent replay."""

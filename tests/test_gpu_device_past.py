@@ -292,3 +292,90 @@ def test_one_captured_step_serves_every_round(cuda_device, loop_model):
     # the recorded step refuses a prefix it was not planned for, on the host
     with pytest.raises(ValueError):
         step.replay(max_start + 1)
+
+
+def test_device_advanced_rounds_match_host_driven_loop(cuda_device, loop_model):
+    """CapturedStep(advance=True): R rounds enqueued back to back, each advancing the device
+    start and root itself (ddt_advance_round), with one host sync at the end; against the same
+    recorded step driven round by round from the host (replay(start), read, commit) on a
+    second cache: the same acceptance lengths, the same committed tokens (the reference's
+    output_ids writes, ddtree.py:488-489) and the same final start and cache length."""
+    from mdflash_b200.cache import TreeKVCache
+    from mdflash_b200.runner import Qwen3VerifyRunner
+    from mdflash_b200.verifier import CapturedStep, TreeVerifier
+    rounds = 8
+    max_start = LOOP_P + 2 * rounds * (LOOP_DEPTHS + 1)
+    cap = max_start + LOOP_BUDGET + 1
+    runner = Qwen3VerifyRunner(loop_model)
+    caches = [TreeKVCache(2, cap).allocate(2, 128, torch.bfloat16, cuda_device) for _ in range(2)]
+    rng = np.random.default_rng(5)
+    ids = torch.from_numpy(rng.integers(0, LOOP_V, LOOP_P)).to(cuda_device)
+    with torch.inference_mode():
+        for c in caches:
+            runner.forward(ids, torch.arange(LOOP_P, device=cuda_device), c, 0, None, causal=True)
+    logits = torch.from_numpy(rng.standard_normal((LOOP_DEPTHS, LOOP_V)).astype(np.float32)
+                              * 3).to(torch.bfloat16).to(cuda_device)
+    root0 = int(rng.integers(0, LOOP_V))
+    steps = []
+    for c in caches:
+        v = TreeVerifier(loop_model, c, LOOP_BUDGET, LOOP_DEPTHS, LOOP_V, cuda_device, fused=True,
+                         runner=runner)
+        st = CapturedStep(v, LOOP_P, max_start=max_start, advance=True)
+        st.draft_logits.copy_(logits)
+        steps.append((v, st))
+    # host-driven
+    v, st = steps[0]
+    st.root_token.fill_(root0)
+    start, host_lengths, host_tokens = LOOP_P, [], []
+    for _ in range(rounds):
+        res = st.replay(start)
+        k = int(res.n_accepted.item())
+        host_tokens += v.tree_device_past.verify_ids[res.accepted[:k]].tolist()
+        v.commit(start, k)
+        host_lengths.append(k)
+        start += k
+        st.root_token.copy_(res.next_token)
+    host_tokens.append(int(st.root_token.item()))
+    # device-advanced: two batches of rounds, one sync each
+    v, st = steps[1]
+    st.begin(LOOP_P, root0)
+    st.run_rounds(rounds // 2)
+    mid, first = st.finish()
+    assert caches[1].get_seq_length() == mid
+    st.run_rounds(rounds - rounds // 2)
+    end, second = st.finish()
+    torch.cuda.synchronize()
+    print(f"[advance] lengths {first + second}, start {LOOP_P} -> {end}")
+    assert first + second == host_lengths
+    assert end == start and caches[1].get_seq_length() == end == caches[0].get_seq_length()
+    assert st.output_ids[0, LOOP_P:end + 1].tolist() == host_tokens
+    for la, lb in zip(caches[0].layers, caches[1].layers):
+        assert torch.equal(la.keys, lb.keys) and torch.equal(la.values, lb.values)
+    # the host refuses a batch that could pass max_start
+    with pytest.raises(ValueError):
+        st.run_rounds(2 * rounds)
+
+
+def test_advance_round_bounds(cuda_device):
+    """ddt_advance_round's own writes, and a full output log: dropped writes, status bit 8."""
+    dev = cuda_device
+    starts = torch.tensor([3, 6], dtype=torch.int64, device=dev)
+    rounds = torch.zeros(2, dtype=torch.int32, device=dev)
+    n_acc = torch.tensor([2, 3], dtype=torch.int32, device=dev)
+    acc = torch.tensor([[0, 2, 0, 0], [0, 1, 3, 0]], dtype=torch.int64, device=dev)
+    vids = torch.tensor([[10, 11, 12, 13], [20, 21, 22, 23]], dtype=torch.int64, device=dev)
+    nxt = torch.tensor([99, 98], dtype=torch.int64, device=dev)
+    roots = torch.zeros(2, dtype=torch.int64, device=dev)
+    out = torch.full((2, 9), -7, dtype=torch.int64, device=dev)
+    lens = torch.zeros((2, 4), dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    K.advance_round(starts, rounds, n_acc, acc, vids, nxt, roots, out, lens, status=status)
+    torch.cuda.synchronize()
+    assert out[0].tolist() == [-7, -7, -7, 10, 12, 99, -7, -7, -7]
+    # request 1: positions 6, 7, 8 fit, 9 (the next token) does not
+    assert out[1].tolist() == [-7] * 6 + [20, 21, 23]
+    assert starts.tolist() == [5, 9] and rounds.tolist() == [1, 1]
+    assert roots.tolist() == [99, 98] and lens[:, 0].tolist() == [2, 3]
+    assert int(status.item()) == K.STATUS_LOG_FULL
+    with pytest.raises(DDTreeError, match="decode-loop log full"):
+        K.check_status(status)
