@@ -5,12 +5,14 @@ Default workload, at every GPU count (one process per GPU under torchrun): a bat
 independent requests on a random-init Qwen3-8B-shaped target (36 layers, hidden 4096,
 32 q / 8 kv heads, head_dim 128, MLP 12288, vocab 151936, bf16).  Prefix lengths are
 log-uniform in 1k..32k, tree budgets uniform over {64, 128, 256, 512}, drafter logits
-seeded per request (15 depths of N(0,1)*3).  A "step" verifies every request once: one
-batched tree-build launch for all of the rank's requests, then per request a CUDA-graph
-replay of the tree-attention verify forward -> greedy posterior, the replays spread over 4
-streams (--lanes) so that one request's launch gaps and kernel tails are filled by another's
-work, then one batched accept walk + KV compaction of all the requests; then the result
-records are all-gathered.
+seeded per request (15 depths of N(0,1)*3).  A "step" verifies every request once, recorded
+as one CUDA graph per rank: one batched tree-build launch for all of the rank's requests,
+one 36-layer verify forward over all their tree rows (the projections and lm_head shared,
+in GEMMs of at most 2048 rows; each request's K/V writes and tree attention on its own
+cache, spread over 4 streams, --lanes), one argmax over all rows, then one batched accept
+walk + KV compaction of all the requests; then the result records are all-gathered.
+(--verify-batch per-request: one graph per request instead, the projections run per
+request.)
 Requests are assigned to ranks by longest-processing-time first; there is no other
 cross-GPU traffic.
 Metric: verified + accepted tokens per second over all GPUs.
@@ -112,6 +114,16 @@ def parse_args():
                          "at once (requests split over the lanes by predicted cost; each lane "
                          "has its own graph "
                          "pool and scratch buffers)")
+    ap.add_argument("--verify-batch", choices=["batched", "per-request"], default="batched",
+                    help="requests workload: one verify forward over all of a rank's requests "
+                         "(shared projections in fixed-size GEMM chunks, per-request K/V writes "
+                         "and attention on --lanes streams), recorded as one CUDA graph; or one "
+                         "graph per request")
+    ap.add_argument("--gemm-chunk", type=int, default=0,
+                    help="--verify-batch batched: rows per projection GEMM, every GEMM exactly "
+                         "that many (the rows padded up), so that a row's result does not "
+                         "depend on the other requests; 0 (default): the fewest chunks of at "
+                         "most 2048 rows, each a multiple of 128, for the rank's rows")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="splitkv workload: partials travel over NVLink peer memory "
                          "(PeerExchange, default) or in an NCCL all-gather")
@@ -390,7 +402,8 @@ def requests_config(args, n):
                         "{64,128,256,512}, 15 drafted depths; one verify step of every request",
             "model": "Qwen3-8B shape, random init", "global_batch": args.requests,
             "seq_len": "1024-32768 (log-uniform)", "parallelism": f"request-dp{n} (LPT)",
-            "l2": "inputs larger than L2: 16 GB of weights streamed per request step"}
+            "l2": "inputs larger than L2: 16 GB of weights streamed per GEMM row chunk, "
+                  "86 GB of prefix K/V"}
 
 
 # ------------------------------------------------------------------------ our arm
@@ -424,6 +437,111 @@ def _fill_prefix(cache, prefix: int, g: torch.Generator):
         layer.length = prefix
         layer.keys = layer.k_buf[..., :prefix, :]
         layer.values = layer.v_buf[..., :prefix, :]
+
+
+def _batched_verify(args, dev, runner, specs, mine, trees, dev_logits, host_logits, host_roots,
+                    g, rank, lanes):
+    """--verify-batch batched: every request of this rank in ONE verify step, recorded as one
+    CUDA graph: the batched tree build, a gather of the tree rows into one row block (request
+    after request), Qwen3VerifyRunner.forward_batch (projections over all rows in GEMMs of
+    --gemm-chunk rows, K/V writes and tree attention per request on `lanes` streams), one
+    argmax over all rows scattered back per request, and the batched walk + compaction.
+    Returns (one_step, check_statuses, records, launches per step, execution)."""
+    from mdflash_b200 import kernels as K
+    from mdflash_b200 import sharding as S
+    from mdflash_b200.cache import TreeKVCache
+    R = len(mine)
+    records = torch.full((R, S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
+    if R == 0:
+        return (lambda e2e: S.gather_results(records)), (lambda: None), records, 0, "no requests"
+    mb1 = trees.max_budget + 1
+    caches, segments, pasts, ancs, src = [], [], [], [], []
+    off = 0
+    for j, i in enumerate(mine):
+        sp = specs[i]
+        n = 1 + K.expected_node_count(DEPTHS, V, sp.budget)
+        cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
+            QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
+        _fill_prefix(cache, sp.prefix, g.manual_seed(1000 + sp.index))
+        caches.append(cache)
+        segments.append((off, n))
+        pasts.append(sp.prefix)
+        ancs.append(trees.anc_bits[j, :n])
+        src += [j * mb1 + t for t in range(n)]
+        off += n
+    T = off
+    chunk = args.gemm_chunk
+    if chunk <= 0:  # the fewest chunks of at most 2048 rows, each a multiple of 128
+        pieces = -(-T // 2048)
+        chunk = -(-(-(-T // pieces)) // 128) * 128
+    t_pad = -(-T // chunk) * chunk
+    idx = torch.tensor(src, dtype=torch.int64, device=dev)
+    ids_buf = torch.zeros(t_pad, dtype=torch.int64, device=dev)
+    pos_buf = torch.zeros(t_pad, dtype=torch.int64, device=dev)
+    post_cat = torch.zeros(T, dtype=torch.int64, device=dev)
+    posteriors = torch.zeros((R, mb1), dtype=torch.int64, device=dev)
+    kvb = K.KvBatch([c.kv_table() for c in caches])
+    past_dev = torch.tensor(pasts, dtype=torch.int64, device=dev)
+    b_acc = torch.zeros((R, mb1), dtype=torch.int64, device=dev)
+    b_n = torch.zeros(R, dtype=torch.int32, device=dev)
+    b_next = torch.zeros(R, dtype=torch.int64, device=dev)
+    status = K.attention_status(dev)
+
+    def step():
+        K.topk_tree_batched(dev_logits, trees)
+        torch.index_select(trees.verify_ids.view(-1), 0, idx, out=ids_buf[:T])
+        torch.index_select(trees.verify_pos.view(-1), 0, idx, out=pos_buf[:T])
+        logits = runner.forward_batch(ids_buf, pos_buf, segments, caches, pasts, ancs,
+                                      status=status, chunk=chunk, lanes=lanes)
+        K.argmax(logits[:T], out=post_cat)
+        posteriors.view(-1).index_copy_(0, idx, post_cat)
+        K.accept_compact_batched(posteriors, trees, kvb, past_dev, b_acc, b_n, b_next,
+                                 status=status)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side), torch.inference_mode():
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    K.STATS.reset()
+    with torch.inference_mode(), torch.cuda.graph(graph):
+        step()
+    launches = K.STATS.launches
+    K.STATS.reset()
+    for j, i in enumerate(mine):
+        records[j, :3] = torch.tensor([specs[i].index, rank, segments[j][1]])
+        records[j, 5] = 0
+    m_path = min(S.MAX_PATH, mb1)
+    nn = torch.tensor([n for _, n in segments], device=dev)
+    path_cols = torch.arange(m_path, device=dev)[None, :] < nn[:, None]
+    # everything the recorded graph reads or writes outside its own pool stays referenced by
+    # the returned closures for as long as the graph is replayed
+    live = (caches, ancs, idx, ids_buf, pos_buf, post_cat, posteriors, kvb, past_dev, status)
+
+    def one_step(e2e: bool):
+        assert live is not None
+        if e2e:  # this step's inputs from pinned host memory
+            dev_logits.copy_(host_logits, non_blocking=True)
+            trees.root_tokens.copy_(host_roots, non_blocking=True)
+        graph.replay()
+        records[:, 3] = b_n
+        records[:, 4] = b_next
+        records[:, 6:6 + m_path] = torch.where(path_cols, b_acc[:, :m_path], -1)
+        return S.gather_results(records)
+
+    def check_statuses():
+        if int(status.item()) != 0:
+            raise RuntimeError(f"device status {int(status.item()):#x} in the batched verify")
+
+    execution = (f"one CUDA graph per step for the rank's {R} requests: batched tree build, one "
+                 f"36-layer verify forward over their {T} tree rows (projections in GEMMs of "
+                 f"{chunk} rows, {t_pad - T} padding rows; K/V writes and tree attention per "
+                 f"request on {lanes} streams), argmax, batched walk + compaction; records "
+                 "all-gathered per step")
+    return one_step, check_statuses, records, launches, execution
 
 
 def run_requests(args):
@@ -477,82 +595,98 @@ def run_requests(args):
             lane_of[j] = ln
     order = [lst[t] for t in range(max((len(x) for x in lane_lists), default=0))
              for lst in lane_lists if t < len(lst)]
-    # the batched walk reads the batched build's trees
-    bcompact = args.compaction == "batched" and batched
-    posteriors = (torch.zeros((len(mine), trees.max_budget + 1), dtype=torch.int64, device=dev)
-                  if mine else None)
-    caps = [None] * len(mine)
-    for j in order:
-        sp = specs[mine[j]]
-        ln = lane_of[j]
-        cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
-            QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
-        # random prefix K / V seeded per request (the verify work does not depend on the
-        # values; the results then do not depend on the rank or the capture order)
-        _fill_prefix(cache, sp.prefix, g.manual_seed(1000 + sp.index))
-        ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner,
-                           posterior=posteriors[j] if bcompact else None, walk=not bcompact)
-        cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pools[ln],
-                           tree=trees.tree(j) if batched else None, lane=ln,
-                           capture_stream=cap_streams[ln] if cap_streams else None)
-        cap.draft_logits.copy_(dev_logits[j])
-        cap.root_token.copy_(trees.root_tokens[j:j + 1])
-        caps[j] = (sp, cap)
-    records = torch.full((len(caps), S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
-    for j, (sp, cap) in enumerate(caps):
-        records[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
-        records[j, 5] = 0
-    if bcompact and caps:
-        kvb = K.KvBatch([cap.verifier.cache.kv_table() for _, cap in caps])
-        K.accept_compact_batched(posteriors, trees, kvb, [sp.prefix for sp, _ in caps])
-        past_dev = torch.tensor([sp.prefix for sp, _ in caps], dtype=torch.int64, device=dev)
-        b_acc = torch.zeros((len(caps), trees.max_budget + 1), dtype=torch.int64, device=dev)
-        b_n = torch.zeros(len(caps), dtype=torch.int32, device=dev)
-        b_next = torch.zeros(len(caps), dtype=torch.int64, device=dev)
-        m_path = min(S.MAX_PATH, trees.max_budget + 1)
-        # path columns a request's record holds: min(MAX_PATH, its node count), the rest -1
-        nn = torch.tensor([cap.result.n_nodes for _, cap in caps], device=dev)
-        path_cols = torch.arange(m_path, device=dev)[None, :] < nn[:, None]
-
-    def one_step(e2e: bool):
-        if e2e and batched and caps:  # this step's inputs from pinned host memory
-            dev_logits.copy_(host_logits, non_blocking=True)
-            trees.root_tokens.copy_(host_roots, non_blocking=True)
-        if batched and caps:
-            K.topk_tree_batched(dev_logits, trees)
-        main = torch.cuda.current_stream(dev)
-        if streams:
-            for st in streams:
-                st.wait_stream(main)
+    if args.verify_batch == "batched":
+        bcompact = True
+        one_step, check_statuses, records, launches_per_step, execution = \
+            _batched_verify(args, dev, runner, specs, mine, trees, dev_logits, host_logits,
+                            host_roots, g, rank, lanes)
+        caps = []
+    else:
+        # the batched walk reads the batched build's trees
+        bcompact = args.compaction == "batched" and batched
+        posteriors = (torch.zeros((len(mine), trees.max_budget + 1), dtype=torch.int64, device=dev)
+                      if mine else None)
+        caps = [None] * len(mine)
         for j in order:
-            sp, cap = caps[j]
-            with torch.cuda.stream(streams[lane_of[j]] if streams else main):
-                if e2e and not batched:
-                    cap.draft_logits.copy_(host_logits[j], non_blocking=True)
-                    cap.root_token.copy_(host_roots[j:j + 1], non_blocking=True)
-                r = cap.replay()
-                if not bcompact:
-                    # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
-                    records[j, 3] = r.n_accepted[0]
-                    records[j, 4] = r.next_token[0]
-                    m = min(S.MAX_PATH, r.n_nodes)
-                    records[j, 6:6 + m] = r.accepted[:m]
-        if streams:
-            for st in streams:
-                main.wait_stream(st)
+            sp = specs[mine[j]]
+            ln = lane_of[j]
+            cache = TreeKVCache(QWEN3_8B["layers"], sp.prefix + sp.budget + 1 + 64).allocate(
+                QWEN3_8B["kv_heads"], QWEN3_8B["head_dim"], torch.bfloat16, dev)
+            # random prefix K / V seeded per request (the verify work does not depend on the
+            # values; the results then do not depend on the rank or the capture order)
+            _fill_prefix(cache, sp.prefix, g.manual_seed(1000 + sp.index))
+            ver = TreeVerifier(model, cache, sp.budget, DEPTHS, V, dev, runner=runner,
+                               posterior=posteriors[j] if bcompact else None, walk=not bcompact)
+            cap = CapturedStep(ver, sp.prefix, warmup=1, pool=pools[ln],
+                               tree=trees.tree(j) if batched else None, lane=ln,
+                               capture_stream=cap_streams[ln] if cap_streams else None)
+            cap.draft_logits.copy_(dev_logits[j])
+            cap.root_token.copy_(trees.root_tokens[j:j + 1])
+            caps[j] = (sp, cap)
+        records = torch.full((len(caps), S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
+        for j, (sp, cap) in enumerate(caps):
+            records[j, :3] = torch.tensor([sp.index, rank, cap.result.n_nodes])
+            records[j, 5] = 0
         if bcompact and caps:
-            # every request's walk and compaction in one batched launch after the replays
-            K.accept_compact_batched(posteriors, trees, kvb, past_dev, b_acc, b_n, b_next)
-            records[:, 3] = b_n
-            records[:, 4] = b_next
-            records[:, 6:6 + m_path] = torch.where(path_cols, b_acc[:, :m_path], -1)
-        return S.gather_results(records)
+            kvb = K.KvBatch([cap.verifier.cache.kv_table() for _, cap in caps])
+            K.accept_compact_batched(posteriors, trees, kvb, [sp.prefix for sp, _ in caps])
+            past_dev = torch.tensor([sp.prefix for sp, _ in caps], dtype=torch.int64, device=dev)
+            b_acc = torch.zeros((len(caps), trees.max_budget + 1), dtype=torch.int64, device=dev)
+            b_n = torch.zeros(len(caps), dtype=torch.int32, device=dev)
+            b_next = torch.zeros(len(caps), dtype=torch.int64, device=dev)
+            m_path = min(S.MAX_PATH, trees.max_budget + 1)
+            # path columns a request's record holds: min(MAX_PATH, its node count), the rest -1
+            nn = torch.tensor([cap.result.n_nodes for _, cap in caps], device=dev)
+            path_cols = torch.arange(m_path, device=dev)[None, :] < nn[:, None]
 
-    def check_statuses():
-        st = torch.stack([cap.verifier.status for _, cap in caps])
-        if int(st.abs().sum().item()) != 0:
-            raise RuntimeError("a tree-attention launch reported a bounded-wait timeout")
+        def one_step(e2e: bool):
+            if e2e and batched and caps:  # this step's inputs from pinned host memory
+                dev_logits.copy_(host_logits, non_blocking=True)
+                trees.root_tokens.copy_(host_roots, non_blocking=True)
+            if batched and caps:
+                K.topk_tree_batched(dev_logits, trees)
+            main = torch.cuda.current_stream(dev)
+            if streams:
+                for st in streams:
+                    st.wait_stream(main)
+            for j in order:
+                sp, cap = caps[j]
+                with torch.cuda.stream(streams[lane_of[j]] if streams else main):
+                    if e2e and not batched:
+                        cap.draft_logits.copy_(host_logits[j], non_blocking=True)
+                        cap.root_token.copy_(host_roots[j:j + 1], non_blocking=True)
+                    r = cap.replay()
+                    if not bcompact:
+                        # record on the device: [index, rank, n_nodes, n_accepted, next, 0, path...]
+                        records[j, 3] = r.n_accepted[0]
+                        records[j, 4] = r.next_token[0]
+                        m = min(S.MAX_PATH, r.n_nodes)
+                        records[j, 6:6 + m] = r.accepted[:m]
+            if streams:
+                for st in streams:
+                    main.wait_stream(st)
+            if bcompact and caps:
+                # every request's walk and compaction in one batched launch after the replays
+                K.accept_compact_batched(posteriors, trees, kvb, past_dev, b_acc, b_n, b_next)
+                records[:, 3] = b_n
+                records[:, 4] = b_next
+                records[:, 6:6 + m_path] = torch.where(path_cols, b_acc[:, :m_path], -1)
+            return S.gather_results(records)
 
+        def check_statuses():
+            st = torch.stack([cap.verifier.status for _, cap in caps])
+            if int(st.abs().sum().item()) != 0:
+                raise RuntimeError("a tree-attention launch reported a bounded-wait timeout")
+
+        launches_per_step = (sum(cap.launches_per_replay for _, cap in caps)
+                             + (1 if batched and caps else 0) + (2 if bcompact and caps else 0))
+        execution = (("one batched tree-build launch for the rank's requests, then "
+                      "one CUDA-graph replay per request (36-layer fused verify forward, argmax"
+                      + (f") on {lanes} lanes, then one batched walk + compaction" if bcompact
+                         else ", accept walk + compaction)") if batched else
+                      "one CUDA-graph replay per request (tree build, 36-layer fused verify "
+                      "forward, argmax, accept walk + compaction)") +
+                     "; records all-gathered per step")
     for _ in range(args.warmup):
         one_step(False)
     torch.cuda.synchronize()
@@ -589,10 +723,9 @@ def run_requests(args):
     e2e_ms, e2e_rec = timed(True)
     e2e_tokens = int((e2e_rec[:, 2] + e2e_rec[:, 3]).sum())
     check_statuses()
-    h2d = (host_logits.numel() * host_logits.element_size() + host_roots.numel() * 8) if caps else 0
+    h2d = (host_logits.numel() * host_logits.element_size() + host_roots.numel() * 8) if mine else 0
     d2h = int(allrec.numel()) * 8
-    launches = (sum(cap.launches_per_replay for _, cap in caps) + (1 if batched and caps else 0)
-                + (2 if bcompact and caps else 0)) * args.steps
+    launches = launches_per_step * args.steps
     sums = torch.tensor([float(h2d), float(launches)], device=dev)
     if world > 1:
         dist.all_reduce(sums, op=dist.ReduceOp.SUM)
@@ -621,18 +754,14 @@ def run_requests(args):
         "step_roofline": {"bound": "max(HBM: weights + prefix K/V once, bf16 FLOPs) per request, "
                                    "the slowest rank's requests back to back",
                           "ms": bound, "frac": bound / ms, "peak_source": peak_kind},
-        "execution": ("one batched tree-build launch for the rank's requests, then "
-                      "one CUDA-graph replay per request (36-layer fused verify forward, argmax"
-                      + (f") on {lanes} lanes, then one batched walk + compaction" if bcompact else
-                         ", accept walk + compaction)") if batched else
-                      "one CUDA-graph replay per request (tree build, 36-layer fused verify "
-                      "forward, argmax, accept walk + compaction)") +
-                     "; records all-gathered per step",
+        "execution": execution,
+        "verify_batch": args.verify_batch,
         "tree_build": args.tree_build,
         "compaction": "batched" if bcompact else "per-request",
         "lanes": lanes,
     }
     del caps
+    one_step = check_statuses = None  # the batched step's graph, caches and buffers
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     if rank == 0 and not args.no_subrecords:

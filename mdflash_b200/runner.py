@@ -93,6 +93,95 @@ class Qwen3VerifyRunner:
                                past_dev)
         return K.lm_head_argmax(h, self.lm_head, out=out)
 
+    def forward_batch(self, ids: torch.Tensor, positions: torch.Tensor,
+                      segments: list[tuple[int, int]], caches: list, pasts: list[int],
+                      anc_bits: list[torch.Tensor], status: torch.Tensor | None = None,
+                      chunk: int = 2048, lanes: int = 1) -> torch.Tensor:
+        """The verify forward of many requests at once.  ids / positions: i64 [T_pad] (device;
+        request r's tree rows at segments[r] = (offset, rows); the rows after the last segment
+        are padding, T_pad a multiple of `chunk`).  Request r's K/V rows go into caches[r] at
+        pasts[r], and its rows attend to that cache under anc_bits[r].  The norms and the
+        projections run over all rows, the projections in GEMMs of exactly `chunk` rows, so
+        that a row's result does not depend on which other requests share the batch; the
+        K/V writes and the attention run per request, spread over `lanes` streams.  Returns
+        logits [T_pad, V] (bf16; padding rows are finite and meaningless)."""
+        lib = _lib.load()
+        T = ids.numel()
+        if T % chunk:
+            raise ValueError(f"{T} rows is not a multiple of the chunk ({chunk})")
+        if not (len(segments) == len(caches) == len(pasts) == len(anc_bits)):
+            raise ValueError("one segment, cache, prefix length and tree per request")
+        for (off, n), c, p in zip(segments, caches, pasts):
+            if off < 0 or n <= 0 or off + n > T or p < 0 or p + n > c.capacity:
+                raise ValueError(f"segment ({off}, {n}) at prefix {p} does not fit")
+        st = self._stream()
+        dev = ids.device
+        H, hq, hkv, d = self.hidden, self.q_heads, self.kv_heads, self.head_dim
+        x = torch.nn.functional.embedding(ids.view(-1), self.embed)  # [T, H] bf16
+        h = torch.empty_like(x)
+        q = torch.zeros((T, hq, d), dtype=x.dtype, device=dev)
+        attn = torch.zeros((T, hq, d), dtype=x.dtype, device=dev)  # padding rows stay 0
+        qkv = torch.empty((T, (hq + 2 * hkv) * d), dtype=x.dtype, device=dev)
+        o = torch.empty((T, H), dtype=x.dtype, device=dev)
+        gu = torch.empty((T, 2 * self.inter), dtype=x.dtype, device=dev)
+        act = torch.empty((T, self.inter), dtype=x.dtype, device=dev)
+        delta = torch.empty((T, H), dtype=x.dtype, device=dev)
+        rope = torch.empty((T, d // 2), dtype=torch.int32, device=dev)
+        check(lib.ddt_rope_table(positions.data_ptr(), T, self.inv_freq.data_ptr(), d,
+                                 self.rope_scale, rope.data_ptr(), st), "ddt_rope_table")
+        K.STATS.launches += 1
+
+        def gemm(a, w, out):
+            for c0 in range(0, T, chunk):
+                torch.matmul(a[c0:c0 + chunk], w.t(), out=out[c0:c0 + chunk])
+            K.STATS.launches += T // chunk
+
+        main = torch.cuda.current_stream(dev)
+        side = [torch.cuda.Stream(dev) for _ in range(lanes)] if lanes > 1 else None
+        first = True
+        for li, w in enumerate(self.layers):
+            check(lib.ddt_add_rmsnorm(x.data_ptr(), None if first else delta.data_ptr(),
+                                      w["ln1"].data_ptr(), T, H, self.eps, x.data_ptr(),
+                                      h.data_ptr(), st), "ddt_add_rmsnorm")
+            first = False
+            gemm(h, w["w_qkv"], qkv)
+            if side:
+                for sst in side:
+                    sst.wait_stream(main)
+            for r, ((off, n), cache, past) in enumerate(zip(segments, caches, pasts)):
+                ln = r % lanes
+                sst = side[ln] if side else main
+                with torch.cuda.stream(sst), K.WORKSPACES.lane(ln):
+                    layer = cache.layers[li]
+                    kbuf, vbuf = layer.k_buf[0], layer.v_buf[0]
+                    check(lib.ddt_qk_norm_rope_cache_table(
+                        qkv[off].data_ptr(), n, hq, hkv, d, w["qn"].data_ptr(),
+                        w["kn"].data_ptr(), self.eps, rope[off].data_ptr(), q[off].data_ptr(),
+                        kbuf.data_ptr(), vbuf.data_ptr(), kbuf.stride(0), kbuf.stride(1), past,
+                        sst.cuda_stream), "ddt_qk_norm_rope_cache_table")
+                    s_len = past + n
+                    K.tree_attention(q[off:off + n], kbuf[:, :s_len], vbuf[:, :s_len],
+                                     anc_bits[r], past, scale=self.scaling, status=status,
+                                     out=attn[off:off + n])
+                K.STATS.launches += 1
+            if side:
+                for sst in side:
+                    main.wait_stream(sst)
+            gemm(attn.view(T, hq * d), w["w_o"], o)
+            check(lib.ddt_add_rmsnorm(x.data_ptr(), o.data_ptr(), w["ln2"].data_ptr(), T, H,
+                                      self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")
+            gemm(h, w["w_gu"], gu)
+            check(lib.ddt_silu_mul(gu.data_ptr(), T, self.inter, act.data_ptr(), st),
+                  "ddt_silu_mul")
+            gemm(act, w["w_down"], delta)
+            K.STATS.launches += 3
+        check(lib.ddt_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.final_norm.data_ptr(), T,
+                                  H, self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")
+        K.STATS.launches += 1
+        logits = torch.empty((T, self.lm_head.shape[0]), dtype=x.dtype, device=dev)
+        gemm(h, self.lm_head, logits)
+        return logits
+
     def _final_hidden(self, ids, positions, cache, past_length, anc_bits, causal, status,
                       past_dev=None):
         lib = _lib.load()
