@@ -463,6 +463,7 @@ def _batched_verify(args, dev, runner, specs, mine, trees, dev_logits, host_logi
     from mdflash_b200 import kernels as K
     from mdflash_b200 import sharding as S
     from mdflash_b200.cache import TreeKVCache
+    from mdflash_b200.runner import gemm_chunk
     R = len(mine)
     records = torch.full((R, S.RECORD_LEN), -1, dtype=torch.int64, device=dev)
     if R == 0:
@@ -483,10 +484,7 @@ def _batched_verify(args, dev, runner, specs, mine, trees, dev_logits, host_logi
         src += [j * mb1 + t for t in range(n)]
         off += n
     T = off
-    chunk = args.gemm_chunk
-    if chunk <= 0:  # the fewest chunks of at most 2048 rows, each a multiple of 128
-        pieces = -(-T // 2048)
-        chunk = -(-(-(-T // pieces)) // 128) * 128
+    chunk = args.gemm_chunk if args.gemm_chunk > 0 else gemm_chunk(T)
     t_pad = -(-T // chunk) * chunk
     idx = torch.tensor(src, dtype=torch.int64, device=dev)
     ids_buf = torch.zeros(t_pad, dtype=torch.int64, device=dev)

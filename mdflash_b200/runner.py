@@ -28,6 +28,16 @@ from . import kernels as K
 from ._lib import check
 
 
+def gemm_chunk(rows: int, max_chunk: int = 2048, align: int = 128) -> int:
+    """Rows per projection GEMM of a batched verify forward over `rows` tree rows: the fewest
+    chunks of at most `max_chunk` rows, each a multiple of `align` (the rows are padded up to
+    a whole number of chunks)."""
+    if rows <= 0 or max_chunk <= 0 or align <= 0 or max_chunk % align:
+        raise ValueError("rows, max_chunk and align must be positive, max_chunk a multiple of align")
+    pieces = -(-rows // max_chunk)
+    return -(-(-(-rows // pieces)) // align) * align
+
+
 class Qwen3VerifyRunner:
     def __init__(self, model):
         cfg = model.config

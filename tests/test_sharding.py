@@ -36,6 +36,27 @@ def test_lpt_assignment_partitions_and_balances(world):
     assert S.assign_requests(costs, world) == parts
 
 
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_gemm_chunk_of_each_rank(world):
+    """The batched verify forward's projection chunk for each rank's tree rows: at most 2048
+    rows, a multiple of 128, the fewest chunks, and under 128 padding rows per chunk."""
+    from mdflash_b200.runner import gemm_chunk
+    specs = S.request_specs(64, seed=0)
+    parts = S.assign_requests([S.request_cost(s) for s in specs], world)
+    for part in parts:
+        rows = sum(specs[i].budget + 1 for i in part)
+        c = gemm_chunk(rows)
+        pieces = -(-rows // c)
+        assert c <= 2048 and c % 128 == 0
+        assert pieces == -(-rows // 2048)
+        assert pieces * c - rows < 128 * pieces
+    if world == 1:
+        assert sum(s.budget + 1 for s in specs) == 18112 and gemm_chunk(18112) == 2048
+    assert gemm_chunk(1) == 128 and gemm_chunk(2049) == 1152
+    with pytest.raises(ValueError):
+        gemm_chunk(0)
+
+
 def test_result_records_roundtrip():
     rec = S.pack_result(7, 257, [0, 3, 9], 1234, time_ns=55, rank=1)
     d = S.unpack_result(rec)
