@@ -79,6 +79,8 @@ class TreeVerifier:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._dtrees: K.TreeBatch | None = None  # one-request batch of step_device_past
         self._kvb: K.KvBatch | None = None
+        # the tree step_device_past builds into (its buffers are rewritten by every step)
+        self.tree_device_past: K.DeviceTree | None = None
 
     @torch.inference_mode()
     def step(self, draft_logits: torch.Tensor, root_token: torch.Tensor, start: int) -> StepResult:
