@@ -226,6 +226,16 @@ int ddt_advance_round(int64_t n_requests, int64_t* starts, int32_t* rounds,
                       int64_t out_stride, int64_t out_capacity, int32_t* acceptance,
                       int64_t len_stride, int64_t len_capacity, int32_t* status, void* stream);
 
+/* Row gather with a device-side count: out[i, :row_bytes] = src[idx[i], :row_bytes] for
+ * i < min(*count, max_rows) (count may be null: max_rows rows); row strides in bytes; rows,
+ * strides and both bases 16-byte aligned; an index outside [0, src_rows) gives a zero row.
+ * Replaces the accepted-row gather of the target's context features,
+ * extract_context_feature(...).index_select(1, accepted) (ddtree.py:487, model/utils.py:17-26),
+ * without reading the accepted count on the host. */
+int ddt_gather_rows(const void* src, int64_t src_rows, int64_t src_row_stride,
+                    const int64_t* idx, const int32_t* count, int64_t max_rows, void* out,
+                    int64_t out_row_stride, int64_t row_bytes, void* stream);
+
 /* ---- tree attention -----------------------------------------------------
  * q: [n_nodes, q_heads, head_dim] bf16 at element strides (q_node_stride, q_head_stride);
  * k, v: [kv_heads, past_length + n_nodes, head_dim] bf16 at (kv_head_stride,

@@ -53,6 +53,7 @@ SIGNATURES = {
     "ddt_tree_attn_workspace_bytes": (_S, [_I, _I, _I, _I]),
     "ddt_tree_attn": (_i, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _i,
                            _F, _I, _P, _S, _P, _P]),
+    "ddt_gather_rows": (_i, [_P, _I, _I, _P, _P, _I, _P, _I, _I, _P]),
     "ddt_advance_round": (_i, [_I, _P, _P, _P, _P, _I, _P, _I, _I, _P, _P, _P, _I, _I, _P, _I, _I,
                                _P, _P]),
     "ddt_tree_attn_device_past": (_i, [_P, _I, _I, _P, _P, _I, _I, _P, _I, _I, _I, _I, _P, _I, _I,

@@ -501,6 +501,26 @@ __global__ void advance_round_kernel(int64_t* __restrict__ starts, int32_t* __re
   }
 }
 
+// out[i] = src[idx[i]] for i < *count (count read on the device, clamped to max_rows), rows of
+// row_vecs 16-byte vectors at the given strides; one warp per output row.  An index outside
+// [0, src_rows) writes zeros.
+__global__ void gather_rows_kernel(const uint4* __restrict__ src, int64_t src_stride_vec,
+                                   int64_t src_rows, const int64_t* __restrict__ idx,
+                                   const int32_t* __restrict__ count, int max_rows,
+                                   uint4* __restrict__ out, int64_t out_stride_vec,
+                                   int64_t row_vecs) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  int n = count ? *count : max_rows;
+  n = n < 0 ? 0 : (n > max_rows ? max_rows : n);
+  if (row >= n) return;
+  const int64_t s = idx[row];
+  const bool ok = s >= 0 && s < src_rows;
+  const uint4* sp = src + (ok ? s : 0) * src_stride_vec;
+  uint4* op = out + static_cast<int64_t>(row) * out_stride_vec;
+  for (int64_t v = lane; v < row_vecs; v += 32) op[v] = ok ? __ldg(sp + v) : make_uint4(0, 0, 0, 0);
+}
+
 }  // namespace accept
 }  // namespace ddt
 
@@ -633,5 +653,24 @@ extern "C" int ddt_advance_round(int64_t n_requests, int64_t* starts, int32_t* r
       starts, rounds, n_accepted, accepted, acc_stride, verify_ids, ids_stride, next_token,
       root_tokens, output_ids, out_stride, out_capacity, acceptance, len_stride, len_capacity,
       static_cast<int>(max_nodes), status);
+  return launch_status();
+}
+
+extern "C" int ddt_gather_rows(const void* src, int64_t src_rows, int64_t src_row_stride,
+                               const int64_t* idx, const int32_t* count, int64_t max_rows,
+                               void* out, int64_t out_row_stride, int64_t row_bytes,
+                               void* stream) {
+  if (!src || !idx || !out || src_rows < 0 || max_rows < 0 || row_bytes < 0) return DDT_ERR_INVALID;
+  if (row_bytes % 16 || src_row_stride % 16 || out_row_stride % 16 || !aligned(src, 16) ||
+      !aligned(out, 16))
+    return DDT_ERR_ALIGN;
+  if (src_row_stride < row_bytes || out_row_stride < row_bytes) return DDT_ERR_INVALID;
+  if (max_rows == 0 || row_bytes == 0) return DDT_OK;
+  if (max_rows > 0x7fffffffLL) return DDT_ERR_CAPACITY;
+  constexpr int kWarps = 4;
+  accept::gather_rows_kernel<<<static_cast<unsigned>((max_rows + kWarps - 1) / kWarps),
+                               kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), src_row_stride / 16, src_rows, idx, count,
+      static_cast<int>(max_rows), static_cast<uint4*>(out), out_row_stride / 16, row_bytes / 16);
   return launch_status();
 }

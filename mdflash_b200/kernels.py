@@ -563,6 +563,33 @@ def advance_round(starts: torch.Tensor, rounds: torch.Tensor, n_accepted: torch.
     STATS.launches += 1
 
 
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, count: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """ddt_gather_rows: out[i] = src[idx[i]] for i < count (a device i32 [1], read on the
+    device; None: every index), rows of src [rows, ...] (the row contiguous); the rows of out
+    at or beyond the count keep their contents."""
+    dev = _require_cuda(src, idx)
+    if idx.dtype != torch.int64 or idx.dim() != 1 or not idx.is_contiguous():
+        raise ValueError("idx must be a contiguous i64 vector")
+    if count is not None and (count.dtype != torch.int32 or count.numel() != 1):
+        raise ValueError("count must be an i32 [1]")
+    rows = src.shape[0]
+    row = src[0].numel() if rows else 0
+    if rows and src[0].is_contiguous() is False:
+        raise ValueError("src rows must be contiguous")
+    if out is None:
+        out = torch.zeros((idx.numel(),) + tuple(src.shape[1:]), dtype=src.dtype, device=dev)
+    if out.shape[1:] != src.shape[1:] or out.dtype != src.dtype or out.shape[0] < idx.numel():
+        raise ValueError("out must match src's row shape and dtype, with a row per index")
+    es = src.element_size()
+    check(_lib.load().ddt_gather_rows(
+        src.data_ptr(), rows, src.stride(0) * es, idx.data_ptr(),
+        count.data_ptr() if count is not None else None, idx.numel(), out.data_ptr(),
+        out.stride(0) * es, row * es, _stream(dev)), "ddt_gather_rows")
+    STATS.launches += 1
+    return out
+
+
 def compact_kv(keep, kv: KvTable, past_length: int) -> None:
     """Moves rows past_length + keep[j] -> past_length + j in every table tensor.  A host
     list is validated (strictly increasing, inside the cache); a device tensor is trusted."""

@@ -78,7 +78,9 @@ class Qwen3VerifyRunner:
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, cache, past_length: int,
                 anc_bits: torch.Tensor | None, causal: bool = False,
                 status: torch.Tensor | None = None,
-                past_dev: torch.Tensor | None = None) -> torch.Tensor:
+                past_dev: torch.Tensor | None = None,
+                features: torch.Tensor | None = None,
+                feature_layers: list[int] | None = None) -> torch.Tensor:
         """ids, positions: i64 [N] (device).  Writes the N new K/V rows into `cache`
         (a TreeKVCache) at [past_length, past_length + N) and returns logits [N, V] (bf16).
         Tree mode attends with anc_bits; causal=True attends causally (prefill).  Attention
@@ -86,21 +88,29 @@ class Qwen3VerifyRunner:
 
         past_dev (i64 [1], device): the prefix length is read from it by the kernels, so that
         a recorded forward serves every prefix length up to past_length (the cache must hold
-        past_length + N rows); the cache's host-side length is then left to the caller."""
+        past_length + N rows); the cache's host-side length is then left to the caller.
+
+        features [N, len(feature_layers) * hidden] (bf16): receives the target's context
+        features of the drafter, extract_context_feature(output.hidden_states, layer_ids)
+        (model/utils.py:17-26): for layer id i, hidden_states[i + 1] in transformers' sense,
+        i.e. the residual stream after decoder layer i, or the final normed state for the
+        last layer."""
         h = self._final_hidden(ids, positions, cache, past_length, anc_bits, causal, status,
-                               past_dev)
+                               past_dev, features, feature_layers)
         return torch.matmul(h, self.lm_head.t())
 
     def forward_posterior(self, ids: torch.Tensor, positions: torch.Tensor, cache,
                           past_length: int, anc_bits: torch.Tensor | None,
                           out: torch.Tensor | None = None,
                           status: torch.Tensor | None = None,
-                          past_dev: torch.Tensor | None = None) -> torch.Tensor:
+                          past_dev: torch.Tensor | None = None,
+                          features: torch.Tensor | None = None,
+                          feature_layers: list[int] | None = None) -> torch.Tensor:
         """The greedy posterior (i64 [N]) of the verify rows without the [N, V] logits: the
         final hidden states go through the fused lm_head -> argmax kernel
-        (ddt_lm_head_argmax).  Same cache effects (and past_dev) as forward."""
+        (ddt_lm_head_argmax).  Same cache effects (and past_dev, features) as forward."""
         h = self._final_hidden(ids, positions, cache, past_length, anc_bits, False, status,
-                               past_dev)
+                               past_dev, features, feature_layers)
         return K.lm_head_argmax(h, self.lm_head, out=out)
 
     def forward_batch(self, ids: torch.Tensor, positions: torch.Tensor,
@@ -192,12 +202,30 @@ class Qwen3VerifyRunner:
         gemm(h, self.lm_head, logits)
         return logits
 
+    def _feature_slots(self, features, feature_layers, n):
+        """hidden-state index (transformers' hidden_states[i], i = layer id + 1) -> the
+        column slices of `features` it fills."""
+        if features is None:
+            return {}
+        L = len(self.layers)
+        H = self.hidden
+        if not feature_layers or features.shape != (n, len(feature_layers) * H) or \
+                features.dtype != torch.bfloat16:
+            raise ValueError("features must be bf16 [N, len(feature_layers) * hidden]")
+        slots = {}
+        for j, lid in enumerate(feature_layers):
+            if not -1 <= lid < L:
+                raise ValueError(f"feature layer {lid} outside [-1, {L})")
+            slots.setdefault(lid + 1, []).append(features[:, j * H:(j + 1) * H])
+        return slots
+
     def _final_hidden(self, ids, positions, cache, past_length, anc_bits, causal, status,
-                      past_dev=None):
+                      past_dev=None, features=None, feature_layers=None):
         lib = _lib.load()
         st = self._stream()
         n = ids.numel()
         H, hq, hkv, d = self.hidden, self.q_heads, self.kv_heads, self.head_dim
+        slots = self._feature_slots(features, feature_layers, n)
         x = torch.nn.functional.embedding(ids.view(-1), self.embed)  # [N, H] bf16
         h = torch.empty_like(x)
         q = torch.empty((n, hq, d), dtype=x.dtype, device=x.device)
@@ -213,6 +241,8 @@ class Qwen3VerifyRunner:
             check(lib.ddt_add_rmsnorm(x.data_ptr(), delta.data_ptr() if delta is not None else None,
                                       w["ln1"].data_ptr(), n, H, self.eps, x.data_ptr(),
                                       h.data_ptr(), st), "ddt_add_rmsnorm")
+            for dst in slots.get(li, ()):  # the residual stream entering layer li
+                dst.copy_(x)
             qkv = torch.matmul(h, w["w_qkv"].t())
             if past_dev is None:
                 check(lib.ddt_qk_norm_rope_cache_table(
@@ -242,6 +272,8 @@ class Qwen3VerifyRunner:
         check(lib.ddt_add_rmsnorm(x.data_ptr(), delta.data_ptr(), self.final_norm.data_ptr(), n, H,
                                   self.eps, x.data_ptr(), h.data_ptr(), st), "ddt_add_rmsnorm")
         K.STATS.launches += 1
+        for dst in slots.get(len(self.layers), ()):  # the last entry: the final normed state
+            dst.copy_(h)
         if past_dev is not None:
             return h
         for layer in cache.layers:

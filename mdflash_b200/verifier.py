@@ -38,13 +38,17 @@ class StepResult:
     posterior: torch.Tensor     # i64 [n_nodes], device
     status: torch.Tensor        # i32 [1], device: non-zero if an attention wait timed out
     logits: torch.Tensor | None = None
+    # the drafter's context features of the accepted rows (first n_accepted rows valid),
+    # [budget + 1, len(feature_layers) * hidden] bf16, when the verifier was given layers
+    target_hidden: torch.Tensor | None = None
 
 
 class TreeVerifier:
     def __init__(self, target: torch.nn.Module, cache: TreeKVCache, budget: int, depths: int,
                  vocab: int, device: torch.device | str = "cuda", keep_logits: bool = False,
                  fused: bool = False, runner=None, fused_head: bool = False,
-                 posterior: torch.Tensor | None = None, walk: bool = True):
+                 posterior: torch.Tensor | None = None, walk: bool = True,
+                 feature_layers: list[int] | None = None):
         """fused=False runs the transformers model with attn_implementation="ddtree_tree";
         fused=True runs its weights through Qwen3VerifyRunner (fused elementwise stages); a
         runner can be shared between verifiers of the same model (runner=...).  With a
@@ -53,7 +57,10 @@ class TreeVerifier:
         keep_logits).  posterior: an i64 buffer (>= budget + 1) to write the greedy posterior
         into, e.g. one row of a batch; walk=False stops the step after the posterior (the
         caller walks and compacts, for instance all requests at once with
-        K.accept_compact_batched)."""
+        K.accept_compact_batched).  feature_layers (fused runner, with the walk): the step also
+        returns the drafter's context features of the accepted rows, target_hidden =
+        extract_context_feature(hidden_states, feature_layers).index_select(1, accepted)
+        (ddtree.py:487), gathered on the device (ddt_gather_rows)."""
         self.target = target
         self.runner = runner
         if fused and runner is None:
@@ -81,6 +88,14 @@ class TreeVerifier:
         self._kvb: K.KvBatch | None = None
         # the tree step_device_past builds into (its buffers are rewritten by every step)
         self.tree_device_past: K.DeviceTree | None = None
+        self.feature_layers = list(feature_layers) if feature_layers else None
+        self.features = self.target_hidden = None
+        if self.feature_layers:
+            if self.runner is None or not self.walk:
+                raise ValueError("feature_layers needs the fused runner and the walk")
+            width = len(self.feature_layers) * self.runner.hidden
+            self.features = torch.zeros((n_cap, width), dtype=torch.bfloat16, device=self.device)
+            self.target_hidden = torch.zeros_like(self.features)
 
     @torch.inference_mode()
     def step(self, draft_logits: torch.Tensor, root_token: torch.Tensor, start: int) -> StepResult:
@@ -105,12 +120,13 @@ class TreeVerifier:
         if self.runner is not None and self.fused_head:
             post = self.runner.forward_posterior(tree.verify_ids[:n], tree.verify_pos[:n],
                                                  self.cache, start, tree.anc_bits,
-                                                 out=self.posterior[:n], status=self.status)
+                                                 out=self.posterior[:n], status=self.status,
+                                                 **self._feature_args(n))
         else:
             if self.runner is not None:
                 logits = self.runner.forward(tree.verify_ids[:n], tree.verify_pos[:n],
                                              self.cache, start, tree.anc_bits,
-                                             status=self.status)
+                                             status=self.status, **self._feature_args(n))
             else:
                 with A.tree_verify(tree, start, n, status=self.status):
                     out = self.target(ids, position_ids=pos, past_key_values=self.cache,
@@ -121,7 +137,21 @@ class TreeVerifier:
             K.accept_compact(post, tree, self.cache.kv_table(), start, accepted=self.accepted,
                              n_accepted=self.n_accepted, next_token=self.next_token, n_nodes=n)
         return StepResult(n, self.accepted, self.n_accepted, self.next_token, post, self.status,
-                          logits if self.keep_logits and logits is not None else None)
+                          logits if self.keep_logits and logits is not None else None,
+                          self._gather_features(n))
+
+    def _feature_args(self, n: int) -> dict:
+        if not self.feature_layers:
+            return {}
+        return {"features": self.features[:n], "feature_layers": self.feature_layers}
+
+    def _gather_features(self, n: int):
+        """The accepted rows' context features (after the walk), or None."""
+        if not self.feature_layers:
+            return None
+        K.gather_rows(self.features[:n], self.accepted, count=self.n_accepted,
+                      out=self.target_hidden)
+        return self.target_hidden
 
     @torch.inference_mode()
     def step_device_past(self, draft_logits: torch.Tensor, root_token: torch.Tensor,
@@ -159,11 +189,11 @@ class TreeVerifier:
             post = self.runner.forward_posterior(tree.verify_ids[:n], tree.verify_pos[:n],
                                                  self.cache, max_past, tree.anc_bits,
                                                  out=self.posterior[:n], status=self.status,
-                                                 past_dev=past_dev)
+                                                 past_dev=past_dev, **self._feature_args(n))
         else:
             logits = self.runner.forward(tree.verify_ids[:n], tree.verify_pos[:n], self.cache,
                                          max_past, tree.anc_bits, status=self.status,
-                                         past_dev=past_dev)
+                                         past_dev=past_dev, **self._feature_args(n))
             post = K.argmax(logits, out=self.posterior[:n])
         if self.walk:
             K.accept_compact_batched(self.posterior[:n_cap].view(1, n_cap), trees, self._kvb,
@@ -172,7 +202,8 @@ class TreeVerifier:
                                      status=self.status)
         self.tree_device_past = tree
         return StepResult(n, self.accepted, self.n_accepted, self.next_token, post, self.status,
-                          logits if self.keep_logits and logits is not None else None)
+                          logits if self.keep_logits and logits is not None else None,
+                          self._gather_features(n) if self.walk else None)
 
     def check(self) -> None:
         """Raises DDTreeError (DDT_ERR_TIMEOUT) if an attention launch of the steps since the

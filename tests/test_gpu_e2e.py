@@ -235,3 +235,43 @@ def test_follow_verified_tree_on_a_foreign_tree(setup, cuda_device):
         post = gin.follow_posterior(spec, node_ids.numpy(), par)
         got = D.follow_verified_tree(child_maps, torch.from_numpy(post).to(cuda_device)[None])
         assert got == oracle.follow_verified_tree(child_maps, post), kind
+
+
+def test_tree_verifier_context_features(setup, cuda_device):
+    """feature_layers: the step returns the drafter's context features of the accepted rows,
+    extract_context_feature(output.hidden_states, layer_ids).index_select(1, accepted)
+    (model/utils.py:17-26, ddtree.py:487), here with layer ids -1 (the embeddings), 0 (the
+    residual stream after layer 0) and 1 (the last layer: the final normed state).  Against
+    transformers' own hidden_states of the same tree on the same prefix (through the plug-in),
+    within the bf16 tolerance; the gathered rows are exactly the accepted rows."""
+    from mdflash_b200.runner import Qwen3VerifyRunner
+    s = setup
+    dev = cuda_device
+    model = s["model"]
+    model.config._attn_implementation = A.ATTN_IMPLEMENTATION
+    layers = [-1, 0, 1]
+    runner = Qwen3VerifyRunner(model)
+    caches = [TreeKVCache(2, P + BUDGET + 8).allocate(2, 128, torch.bfloat16, dev)
+              for _ in range(2)]
+    with torch.inference_mode():
+        for c in caches:
+            runner.forward(s["ids"][0], torch.arange(P, device=dev), c, 0, None, causal=True)
+        ver = TreeVerifier(model, caches[0], BUDGET, DEPTHS, V, dev, fused=True, runner=runner,
+                           feature_layers=layers)
+        res = ver.step(s["logits"].to(dev), s["root"].view(1), P)
+        tree, n = ver.tree, res.n_nodes
+        with A.tree_verify(tree, P, n, status=ver.status):
+            out = model(tree.verify_ids[:n].view(1, n),
+                        position_ids=tree.verify_pos[:n].view(1, n),
+                        past_key_values=caches[1], use_cache=True, output_hidden_states=True)
+    torch.cuda.synchronize()
+    ver.check()
+    H = model.config.hidden_size
+    ref = torch.cat([out.hidden_states[lid + 1][0] for lid in layers], dim=-1)
+    for j, lid in enumerate(layers):
+        a, b = ver.features[:n, j * H:(j + 1) * H], ref[:, j * H:(j + 1) * H]
+        print(f"[features] layer {lid}: rel {_rel(a, b):.2e}, elem {elem_rel_err(a, b):.2e}")
+        assert _rel(a, b) <= TOL and elem_rel_err(a, b) <= TOL
+    k = int(res.n_accepted.item())
+    acc = res.accepted[:k]
+    assert torch.equal(res.target_hidden[:k], ver.features[:n].index_select(0, acc))

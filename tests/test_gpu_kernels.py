@@ -358,3 +358,22 @@ def test_mask_to_bits_roundtrip(cuda_device):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32),
                                   oracle.ancestor_bits(parents))
+
+
+def test_gather_rows_device_count(cuda_device):
+    """ddt_gather_rows: rows idx[i] for i < the device count, out-of-range indices give zero
+    rows, rows past the count keep their contents."""
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    src = torch.randn((40, 3, 64), generator=g, device=cuda_device).to(torch.bfloat16)
+    idx = torch.tensor([5, 0, 39, 7, 40, -1, 2], dtype=torch.int64, device=cuda_device)
+    out = torch.full((7, 3, 64), 9.0, dtype=torch.bfloat16, device=cuda_device)
+    count = torch.tensor([6], dtype=torch.int32, device=cuda_device)
+    K.gather_rows(src, idx, count=count, out=out)
+    torch.cuda.synchronize()
+    for i, j in enumerate([5, 0, 39, 7]):
+        assert torch.equal(out[i], src[j])
+    assert bool((out[4] == 0).all()) and bool((out[5] == 0).all())
+    assert bool((out[6] == 9.0).all())
+    full = K.gather_rows(src, idx[:4])
+    torch.cuda.synchronize()
+    assert torch.equal(full, src[idx[:4]])
