@@ -9,8 +9,9 @@ seeded per request (15 depths of N(0,1)*3).  A "step" verifies every request onc
 as one CUDA graph per rank: one batched tree-build launch for all of the rank's requests,
 one 36-layer verify forward over all their tree rows (the projections and lm_head shared,
 in GEMMs of at most 2048 rows; each request's K/V writes and tree attention on its own
-cache, spread over 4 streams, --lanes), one argmax over all rows, then one batched accept
-walk + KV compaction of all the requests; then the result records are all-gathered.
+cache, unsplit, spread over 8 streams, --lanes), one argmax over all rows, then one
+batched accept walk + KV compaction of all the requests; then the result records are
+all-gathered.
 (--verify-batch per-request: one graph per request instead, the projections run per
 request.)
 Requests are assigned to ranks by longest-processing-time first; there is no other
@@ -109,11 +110,11 @@ def parse_args():
                     help="requests workload: one batched walk + compaction of all of the rank's "
                          "requests after their verify replays (default), or each request's walk "
                          "and compaction inside its graph")
-    ap.add_argument("--lanes", type=int, default=4,
-                    help="requests workload: replay the per-request graphs on this many streams "
-                         "at once (requests split over the lanes by predicted cost; each lane "
-                         "has its own graph "
-                         "pool and scratch buffers)")
+    ap.add_argument("--lanes", type=int, default=0,
+                    help="requests workload: streams that run requests at once: the batched "
+                         "forward's per-request attention (default 8), or the per-request "
+                         "graphs' replays (default 4; requests split over the lanes by "
+                         "predicted cost, each lane with its own graph pool and scratch buffers)")
     ap.add_argument("--verify-batch", choices=["batched", "per-request"], default="batched",
                     help="requests workload: one verify forward over all of a rank's requests "
                          "(shared projections in fixed-size GEMM chunks, per-request K/V writes "
@@ -124,6 +125,10 @@ def parse_args():
                          "that many (the rows padded up), so that a row's result does not "
                          "depend on the other requests; 0 (default): the fewest chunks of at "
                          "most 2048 rows, each a multiple of 128, for the rank's rows")
+    ap.add_argument("--batch-attn-splits", type=int, default=1,
+                    help="--verify-batch batched: key splits of each request's attention "
+                         "launch (1, default: one CTA per work unit and no merge, the lanes "
+                         "filling the GPU with other requests' launches; 0: the library's plan)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="splitkv workload: partials travel over NVLink peer memory "
                          "(PeerExchange, default) or in an NCCL all-gather")
@@ -503,7 +508,8 @@ def _batched_verify(args, dev, runner, specs, mine, trees, dev_logits, host_logi
         torch.index_select(trees.verify_ids.view(-1), 0, idx, out=ids_buf[:T])
         torch.index_select(trees.verify_pos.view(-1), 0, idx, out=pos_buf[:T])
         logits = runner.forward_batch(ids_buf, pos_buf, segments, caches, pasts, ancs,
-                                      status=status, chunk=chunk, lanes=lanes)
+                                      status=status, chunk=chunk, lanes=lanes,
+                                      kv_splits=args.batch_attn_splits)
         K.argmax(logits[:T], out=post_cat)
         posteriors.view(-1).index_copy_(0, idx, post_cat)
         K.accept_compact_batched(posteriors, trees, kvb, past_dev, b_acc, b_n, b_next,
@@ -574,7 +580,7 @@ def run_requests(args):
     specs = S.request_specs(args.requests, seed=0)
     assignment = S.assign_requests([S.request_cost(s) for s in specs], world)
     mine = assignment[rank]
-    lanes = max(1, args.lanes)
+    lanes = args.lanes if args.lanes > 0 else (8 if args.verify_batch == "batched" else 4)
     pools = [torch.cuda.graph_pool_handle() for _ in range(lanes)]
     streams = [torch.cuda.Stream(dev) for _ in range(lanes)] if lanes > 1 else None
     cap_streams = [torch.cuda.Stream(dev) for _ in range(lanes)] if lanes > 1 else None
@@ -765,7 +771,8 @@ def run_requests(args):
         "gpu_launches": int(sums[1].item()),
         "tokens_per_step": tokens,
         # digest of the gathered result records (accepted paths, next tokens) without their
-        # rank field: the same at every GPU count and --lanes / --tree-build setting, since
+        # rank field: the same at every GPU count and --lanes / --tree-build setting (for one
+        # --verify-batch / --batch-attn-splits choice: their attention plans round apart), since
         # every request's step is deterministic
         "records_digest": hashlib.sha1(
             allrec.index_fill(1, torch.tensor([1]), 0).numpy().tobytes()).hexdigest()[:16],

@@ -116,14 +116,16 @@ class Qwen3VerifyRunner:
     def forward_batch(self, ids: torch.Tensor, positions: torch.Tensor,
                       segments: list[tuple[int, int]], caches: list, pasts: list[int],
                       anc_bits: list[torch.Tensor], status: torch.Tensor | None = None,
-                      chunk: int = 2048, lanes: int = 1) -> torch.Tensor:
+                      chunk: int = 2048, lanes: int = 1, kv_splits: int = 0) -> torch.Tensor:
         """The verify forward of many requests at once.  ids / positions: i64 [T_pad] (device;
         request r's tree rows at segments[r] = (offset, rows); the rows after the last segment
         are padding, T_pad a multiple of `chunk`).  Request r's K/V rows go into caches[r] at
         pasts[r], and its rows attend to that cache under anc_bits[r].  The norms and the
         projections run over all rows, the projections in GEMMs of exactly `chunk` rows, so
         that a row's result does not depend on which other requests share the batch; the
-        K/V writes and the attention run per request, spread over `lanes` streams.  Returns
+        K/V writes and the attention run per request, spread over `lanes` streams (kv_splits:
+        the attention's key splits per request, 0 lets the library choose; 1 runs one CTA per
+        work unit and no merge, leaving the GPU to the other lanes' launches).  Returns
         logits [T_pad, V] (bf16; padding rows are finite and meaningless)."""
         lib = _lib.load()
         T = ids.numel()
@@ -182,7 +184,7 @@ class Qwen3VerifyRunner:
                     s_len = past + n
                     K.tree_attention(q[off:off + n], kbuf[:, :s_len], vbuf[:, :s_len],
                                      anc_bits[r], past, scale=self.scaling, status=status,
-                                     out=attn[off:off + n])
+                                     out=attn[off:off + n], kv_splits=kv_splits)
                 K.STATS.launches += 1
             if side:
                 for sst in side:
